@@ -1,0 +1,592 @@
+"""Benchmark of the tensor-op hot path on B200.
+
+Headline workload (one "step"): the Mistral-7B-shaped elementwise/broadcast
+config -- h = a + b (a, b [8192, 4096] f32), y = h * s (s [4096], row
+broadcast), o = silu(gate) * up (gate, up [8192, 14336] f32) -- three kernels
+of liboxide_b200.so per step.  Metric: achieved HBM GB/s = algorithmic bytes
+(each input read once, each output written once) / time.
+
+  value     device time (CUDA events), inputs resident in HBM; inputs are
+            1.2 GB per rank, larger than L2, so no flush is needed.
+  e2e       the same step through the host-buffer C ABI (oxide_pipe_*),
+            pinned host inputs copied in and outputs copied back every step.
+  roofline  the dominant kernel (silu_mul): its bytes per launch / its mean
+            CUDA-event launch time, against the measured HBM copy bandwidth.
+  per_op    every other op at its config's shape, timed by CUDA-graph replay
+            over rotating buffer sets larger than L2 (C1, C3, C4) and the full
+            bf16 decoder-layer chain at 64 x 2048 tokens (C5).
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own batch (weak
+scaling, no data-path collective); time = max over ranks.
+
+`--impl reference` times the reference's CPU arithmetic (the oracle restatement
+of src/ops, compiled C) with all host threads on the same step and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mistralrs-oxide_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+METRIC = "achieved HBM GB/s (% of B200 peak) per op at Mistral-7B shapes, 1/2/4/8 GPU"
+UNIT = "GB/s"
+WORKLOAD = "C2 elementwise+broadcast f32: add [8192x4096] + rowbcast mul [4096] + silu*mul [8192x14336]"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(kernel: str):
+    """dram bytes per launch recorded from an ncu capture in profiles/ (or None)."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    try:
+        for line in open(path):
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == kernel:
+                return int(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", gpu_id, "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sms, mx, reasons, samples = [], None, set(), 0
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sms.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            samples += 1
+            for nm, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": samples}
+
+
+# --------------------------------------------------------------------- dist
+def dist_init(n_gpus: int):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------- CPU arms
+_CPU_CACHE: dict = {}
+
+
+def cpu_step_sample(rows: int, threads: int):
+    """One C2 step on `rows` rows through the oracle with preallocated outputs;
+    returns (seconds, algorithmic bytes)."""
+    from oracle import oracle as orc
+    from oxide_b200.workloads import C2
+
+    if rows not in _CPU_CACHE:
+        _CPU_CACHE.clear()
+        cfg = C2(rows=rows)
+        a, b, s, gate, up = cfg.inputs()
+        outs = (np.empty(a.size, np.float32), np.empty(a.size, np.float32),
+                np.empty(gate.size, np.float32))
+        for o in outs:
+            o.fill(0.0)  # fault the pages in before timing
+        _CPU_CACHE[rows] = (cfg, a, b, s, gate, up, outs)
+    cfg, a, b, s, gate, up, (h, y, o) = _CPU_CACHE[rows]
+    t0 = time.perf_counter()
+    orc.binary(0, a, b, threads=threads, out=h)
+    orc.binary(2, h, s, n=h.size, threads=threads, out=y)
+    orc.silu_mul(gate, up, threads=threads, out=o)
+    return time.perf_counter() - t0, cfg.bytes()
+
+
+def cpu_baseline(budget_s: float = 12.0):
+    """Single-thread oracle port (the reference is single-threaded) on a
+    bounded sample of the C2 step, repeated for about `budget_s` seconds."""
+    rows = 1024
+    times, nbytes = [], 0
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 2:
+        dt, nbytes = cpu_step_sample(rows, 1)
+        times.append(dt)
+    gbs = nbytes / statistics.median(times) / 1e9
+    return {"value": round(gbs, 3), "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"C2 step on {rows} of 8192 rows, single thread, {len(times)} reps, median"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    threads = orc.max_threads()
+    rows = 8192
+    dt, _ = cpu_step_sample(rows, threads)  # size the sample: <= ~3 s per step
+    while dt > 3.0 and rows > 256:
+        rows //= 2
+        dt, _ = cpu_step_sample(rows, threads)
+    for _ in range(max(0, args.warmup - 1)):
+        cpu_step_sample(rows, threads)
+    times, nbytes = [], 0
+    for _ in range(args.steps):
+        dt, nbytes = cpu_step_sample(rows, threads)
+        times.append(dt)
+    total = sum(times)
+    value = nbytes * args.steps / total / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample_rows": rows},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
+                         "kind": "port",
+                         "sample": f"C2 step on {rows} of 8192 rows per step, {threads} OpenMP threads"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- GPU pieces
+def graph_time_per_launch(fn_list, reps=20):
+    """Capture fn_list (each issues launches on the current stream) in one CUDA
+    graph, replay it `reps` times, return seconds per fn."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for fn in fn_list:  # warm-up outside capture (occupancy queries, lazy init)
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for fn in fn_list:
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    secs = e0.elapsed_time(e1) / 1e3 / reps / len(fn_list)
+    del g
+    return secs
+
+
+def rotating_sets(bytes_per_set: int):
+    """Enough buffer sets to cycle through more than twice the L2 size."""
+    import torch
+
+    l2 = getattr(torch.cuda.get_device_properties(0), "L2_cache_size", 126 << 20)
+    return max(2, math.ceil(2.5 * l2 / max(1, bytes_per_set)))
+
+
+def per_op_lines(peak):
+    """Per-op GB/s at the C1/C3/C4 shapes (CUDA-graph replay, rotating inputs)."""
+    import torch
+
+    from oxide_b200 import ops
+    from oxide_b200.workloads import C1, C3, C4
+
+    dev = torch.device("cuda")
+    res = {}
+
+    def rec(name, nbytes, secs, shape):
+        gbs = nbytes / secs / 1e9
+        res[name] = {"gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4),
+                     "us_per_launch": round(secs * 1e6, 2), "bytes": nbytes, "shape": shape}
+
+    # C1 RMSNorm f32
+    c1 = C1()
+    x, w = c1.inputs()
+    nset = rotating_sets(c1.bytes())
+    xs = [torch.from_numpy(x).to(dev) for _ in range(nset)]
+    outs = [torch.empty_like(xs[0]) for _ in range(nset)]
+    tw = torch.from_numpy(w).to(dev)
+    fns = [(lambda i=i: ops.rms_norm(xs[i], tw, c1.eps, out=outs[i])) for i in range(nset)]
+    rec("rms_norm_f32[C1]", c1.bytes(), graph_time_per_launch(fns), "[2048,4096]")
+    del xs, outs
+
+    # C3 masked decode softmax f32 + argmax
+    c3 = C3()
+    scores, lens, logits = c3.inputs()
+    sb = c3.bytes_softmax(lens)
+    nset = rotating_sets(c3.bytes_softmax_full())
+    ss = [torch.from_numpy(scores).to(dev) for _ in range(nset)]
+    po = [torch.empty_like(ss[0]) for _ in range(nset)]
+    tl = torch.from_numpy(lens).to(dev)
+    fns = [(lambda i=i: ops.scale_mask_softmax(ss[i], c3.scale, lens=tl, rows_per_len=c3.heads,
+                                               out=po[i])) for i in range(nset)]
+    rec("scale_mask_softmax_f32[C3]", sb, graph_time_per_launch(fns), "[8,32,1,32768] lens-masked")
+    del ss, po
+    nset = rotating_sets(c3.bytes_argmax())
+    ls = [torch.from_numpy(logits).to(dev) for _ in range(nset)]
+    idx = torch.empty(c3.logit_rows, dtype=torch.int32, device=dev)
+    from oxide_b200._lib import call
+
+    fns = [(lambda i=i: call("oxide_argmax_rows_f32", ls[i].data_ptr(), c3.logit_rows, c3.vocab,
+                             idx.data_ptr(), torch.cuda.current_stream().cuda_stream))
+           for i in range(nset)]
+    rec("argmax_f32[C3]", c3.bytes_argmax(), graph_time_per_launch(fns), "[64,32000]")
+    del ls
+
+    # C4 RoPE bf16
+    c4 = C4()
+    q, k = c4.inputs()
+    cos, sin = ops.rope_table(c4.theta, c4.head_dim, c4.tokens)
+    tc, tsn = cos.to(dev), sin.to(dev)
+    nset = rotating_sets(c4.bytes())
+    qs = [torch.from_numpy(q.view(np.int16)).to(dev).view(torch.bfloat16) for _ in range(nset)]
+    ks = [torch.from_numpy(k.view(np.int16)).to(dev).view(torch.bfloat16) for _ in range(nset)]
+    qo = [torch.empty_like(qs[0]) for _ in range(nset)]
+    ko = [torch.empty_like(ks[0]) for _ in range(nset)]
+    fns = [(lambda i=i: ops.rope(qs[i], ks[i], tc, tsn, q_out=qo[i], k_out=ko[i]))
+           for i in range(nset)]
+    rec("rope_bf16[C4]", c4.bytes(), graph_time_per_launch(fns), "q[4096,32,128] k[4096,8,128]")
+    del qs, ks, qo, ko
+    torch.cuda.empty_cache()
+    return res
+
+
+def chain_c5(peak, world, steps=3, warmup=2):
+    """Full bf16 non-GEMM chain of a decoder layer at 64 x 2048 tokens (C5)."""
+    import torch
+
+    from oxide_b200 import ops
+    from oxide_b200.workloads import C5
+
+    c = C5()
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev)
+    g.manual_seed(c.seed)
+    R, H, I, T = c.rows, c.hidden, c.inter, c.seq_len
+    bf = torch.bfloat16
+
+    def randn(*shape):
+        return torch.randn(shape, generator=g, device=dev, dtype=bf)
+
+    x, r = randn(R, H), randn(R, H)
+    w = torch.ones(H, dtype=bf, device=dev)
+    q, k = randn(R, c.q_heads, c.head_dim), randn(R, c.k_heads, c.head_dim)
+    scores = randn(c.seqs * c.q_heads * T, T)
+    probs = torch.empty_like(scores)
+    gate, up = randn(R, I), randn(R, I)
+    act = torch.empty_like(gate)
+    mlp = randn(R, H)
+    logits = randn(R, c.vocab)
+    h, y, h2, yf = (torch.empty_like(x) for _ in range(4))
+    cos, sin = ops.rope_table(c.theta, c.head_dim, T)
+    cos, sin = cos.to(dev), sin.to(dev)
+    pos = (torch.arange(R, device=dev, dtype=torch.int32) % T).contiguous()
+    ws = torch.empty(ops.workspace_bytes(R * H), dtype=torch.uint8, device=dev)
+    ssq = torch.empty((), dtype=torch.float64, device=dev)
+    scale = 1.0 / math.sqrt(c.head_dim)
+    names = ["add_rms_norm", "rope", "softmax", "silu_mul", "add", "rms_norm", "argmax", "sumsq"]
+
+    def step(ev=None):
+        def mark(i):
+            if ev is not None:
+                ev[i].record()
+        mark(0)
+        ops.add_rms_norm(x, r, w, c.eps, h=h, y=y)
+        mark(1)
+        ops.rope(q, k, cos, sin, pos, q_out=q, k_out=k)
+        mark(2)
+        ops.scale_mask_softmax(scores, scale, causal_q_len=T, out=probs)
+        mark(3)
+        ops.silu_mul(gate, up, out=act)
+        mark(4)
+        from oxide_b200._lib import call
+        st = torch.cuda.current_stream().cuda_stream
+        call("oxide_add_bf16", h.data_ptr(), mlp.data_ptr(), h2.data_ptr(), R * H, st)
+        mark(5)
+        ops.rms_norm(h2, w, c.eps, out=yf)
+        mark(6)
+        idx = ops.argmax(logits)
+        mark(7)
+        ops.reduce(yf, 2, workspace=ws, out=ssq)
+        mark(8)
+        return idx
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    per = {n: 0.0 for n in names}
+    total = 0.0
+    for _ in range(steps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(9)]
+        step(ev)
+        torch.cuda.synchronize()
+        for i, n in enumerate(names):
+            per[n] += ev[i].elapsed_time(ev[i + 1]) / 1e3
+        total += ev[0].elapsed_time(ev[8]) / 1e3
+    if world > 1:
+        import torch.distributed as dist
+
+        t = ssq.clone()
+        dist.all_reduce(t)  # the one cross-GPU exchange: a single f64 partial
+    sb = c.step_bytes()
+    out = {"ms_per_step": round(total / steps * 1e3, 3),
+           "gbs": round(c.bytes() / (total / steps) / 1e9, 1),
+           "frac_of_peak": round(c.bytes() / (total / steps) / 1e9 / peak, 4),
+           "bytes_per_step": c.bytes(), "ops": {}}
+    for n in names:
+        secs = per[n] / steps
+        out["ops"][n] = {"gbs": round(sb[n] / secs / 1e9, 1),
+                         "frac_of_peak": round(sb[n] / secs / 1e9 / peak, 4),
+                         "ms": round(secs * 1e3, 4)}
+    del x, r, q, k, scores, probs, gate, up, act, mlp, logits, h, y, h2, yf
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_oxide(args):
+    import torch
+
+    from oxide_b200 import _lib, ops
+    from oxide_b200.workloads import C2
+
+    rank, world, local = dist_init(args.gpus)
+    _lib.lib()
+    peak, peak_kind = measured_peak()
+    dev = torch.device("cuda", local)
+    cfg = C2()
+    a, b, s, gate, up = cfg.inputs()
+    ta, tb, ts = (torch.from_numpy(v).to(dev) for v in (a, b, s))
+    tg, tu = torch.from_numpy(gate).to(dev), torch.from_numpy(up).to(dev)
+    th, ty, to = torch.empty_like(ta), torch.empty_like(ta), torch.empty_like(tg)
+    st = torch.cuda.current_stream()
+    rows, cols = cfg.rows, cfg.cols
+
+    def step(ev=None, k=0):
+        sp = st.cuda_stream
+        if ev is not None:
+            ev[k][0].record()
+        _lib.call("oxide_add_f32", ta.data_ptr(), tb.data_ptr(), th.data_ptr(), rows * cols, sp)
+        if ev is not None:
+            ev[k][1].record()
+        _lib.call("oxide_mul_rowbcast_f32", th.data_ptr(), ts.data_ptr(), ty.data_ptr(), rows, cols, sp)
+        if ev is not None:
+            ev[k][2].record()
+        _lib.call("oxide_silu_mul_f32", tg.data_ptr(), tu.data_ptr(), to.data_ptr(), tg.numel(), sp)
+        if ev is not None:
+            ev[k][3].record()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # Soak under load while the clock sampler starts (part of warm-up).
+    props = torch.cuda.get_device_properties(dev)
+    gpu_id = str(getattr(props, "uuid", "")) or str(local)
+    if gpu_id and not gpu_id.startswith("GPU-") and len(gpu_id) > 8:
+        gpu_id = "GPU-" + gpu_id
+    sampler = ClockSampler(gpu_id)
+    t_soak = time.perf_counter() + 1.5
+    while time.perf_counter() < t_soak:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    for k in range(args.steps):
+        step(ev, k)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    total = ev[0][0].elapsed_time(ev[-1][3]) / 1e3
+    t_add = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3 / args.steps
+    t_mul = sum(e[1].elapsed_time(e[2]) for e in ev) / 1e3 / args.steps
+    t_sm = sum(e[2].elapsed_time(e[3]) for e in ev) / 1e3 / args.steps
+    total_max = max_over_ranks(total, world)
+    value = world * cfg.bytes() * args.steps / total_max / 1e9
+    ms_per_step = total_max / args.steps * 1e3
+
+    # ---- e2e through the host-buffer C ABI ----
+    import ctypes as C
+
+    pa = torch.from_numpy(a).pin_memory()
+    pb = torch.from_numpy(b).pin_memory()
+    ps = torch.from_numpy(s).pin_memory()
+    pg = torch.from_numpy(gate).pin_memory()
+    pu = torch.from_numpy(up).pin_memory()
+    ph = torch.empty_like(pa).pin_memory()
+    py = torch.empty_like(pa).pin_memory()
+    po = torch.empty_like(pg).pin_memory()
+    pipe = C.c_void_p()
+    _lib.call("oxide_pipe_create", local, 16 << 20, 4, C.byref(pipe))
+
+    def e2e_step():
+        _lib.call("oxide_pipe_binary_f32", pipe, 0, pa.data_ptr(), pa.numel(), pb.data_ptr(),
+                  pb.numel(), ph.data_ptr(), pa.numel())
+        _lib.call("oxide_pipe_binary_f32", pipe, 2, ph.data_ptr(), ph.numel(), ps.data_ptr(),
+                  ps.numel(), py.data_ptr(), ph.numel())
+        _lib.call("oxide_pipe_silu_mul_f32", pipe, pg.data_ptr(), pu.data_ptr(), po.data_ptr(),
+                  pg.numel())
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_secs = max_over_ranks(time.perf_counter() - t0, world)
+    barrier(world)
+    _lib.call("oxide_pipe_destroy", pipe)
+    e2e_ok = bool(np.array_equal(po.numpy()[:4096], to.cpu().numpy().reshape(-1)[:4096]))
+    h2d = 4 * (a.size + b.size + a.size + s.size + gate.size + up.size)
+    d2h = 4 * (a.size + a.size + gate.size)
+    e2e_value = world * cfg.bytes() * args.steps / e2e_secs / 1e9
+
+    sm_bytes = cfg.bytes_silu_mul()
+    achieved = sm_bytes / t_sm / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (numpy PCG64 seed 1, N(0,1) / U(0.5,1.5))",
+        "config": {"workload": WORKLOAD, "bytes_per_step_per_gpu": cfg.bytes(),
+                   "l2": "inputs (1.2 GB per rank) larger than L2; no flush",
+                   "parallelism": f"rows: one batch per rank x{world} (weak)"},
+        "frac_of_peak": round(value / world / peak, 4),
+        "per_kernel_gbs": {"add": round(cfg.bytes_add() / t_add / 1e9, 1),
+                           "mul_rowbcast": round(cfg.bytes_mul() / t_mul / 1e9, 1),
+                           "silu_mul": round(achieved, 1)},
+        "roofline": {"bound": "hbm", "kernel": "ew_vec_kernel<silu_mul f32>",
+                     "achieved": round(achieved, 1), "peak": peak,
+                     "peak_kind": f"{peak_kind} HBM copy GB/s", "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": profiled_traffic("silu_mul_f32_c2"),
+                     "algorithmic_bytes_per_launch": sm_bytes},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "api": "oxide_pipe_* (host buffers, pinned)",
+                "timing": "host wall clock around synchronous calls, max over ranks",
+                "output_matches_device": e2e_ok},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if not args.no_extras:
+        try:
+            line["per_op"] = per_op_lines(peak) if rank == 0 or True else {}
+        except Exception as e:  # keep the headline line; report the failure
+            line["per_op"] = {"error": repr(e)}
+        try:
+            line["chain_c5"] = chain_c5(peak, world)
+        except Exception as e:
+            line["chain_c5"] = {"error": repr(e)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="oxide", choices=["oxide", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_oxide(args)
+
+
+if __name__ == "__main__":
+    main()

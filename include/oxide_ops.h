@@ -1,0 +1,253 @@
+/*
+ * oxide_ops.h -- C ABI of the B200 (sm_100a) tensor-op library.
+ *
+ * Drop-in boundary for mistralrs-oxide's tensor-op hot path: the elementwise,
+ * broadcast and row-reduction ops in src/ops that src/layers calls for every
+ * Mistral decoder layer, and the launch_* methods of
+ * src/cuda_backend/kernels.rs (KernelManager) that were meant to run them on
+ * the GPU.  A Rust (or any C-FFI) caller binds these symbols directly.
+ *
+ * Conventions (all entry points):
+ *   - Pointers are device pointers unless the name says `host`.  The caller
+ *     owns every buffer; nothing here allocates, frees or synchronises.
+ *   - Work is enqueued on `stream` (NULL = legacy default stream) and returns
+ *     immediately, like cudarc's CudaFunction::launch.
+ *   - Tensors are contiguous row-major.  bf16 tensors are raw 16-bit
+ *     patterns (`oxide_bf16`).
+ *   - A size of 0 elements or rows is a valid no-op.
+ *   - The return value is an oxide_status: 0 on success, a negative code
+ *     otherwise; oxide_last_error() gives the message of the calling thread's
+ *     last failure.  No entry point aborts the process.
+ *   - Outputs may alias inputs element-for-element (in-place use) unless the
+ *     entry point says otherwise.
+ *   - Arithmetic follows the reference's sequential f32 formulas with IEEE
+ *     rounding at every step (no FMA contraction, IEEE divide and sqrt).  bf16
+ *     operands are widened to f32, and each tensor the reference materialises
+ *     is rounded to bf16 (nearest-even) once at its store.
+ */
+#ifndef OXIDE_OPS_H
+#define OXIDE_OPS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* oxide_stream_t; /* identical to cudaStream_t */
+typedef uint16_t oxide_bf16;
+
+/* Status codes.  They mirror the error classes of
+ * src/cuda_backend/errors.rs:10-31 (CudaError) and src/error.rs:3-45
+ * (OxideError::InvalidArgument / UnsupportedOperation / CudaError). */
+typedef enum {
+    OXIDE_OK = 0,
+    OXIDE_ERR_INVALID_ARG = -1,  /* null pointer, bad size, size overflow      */
+    OXIDE_ERR_LAUNCH = -2,       /* kernel launch failed (cudaGetLastError)   */
+    OXIDE_ERR_UNSUPPORTED = -3,  /* shape or device this build cannot run     */
+    OXIDE_ERR_CUDA = -4,         /* other CUDA runtime error                  */
+    OXIDE_ERR_WORKSPACE = -5,    /* workspace missing or too small            */
+    OXIDE_ERR_INJECTED = -6,     /* failure injected by oxide_debug_fail_next */
+    OXIDE_ERR_TIMEOUT = -7       /* bounded host wait expired                 */
+} oxide_status;
+
+/* Binary operator selector for oxide_binary_*. */
+typedef enum { OXIDE_ADD = 0, OXIDE_SUB = 1, OXIDE_MUL = 2, OXIDE_DIV = 3 } oxide_binop;
+
+/* Reduction selector for oxide_reduce_*. */
+typedef enum { OXIDE_RED_SUM = 0, OXIDE_RED_MAX = 1, OXIDE_RED_SUMSQ = 2 } oxide_redop;
+
+/* ---- library / status --------------------------------------------------- */
+
+/* Human-readable name of a status code (never NULL). */
+const char* oxide_status_string(int status);
+/* Message of the calling thread's most recent failure ("" if none). */
+const char* oxide_last_error(void);
+/* Library version string. */
+const char* oxide_version(void);
+/* Host-side fault injection for tests: the next call of entry point `op`
+ * (e.g. "oxide_rms_norm_f32"; "*" = any) made by any thread returns
+ * OXIDE_ERR_INJECTED before launching anything.  NULL clears. */
+void oxide_debug_fail_next(const char* op);
+
+/* ---- elementwise binary with broadcast ------------------------------------
+ * Replaces src/ops/matmul.rs:74-134 (add/mul/sub/div) whose loop body is
+ * elementwise_op_cpu, src/ops/matmul.rs:136-158:
+ *     out[i] = a[i % na] op b[i % nb],  i in [0, n)
+ * and KernelManager::launch_vecadd / launch_sub / launch_mul / launch_div
+ * (src/cuda_backend/kernels.rs:75-156, na = nb = n).  A row-broadcast
+ * multiply x[rows, cols] * s[cols] is na = rows*cols, nb = cols. */
+int oxide_binary_f32(int op, const float* a, uint64_t na, const float* b, uint64_t nb,
+                     float* out, uint64_t n, oxide_stream_t stream);
+int oxide_binary_bf16(int op, const oxide_bf16* a, uint64_t na, const oxide_bf16* b,
+                      uint64_t nb, oxide_bf16* out, uint64_t n, oxide_stream_t stream);
+
+/* Named forms of oxide_binary_* with na = nb = n for add, sub and div
+ * (KernelManager::launch_vecadd/sub/div, kernels.rs:75,96,138) and the
+ * trailing-dimension broadcast for mul (ops::mul(x[rows,cols], s[cols]),
+ * matmul.rs:97-108; launch_mul kernels.rs:117 is rows = 1). */
+int oxide_add_f32(const float* a, const float* b, float* out, uint64_t n, oxide_stream_t stream);
+int oxide_add_bf16(const oxide_bf16* a, const oxide_bf16* b, oxide_bf16* out, uint64_t n,
+                   oxide_stream_t stream);
+int oxide_sub_f32(const float* a, const float* b, float* out, uint64_t n, oxide_stream_t stream);
+int oxide_div_f32(const float* a, const float* b, float* out, uint64_t n, oxide_stream_t stream);
+int oxide_mul_rowbcast_f32(const float* x, const float* s, float* out, uint64_t rows,
+                           uint64_t cols, oxide_stream_t stream);
+int oxide_mul_rowbcast_bf16(const oxide_bf16* x, const oxide_bf16* s, oxide_bf16* out,
+                            uint64_t rows, uint64_t cols, oxide_stream_t stream);
+
+/* out = x * scale.  Replaces KernelManager::launch_scale
+ * (src/cuda_backend/kernels.rs:159-177; PTX scale_f32 build.rs:240-276). */
+int oxide_scale_f32(const float* x, float* out, float scale, uint64_t n, oxide_stream_t stream);
+int oxide_scale_bf16(const oxide_bf16* x, oxide_bf16* out, float scale, uint64_t n,
+                     oxide_stream_t stream);
+
+/* ---- activations -----------------------------------------------------------
+ * out = x * (1 / (1 + exp(-x))).  Replaces ops::silu
+ * (src/ops/activation.rs:21-37) and KernelManager::launch_silu
+ * (src/cuda_backend/kernels.rs:231-248). */
+int oxide_silu_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream);
+int oxide_silu_bf16(const oxide_bf16* x, oxide_bf16* out, uint64_t n, oxide_stream_t stream);
+
+/* out = silu(gate) * up in one pass.  Replaces the pair
+ * silu(&gate) then ops::mul(&gated, &up) of MLP::forward
+ * (src/layers/attention.rs:144-145).  The bf16 form rounds silu(gate) to
+ * bf16 before the multiply, exactly as the composed pair would. */
+int oxide_silu_mul_f32(const float* gate, const float* up, float* out, uint64_t n,
+                       oxide_stream_t stream);
+int oxide_silu_mul_bf16(const oxide_bf16* gate, const oxide_bf16* up, oxide_bf16* out,
+                        uint64_t n, oxide_stream_t stream);
+
+/* ---- normalisation ----------------------------------------------------------
+ * Per row of x[rows, cols]: rms = sqrt(sum(x*x) / cols + eps);
+ * out = (x / rms) * w.  Replaces ops::rms_norm (src/ops/norm.rs:4-51) and
+ * KernelManager::launch_rms_norm (src/cuda_backend/kernels.rs:311-331). */
+int oxide_rms_norm_f32(const float* x, const float* w, float* out, uint64_t rows,
+                       uint64_t cols, float eps, oxide_stream_t stream);
+int oxide_rms_norm_bf16(const oxide_bf16* x, const oxide_bf16* w, oxide_bf16* out,
+                        uint64_t rows, uint64_t cols, float eps, oxide_stream_t stream);
+
+/* h = x + r (stored: it is the next residual), then y = rms_norm(h, w, eps).
+ * Replaces ops::add (src/layers/transformer.rs:64) followed by
+ * post_attention_layernorm (transformer.rs:67); fusion intent of
+ * rms_norm_fused_add_f32 (src/kernels/normalization.rs:41-77).  The norm reads
+ * h as stored (bf16-rounded in the bf16 form).  h and y must not alias. */
+int oxide_add_rms_norm_f32(const float* x, const float* r, const float* w, float* h, float* y,
+                           uint64_t rows, uint64_t cols, float eps, oxide_stream_t stream);
+int oxide_add_rms_norm_bf16(const oxide_bf16* x, const oxide_bf16* r, const oxide_bf16* w,
+                            oxide_bf16* h, oxide_bf16* y, uint64_t rows, uint64_t cols,
+                            float eps, oxide_stream_t stream);
+
+/* ---- softmax ---------------------------------------------------------------
+ * softmax(x, dim) of a tensor viewed as [outer, dim, inner] (inner = product
+ * of the dims after `dim`).  Replaces ops::softmax (src/ops/activation.rs:76-124)
+ * and KernelManager::launch_softmax (src/cuda_backend/kernels.rs:358-376,
+ * inner = 1).  out must not alias x when inner > 1. */
+int oxide_softmax_f32(const float* x, float* out, uint64_t outer, uint64_t dim, uint64_t inner,
+                      oxide_stream_t stream);
+int oxide_softmax_bf16(const oxide_bf16* x, oxide_bf16* out, uint64_t outer, uint64_t dim,
+                       uint64_t inner, oxide_stream_t stream);
+
+/* Scale + mask + softmax over rows of x[rows, cols] (raw attention scores):
+ *     s_j = x_j * scale;  s_j += mask[j % mask_len]  (if mask != NULL);
+ *     s_j = -inf for j >= L_r;   out = softmax(s)
+ * the scale/mask/softmax block of scaled_dot_product_attention
+ * (src/ops/attention.rs:41,60,63-79).  L_r (API addition) is cols, lowered
+ * to lens[r / rows_per_len] when lens != NULL (per-sequence KV length) and to
+ * (r % causal_q_len) + 1 + cols - causal_q_len when causal_q_len > 0 (causal
+ * mask, query r % causal_q_len of a q_len-row block).  Keys j >= L_r are
+ * written as 0 without being read; a row with L_r = 0 is all zeros. */
+int oxide_scale_mask_softmax_f32(const float* x, float* out, uint64_t rows, uint64_t cols,
+                                 float scale, const float* mask, uint64_t mask_len,
+                                 const int32_t* lens, uint64_t rows_per_len,
+                                 uint64_t causal_q_len, oxide_stream_t stream);
+int oxide_scale_mask_softmax_bf16(const oxide_bf16* x, oxide_bf16* out, uint64_t rows,
+                                  uint64_t cols, float scale, const float* mask,
+                                  uint64_t mask_len, const int32_t* lens,
+                                  uint64_t rows_per_len, uint64_t causal_q_len,
+                                  oxide_stream_t stream);
+
+/* ---- rotary embedding --------------------------------------------------------
+ * Rotate-half RoPE of q and (optionally) k in one launch, replacing the two
+ * apply_rotary_emb calls of MultiHeadAttention::forward
+ * (src/layers/attention.rs:88-94; op body src/ops/attention.rs:139-155):
+ *     o[d] = x1*c - x2*s,  o[d+half] = x1*s + x2*c,  d < half = head_dim/2
+ * with c = cos[p, d], s = sin[p, d] from f32 tables [table_rows, half] and
+ * p = positions[t] (positions may be NULL: p = t).
+ * layout 0 = token-major [tokens, heads, head_dim] (src/kernels/attention.rs:91-118),
+ * layout 1 = head-major [heads, tokens, head_dim] (src/ops/attention.rs:139-144).
+ * k may be NULL (k_heads ignored).  Outputs may alias their inputs. */
+int oxide_rope_f32(const float* q, float* q_out, uint64_t q_heads, const float* k, float* k_out,
+                   uint64_t k_heads, const float* cos_t, const float* sin_t, uint64_t table_rows,
+                   const int32_t* positions, uint64_t tokens, uint64_t head_dim, int layout,
+                   oxide_stream_t stream);
+int oxide_rope_bf16(const oxide_bf16* q, oxide_bf16* q_out, uint64_t q_heads,
+                    const oxide_bf16* k, oxide_bf16* k_out, uint64_t k_heads,
+                    const float* cos_t, const float* sin_t, uint64_t table_rows,
+                    const int32_t* positions, uint64_t tokens, uint64_t head_dim, int layout,
+                    oxide_stream_t stream);
+
+/* Host-side table build with the formula of precompute_rope_cache
+ * (src/models/mistral.rs:91-115): freq_i = theta^(-2i/head_dim) (powf),
+ * angle = pos * freq_i, cos/sin into host arrays [max_pos, head_dim/2].
+ * Model set-up, not a per-layer op; host pointers. */
+int oxide_rope_table_host_f32(float theta, uint64_t head_dim, uint64_t max_pos,
+                              float* cos_host, float* sin_host);
+
+/* ---- argmax ----------------------------------------------------------------
+ * Index of the largest element of each row of x[rows, cols] (cols < 2^32):
+ * the lowest index among equal maxima (+0 == -0), NaN ranks below every
+ * number.  API addition: the reference's only argmax-like path is
+ * sample_top_k with k = 1 after a stable descending sort
+ * (src/tokenizer.rs:213-232, called from src/pipeline.rs:181-205). */
+int oxide_argmax_rows_f32(const float* x, uint64_t rows, uint64_t cols, uint32_t* idx,
+                          oxide_stream_t stream);
+int oxide_argmax_rows_bf16(const oxide_bf16* x, uint64_t rows, uint64_t cols, uint32_t* idx,
+                           oxide_stream_t stream);
+
+/* ---- reductions --------------------------------------------------------------
+ * Per-row sum / max / sum of squares of x[rows, cols] into f32 out[rows].
+ * API addition; the reference has them only inline (sum of squares
+ * src/ops/norm.rs:36-40, max src/ops/activation.rs:99-103). */
+int oxide_reduce_rows_f32(int op, const float* x, uint64_t rows, uint64_t cols, float* out,
+                          oxide_stream_t stream);
+int oxide_reduce_rows_bf16(int op, const oxide_bf16* x, uint64_t rows, uint64_t cols,
+                           float* out, oxide_stream_t stream);
+
+/* Whole-tensor sum / max / sum of squares of x[n] into one f64 at *out
+ * (device pointer), deterministic for a given n: a fixed partition into at
+ * most 1024 blocks, f32 lane sums inside a block, f64 above.  `workspace`
+ * is caller-owned device memory of at least oxide_reduce_workspace_bytes(n)
+ * bytes; it needs no initialisation.  Across GPUs, the per-GPU results are
+ * combined with one NCCL allreduce (sum, or max) of a single f64. */
+uint64_t oxide_reduce_workspace_bytes(uint64_t n);
+int oxide_reduce_f32(int op, const float* x, uint64_t n, double* out, void* workspace,
+                     uint64_t workspace_bytes, oxide_stream_t stream);
+int oxide_reduce_bf16(int op, const oxide_bf16* x, uint64_t n, double* out, void* workspace,
+                      uint64_t workspace_bytes, oxide_stream_t stream);
+
+/* ---- host-buffer pipeline ----------------------------------------------------
+ * The reference's ops take host tensors and return host tensors
+ * (src/ops/*: Tensor::zeros + as_f32_slice) and its GPU path copies through
+ * CudaBackend::copy_host_to_device / copy_device_to_host
+ * (src/cuda_backend/mod.rs:76-85).  A pipeline runs one op on host buffers:
+ * it splits the rows into chunks and, on `depth` streams, overlaps the
+ * host->device copy of chunk i+1, the kernel of chunk i and the device->host
+ * copy of chunk i-1.  Host buffers should be page-locked (cudaHostRegister
+ * or cudaMallocHost) for the copies to overlap.  The pipeline owns its
+ * device staging buffers (allocated once by oxide_pipe_create); the op calls
+ * allocate nothing and return after the output is in host memory. */
+typedef struct oxide_pipe* oxide_pipe_t;
+int oxide_pipe_create(int device, uint64_t chunk_bytes, int depth, oxide_pipe_t* out);
+int oxide_pipe_destroy(oxide_pipe_t pipe);
+int oxide_pipe_binary_f32(oxide_pipe_t pipe, int op, const float* a_host, uint64_t na,
+                          const float* b_host, uint64_t nb, float* out_host, uint64_t n);
+int oxide_pipe_silu_mul_f32(oxide_pipe_t pipe, const float* gate_host, const float* up_host,
+                            float* out_host, uint64_t n);
+int oxide_pipe_rms_norm_f32(oxide_pipe_t pipe, const float* x_host, const float* w_host,
+                            float* out_host, uint64_t rows, uint64_t cols, float eps);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OXIDE_OPS_H */

@@ -1,0 +1,271 @@
+// k_elementwise.cu -- elementwise and broadcast ops (HBM-bound streaming).
+//
+// Reference semantics (src/ops/matmul.rs:136-158, elementwise_op_cpu):
+//     out[i] = a[i % na] op b[i % nb]
+// plus scale (build.rs:240-276), silu (src/ops/activation.rs:21-37) and the
+// MLP pair silu-then-mul (src/layers/attention.rs:144-145) fused in one pass.
+//
+// Design: a persistent grid (resident CTAs x SMs) streams 16-byte vectors;
+// each thread keeps UNROLL independent vectors per operand in flight, reads
+// with ld.global.nc.L1::no_allocate and writes with st.global.cs (evict-first),
+// so the only traffic is one read of each input and one write of the output.
+// A broadcast operand (e.g. a [cols] row vector) is addressed by a fast
+// modulo on the vector index and stays resident in L1/L2.
+#include "oxide_common.cuh"
+
+namespace oxide {
+
+constexpr int EW_THREADS = 256;
+constexpr int EW_UNROLL = 4;
+
+// ---- per-element functors (f32 math, IEEE rounding per reference step) ----
+template <int OP>
+struct FBin {
+    __device__ __forceinline__ float operator()(float x, float y) const {
+        if (OP == OXIDE_ADD) return fadd(x, y);
+        if (OP == OXIDE_SUB) return fsub(x, y);
+        if (OP == OXIDE_MUL) return fmul(x, y);
+        return fdiv(x, y);
+    }
+};
+
+// silu(x) = x * (1 / (1 + exp(-x))), src/ops/activation.rs:30-33.
+__device__ __forceinline__ float silu_f(float x) {
+    float e = expf(-x);
+    float r = fdiv(1.0f, fadd(1.0f, e));
+    return fmul(x, r);
+}
+
+template <typename T>
+struct FSiluMul {  // mul(silu(g), u); silu(g) rounded to T as the pair stores it
+    __device__ __forceinline__ float operator()(float g, float u) const {
+        return fmul(Vec<T>::rnd(silu_f(g)), u);
+    }
+};
+
+struct FSilu {
+    __device__ __forceinline__ float operator()(float x, float) const { return silu_f(x); }
+};
+
+struct FScale {
+    float s;
+    __device__ __forceinline__ float operator()(float x, float) const { return fmul(x, s); }
+};
+
+// ---- vectorised kernel ------------------------------------------------------
+// NIN = 1 (b unused) or 2.  AMOD/BMOD: operand indexed modulo its length
+// (in vectors).  Requires 16-byte aligned pointers and, for modulo operands,
+// lengths that are multiples of the vector width.
+template <typename T, typename F, int NIN, bool AMOD, bool BMOD>
+__global__ void __launch_bounds__(EW_THREADS)
+    ew_vec_kernel(const T* a, const T* b, T* out, uint64_t nvec, uint64_t nav, uint64_t nbv,
+                  FastDiv adiv, FastDiv bdiv, bool wide, uint64_t tail_lo, uint64_t n, F f) {
+    constexpr int V = Vec<T>::N;
+    const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
+    for (uint64_t base = (uint64_t)blockIdx.x * EW_THREADS + threadIdx.x; base < nvec;
+         base += stride * EW_UNROLL) {
+        uint4 va[EW_UNROLL], vb[EW_UNROLL];
+#pragma unroll
+        for (int k = 0; k < EW_UNROLL; ++k) {
+            const uint64_t i = base + k * stride;
+            if (i < nvec) {
+                uint64_t ia = i, ib = i;
+                if (AMOD) ia = wide ? i % nav : adiv.mod((uint32_t)i);
+                if (BMOD) ib = wide ? i % nbv : bdiv.mod((uint32_t)i);
+                va[k] = AMOD ? ld_keep(a + ia * V) : ld_stream(a + ia * V);
+                if (NIN == 2) vb[k] = BMOD ? ld_keep(b + ib * V) : ld_stream(b + ib * V);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < EW_UNROLL; ++k) {
+            const uint64_t i = base + k * stride;
+            if (i < nvec) {
+                float x[V], y[V], o[V];
+                Vec<T>::unpack(va[k], x);
+                if (NIN == 2) Vec<T>::unpack(vb[k], y);
+#pragma unroll
+                for (int e = 0; e < V; ++e) o[e] = f(x[e], NIN == 2 ? y[e] : 0.0f);
+                st_stream(out + i * V, Vec<T>::pack(o));
+            }
+        }
+    }
+    // Scalar tail of a full-length (non-modulo) op: elements [tail_lo, n).
+    if (blockIdx.x == 0) {
+        for (uint64_t i = tail_lo + threadIdx.x; i < n; i += EW_THREADS) {
+            float x = Vec<T>::load1(a + i);
+            float y = NIN == 2 ? Vec<T>::load1(b + i) : 0.0f;
+            Vec<T>::store1(out + i, f(x, y));
+        }
+    }
+}
+
+// ---- scalar kernel (any alignment, any lengths) ------------------------------
+template <typename T, typename F, int NIN>
+__global__ void __launch_bounds__(EW_THREADS)
+    ew_scalar_kernel(const T* a, uint64_t na, const T* b, uint64_t nb, T* out, uint64_t n, F f) {
+    const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
+    for (uint64_t i = (uint64_t)blockIdx.x * EW_THREADS + threadIdx.x; i < n; i += stride) {
+        float x = Vec<T>::load1(a + (na == n ? i : i % na));
+        float y = NIN == 2 ? Vec<T>::load1(b + (nb == n ? i : i % nb)) : 0.0f;
+        Vec<T>::store1(out + i, f(x, y));
+    }
+}
+
+template <typename K>
+static int resident_grid(K kernel, uint64_t work_items) {
+    const int cap = resident_blocks(reinterpret_cast<const void*>(kernel), EW_THREADS, 0);
+    uint64_t need = (work_items + EW_THREADS - 1) / EW_THREADS;
+    if (need < 1) need = 1;
+    return (int)(need < (uint64_t)cap ? need : (uint64_t)cap);
+}
+
+// Launch a vectorised kernel instance chosen by the modulo flags.
+template <typename T, typename F, int NIN, bool AMOD, bool BMOD>
+static void launch_vec(const T* a, uint64_t na, const T* b, uint64_t nb, T* out, uint64_t n,
+                       F f, cudaStream_t st) {
+    constexpr int V = Vec<T>::N;
+    const uint64_t nvec = n / V;
+    const uint64_t nav = na / V, nbv = nb / V;
+    const bool wide = nvec >= 0xffffffffull;
+    FastDiv adiv(AMOD && !wide ? (uint32_t)nav : 1u);
+    FastDiv bdiv(BMOD && !wide ? (uint32_t)nbv : 1u);
+    auto kern = ew_vec_kernel<T, F, NIN, AMOD, BMOD>;
+    uint64_t items = (nvec + EW_UNROLL - 1) / EW_UNROLL;
+    int grid = resident_grid(kern, items > 0 ? items : 1);
+    kern<<<grid, EW_THREADS, 0, st>>>(a, b, out, nvec, nav, nbv, adiv, bdiv, wide, nvec * V, n,
+                                      f);
+}
+
+// Dispatch: vector path when every pointer is 16-byte aligned and every
+// length that is indexed modulo is a multiple of the vector width; scalar
+// path otherwise (still on the GPU).
+template <typename T, typename F, int NIN>
+static int ew_dispatch(const char* name, const T* a, uint64_t na, const T* b, uint64_t nb,
+                       T* out, uint64_t n, F f, cudaStream_t st) {
+    constexpr int V = Vec<T>::N;
+    const bool amod = na != n, bmod = NIN == 2 && nb != n;
+    bool vec = aligned16(a) && aligned16(out) && (NIN == 1 || aligned16(b));
+    if (amod || bmod) vec = vec && n % V == 0 && na % V == 0 && (NIN == 1 || nb % V == 0);
+    if (vec) {
+        if (!amod && !bmod) launch_vec<T, F, NIN, false, false>(a, na, b, nb, out, n, f, st);
+        else if (!amod && bmod) launch_vec<T, F, NIN, false, true>(a, na, b, nb, out, n, f, st);
+        else if (amod && !bmod) launch_vec<T, F, NIN, true, false>(a, na, b, nb, out, n, f, st);
+        else launch_vec<T, F, NIN, true, true>(a, na, b, nb, out, n, f, st);
+    } else {
+        auto kern = ew_scalar_kernel<T, F, NIN>;
+        int grid = resident_grid(kern, n);
+        kern<<<grid, EW_THREADS, 0, st>>>(a, na, b, nb, out, n, f);
+    }
+    return check_launch(name);
+}
+
+template <typename T>
+static int binary_entry(const char* name, int op, const T* a, uint64_t na, const T* b,
+                        uint64_t nb, T* out, uint64_t n, cudaStream_t st) {
+    OXIDE_INJECT(name);
+    OXIDE_REQUIRE(op >= OXIDE_ADD && op <= OXIDE_DIV, name, "unknown binary operator");
+    if (n == 0) return OXIDE_OK;
+    OXIDE_REQUIRE(a && b && out, name, "null pointer");
+    OXIDE_REQUIRE(na >= 1 && nb >= 1 && na <= n && nb <= n, name,
+                  "operand lengths must be in [1, n]");
+    // The reference's broadcast_shape (matmul.rs:160-177) only admits operands
+    // whose length divides the output; out[i] reads a[i % na], b[i % nb].
+    OXIDE_REQUIRE(n % na == 0 && n % nb == 0, name,
+                  "operand lengths must divide the output length");
+    switch (op) {
+        case OXIDE_ADD: return ew_dispatch<T, FBin<OXIDE_ADD>, 2>(name, a, na, b, nb, out, n, {}, st);
+        case OXIDE_SUB: return ew_dispatch<T, FBin<OXIDE_SUB>, 2>(name, a, na, b, nb, out, n, {}, st);
+        case OXIDE_MUL: return ew_dispatch<T, FBin<OXIDE_MUL>, 2>(name, a, na, b, nb, out, n, {}, st);
+        default: return ew_dispatch<T, FBin<OXIDE_DIV>, 2>(name, a, na, b, nb, out, n, {}, st);
+    }
+}
+
+template <typename T>
+static int rowbcast_entry(const char* name, const T* x, const T* s, T* out, uint64_t rows,
+                          uint64_t cols, cudaStream_t st) {
+    OXIDE_INJECT(name);
+    if (rows == 0 || cols == 0) return OXIDE_OK;
+    OXIDE_REQUIRE(x && s && out, name, "null pointer");
+    OXIDE_REQUIRE(rows <= UINT64_MAX / cols, name, "rows * cols overflows");
+    const uint64_t n = rows * cols;
+    return ew_dispatch<T, FBin<OXIDE_MUL>, 2>(name, x, n, s, cols, out, n, {}, st);
+}
+
+template <typename T, typename F, int NIN>
+static int full_entry(const char* name, const T* a, const T* b, T* out, uint64_t n, F f,
+                      cudaStream_t st) {
+    OXIDE_INJECT(name);
+    if (n == 0) return OXIDE_OK;
+    OXIDE_REQUIRE(a && out && (NIN == 1 || b), name, "null pointer");
+    return ew_dispatch<T, F, NIN>(name, a, n, NIN == 2 ? b : a, n, out, n, f, st);
+}
+
+}  // namespace oxide
+
+using oxide::bf16_t;
+
+extern "C" {
+
+int oxide_binary_f32(int op, const float* a, uint64_t na, const float* b, uint64_t nb,
+                     float* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::binary_entry<float>("oxide_binary_f32", op, a, na, b, nb, out, n, stream);
+}
+int oxide_binary_bf16(int op, const oxide_bf16* a, uint64_t na, const oxide_bf16* b,
+                      uint64_t nb, oxide_bf16* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::binary_entry<bf16_t>("oxide_binary_bf16", op, a, na, b, nb, out, n, stream);
+}
+int oxide_add_f32(const float* a, const float* b, float* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::full_entry<float, oxide::FBin<OXIDE_ADD>, 2>("oxide_add_f32", a, b, out, n, {},
+                                                                stream);
+}
+int oxide_add_bf16(const oxide_bf16* a, const oxide_bf16* b, oxide_bf16* out, uint64_t n,
+                   oxide_stream_t stream) {
+    return oxide::full_entry<bf16_t, oxide::FBin<OXIDE_ADD>, 2>("oxide_add_bf16", a, b, out, n,
+                                                                 {}, stream);
+}
+int oxide_sub_f32(const float* a, const float* b, float* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::full_entry<float, oxide::FBin<OXIDE_SUB>, 2>("oxide_sub_f32", a, b, out, n, {},
+                                                                stream);
+}
+int oxide_div_f32(const float* a, const float* b, float* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::full_entry<float, oxide::FBin<OXIDE_DIV>, 2>("oxide_div_f32", a, b, out, n, {},
+                                                                stream);
+}
+int oxide_mul_rowbcast_f32(const float* x, const float* s, float* out, uint64_t rows,
+                           uint64_t cols, oxide_stream_t stream) {
+    return oxide::rowbcast_entry<float>("oxide_mul_rowbcast_f32", x, s, out, rows, cols, stream);
+}
+int oxide_mul_rowbcast_bf16(const oxide_bf16* x, const oxide_bf16* s, oxide_bf16* out,
+                            uint64_t rows, uint64_t cols, oxide_stream_t stream) {
+    return oxide::rowbcast_entry<bf16_t>("oxide_mul_rowbcast_bf16", x, s, out, rows, cols,
+                                         stream);
+}
+int oxide_scale_f32(const float* x, float* out, float scale, uint64_t n, oxide_stream_t stream) {
+    return oxide::full_entry<float, oxide::FScale, 1>("oxide_scale_f32", x, nullptr, out, n,
+                                                      oxide::FScale{scale}, stream);
+}
+int oxide_scale_bf16(const oxide_bf16* x, oxide_bf16* out, float scale, uint64_t n,
+                     oxide_stream_t stream) {
+    return oxide::full_entry<bf16_t, oxide::FScale, 1>("oxide_scale_bf16", x, nullptr, out, n,
+                                                       oxide::FScale{scale}, stream);
+}
+int oxide_silu_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::full_entry<float, oxide::FSilu, 1>("oxide_silu_f32", x, nullptr, out, n, {},
+                                                     stream);
+}
+int oxide_silu_bf16(const oxide_bf16* x, oxide_bf16* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::full_entry<bf16_t, oxide::FSilu, 1>("oxide_silu_bf16", x, nullptr, out, n, {},
+                                                      stream);
+}
+int oxide_silu_mul_f32(const float* gate, const float* up, float* out, uint64_t n,
+                       oxide_stream_t stream) {
+    return oxide::full_entry<float, oxide::FSiluMul<float>, 2>("oxide_silu_mul_f32", gate, up,
+                                                               out, n, {}, stream);
+}
+int oxide_silu_mul_bf16(const oxide_bf16* gate, const oxide_bf16* up, oxide_bf16* out,
+                        uint64_t n, oxide_stream_t stream) {
+    return oxide::full_entry<bf16_t, oxide::FSiluMul<bf16_t>, 2>("oxide_silu_mul_bf16", gate, up,
+                                                                 out, n, {}, stream);
+}
+
+}  // extern "C"

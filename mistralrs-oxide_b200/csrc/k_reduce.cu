@@ -1,0 +1,263 @@
+// k_reduce.cu -- row and whole-tensor sum / max / sum of squares.
+//
+// API additions: the reference has these only inline (sum of squares
+// src/ops/norm.rs:36-40, max src/ops/activation.rs:99-103, running sum
+// src/ops/activation.rs:105-110).  Row results are f32 like those loops; the
+// whole-tensor result is f64, because a sequential f32 sum over ~10^8-10^9
+// terms stalls once the running sum's ulp exceeds the terms.
+//
+// Whole-tensor design (deterministic for a given n): stage 1 splits x into
+// at most RED_BLOCKS contiguous slices of whole 16-byte vectors, one CTA per
+// slice; each thread keeps per-lane f32 partials, the CTA combines them in
+// f64 with a fixed tree and writes one f64 partial to the workspace.  Stage 2,
+// one CTA, combines the partials in a fixed order.  No atomics, no
+// initialised state: the workspace is only ever written before it is read.
+#include "oxide_common.cuh"
+
+namespace oxide {
+
+constexpr int RED_BLOCKS = 1024;
+constexpr int RED_THREADS = 256;
+
+template <int OP>
+__device__ __forceinline__ float red_step(float acc, float v) {
+    if (OP == OXIDE_RED_SUM) return fadd(acc, v);
+    if (OP == OXIDE_RED_MAX) return fmaxf(acc, v);
+    return fadd(acc, fmul(v, v));
+}
+template <int OP>
+__device__ __forceinline__ double red_comb(double a, double b) {
+    return OP == OXIDE_RED_MAX ? fmax(a, b) : a + b;
+}
+template <int OP>
+__device__ __forceinline__ float red_init() {
+    return OP == OXIDE_RED_MAX ? -INFINITY : 0.0f;
+}
+
+template <int OP>
+struct OpComb {
+    __device__ __forceinline__ double operator()(double a, double b) const { return red_comb<OP>(a, b); }
+};
+template <int OP>
+struct OpCombF {
+    __device__ __forceinline__ float operator()(float a, float b) const {
+        return OP == OXIDE_RED_MAX ? fmaxf(a, b) : fadd(a, b);
+    }
+};
+
+// ---- row reductions -----------------------------------------------------------
+template <typename T, int OP, bool VEC>
+__global__ void __launch_bounds__(256)
+    reduce_rows_kernel(const T* x, uint64_t rows, uint32_t cols, float* out, int tpr) {
+    constexpr int V = VEC ? Vec<T>::N : 1;
+    __shared__ float red[8];
+    const int rpc = blockDim.x / tpr;
+    const int sub = threadIdx.x / tpr, t = threadIdx.x % tpr;
+    const uint32_t n = cols / V;
+    for (uint64_t row0 = (uint64_t)blockIdx.x * rpc; row0 < rows; row0 += (uint64_t)gridDim.x * rpc) {
+        const uint64_t row = row0 + sub;
+        float acc = red_init<OP>();
+        if (row < rows) {
+            const T* xr = x + row * cols;
+            for (uint32_t u = t; u < n; u += tpr) {
+                if (VEC) {
+                    float f[Vec<T>::N];
+                    Vec<T>::unpack(ld_stream(xr + (uint64_t)u * Vec<T>::N), f);
+#pragma unroll
+                    for (int e = 0; e < Vec<T>::N; ++e) acc = red_step<OP>(acc, f[e]);
+                } else {
+                    acc = red_step<OP>(acc, Vec<T>::load1(xr + u));
+                }
+            }
+        }
+        acc = group_reduce(acc, red, tpr, OpCombF<OP>());
+        if (row < rows && t == 0) out[row] = acc;
+    }
+}
+
+// ---- whole-tensor, stage 1 ------------------------------------------------------
+template <typename T, int OP>
+__global__ void __launch_bounds__(RED_THREADS)
+    reduce_stage1_kernel(const T* x, uint64_t n, uint64_t nvec, uint64_t per_block,
+                         double* partial) {
+    constexpr int V = Vec<T>::N;
+    __shared__ double red[RED_THREADS / 32];
+    const uint64_t lo = (uint64_t)blockIdx.x * per_block;
+    const uint64_t hi = lo + per_block < nvec ? lo + per_block : nvec;
+    float lane[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) lane[e] = red_init<OP>();
+    constexpr int UNROLL = 4;
+    for (uint64_t u0 = lo + threadIdx.x; u0 < hi; u0 += RED_THREADS * UNROLL) {
+        uint4 raw[UNROLL];
+#pragma unroll
+        for (int k = 0; k < UNROLL; ++k) {
+            const uint64_t u = u0 + (uint64_t)k * RED_THREADS;
+            if (u < hi) raw[k] = ld_stream(x + u * V);
+        }
+#pragma unroll
+        for (int k = 0; k < UNROLL; ++k) {
+            const uint64_t u = u0 + (uint64_t)k * RED_THREADS;
+            if (u < hi) {
+                float f[V];
+                Vec<T>::unpack(raw[k], f);
+#pragma unroll
+                for (int e = 0; e < V; ++e) lane[e] = red_step<OP>(lane[e], f[e]);
+            }
+        }
+    }
+    double acc = OP == OXIDE_RED_MAX ? -INFINITY : 0.0;
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc = red_comb<OP>(acc, (double)lane[e]);
+    // Elements after the last whole vector belong to the last block.
+    if (blockIdx.x == gridDim.x - 1) {
+        for (uint64_t i = nvec * V + threadIdx.x; i < n; i += RED_THREADS) {
+            const double v = (double)Vec<T>::load1(x + i);
+            acc = red_comb<OP>(acc, OP == OXIDE_RED_SUMSQ ? v * v : v);
+        }
+    }
+    acc = group_reduce(acc, red, RED_THREADS, OpComb<OP>());
+    if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+}
+
+// ---- whole-tensor, stage 2 (one CTA) ----------------------------------------------
+template <int OP>
+__global__ void __launch_bounds__(RED_THREADS)
+    reduce_stage2_kernel(const double* partial, int nblocks, double* out) {
+    __shared__ double red[RED_THREADS / 32];
+    double acc = OP == OXIDE_RED_MAX ? -INFINITY : 0.0;
+    for (int i = threadIdx.x; i < nblocks; i += RED_THREADS) acc = red_comb<OP>(acc, partial[i]);
+    acc = group_reduce(acc, red, RED_THREADS, OpComb<OP>());
+    if (threadIdx.x == 0) *out = acc;
+}
+
+// Scalar whole-tensor stage 1 for unaligned bases.
+template <typename T, int OP>
+__global__ void __launch_bounds__(RED_THREADS)
+    reduce_stage1_scalar_kernel(const T* x, uint64_t n, uint64_t per_block, double* partial) {
+    __shared__ double red[RED_THREADS / 32];
+    const uint64_t lo = (uint64_t)blockIdx.x * per_block;
+    const uint64_t hi = lo + per_block < n ? lo + per_block : n;
+    float acc32 = red_init<OP>();
+    for (uint64_t i = lo + threadIdx.x; i < hi; i += RED_THREADS)
+        acc32 = red_step<OP>(acc32, Vec<T>::load1(x + i));
+    double acc = group_reduce((double)acc32, red, RED_THREADS, OpComb<OP>());
+    if (threadIdx.x == 0) partial[blockIdx.x] = acc;
+}
+
+static uint64_t stage1_blocks(uint64_t units) {
+    // At least 16 units per thread before a slice is split further.
+    const uint64_t min_units = (uint64_t)RED_THREADS * 16;
+    uint64_t b = (units + min_units - 1) / min_units;
+    if (b < 1) b = 1;
+    if (b > RED_BLOCKS) b = RED_BLOCKS;
+    return b;
+}
+
+template <typename T, int OP>
+static void launch_reduce(const T* x, uint64_t n, double* out, double* partial, cudaStream_t st) {
+    constexpr int V = Vec<T>::N;
+    if (aligned16(x)) {
+        const uint64_t nvec = n / V;
+        const uint64_t blocks = stage1_blocks(nvec);
+        const uint64_t per = (nvec + blocks - 1) / blocks;
+        reduce_stage1_kernel<T, OP><<<(unsigned)blocks, RED_THREADS, 0, st>>>(x, n, nvec, per, partial);
+        reduce_stage2_kernel<OP><<<1, RED_THREADS, 0, st>>>(partial, (int)blocks, out);
+    } else {
+        const uint64_t blocks = stage1_blocks(n);
+        const uint64_t per = (n + blocks - 1) / blocks;
+        reduce_stage1_scalar_kernel<T, OP><<<(unsigned)blocks, RED_THREADS, 0, st>>>(x, n, per, partial);
+        reduce_stage2_kernel<OP><<<1, RED_THREADS, 0, st>>>(partial, (int)blocks, out);
+    }
+}
+
+template <typename T>
+static int reduce_entry(const char* name, int op, const T* x, uint64_t n, double* out,
+                        void* ws, uint64_t ws_bytes, cudaStream_t st) {
+    OXIDE_INJECT(name);
+    OXIDE_REQUIRE(op >= OXIDE_RED_SUM && op <= OXIDE_RED_SUMSQ, name, "unknown reduction");
+    OXIDE_REQUIRE(out, name, "null output pointer");
+    OXIDE_REQUIRE(n == 0 || x, name, "null input pointer");
+    if (!ws || ws_bytes < oxide_reduce_workspace_bytes(n) || (reinterpret_cast<uintptr_t>(ws) & 7))
+        return set_error(OXIDE_ERR_WORKSPACE, "%s: workspace must be 8-byte aligned and >= %llu bytes",
+                         name, (unsigned long long)oxide_reduce_workspace_bytes(n));
+    double* partial = static_cast<double*>(ws);
+    if (n == 0) {
+        // Empty input: the identity of the operation, written by a kernel so
+        // the result is stream-ordered like every other result.
+        if (op == OXIDE_RED_MAX)
+            reduce_stage2_kernel<OXIDE_RED_MAX><<<1, RED_THREADS, 0, st>>>(partial, 0, out);
+        else
+            reduce_stage2_kernel<OXIDE_RED_SUM><<<1, RED_THREADS, 0, st>>>(partial, 0, out);
+        return check_launch(name);
+    }
+    switch (op) {
+        case OXIDE_RED_SUM: launch_reduce<T, OXIDE_RED_SUM>(x, n, out, partial, st); break;
+        case OXIDE_RED_MAX: launch_reduce<T, OXIDE_RED_MAX>(x, n, out, partial, st); break;
+        default: launch_reduce<T, OXIDE_RED_SUMSQ>(x, n, out, partial, st); break;
+    }
+    return check_launch(name);
+}
+
+template <typename T>
+static int reduce_rows_entry(const char* name, int op, const T* x, uint64_t rows, uint64_t cols,
+                             float* out, cudaStream_t st) {
+    OXIDE_INJECT(name);
+    OXIDE_REQUIRE(op >= OXIDE_RED_SUM && op <= OXIDE_RED_SUMSQ, name, "unknown reduction");
+    if (rows == 0) return OXIDE_OK;
+    OXIDE_REQUIRE(x && out, name, "null pointer");
+    OXIDE_REQUIRE(cols >= 1 && cols < (1ull << 32), name, "cols must be in [1, 2^32)");
+    OXIDE_REQUIRE(rows <= UINT64_MAX / cols, name, "rows * cols overflows");
+    constexpr int V = Vec<T>::N;
+    const bool vec = cols % V == 0 && aligned16(x);
+    const uint64_t units = vec ? cols / V : cols;
+    int tpr = 32;
+    while (tpr < 256 && (uint64_t)tpr * 8 < units) tpr *= 2;
+    const int rpc = 256 / tpr;
+    const uint64_t want = (rows + rpc - 1) / rpc, cap = (uint64_t)1 << 30;
+    const unsigned grid = (unsigned)(want < cap ? want : cap);
+    const uint32_t c32 = (uint32_t)cols;
+#define OXIDE_ROWS_LAUNCH(OPV)                                                              \
+    (vec ? reduce_rows_kernel<T, OPV, true><<<grid, 256, 0, st>>>(x, rows, c32, out, tpr) \
+         : reduce_rows_kernel<T, OPV, false><<<grid, 256, 0, st>>>(x, rows, c32, out, tpr))
+    switch (op) {
+        case OXIDE_RED_SUM: OXIDE_ROWS_LAUNCH(OXIDE_RED_SUM); break;
+        case OXIDE_RED_MAX: OXIDE_ROWS_LAUNCH(OXIDE_RED_MAX); break;
+        default: OXIDE_ROWS_LAUNCH(OXIDE_RED_SUMSQ); break;
+    }
+#undef OXIDE_ROWS_LAUNCH
+    return check_launch(name);
+}
+
+}  // namespace oxide
+
+using oxide::bf16_t;
+
+extern "C" {
+
+uint64_t oxide_reduce_workspace_bytes(uint64_t n) {
+    (void)n;
+    return (uint64_t)oxide::RED_BLOCKS * sizeof(double);
+}
+
+int oxide_reduce_f32(int op, const float* x, uint64_t n, double* out, void* workspace,
+                     uint64_t workspace_bytes, oxide_stream_t stream) {
+    return oxide::reduce_entry<float>("oxide_reduce_f32", op, x, n, out, workspace,
+                                      workspace_bytes, stream);
+}
+int oxide_reduce_bf16(int op, const oxide_bf16* x, uint64_t n, double* out, void* workspace,
+                      uint64_t workspace_bytes, oxide_stream_t stream) {
+    return oxide::reduce_entry<bf16_t>("oxide_reduce_bf16", op, x, n, out, workspace,
+                                       workspace_bytes, stream);
+}
+int oxide_reduce_rows_f32(int op, const float* x, uint64_t rows, uint64_t cols, float* out,
+                          oxide_stream_t stream) {
+    return oxide::reduce_rows_entry<float>("oxide_reduce_rows_f32", op, x, rows, cols, out, stream);
+}
+int oxide_reduce_rows_bf16(int op, const oxide_bf16* x, uint64_t rows, uint64_t cols,
+                           float* out, oxide_stream_t stream) {
+    return oxide::reduce_rows_entry<bf16_t>("oxide_reduce_rows_bf16", op, x, rows, cols, out,
+                                            stream);
+}
+
+}  // extern "C"

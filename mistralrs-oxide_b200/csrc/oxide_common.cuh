@@ -1,0 +1,220 @@
+// oxide_common.cuh -- device helpers shared by every oxide kernel (sm_100a).
+//
+// Arithmetic that must match the reference's Rust f32 semantics goes through
+// the explicitly rounded intrinsics below (__fmul_rn, __fadd_rn, __fsub_rn,
+// __fdiv_rn, __fsqrt_rn).  nvcc never contracts those into an FMA and never
+// replaces the IEEE divide by a reciprocal-multiply, so each step rounds
+// exactly as the corresponding Rust expression does.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "oxide_ops.h"
+
+namespace oxide {
+
+typedef uint16_t bf16_t;  // raw bf16 bits (high half of an f32)
+
+// ---------------------------------------------------------------------------
+// IEEE-rounded scalar arithmetic (no contraction)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float fsqrt(float a) { return __fsqrt_rn(a); }
+
+// ---------------------------------------------------------------------------
+// bf16 <-> f32
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ float bf16_to_f32(bf16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+// Round two floats to bf16 (nearest-even) and pack: lo in bits 0..15.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ bf16_t f32_to_bf16(float f) {
+    __nv_bfloat16 v = __float2bfloat16_rn(f);
+    return *reinterpret_cast<bf16_t*>(&v);
+}
+// Round-trip through bf16: the value a bf16 tensor store would hold.
+__device__ __forceinline__ float round_bf16(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+// ---------------------------------------------------------------------------
+// 128-bit global memory access
+// ---------------------------------------------------------------------------
+// Streaming read of data touched once: read-only path, no L1 allocation, L2
+// prefetch of the surrounding 256 B sector group.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+// Read of small operands reused by many threads (weights, tables, masks).
+__device__ __forceinline__ uint4 ld_keep(const void* p) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+}
+// Streaming write (evict-first in L2).
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// A 16-byte vector viewed as V floats (V = 4 for f32, 8 for bf16).
+template <typename T>
+struct Vec;
+
+template <>
+struct Vec<float> {
+    static constexpr int N = 4;
+    __device__ __forceinline__ static void unpack(uint4 v, float* f) {
+        f[0] = __uint_as_float(v.x);
+        f[1] = __uint_as_float(v.y);
+        f[2] = __uint_as_float(v.z);
+        f[3] = __uint_as_float(v.w);
+    }
+    __device__ __forceinline__ static uint4 pack(const float* f) {
+        return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                          __float_as_uint(f[3]));
+    }
+    // Value a store of this dtype would hold (identity for f32).
+    __device__ __forceinline__ static float rnd(float f) { return f; }
+    __device__ __forceinline__ static float load1(const float* p) { return __ldg(p); }
+    __device__ __forceinline__ static void store1(float* p, float f) { *p = f; }
+};
+
+template <>
+struct Vec<bf16_t> {
+    static constexpr int N = 8;
+    __device__ __forceinline__ static void unpack(uint4 v, float* f) {
+        f[0] = bf16_lo(v.x);
+        f[1] = bf16_hi(v.x);
+        f[2] = bf16_lo(v.y);
+        f[3] = bf16_hi(v.y);
+        f[4] = bf16_lo(v.z);
+        f[5] = bf16_hi(v.z);
+        f[6] = bf16_lo(v.w);
+        f[7] = bf16_hi(v.w);
+    }
+    __device__ __forceinline__ static uint4 pack(const float* f) {
+        return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                          pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+    }
+    __device__ __forceinline__ static float rnd(float f) { return round_bf16(f); }
+    __device__ __forceinline__ static float load1(const bf16_t* p) {
+        return bf16_to_f32(__ldg(reinterpret_cast<const unsigned short*>(p)));
+    }
+    __device__ __forceinline__ static void store1(bf16_t* p, float f) { *p = f32_to_bf16(f); }
+};
+
+// ---------------------------------------------------------------------------
+// Unsigned 32-bit division by a run-time constant (multiply-high + shift).
+// For divisor d >= 1: s = ceil(log2 d), m = floor(2^32 (2^s - d) / d) + 1,
+// q = (umulhi(n, m) + n) >> s, exact for every n < 2^32.
+// ---------------------------------------------------------------------------
+struct FastDiv {
+    uint32_t d, m, s;
+    __host__ __device__ FastDiv() : d(1), m(0), s(0) {}
+    __host__ explicit FastDiv(uint32_t div) : d(div) {
+        s = 0;
+        while ((1ull << s) < div) ++s;
+        m = (uint32_t)((((1ull << s) - div) << 32) / div + 1);
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        uint64_t t = (uint64_t)__umulhi(n, m) + n;
+        return (uint32_t)(t >> s);
+    }
+    __device__ __forceinline__ uint32_t mod(uint32_t n) const { return n - div(n) * d; }
+};
+
+// ---------------------------------------------------------------------------
+// Warp / block reductions (fixed shuffle trees: deterministic)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fadd(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = w > v ? w : v;
+    }
+    return v;
+}
+
+// Reduce within groups of `group_threads` consecutive threads (a multiple of
+// 32) of a block.  Every thread of a group receives the group's result.
+// `red` must hold blockDim.x / 32 elements.  Contains __syncthreads().
+template <typename T, typename Op>
+__device__ __forceinline__ T group_reduce(T v, T* red, int group_threads, Op op) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (group_threads == 32) return v;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    const int wpg = group_threads >> 5;
+    const int first = (warp / wpg) * wpg;
+    T r = red[first];
+    for (int i = 1; i < wpg; ++i) r = op(r, red[first + i]);
+    __syncthreads();  // red may be reused right after
+    return r;
+}
+
+struct OpAddF {
+    __device__ __forceinline__ float operator()(float a, float b) const { return fadd(a, b); }
+};
+struct OpMaxF {
+    __device__ __forceinline__ float operator()(float a, float b) const { return fmaxf(a, b); }
+};
+struct OpMaxU64 {
+    __device__ __forceinline__ uint64_t operator()(uint64_t a, uint64_t b) const {
+        return a > b ? a : b;
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Host-side helpers (defined in oxide_runtime.cu)
+// ---------------------------------------------------------------------------
+int sm_count();                      // SMs of the current device (cached)
+// Resident CTAs of `kernel` across the whole current device (occupancy x SMs),
+// cached per (device, kernel, block size, dynamic smem).
+int resident_blocks(const void* kernel, int threads, size_t smem);
+int set_error(int code, const char* fmt, ...);  // records message, returns code
+int check_launch(const char* op);    // cudaGetLastError -> status
+int injected_failure(const char* op);  // host-side fault injection hook
+bool aligned16(const void* p);
+
+}  // namespace oxide
+
+// Common argument checks: every entry point returns a status instead of
+// aborting.  OXIDE_INJECT runs first so fault-injection tests never launch.
+#define OXIDE_INJECT(op)                                      \
+    do {                                                      \
+        int _inj = ::oxide::injected_failure(op);             \
+        if (_inj) return _inj;                                \
+    } while (0)
+#define OXIDE_REQUIRE(cond, op, msg)                                                     \
+    do {                                                                                 \
+        if (!(cond)) return ::oxide::set_error(OXIDE_ERR_INVALID_ARG, "%s: %s", op, msg); \
+    } while (0)

@@ -1,0 +1,288 @@
+"""Tensor-level ops over the C ABI, named after mistralrs-oxide's ``src/ops``.
+
+Each function mirrors a reference free function (``fn(&Tensor, ...) ->
+OxideResult<Tensor>``): inputs are borrowed, a new output is allocated and
+returned, and invalid shapes raise (``OxideError`` with status
+OXIDE_ERR_INVALID_ARG, like ``OxideError::InvalidArgument``).  Tensors must be
+contiguous CUDA tensors of dtype float32 or bfloat16; work runs on the current
+torch CUDA stream.  PyTorch only supplies device memory and the stream: every
+op is one call into liboxide_b200.so.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import ADD, DIV, MUL, RED_MAX, RED_SUM, RED_SUMSQ, SUB, OxideError, call
+
+_SFX = {torch.float32: "f32", torch.bfloat16: "bf16"}
+
+
+def _sfx(t: torch.Tensor) -> str:
+    if t.dtype not in _SFX:
+        raise OxideError(_lib.ERR_UNSUPPORTED, "oxide", f"dtype {t.dtype} is not float32/bfloat16")
+    return _SFX[t.dtype]
+
+
+def _check(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise OxideError(_lib.ERR_INVALID_ARG, "oxide", "tensor is not on a CUDA device")
+        if not t.is_contiguous():
+            raise OxideError(_lib.ERR_INVALID_ARG, "oxide", "tensor is not contiguous")
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def broadcast_shape(a: Sequence[int], b: Sequence[int]) -> list[int]:
+    """Output shape of a binary op; src/ops/matmul.rs:160-177."""
+    out = []
+    for i in range(max(len(a), len(b))):
+        da = a[len(a) - 1 - i] if i < len(a) else 1
+        db = b[len(b) - 1 - i] if i < len(b) else 1
+        if da != db and da != 1 and db != 1:
+            raise OxideError(_lib.ERR_INVALID_ARG, "broadcast",
+                             f"shape mismatch {list(a)} and {list(b)}")
+        out.append(max(da, db))
+    return out[::-1]
+
+
+def binary(op: int, a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """out[i] = a[i % a.numel()] op b[i % b.numel()] (src/ops/matmul.rs:136-158)."""
+    _check(a, b)
+    if a.dtype != b.dtype:
+        raise OxideError(_lib.ERR_INVALID_ARG, "binary", "operand dtypes differ")
+    out = torch.empty(broadcast_shape(a.shape, b.shape), dtype=a.dtype, device=a.device)
+    call(f"oxide_binary_{_sfx(a)}", op, _p(a), a.numel(), _p(b), b.numel(), _p(out), out.numel(),
+         _stream())
+    return out
+
+
+def add(a, b):  # src/ops/matmul.rs:74
+    return binary(ADD, a, b)
+
+
+def sub(a, b):  # src/ops/matmul.rs:110
+    return binary(SUB, a, b)
+
+
+def mul(a, b):  # src/ops/matmul.rs:97
+    return binary(MUL, a, b)
+
+
+def div(a, b):  # src/ops/matmul.rs:123
+    return binary(DIV, a, b)
+
+
+def mul_rowbcast(x: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+    """x[rows, cols] * s[cols] (ops::mul with a trailing-dim broadcast)."""
+    _check(x, s)
+    cols = s.numel()
+    out = torch.empty_like(x)
+    call(f"oxide_mul_rowbcast_{_sfx(x)}", _p(x), _p(s), _p(out), x.numel() // cols, cols, _stream())
+    return out
+
+
+def scale(x: torch.Tensor, s: float) -> torch.Tensor:
+    """x * s (KernelManager::launch_scale, src/cuda_backend/kernels.rs:159)."""
+    _check(x)
+    out = torch.empty_like(x)
+    call(f"oxide_scale_{_sfx(x)}", _p(x), _p(out), float(s), x.numel(), _stream())
+    return out
+
+
+def silu(x: torch.Tensor) -> torch.Tensor:
+    """src/ops/activation.rs:21-37."""
+    _check(x)
+    out = torch.empty_like(x)
+    call(f"oxide_silu_{_sfx(x)}", _p(x), _p(out), x.numel(), _stream())
+    return out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """mul(silu(gate), up) in one pass (src/layers/attention.rs:144-145)."""
+    _check(gate, up, out)
+    if gate.shape != up.shape:
+        raise OxideError(_lib.ERR_INVALID_ARG, "silu_mul", "gate and up shapes differ")
+    out = torch.empty_like(gate) if out is None else out
+    call(f"oxide_silu_mul_{_sfx(gate)}", _p(gate), _p(up), _p(out), gate.numel(), _stream())
+    return out
+
+
+def _norm_check(x: torch.Tensor, w: torch.Tensor) -> int:
+    if x.dim() < 1:
+        raise OxideError(_lib.ERR_INVALID_ARG, "rms_norm", "rms_norm requires at least 1D tensor")
+    if w.dim() != 1 or w.shape[0] != x.shape[-1]:
+        raise OxideError(_lib.ERR_INVALID_ARG, "rms_norm",
+                         f"rms_norm weight shape {list(w.shape)} doesn't match input last dim {x.shape[-1]}")
+    return x.shape[-1]
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """src/ops/norm.rs:4-51."""
+    _check(x, w, out)
+    cols = _norm_check(x, w)
+    out = torch.empty_like(x) if out is None else out
+    call(f"oxide_rms_norm_{_sfx(x)}", _p(x), _p(w), _p(out), x.numel() // cols, cols, float(eps),
+         _stream())
+    return out
+
+
+def add_rms_norm(x: torch.Tensor, r: torch.Tensor, w: torch.Tensor, eps: float,
+                 h: Optional[torch.Tensor] = None, y: Optional[torch.Tensor] = None):
+    """(h, y) with h = x + r and y = rms_norm(h) (src/layers/transformer.rs:64-67)."""
+    _check(x, r, w, h, y)
+    cols = _norm_check(x, w)
+    h = torch.empty_like(x) if h is None else h
+    y = torch.empty_like(x) if y is None else y
+    call(f"oxide_add_rms_norm_{_sfx(x)}", _p(x), _p(r), _p(w), _p(h), _p(y), x.numel() // cols, cols,
+         float(eps), _stream())
+    return h, y
+
+
+def softmax(x: torch.Tensor, dim: int) -> torch.Tensor:
+    """softmax along `dim` (src/ops/activation.rs:76-124)."""
+    _check(x)
+    if dim >= x.dim() or dim < 0:
+        raise OxideError(_lib.ERR_INVALID_ARG, "softmax",
+                         f"softmax dim {dim} out of range for rank {x.dim()}")
+    outer = 1
+    for d in x.shape[:dim]:
+        outer *= d
+    inner = 1
+    for d in x.shape[dim + 1:]:
+        inner *= d
+    out = torch.empty_like(x)
+    call(f"oxide_softmax_{_sfx(x)}", _p(x), _p(out), outer, x.shape[dim], inner, _stream())
+    return out
+
+
+def scale_mask_softmax(x: torch.Tensor, scale: float, mask: Optional[torch.Tensor] = None,
+                       lens: Optional[torch.Tensor] = None, rows_per_len: int = 1,
+                       causal_q_len: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """softmax(x * scale + mask) over the last dim (src/ops/attention.rs:41,60,63-79).
+
+    ``mask`` (f32) is added as mask[j % mask.numel()]; ``lens`` (int32, one per
+    group of ``rows_per_len`` rows) and ``causal_q_len`` cut each row's valid
+    length; keys beyond it are 0."""
+    _check(x, mask, lens, out)
+    if mask is not None and mask.dtype != torch.float32:
+        raise OxideError(_lib.ERR_INVALID_ARG, "scale_mask_softmax", "mask must be float32")
+    if lens is not None and lens.dtype != torch.int32:
+        raise OxideError(_lib.ERR_INVALID_ARG, "scale_mask_softmax", "lens must be int32")
+    cols = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    call(f"oxide_scale_mask_softmax_{_sfx(x)}", _p(x), _p(out), x.numel() // cols, cols,
+         float(scale), _p(mask), 0 if mask is None else mask.numel(), _p(lens), rows_per_len,
+         causal_q_len, _stream())
+    return out
+
+
+def rope_table(theta: float, head_dim: int, max_pos: int):
+    """(cos, sin) f32 tables [max_pos, head_dim/2] (src/models/mistral.rs:91-115), on the host."""
+    half = head_dim // 2
+    cos = torch.empty((max_pos, half), dtype=torch.float32)
+    sin = torch.empty((max_pos, half), dtype=torch.float32)
+    call("oxide_rope_table_host_f32", float(theta), head_dim, max_pos, cos.data_ptr(), sin.data_ptr())
+    return cos, sin
+
+
+def rope(q: torch.Tensor, k: Optional[torch.Tensor], cos: torch.Tensor, sin: torch.Tensor,
+         positions: Optional[torch.Tensor] = None, layout: str = "token",
+         q_out: Optional[torch.Tensor] = None, k_out: Optional[torch.Tensor] = None):
+    """Rotate-half RoPE of q (and k) in one launch (src/ops/attention.rs:139-155).
+
+    layout "token": [tokens, heads, head_dim]; "head": [heads, tokens, head_dim]
+    (any leading dims fold into heads).  Pass q_out=q / k_out=k for in-place."""
+    _check(q, k, cos, sin, positions, q_out, k_out)
+    head_dim = q.shape[-1]
+    if layout == "token":
+        tokens, qh = q.shape[0], q.numel() // (q.shape[0] * head_dim)
+        kh = 0 if k is None else k.numel() // (k.shape[0] * head_dim)
+        lay = 0
+    elif layout == "head":
+        tokens = q.shape[-2]
+        qh = q.numel() // (tokens * head_dim)
+        kh = 0 if k is None else k.numel() // (tokens * head_dim)
+        lay = 1
+    else:
+        raise OxideError(_lib.ERR_INVALID_ARG, "rope", f"unknown layout {layout!r}")
+    if cos.shape != sin.shape or cos.dim() != 2 or cos.shape[1] != head_dim // 2:
+        raise OxideError(_lib.ERR_INVALID_ARG, "rope",
+                         f"cos/sin shape {list(cos.shape)} doesn't match [*, {head_dim // 2}]")
+    if positions is not None and positions.dtype != torch.int32:
+        raise OxideError(_lib.ERR_INVALID_ARG, "rope", "positions must be int32")
+    q_out = torch.empty_like(q) if q_out is None else q_out
+    if k is not None:
+        k_out = torch.empty_like(k) if k_out is None else k_out
+    call(f"oxide_rope_{_sfx(q)}", _p(q), _p(q_out), qh, _p(k), _p(k_out) if k is not None else None,
+         kh, _p(cos), _p(sin), cos.shape[0], _p(positions), tokens, head_dim, lay, _stream())
+    return (q_out, k_out) if k is not None else q_out
+
+
+def apply_rotary_emb(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """src/ops/attention.rs:96-159: x [..., seq_len, head_dim], cos/sin [seq_len, half]."""
+    if x.dim() < 3:
+        raise OxideError(_lib.ERR_INVALID_ARG, "apply_rotary_emb",
+                         "apply_rotary_emb requires at least 3D tensor")
+    seq_len, head_dim = x.shape[-2], x.shape[-1]
+    if list(cos.shape) != [seq_len, head_dim // 2] or list(sin.shape) != [seq_len, head_dim // 2]:
+        raise OxideError(_lib.ERR_INVALID_ARG, "apply_rotary_emb",
+                         f"cos shape {list(cos.shape)} doesn't match expected {[seq_len, head_dim // 2]}")
+    return rope(x, None, cos, sin, layout="head")
+
+
+def argmax(x: torch.Tensor) -> torch.Tensor:
+    """Row argmax over the last dim -> int32 indices (lowest index on ties)."""
+    _check(x)
+    cols = x.shape[-1]
+    idx = torch.empty(x.shape[:-1], dtype=torch.int32, device=x.device)
+    call(f"oxide_argmax_rows_{_sfx(x)}", _p(x), x.numel() // cols, cols, _p(idx), _stream())
+    return idx
+
+
+def reduce_rows(x: torch.Tensor, op: int) -> torch.Tensor:
+    """Per-row sum / max / sum of squares over the last dim -> f32."""
+    _check(x)
+    cols = x.shape[-1]
+    out = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    call(f"oxide_reduce_rows_{_sfx(x)}", op, _p(x), x.numel() // cols, cols, _p(out), _stream())
+    return out
+
+
+def workspace_bytes(n: int) -> int:
+    return int(_lib.lib().oxide_reduce_workspace_bytes(n))
+
+
+def reduce(x: torch.Tensor, op: int, workspace: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Whole-tensor sum / max / sum of squares -> f64 scalar tensor on the device."""
+    _check(x)
+    n = x.numel()
+    if workspace is None:
+        workspace = torch.empty(workspace_bytes(n), dtype=torch.uint8, device=x.device)
+    out = torch.empty((), dtype=torch.float64, device=x.device) if out is None else out
+    call(f"oxide_reduce_{_sfx(x)}", op, _p(x), n, _p(out), _p(workspace), workspace.numel(), _stream())
+    return out
+
+
+def reduce_sum(x):
+    return reduce(x, RED_SUM)
+
+
+def reduce_max(x):
+    return reduce(x, RED_MAX)
+
+
+def reduce_sumsq(x):
+    return reduce(x, RED_SUMSQ)

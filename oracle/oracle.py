@@ -1,0 +1,226 @@
+"""numpy front end of the CPU oracle (oxide_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: the parity checker and the timed CPU baseline.  It
+may be imported by tests/, __graft_entry__.smoke() and bench.py's CPU legs,
+never by the product package.  PARITY UNPINNED by reference outputs (the Rust
+reference cannot be built); pinned by known-answer tests and an independent
+numpy restatement (tests/test_oracle_kat.py, tests/test_oracle_numpy.py).
+
+bf16 arrays are numpy uint16 holding raw bf16 bit patterns.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_DIR, "liboxide_oracle.so")
+
+ADD, SUB, MUL, DIV = 0, 1, 2, 3
+RED_SUM, RED_MAX, RED_SUMSQ = 0, 1, 2
+
+_lib = None
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", _DIR], check=True)
+    return LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        h = C.CDLL(LIB_PATH)
+        u64, i32, f32, vp = C.c_uint64, C.c_int, C.c_float, C.c_void_p
+        sig = {
+            "orc_binary_f32": [i32, vp, u64, vp, u64, vp, u64, i32],
+            "orc_binary_bf16": [i32, vp, u64, vp, u64, vp, u64, i32],
+            "orc_scale_f32": [vp, vp, f32, u64, i32],
+            "orc_scale_bf16": [vp, vp, f32, u64, i32],
+            "orc_silu_f32": [vp, vp, u64, i32],
+            "orc_silu_bf16": [vp, vp, u64, i32],
+            "orc_silu_mul_f32": [vp, vp, vp, u64, i32],
+            "orc_silu_mul_bf16": [vp, vp, vp, u64, i32],
+            "orc_rms_norm_f32": [vp, vp, vp, u64, u64, f32, i32],
+            "orc_rms_norm_bf16": [vp, vp, vp, u64, u64, f32, i32],
+            "orc_add_rms_norm_f32": [vp, vp, vp, vp, vp, u64, u64, f32, i32],
+            "orc_add_rms_norm_bf16": [vp, vp, vp, vp, vp, u64, u64, f32, i32],
+            "orc_softmax_f32": [vp, vp, u64, u64, u64, i32],
+            "orc_softmax_bf16": [vp, vp, u64, u64, u64, i32],
+            "orc_scale_mask_softmax_f32": [vp, vp, u64, u64, f32, vp, u64, vp, u64, u64, i32],
+            "orc_scale_mask_softmax_bf16": [vp, vp, u64, u64, f32, vp, u64, vp, u64, u64, i32],
+            "orc_rope_table_f32": [f32, u64, u64, vp, vp],
+            "orc_rope_f32": [vp, vp, u64, u64, u64, i32, vp, vp, vp, i32],
+            "orc_rope_bf16": [vp, vp, u64, u64, u64, i32, vp, vp, vp, i32],
+            "orc_argmax_rows_f32": [vp, u64, u64, vp, i32],
+            "orc_argmax_rows_bf16": [vp, u64, u64, vp, i32],
+            "orc_reduce_rows_f32": [i32, vp, u64, u64, vp, i32],
+            "orc_reduce_rows_bf16": [i32, vp, u64, u64, vp, i32],
+        }
+        for name, args in sig.items():
+            fn = getattr(h, name)
+            fn.argtypes = args
+            fn.restype = None
+        for name in ("orc_reduce_f32", "orc_reduce_bf16"):
+            fn = getattr(h, name)
+            fn.argtypes = [i32, vp, u64, i32]
+            fn.restype = C.c_double
+        h.orc_reduce_seq_f32.argtypes = [i32, vp, u64]
+        h.orc_reduce_seq_f32.restype = C.c_float
+        h.orc_max_threads.restype = i32
+        h.orc_f32_to_bf16.argtypes = [C.c_float]
+        h.orc_f32_to_bf16.restype = C.c_uint16
+        _lib = h
+    return _lib
+
+
+def max_threads() -> int:
+    return int(lib().orc_max_threads())
+
+
+# ---- helpers ------------------------------------------------------------------
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def _sfx(a: np.ndarray) -> str:
+    if a.dtype == np.float32:
+        return "f32"
+    if a.dtype == np.uint16:
+        return "bf16"
+    raise TypeError(f"oracle arrays are float32 or uint16 (bf16 bits), got {a.dtype}")
+
+
+def _c(a):
+    return None if a is None else np.ascontiguousarray(a)
+
+
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f32 -> bf16 bits (numpy; NaN -> quiet NaN)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def bf16_to_f32(h: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(h, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ---- ops ----------------------------------------------------------------------
+def binary(op, a, b, n=None, threads=1, out=None):
+    a, b = _c(a), _c(b)
+    n = max(a.size, b.size) if n is None else n
+    out = np.empty(n, dtype=a.dtype) if out is None else out
+    getattr(lib(), f"orc_binary_{_sfx(a)}")(op, _p(a), a.size, _p(b), b.size, _p(out), n, threads)
+    return out
+
+
+def scale(x, s, threads=1):
+    x = _c(x)
+    out = np.empty_like(x)
+    getattr(lib(), f"orc_scale_{_sfx(x)}")(_p(x), _p(out), float(s), x.size, threads)
+    return out
+
+
+def silu(x, threads=1):
+    x = _c(x)
+    out = np.empty_like(x)
+    getattr(lib(), f"orc_silu_{_sfx(x)}")(_p(x), _p(out), x.size, threads)
+    return out
+
+
+def silu_mul(g, u, threads=1, out=None):
+    g, u = _c(g), _c(u)
+    out = np.empty_like(g) if out is None else out
+    getattr(lib(), f"orc_silu_mul_{_sfx(g)}")(_p(g), _p(u), _p(out), g.size, threads)
+    return out
+
+
+def rms_norm(x, w, eps, threads=1):
+    x, w = _c(x), _c(w)
+    cols = w.size
+    out = np.empty_like(x)
+    getattr(lib(), f"orc_rms_norm_{_sfx(x)}")(_p(x), _p(w), _p(out), x.size // cols, cols,
+                                              float(eps), threads)
+    return out
+
+
+def add_rms_norm(x, r, w, eps, threads=1):
+    x, r, w = _c(x), _c(r), _c(w)
+    cols = w.size
+    h = np.empty_like(x)
+    y = np.empty_like(x)
+    getattr(lib(), f"orc_add_rms_norm_{_sfx(x)}")(_p(x), _p(r), _p(w), _p(h), _p(y),
+                                                  x.size // cols, cols, float(eps), threads)
+    return h, y
+
+
+def softmax(x, outer, dim, inner, threads=1):
+    x = _c(x)
+    out = np.empty_like(x)
+    getattr(lib(), f"orc_softmax_{_sfx(x)}")(_p(x), _p(out), outer, dim, inner, threads)
+    return out
+
+
+def scale_mask_softmax(x, cols, scale, mask=None, lens=None, rows_per_len=1, causal_q_len=0,
+                       threads=1):
+    x = _c(x)
+    mask = None if mask is None else _c(np.asarray(mask, dtype=np.float32))
+    lens = None if lens is None else _c(np.asarray(lens, dtype=np.int32))
+    out = np.empty_like(x)
+    getattr(lib(), f"orc_scale_mask_softmax_{_sfx(x)}")(
+        _p(x), _p(out), x.size // cols, cols, float(scale), _p(mask),
+        0 if mask is None else mask.size, _p(lens), rows_per_len, causal_q_len, threads)
+    return out
+
+
+def rope_table(theta, head_dim, max_pos):
+    half = head_dim // 2
+    cos = np.empty((max_pos, half), dtype=np.float32)
+    sin = np.empty((max_pos, half), dtype=np.float32)
+    lib().orc_rope_table_f32(float(theta), head_dim, max_pos, _p(cos), _p(sin))
+    return cos, sin
+
+
+def rope(x, tokens, heads, head_dim, layout, cos, sin, positions=None, threads=1):
+    x = _c(x)
+    cos, sin = _c(cos), _c(sin)
+    positions = None if positions is None else _c(np.asarray(positions, dtype=np.int32))
+    out = np.empty_like(x)
+    getattr(lib(), f"orc_rope_{_sfx(x)}")(_p(x), _p(out), tokens, heads, head_dim, layout,
+                                          _p(cos), _p(sin), _p(positions), threads)
+    return out
+
+
+def argmax_rows(x, cols, threads=1):
+    x = _c(x)
+    rows = x.size // cols
+    idx = np.empty(rows, dtype=np.uint32)
+    getattr(lib(), f"orc_argmax_rows_{_sfx(x)}")(_p(x), rows, cols, _p(idx), threads)
+    return idx
+
+
+def reduce_rows(op, x, cols, threads=1):
+    x = _c(x)
+    rows = x.size // cols
+    out = np.empty(rows, dtype=np.float32)
+    getattr(lib(), f"orc_reduce_rows_{_sfx(x)}")(op, _p(x), rows, cols, _p(out), threads)
+    return out
+
+
+def reduce(op, x, threads=1) -> float:
+    x = _c(x)
+    return float(getattr(lib(), f"orc_reduce_{_sfx(x)}")(op, _p(x), x.size, threads))
+
+
+def reduce_seq_f32(op, x) -> float:
+    x = _c(np.asarray(x, dtype=np.float32))
+    return float(lib().orc_reduce_seq_f32(op, _p(x), x.size))

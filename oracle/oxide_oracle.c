@@ -1,0 +1,478 @@
+/*
+ * oxide_oracle.c -- CPU restatement of mistralrs-oxide's src/ops loop bodies.
+ *
+ * TEST INFRASTRUCTURE ONLY (parity checker and timed CPU baseline); see
+ * oxide_oracle.h for the contract, the bf16 convention and why parity is
+ * unpinned by reference outputs.
+ *
+ * Build with -ffp-contract=off and without fast-math: Rust never contracts
+ * a*b+c into an FMA and never reassociates, and neither may this file.
+ * f32 transcendental calls go to glibc (expf, powf, cosf, sinf), which is what
+ * Rust's f32::exp / powf / cos / sin lower to on Linux.
+ */
+#include "oxide_oracle.h"
+
+#include <math.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define OMP_FOR _Pragma("omp parallel for schedule(static) num_threads(threads)")
+
+int orc_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+float orc_bf16_to_f32(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+uint16_t orc_f32_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u); /* quiet NaN */
+    u += 0x7fffu + ((u >> 16) & 1u); /* round to nearest, ties to even */
+    return (uint16_t)(u >> 16);
+}
+
+#define B2F orc_bf16_to_f32
+#define F2B orc_f32_to_bf16
+
+static inline float apply_op(int op, float x, float y) {
+    switch (op) {
+        case ORC_ADD: return x + y;
+        case ORC_SUB: return x - y;
+        case ORC_MUL: return x * y;
+        default: return x / y;
+    }
+}
+
+/* ---- binary ops: src/ops/matmul.rs:136-158 (elementwise_op_cpu) --------- */
+void orc_binary_f32(int op, const float* a, uint64_t na, const float* b, uint64_t nb,
+                    float* out, uint64_t n, int threads) {
+    if (na == n && nb == n) {
+        OMP_FOR for (uint64_t i = 0; i < n; ++i) out[i] = apply_op(op, a[i], b[i]);
+        return;
+    }
+    OMP_FOR for (uint64_t i = 0; i < n; ++i) out[i] = apply_op(op, a[i % na], b[i % nb]);
+}
+
+void orc_binary_bf16(int op, const uint16_t* a, uint64_t na, const uint16_t* b, uint64_t nb,
+                     uint16_t* out, uint64_t n, int threads) {
+    OMP_FOR for (uint64_t i = 0; i < n; ++i)
+        out[i] = F2B(apply_op(op, B2F(a[i % na]), B2F(b[i % nb])));
+}
+
+/* ---- scale: build.rs:240-276 / src/cuda_backend/kernels.rs:159-177 ------- */
+void orc_scale_f32(const float* x, float* out, float s, uint64_t n, int threads) {
+    OMP_FOR for (uint64_t i = 0; i < n; ++i) out[i] = x[i] * s;
+}
+
+void orc_scale_bf16(const uint16_t* x, uint16_t* out, float s, uint64_t n, int threads) {
+    OMP_FOR for (uint64_t i = 0; i < n; ++i) out[i] = F2B(B2F(x[i]) * s);
+}
+
+/* ---- SiLU: src/ops/activation.rs:30-33 ---------------------------------- */
+static inline float silu1(float x) {
+    float e = expf(-x);
+    float d = 1.0f + e;
+    float r = 1.0f / d;
+    return x * r;
+}
+
+void orc_silu_f32(const float* x, float* out, uint64_t n, int threads) {
+    OMP_FOR for (uint64_t i = 0; i < n; ++i) out[i] = silu1(x[i]);
+}
+
+void orc_silu_bf16(const uint16_t* x, uint16_t* out, uint64_t n, int threads) {
+    OMP_FOR for (uint64_t i = 0; i < n; ++i) out[i] = F2B(silu1(B2F(x[i])));
+}
+
+/* ---- SiLU * up: src/layers/attention.rs:144-145 (silu, then ops::mul) ---- */
+void orc_silu_mul_f32(const float* g, const float* u, float* out, uint64_t n, int threads) {
+    OMP_FOR for (uint64_t i = 0; i < n; ++i) out[i] = silu1(g[i]) * u[i];
+}
+
+void orc_silu_mul_bf16(const uint16_t* g, const uint16_t* u, uint16_t* out, uint64_t n,
+                       int threads) {
+    /* The composed reference materialises silu(gate) as a bf16 tensor. */
+    OMP_FOR for (uint64_t i = 0; i < n; ++i) {
+        float gated = B2F(F2B(silu1(B2F(g[i]))));
+        out[i] = F2B(gated * B2F(u[i]));
+    }
+}
+
+/* ---- RMSNorm: src/ops/norm.rs:33-47 --------------------------------------- */
+static inline float rms_of_row_f32(const float* x, uint64_t cols, float eps) {
+    float ss = 0.0f;
+    for (uint64_t i = 0; i < cols; ++i) {
+        float v = x[i];
+        ss += v * v;
+    }
+    return sqrtf(ss / (float)cols + eps);
+}
+
+void orc_rms_norm_f32(const float* x, const float* w, float* out, uint64_t rows,
+                      uint64_t cols, float eps, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        const float* xr = x + r * cols;
+        float* orow = out + r * cols;
+        float rms = rms_of_row_f32(xr, cols, eps);
+        for (uint64_t i = 0; i < cols; ++i) {
+            float normalized = xr[i] / rms;
+            orow[i] = normalized * w[i];
+        }
+    }
+}
+
+void orc_rms_norm_bf16(const uint16_t* x, const uint16_t* w, uint16_t* out, uint64_t rows,
+                       uint64_t cols, float eps, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        const uint16_t* xr = x + r * cols;
+        uint16_t* orow = out + r * cols;
+        float ss = 0.0f;
+        for (uint64_t i = 0; i < cols; ++i) {
+            float v = B2F(xr[i]);
+            ss += v * v;
+        }
+        float rms = sqrtf(ss / (float)cols + eps);
+        for (uint64_t i = 0; i < cols; ++i) {
+            float normalized = B2F(xr[i]) / rms;
+            orow[i] = F2B(normalized * B2F(w[i]));
+        }
+    }
+}
+
+/* ---- add + RMSNorm: src/layers/transformer.rs:64 then :67 ---------------- */
+void orc_add_rms_norm_f32(const float* x, const float* r, const float* w, float* h,
+                          float* y, uint64_t rows, uint64_t cols, float eps, int threads) {
+    OMP_FOR for (uint64_t row = 0; row < rows; ++row) {
+        const float* xr = x + row * cols;
+        const float* rr = r + row * cols;
+        float* hr = h + row * cols;
+        float* yr = y + row * cols;
+        for (uint64_t i = 0; i < cols; ++i) hr[i] = xr[i] + rr[i];
+        float rms = rms_of_row_f32(hr, cols, eps);
+        for (uint64_t i = 0; i < cols; ++i) {
+            float normalized = hr[i] / rms;
+            yr[i] = normalized * w[i];
+        }
+    }
+}
+
+void orc_add_rms_norm_bf16(const uint16_t* x, const uint16_t* r, const uint16_t* w,
+                           uint16_t* h, uint16_t* y, uint64_t rows, uint64_t cols, float eps,
+                           int threads) {
+    OMP_FOR for (uint64_t row = 0; row < rows; ++row) {
+        const uint16_t* xr = x + row * cols;
+        const uint16_t* rr = r + row * cols;
+        uint16_t* hr = h + row * cols;
+        uint16_t* yr = y + row * cols;
+        float ss = 0.0f;
+        for (uint64_t i = 0; i < cols; ++i) {
+            hr[i] = F2B(B2F(xr[i]) + B2F(rr[i]));
+            float v = B2F(hr[i]);
+            ss += v * v;
+        }
+        float rms = sqrtf(ss / (float)cols + eps);
+        for (uint64_t i = 0; i < cols; ++i) {
+            float normalized = B2F(hr[i]) / rms;
+            yr[i] = F2B(normalized * B2F(w[i]));
+        }
+    }
+}
+
+/* ---- softmax(x, dim): src/ops/activation.rs:95-120 ------------------------ */
+void orc_softmax_f32(const float* x, float* out, uint64_t outer, uint64_t dim,
+                     uint64_t inner, int threads) {
+    OMP_FOR for (uint64_t oi = 0; oi < outer * inner; ++oi) {
+        uint64_t base = (oi / inner) * dim * inner + (oi % inner);
+        float max_val = -INFINITY;
+        for (uint64_t d = 0; d < dim; ++d) max_val = fmaxf(max_val, x[base + d * inner]);
+        float sum = 0.0f;
+        for (uint64_t d = 0; d < dim; ++d) {
+            float e = expf(x[base + d * inner] - max_val);
+            out[base + d * inner] = e;
+            sum += e;
+        }
+        for (uint64_t d = 0; d < dim; ++d) out[base + d * inner] /= sum;
+    }
+}
+
+void orc_softmax_bf16(const uint16_t* x, uint16_t* out, uint64_t outer, uint64_t dim,
+                      uint64_t inner, int threads) {
+    OMP_FOR for (uint64_t oi = 0; oi < outer * inner; ++oi) {
+        uint64_t base = (oi / inner) * dim * inner + (oi % inner);
+        float max_val = -INFINITY;
+        for (uint64_t d = 0; d < dim; ++d) max_val = fmaxf(max_val, B2F(x[base + d * inner]));
+        float sum = 0.0f;
+        for (uint64_t d = 0; d < dim; ++d) sum += expf(B2F(x[base + d * inner]) - max_val);
+        for (uint64_t d = 0; d < dim; ++d)
+            out[base + d * inner] = F2B(expf(B2F(x[base + d * inner]) - max_val) / sum);
+    }
+}
+
+/* ---- scale + mask + softmax: src/ops/attention.rs:41,60,63-79 ------------- */
+static inline uint64_t valid_len(uint64_t r, uint64_t cols, const int32_t* lens,
+                                 uint64_t rows_per_len, uint64_t causal_q_len) {
+    uint64_t len = cols;
+    if (lens) {
+        int64_t l = lens[r / rows_per_len];
+        if (l < 0) l = 0;
+        if ((uint64_t)l < len) len = (uint64_t)l;
+    }
+    if (causal_q_len) {
+        uint64_t q = r % causal_q_len;
+        uint64_t lim = q + 1 + (cols - causal_q_len);
+        if (lim < len) len = lim;
+    }
+    return len;
+}
+
+static void smax_row(const float* s_in, float* p, uint64_t cols, uint64_t len) {
+    /* s_in already holds scaled+masked scores for j < len. */
+    if (len == 0) {
+        for (uint64_t j = 0; j < cols; ++j) p[j] = 0.0f;
+        return;
+    }
+    float m = -INFINITY;
+    for (uint64_t j = 0; j < len; ++j) m = fmaxf(m, s_in[j]);
+    float sum = 0.0f;
+    for (uint64_t j = 0; j < len; ++j) {
+        p[j] = expf(s_in[j] - m);
+        sum += p[j];
+    }
+    /* keys beyond len carry s = -inf: exp(-inf - m) = 0 contributes nothing */
+    for (uint64_t j = 0; j < len; ++j) p[j] /= sum;
+    for (uint64_t j = len; j < cols; ++j) p[j] = 0.0f;
+}
+
+void orc_scale_mask_softmax_f32(const float* x, float* out, uint64_t rows, uint64_t cols,
+                                float scale, const float* mask, uint64_t mask_len,
+                                const int32_t* lens, uint64_t rows_per_len,
+                                uint64_t causal_q_len, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        const float* xr = x + r * cols;
+        float* pr = out + r * cols;
+        uint64_t len = valid_len(r, cols, lens, rows_per_len, causal_q_len);
+        for (uint64_t j = 0; j < len; ++j) {
+            float s = xr[j] * scale;
+            if (mask) s += mask[j % mask_len];
+            pr[j] = s;
+        }
+        smax_row(pr, pr, cols, len);
+    }
+}
+
+void orc_scale_mask_softmax_bf16(const uint16_t* x, uint16_t* out, uint64_t rows,
+                                 uint64_t cols, float scale, const float* mask,
+                                 uint64_t mask_len, const int32_t* lens,
+                                 uint64_t rows_per_len, uint64_t causal_q_len, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        const uint16_t* xr = x + r * cols;
+        uint16_t* orow = out + r * cols;
+        uint64_t len = valid_len(r, cols, lens, rows_per_len, causal_q_len);
+        float buf_stack[4096];
+        float* buf = buf_stack;
+        float* heap = 0;
+        if (cols > 4096) {
+            heap = (float*)__builtin_malloc(cols * sizeof(float));
+            buf = heap;
+        }
+        for (uint64_t j = 0; j < len; ++j) {
+            float s = B2F(xr[j]) * scale;
+            if (mask) s += mask[j % mask_len];
+            buf[j] = s;
+        }
+        smax_row(buf, buf, cols, len);
+        for (uint64_t j = 0; j < cols; ++j) orow[j] = F2B(buf[j]);
+        if (heap) __builtin_free(heap);
+    }
+}
+
+/* ---- RoPE table: src/models/mistral.rs:102-108 ---------------------------- */
+void orc_rope_table_f32(float theta, uint64_t head_dim, uint64_t max_pos, float* cos_out,
+                        float* sin_out) {
+    uint64_t half = head_dim / 2;
+    for (uint64_t pos = 0; pos < max_pos; ++pos) {
+        for (uint64_t i = 0; i < half; ++i) {
+            float freq = powf(theta, (-2.0f * (float)i) / (float)head_dim);
+            float angle = (float)pos * freq;
+            cos_out[pos * half + i] = cosf(angle);
+            sin_out[pos * half + i] = sinf(angle);
+        }
+    }
+}
+
+/* ---- RoPE: src/ops/attention.rs:139-155 ----------------------------------- */
+static inline uint64_t rope_base(uint64_t t, uint64_t h, uint64_t tokens, uint64_t heads,
+                                 uint64_t head_dim, int layout) {
+    return layout == 0 ? (t * heads + h) * head_dim : (h * tokens + t) * head_dim;
+}
+
+void orc_rope_f32(const float* x, float* out, uint64_t tokens, uint64_t heads,
+                  uint64_t head_dim, int layout, const float* cos_t, const float* sin_t,
+                  const int32_t* positions, int threads) {
+    uint64_t half = head_dim / 2;
+    OMP_FOR for (uint64_t th = 0; th < tokens * heads; ++th) {
+        uint64_t t = th / heads, h = th % heads;
+        uint64_t base = rope_base(t, h, tokens, heads, head_dim, layout);
+        uint64_t p = positions ? (uint64_t)positions[t] : t;
+        for (uint64_t d = 0; d < half; ++d) {
+            float x1 = x[base + d];
+            float x2 = x[base + d + half];
+            float c = cos_t[p * half + d];
+            float s = sin_t[p * half + d];
+            out[base + d] = x1 * c - x2 * s;
+            out[base + d + half] = x1 * s + x2 * c;
+        }
+    }
+}
+
+void orc_rope_bf16(const uint16_t* x, uint16_t* out, uint64_t tokens, uint64_t heads,
+                   uint64_t head_dim, int layout, const float* cos_t, const float* sin_t,
+                   const int32_t* positions, int threads) {
+    uint64_t half = head_dim / 2;
+    OMP_FOR for (uint64_t th = 0; th < tokens * heads; ++th) {
+        uint64_t t = th / heads, h = th % heads;
+        uint64_t base = rope_base(t, h, tokens, heads, head_dim, layout);
+        uint64_t p = positions ? (uint64_t)positions[t] : t;
+        for (uint64_t d = 0; d < half; ++d) {
+            float x1 = B2F(x[base + d]);
+            float x2 = B2F(x[base + d + half]);
+            float c = cos_t[p * half + d];
+            float s = sin_t[p * half + d];
+            float o1 = x1 * c - x2 * s;
+            float o2 = x1 * s + x2 * c;
+            out[base + d] = F2B(o1);
+            out[base + d + half] = F2B(o2);
+        }
+    }
+}
+
+/* ---- argmax: src/tokenizer.rs:213-232 with k = 1 -------------------------- */
+static inline uint32_t argmax_row(const float* v, uint64_t cols) {
+    uint32_t bi = 0;
+    float bv = v[0];
+    for (uint64_t j = 1; j < cols; ++j) {
+        float x = v[j];
+        if (isnan(x)) continue;
+        if (isnan(bv) || x > bv) {
+            bv = x;
+            bi = (uint32_t)j;
+        }
+    }
+    return bi;
+}
+
+void orc_argmax_rows_f32(const float* x, uint64_t rows, uint64_t cols, uint32_t* idx,
+                         int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) idx[r] = argmax_row(x + r * cols, cols);
+}
+
+void orc_argmax_rows_bf16(const uint16_t* x, uint64_t rows, uint64_t cols, uint32_t* idx,
+                          int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        const uint16_t* xr = x + r * cols;
+        uint32_t bi = 0;
+        float bv = B2F(xr[0]);
+        for (uint64_t j = 1; j < cols; ++j) {
+            float v = B2F(xr[j]);
+            if (isnan(v)) continue;
+            if (isnan(bv) || v > bv) {
+                bv = v;
+                bi = (uint32_t)j;
+            }
+        }
+        idx[r] = bi;
+    }
+}
+
+/* ---- row reductions (reference inline loops) ------------------------------ */
+static inline float reduce_step(int op, float acc, float v) {
+    if (op == ORC_RED_SUM) return acc + v;
+    if (op == ORC_RED_MAX) return fmaxf(acc, v);
+    return acc + v * v;
+}
+
+void orc_reduce_rows_f32(int op, const float* x, uint64_t rows, uint64_t cols, float* out,
+                         int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        float acc = op == ORC_RED_MAX ? -INFINITY : 0.0f;
+        for (uint64_t j = 0; j < cols; ++j) acc = reduce_step(op, acc, x[r * cols + j]);
+        out[r] = acc;
+    }
+}
+
+void orc_reduce_rows_bf16(int op, const uint16_t* x, uint64_t rows, uint64_t cols,
+                          float* out, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        float acc = op == ORC_RED_MAX ? -INFINITY : 0.0f;
+        for (uint64_t j = 0; j < cols; ++j) acc = reduce_step(op, acc, B2F(x[r * cols + j]));
+        out[r] = acc;
+    }
+}
+
+/* ---- whole-tensor reductions in f64 --------------------------------------- */
+#define ORC_CHUNK ((uint64_t)1 << 20)
+
+static double combine_chunks(int op, const double* part, uint64_t nchunks) {
+    double acc = op == ORC_RED_MAX ? -INFINITY : 0.0;
+    for (uint64_t c = 0; c < nchunks; ++c)
+        acc = op == ORC_RED_MAX ? fmax(acc, part[c]) : acc + part[c];
+    return acc;
+}
+
+double orc_reduce_f32(int op, const float* x, uint64_t n, int threads) {
+    uint64_t nchunks = (n + ORC_CHUNK - 1) / ORC_CHUNK;
+    if (nchunks == 0) return op == ORC_RED_MAX ? -INFINITY : 0.0;
+    double* part = (double*)__builtin_malloc(nchunks * sizeof(double));
+    OMP_FOR for (uint64_t c = 0; c < nchunks; ++c) {
+        uint64_t lo = c * ORC_CHUNK, hi = lo + ORC_CHUNK < n ? lo + ORC_CHUNK : n;
+        double acc = op == ORC_RED_MAX ? -INFINITY : 0.0;
+        for (uint64_t i = lo; i < hi; ++i) {
+            double v = (double)x[i];
+            if (op == ORC_RED_SUM) acc += v;
+            else if (op == ORC_RED_MAX) acc = fmax(acc, v);
+            else acc += v * v;
+        }
+        part[c] = acc;
+    }
+    double r = combine_chunks(op, part, nchunks);
+    __builtin_free(part);
+    return r;
+}
+
+double orc_reduce_bf16(int op, const uint16_t* x, uint64_t n, int threads) {
+    uint64_t nchunks = (n + ORC_CHUNK - 1) / ORC_CHUNK;
+    if (nchunks == 0) return op == ORC_RED_MAX ? -INFINITY : 0.0;
+    double* part = (double*)__builtin_malloc(nchunks * sizeof(double));
+    OMP_FOR for (uint64_t c = 0; c < nchunks; ++c) {
+        uint64_t lo = c * ORC_CHUNK, hi = lo + ORC_CHUNK < n ? lo + ORC_CHUNK : n;
+        double acc = op == ORC_RED_MAX ? -INFINITY : 0.0;
+        for (uint64_t i = lo; i < hi; ++i) {
+            double v = (double)B2F(x[i]);
+            if (op == ORC_RED_SUM) acc += v;
+            else if (op == ORC_RED_MAX) acc = fmax(acc, v);
+            else acc += v * v;
+        }
+        part[c] = acc;
+    }
+    double r = combine_chunks(op, part, nchunks);
+    __builtin_free(part);
+    return r;
+}
+
+float orc_reduce_seq_f32(int op, const float* x, uint64_t n) {
+    float acc = op == ORC_RED_MAX ? -INFINITY : 0.0f;
+    for (uint64_t i = 0; i < n; ++i) acc = reduce_step(op, acc, x[i]);
+    return acc;
+}

@@ -1,0 +1,477 @@
+"""CUDA kernels vs the CPU oracle on seeded inputs, through the C ABI.
+
+Tolerances (stated by the parity contract):
+  * add / sub / mul / div / scale / row-broadcast mul, RoPE, argmax indices,
+    row max: bit-exact (RoPE uses no transcendental on the device: the tables
+    are inputs, so its IEEE arithmetic matches exactly);
+  * SiLU and SiLU*mul f32: <= 2 ulp (CUDA expf vs glibc expf);
+  * RMSNorm, softmax, sums: <= 1e-5 relative (f32; tree vs sequential order);
+  * every bf16 result: <= 1 bf16 ulp.
+"""
+import numpy as np
+import pytest
+import torch
+
+from _util import (assert_bits_equal, assert_close_rel, assert_ulp, bf16_to_f32, misaligned_copy,
+                   to_dev, to_np)
+
+pytestmark = pytest.mark.gpu
+
+F32_REL = 1e-5
+SILU_F32_ULP = 2
+BF16_ULP = 1
+
+F = np.float32
+
+
+def rand(shape, seed, dtype="f32", scale=1.0, orc=None):
+    x = (np.random.default_rng(seed).standard_normal(shape, dtype=F) * F(scale)).astype(F)
+    return x if dtype == "f32" else orc.f32_to_bf16(x).reshape(shape)
+
+
+def close(got, ref, dtype, rel=F32_REL):
+    if dtype == "bf16":
+        assert_ulp(got, ref, BF16_ULP)
+    else:
+        assert_close_rel(got, ref, rel)
+
+
+# ---------------------------------------------------------------- binary ops
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("op", [0, 1, 2, 3])
+@pytest.mark.parametrize("na,nb,n", [
+    (4096 * 16, 4096 * 16, 4096 * 16),  # full, vector path
+    (1001, 1001, 1001),                 # vector path + scalar tail
+    (8192 * 3, 4096, 8192 * 3),         # row broadcast of b
+    (512, 512 * 6, 512 * 6),            # broadcast of a
+    (40, 24, 120),                      # both indexed modulo
+    (6, 10, 30),                        # modulo lengths not vector multiples -> scalar
+    (1, 1, 1),
+])
+def test_binary(cuda, orc, dtype, op, na, nb, n):
+    from oxide_b200 import ops
+
+    a = rand(na, 1, dtype, orc=orc)
+    b = rand(nb, 2, dtype, orc=orc)
+    if op == 3:
+        b = (np.abs(bf16_to_f32(b) if dtype == "bf16" else b) + F(0.5)).astype(F)
+        b = b if dtype == "f32" else orc.f32_to_bf16(b)
+    ref = orc.binary(op, a, b, n)
+    out = torch.empty(n, dtype=torch.float32 if dtype == "f32" else torch.bfloat16, device=cuda)
+    from oxide_b200._lib import call
+
+    call(f"oxide_binary_{dtype}", op, to_dev(a).data_ptr(), na, to_dev(b).data_ptr(), nb,
+         out.data_ptr(), n, None)
+    torch.cuda.synchronize()
+    assert_bits_equal(to_np(out), ref)
+    if nb < na == n:
+        # tensor-level API with reference broadcasting: [rows, cols] op [cols]
+        got = ops.binary(op, to_dev(a).view(n // nb, nb), to_dev(b))
+        assert_bits_equal(to_np(got).reshape(-1), ref)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_binary_misaligned_pointers(cuda, orc, dtype):
+    from oxide_b200._lib import call
+
+    n = 4099
+    a, b = rand(n, 3, dtype, orc=orc), rand(n, 4, dtype, orc=orc)
+    ta, tb = misaligned_copy(a), misaligned_copy(b)
+    out = misaligned_copy(np.zeros_like(a))
+    call(f"oxide_binary_{dtype}", 0, ta.data_ptr(), n, tb.data_ptr(), n, out.data_ptr(), n, None)
+    torch.cuda.synchronize()
+    assert_bits_equal(to_np(out), orc.binary(0, a, b, n))
+
+
+def test_named_binary_wrappers(cuda, orc):
+    from oxide_b200._lib import call
+
+    rows, cols = 300, 4096
+    a, b = rand((rows, cols), 5), rand((rows, cols), 6)
+    s = np.random.default_rng(7).uniform(0.5, 1.5, cols).astype(F)
+    ta, tb, ts = to_dev(a), to_dev(b), to_dev(s)
+    out = torch.empty_like(ta)
+    for name, op in (("oxide_add_f32", 0), ("oxide_sub_f32", 1), ("oxide_div_f32", 3)):
+        call(name, ta.data_ptr(), tb.data_ptr(), out.data_ptr(), a.size, None)
+        torch.cuda.synchronize()
+        assert_bits_equal(to_np(out), orc.binary(op, a, b))
+    call("oxide_mul_rowbcast_f32", ta.data_ptr(), ts.data_ptr(), out.data_ptr(), rows, cols, None)
+    torch.cuda.synchronize()
+    assert_bits_equal(to_np(out), orc.binary(2, a, s, a.size))
+    ab, bb, sb = orc.f32_to_bf16(a), orc.f32_to_bf16(b), orc.f32_to_bf16(s)
+    tab, tbb, tsb = to_dev(ab), to_dev(bb), to_dev(sb)
+    outb = torch.empty_like(tab)
+    call("oxide_add_bf16", tab.data_ptr(), tbb.data_ptr(), outb.data_ptr(), a.size, None)
+    torch.cuda.synchronize()
+    assert_bits_equal(to_np(outb), orc.binary(0, ab, bb))
+    call("oxide_mul_rowbcast_bf16", tab.data_ptr(), tsb.data_ptr(), outb.data_ptr(), rows, cols, None)
+    torch.cuda.synchronize()
+    assert_bits_equal(to_np(outb), orc.binary(2, ab, sb, a.size))
+
+
+def test_in_place_add(cuda, orc):
+    from oxide_b200._lib import call
+
+    a, b = rand(1 << 20, 8), rand(1 << 20, 9)
+    ta, tb = to_dev(a), to_dev(b)
+    call("oxide_add_f32", ta.data_ptr(), tb.data_ptr(), ta.data_ptr(), a.size, None)
+    torch.cuda.synchronize()
+    assert_bits_equal(to_np(ta), orc.binary(0, a, b))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_scale(cuda, orc, dtype):
+    from oxide_b200 import ops
+
+    x = rand(12345, 10, dtype, orc=orc)
+    got = ops.scale(to_dev(x), 0.0883883)
+    assert_bits_equal(to_np(got), orc.scale(x, 0.0883883))
+
+
+# ---------------------------------------------------------------- activations
+@pytest.mark.parametrize("n", [1, 7, 4096, 1 << 20, (1 << 20) + 3])
+def test_silu_mul_f32(cuda, orc, n):
+    from oxide_b200 import ops
+
+    g, u = rand(n, 11, scale=4.0), rand(n, 12)
+    got = ops.silu_mul(to_dev(g), to_dev(u))
+    assert_ulp(to_np(got), orc.silu_mul(g, u), SILU_F32_ULP)
+    got = ops.silu(to_dev(g))
+    assert_ulp(to_np(got), orc.silu(g), SILU_F32_ULP)
+
+
+@pytest.mark.parametrize("n", [9, 1 << 20])
+def test_silu_mul_bf16(cuda, orc, n):
+    from oxide_b200 import ops
+
+    g, u = rand(n, 13, "bf16", 4.0, orc), rand(n, 14, "bf16", orc=orc)
+    got = ops.silu_mul(to_dev(g), to_dev(u))
+    assert_ulp(to_np(got), orc.silu_mul(g, u), BF16_ULP)
+    assert_ulp(to_np(ops.silu(to_dev(g))), orc.silu(g), BF16_ULP)
+
+
+def test_silu_extremes(cuda, orc):
+    from oxide_b200 import ops
+
+    x = np.array([0.0, -0.0, -100.0, 100.0, -88.0, 88.0, 1e-30, -1e-30], dtype=F)
+    got = to_np(ops.silu(to_dev(x)))
+    assert_ulp(got, orc.silu(x), SILU_F32_ULP)
+
+
+def test_fused_silu_mul_equals_unfused(cuda, orc):
+    """silu then mul (two kernels) == the fused kernel, bit for bit, both dtypes."""
+    from oxide_b200 import ops
+
+    for dtype in ("f32", "bf16"):
+        g, u = rand(1 << 18, 15, dtype, 3.0, orc), rand(1 << 18, 16, dtype, orc=orc)
+        tg, tu = to_dev(g), to_dev(u)
+        fused = to_np(ops.silu_mul(tg, tu))
+        unfused = to_np(ops.mul(ops.silu(tg), tu))
+        assert_bits_equal(fused, unfused)
+
+
+# ---------------------------------------------------------------- RMSNorm
+NORM_SHAPES = [(1, 1), (3, 17), (7, 128), (64, 4096), (33, 5000), (2, 65536), (2, 70000)]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,cols", NORM_SHAPES)
+def test_rms_norm(cuda, orc, dtype, rows, cols):
+    from oxide_b200 import ops
+
+    x = rand((rows, cols), 20 + cols, dtype, orc=orc)
+    w = np.random.default_rng(21).uniform(0.5, 1.5, cols).astype(F)
+    w = w if dtype == "f32" else orc.f32_to_bf16(w)
+    got = ops.rms_norm(to_dev(x), to_dev(w), 1e-5)
+    close(to_np(got), orc.rms_norm(x, w, 1e-5), dtype)
+
+
+def test_rms_norm_misaligned(cuda, orc):
+    from oxide_b200 import ops
+
+    x = rand((5, 256), 22)
+    w = np.random.default_rng(23).uniform(0.5, 1.5, 256).astype(F)
+    tx = misaligned_copy(x)
+    got = ops.rms_norm(tx, to_dev(w), 1e-6)
+    assert_close_rel(to_np(got), orc.rms_norm(x, w, 1e-6), F32_REL)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,cols", [(3, 17), (128, 4096), (2, 70000)])
+def test_add_rms_norm(cuda, orc, dtype, rows, cols):
+    from oxide_b200 import ops
+
+    x = rand((rows, cols), 24, dtype, orc=orc)
+    r = rand((rows, cols), 25, dtype, orc=orc)
+    w = np.ones(cols, F) if dtype == "f32" else orc.f32_to_bf16(np.ones(cols, F))
+    h, y = ops.add_rms_norm(to_dev(x), to_dev(r), to_dev(w), 1e-5)
+    rh, ry = orc.add_rms_norm(x, r, w, 1e-5)
+    assert_bits_equal(to_np(h), rh)
+    close(to_np(y), ry, dtype)
+    # the fused kernel equals add followed by rms_norm on the device
+    h2 = ops.add(to_dev(x), to_dev(r))
+    y2 = ops.rms_norm(h2, to_dev(w), 1e-5)
+    assert_bits_equal(to_np(h), to_np(h2))
+    assert_bits_equal(to_np(y), to_np(y2))
+
+
+def test_add_rms_norm_in_place_residual(cuda, orc):
+    from oxide_b200 import ops
+
+    x, r = rand((64, 4096), 26, "bf16", orc=orc), rand((64, 4096), 27, "bf16", orc=orc)
+    w = orc.f32_to_bf16(np.random.default_rng(28).uniform(0.5, 1.5, 4096).astype(F))
+    tx = to_dev(x)
+    h, y = ops.add_rms_norm(tx, to_dev(r), to_dev(w), 1e-5, h=tx)
+    rh, ry = orc.add_rms_norm(x, r, w, 1e-5)
+    assert_bits_equal(to_np(tx), rh)
+    assert_ulp(to_np(y), ry, BF16_ULP)
+
+
+# ---------------------------------------------------------------- softmax
+SMAX_SHAPES = [(5, 1), (8, 33), (16, 128), (4, 2048), (4, 4096), (6, 6000), (3, 32768),
+               (2, 100000), (1, 200000)]
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,cols", SMAX_SHAPES)
+def test_softmax_rows(cuda, orc, dtype, rows, cols):
+    from oxide_b200 import ops
+
+    x = rand((rows, cols), 30 + cols, dtype, 3.0, orc)
+    got = ops.softmax(to_dev(x), 1)
+    close(to_np(got), orc.softmax(x, rows, cols, 1), dtype)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_softmax_inner_dim(cuda, orc, dtype):
+    from oxide_b200 import ops
+
+    x = rand((3, 50, 7), 31, dtype, 2.0, orc)
+    got = ops.softmax(to_dev(x), 1)
+    close(to_np(got), orc.softmax(x, 3, 50, 7).reshape(3, 50, 7), dtype)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_decode_masked_softmax_lens(cuda, orc, dtype):
+    """C3 shape family: [batch x heads x 1 x keys] with per-batch KV lengths."""
+    from oxide_b200 import ops
+
+    batch, heads, keys = 4, 8, 32768
+    x = rand((batch, heads, 1, keys), 32, dtype, float(np.sqrt(128.0)), orc)
+    lens = np.array([1024, 32768, 5000, 0], dtype=np.int32)  # includes a fully masked batch
+    scale = float(F(1.0) / np.sqrt(F(128)))
+    got = ops.scale_mask_softmax(to_dev(x), scale, lens=to_dev(lens), rows_per_len=heads)
+    ref = orc.scale_mask_softmax(x, keys, scale, lens=lens, rows_per_len=heads)
+    close(to_np(got), ref, dtype)
+    g = to_np(got).reshape(batch * heads, keys)
+    if dtype == "f32":
+        assert np.all(g[-heads:] == 0)  # len 0 -> zeros
+        assert np.all(g[:heads, 1024:] == 0)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_additive_mask_softmax(cuda, orc, dtype):
+    from oxide_b200 import ops
+
+    rows, cols = 12, 1000
+    x = rand((rows, cols), 33, dtype, 5.0, orc)
+    mask = np.where(np.random.default_rng(34).random(cols) < 0.3, -np.inf, 0.25).astype(F)
+    got = ops.scale_mask_softmax(to_dev(x), 0.125, mask=to_dev(mask))
+    close(to_np(got), orc.scale_mask_softmax(x, cols, 0.125, mask=mask), dtype)
+    # a short mask repeats (mask[j % mask_len])
+    short = np.array([0.0, -1.0, -np.inf], F)
+    got = ops.scale_mask_softmax(to_dev(x), 0.125, mask=to_dev(short))
+    close(to_np(got), orc.scale_mask_softmax(x, cols, 0.125, mask=short), dtype)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("q_len,cols", [(256, 256), (64, 300), (2048, 2048)])
+def test_causal_softmax(cuda, orc, dtype, q_len, cols):
+    """C5 shape family: [seqs x heads x q_len x keys] with a causal mask."""
+    from oxide_b200 import ops
+
+    rows = 2 * q_len
+    x = rand((rows, cols), 35 + cols, dtype, 4.0, orc)
+    got = ops.scale_mask_softmax(to_dev(x), 0.0883883, causal_q_len=q_len)
+    close(to_np(got), orc.scale_mask_softmax(x, cols, 0.0883883, causal_q_len=q_len), dtype)
+
+
+def test_softmax_rows_sum_to_one_and_deterministic(cuda, orc):
+    from oxide_b200 import ops
+
+    x = to_dev(rand((256, 32768), 36, scale=11.3))
+    p1 = ops.softmax(x, 1)
+    p2 = ops.softmax(x, 1)
+    assert torch.equal(p1, p2)
+    assert torch.allclose(p1.double().sum(1), torch.ones(256, dtype=torch.float64, device=cuda),
+                          atol=1e-5)
+
+
+def test_all_neg_inf_additive_mask_is_nan_like_reference(cuda, orc):
+    from oxide_b200 import ops
+
+    x = to_dev(np.zeros((2, 64), F))
+    got = to_np(ops.scale_mask_softmax(x, 1.0, mask=to_dev(np.full(64, -np.inf, F))))
+    assert np.all(np.isnan(got))
+
+
+# ---------------------------------------------------------------- RoPE
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("layout", ["token", "head"])
+def test_rope(cuda, orc, dtype, layout):
+    from oxide_b200 import ops
+
+    tokens, qh, kh, d = 300, 8, 2, 128
+    cos, sin = orc.rope_table(1e6, d, 512)
+    shape_q = (tokens, qh, d) if layout == "token" else (qh, tokens, d)
+    shape_k = (tokens, kh, d) if layout == "token" else (kh, tokens, d)
+    q, k = rand(shape_q, 40, dtype, orc=orc), rand(shape_k, 41, dtype, orc=orc)
+    pos = np.random.default_rng(42).integers(0, 512, tokens).astype(np.int32)
+    tq, tk = ops.rope(to_dev(q), to_dev(k), to_dev(cos), to_dev(sin), to_dev(pos), layout)
+    lay = 0 if layout == "token" else 1
+    assert_bits_equal(to_np(tq), orc.rope(q, tokens, qh, d, lay, cos, sin, pos))
+    assert_bits_equal(to_np(tk), orc.rope(k, tokens, kh, d, lay, cos, sin, pos))
+
+
+def test_rope_in_place_no_positions_no_k(cuda, orc):
+    from oxide_b200 import ops
+
+    tokens, h, d = 64, 4, 64
+    cos, sin = orc.rope_table(1e4, d, tokens)
+    q = rand((tokens, h, d), 43, "bf16", orc=orc)
+    tq = to_dev(q)
+    ops.rope(tq, None, to_dev(cos), to_dev(sin), q_out=tq)
+    assert_bits_equal(to_np(tq), orc.rope(q, tokens, h, d, 0, cos, sin))
+
+
+def test_apply_rotary_emb_reference_layout(cuda, orc):
+    """ops::apply_rotary_emb: x [batch, heads, seq, d] with tables [seq, half]."""
+    from oxide_b200 import ops
+
+    b, h, s, d = 2, 3, 40, 32
+    cos, sin = orc.rope_table(1e4, d, s)
+    x = rand((b, h, s, d), 44)
+    got = ops.apply_rotary_emb(to_dev(x), to_dev(cos), to_dev(sin))
+    assert_bits_equal(to_np(got), orc.rope(x, s, b * h, d, 1, cos, sin))
+
+
+def test_rope_unaligned_head_dim_and_bad_position(cuda, orc):
+    from oxide_b200 import ops
+
+    tokens, h, d = 10, 3, 6  # half = 3: scalar kernel
+    cos, sin = orc.rope_table(1e4, d, 16)
+    q = rand((tokens, h, d), 45)
+    pos = np.arange(tokens, dtype=np.int32)
+    pos[4] = 99  # beyond the table -> NaN for that token, no out-of-bounds read
+    got = to_np(ops.rope(to_dev(q), None, to_dev(cos), to_dev(sin), to_dev(pos)))
+    ref = orc.rope(q, tokens, h, d, 0, cos, sin, np.where(pos == 99, 0, pos))
+    assert np.all(np.isnan(got[4]))
+    keep = np.arange(tokens) != 4
+    assert_bits_equal(got[keep], ref[keep])
+
+
+# ---------------------------------------------------------------- argmax
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,cols", [(64, 32000), (1000, 100), (3, 7), (1, 1), (2, 300001)])
+def test_argmax(cuda, orc, dtype, rows, cols):
+    from oxide_b200 import ops
+
+    x = rand((rows, cols), 50 + cols, dtype, orc=orc)
+    got = ops.argmax(to_dev(x))
+    assert np.array_equal(to_np(got).astype(np.uint32), orc.argmax_rows(x, cols))
+
+
+def test_argmax_ties_nan_signed_zero(cuda, orc):
+    from oxide_b200 import ops
+
+    x = np.random.default_rng(51).standard_normal((6, 4096), dtype=F)
+    x[0, [5, 77, 4000]] = 50.0                      # tie
+    x[1] = -0.0
+    x[1, 9] = 0.0                                    # -0 == +0 -> index 0
+    x[2] = np.nan
+    x[2, 1234] = -np.inf                             # NaN below everything
+    x[3] = np.nan                                    # all NaN -> 0
+    x[4, 4095] = np.inf
+    x[5] = -np.inf
+    got = to_np(ops.argmax(to_dev(x))).astype(np.uint32)
+    assert np.array_equal(got, orc.argmax_rows(x, 4096))
+    assert got.tolist()[:5] == [5, 0, 1234, 0, 4095]
+
+
+def test_argmax_misaligned(cuda, orc):
+    from oxide_b200 import ops
+
+    x = rand((5, 1000), 52)
+    got = ops.argmax(misaligned_copy(x))
+    assert np.array_equal(to_np(got).astype(np.uint32), orc.argmax_rows(x, 1000))
+
+
+# ---------------------------------------------------------------- reductions
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,cols", [(1, 1), (17, 333), (64, 4096), (4, 100000)])
+def test_reduce_rows(cuda, orc, dtype, rows, cols):
+    from oxide_b200 import ops
+
+    x = rand((rows, cols), 60 + cols, dtype, orc=orc)
+    xf = x if dtype == "f32" else bf16_to_f32(x).reshape(rows, cols)
+    scale = np.sum(np.abs(xf.astype(np.float64)), axis=1) + 1e-30
+    for op in (0, 1, 2):
+        got = to_np(ops.reduce_rows(to_dev(x), op))
+        ref = orc.reduce_rows(op, x, cols)
+        if op == 1:
+            assert_bits_equal(got, ref)
+        else:
+            lim = F32_REL * (scale if op == 0 else np.abs(ref.astype(np.float64)))
+            assert np.all(np.abs(got.astype(np.float64) - ref) <= lim + 1e-30)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("n", [1, 12345, 1 << 20, 10_000_003])
+def test_reduce_global(cuda, orc, dtype, n):
+    from oxide_b200 import ops
+
+    x = rand(n, 70 + n % 97, dtype, orc=orc)
+    tx = to_dev(x)
+    absum = float(np.sum(np.abs((x if dtype == "f32" else bf16_to_f32(x)).astype(np.float64))))
+    for op in (0, 1, 2):
+        got = float(ops.reduce(tx, op).item())
+        ref = orc.reduce(op, x)
+        if op == 1:
+            assert got == ref
+        elif op == 0:
+            assert abs(got - ref) <= F32_REL * absum
+        else:
+            assert abs(got - ref) <= F32_REL * abs(ref)
+    # deterministic: the same bits on a second run
+    a = ops.reduce(tx, 2)
+    b = ops.reduce(tx, 2)
+    assert a.item() == b.item()
+
+
+def test_reduce_global_misaligned_and_empty(cuda, orc):
+    from oxide_b200 import ops
+
+    x = rand(100001, 80)
+    got = float(ops.reduce(misaligned_copy(x), 2).item())
+    assert abs(got - orc.reduce(2, x)) <= F32_REL * orc.reduce(2, x)
+    e = torch.empty(0, dtype=torch.float32, device=cuda)
+    assert float(ops.reduce(e, 0).item()) == 0.0
+    assert float(ops.reduce(e, 1).item()) == float("-inf")
+
+
+# ---------------------------------------------------------------- status on the GPU path
+def test_injected_failure_does_not_launch(cuda, orc):
+    from oxide_b200 import _lib, ops
+
+    x = to_dev(rand((4, 64), 90))
+    w = to_dev(np.ones(64, F))
+    out = torch.full_like(x, 7.0)
+    _lib.lib().oxide_debug_fail_next(b"oxide_rms_norm_f32")
+    with pytest.raises(_lib.OxideError) as e:
+        ops.rms_norm(x, w, 1e-5, out=out)
+    assert e.value.status == _lib.ERR_INJECTED
+    torch.cuda.synchronize()
+    assert torch.all(out == 7.0)  # nothing ran
+    ops.rms_norm(x, w, 1e-5, out=out)  # next call runs normally
+    torch.cuda.synchronize()
+    assert not torch.all(out == 7.0)
