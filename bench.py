@@ -520,7 +520,8 @@ def run_oxide(args):
     e2e_secs = max_over_ranks(time.perf_counter() - t0, world)
     barrier(world)
     _lib.call("oxide_pipe_destroy", pipe)
-    e2e_ok = bool(np.array_equal(po.numpy()[:4096], to.cpu().numpy().reshape(-1)[:4096]))
+    e2e_ok = bool(np.array_equal(po.numpy().reshape(-1), to.cpu().numpy().reshape(-1)) and
+                  np.array_equal(py.numpy().reshape(-1), ty.cpu().numpy().reshape(-1)))
     h2d = 4 * (a.size + b.size + a.size + s.size + gate.size + up.size)
     d2h = 4 * (a.size + a.size + gate.size)
     e2e_value = world * cfg.bytes() * args.steps / e2e_secs / 1e9

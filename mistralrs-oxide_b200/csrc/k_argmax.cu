@@ -5,12 +5,14 @@
 // the lowest index among equal maxima.  This kernel reproduces that choice,
 // with +0 == -0 and NaN ranked below every number.
 //
-// Design: every element becomes one 64-bit key
-//     (order-preserving 32-bit image of the value) << 32 | (0xffffffff - index)
-// so "largest value, then lowest index" is a plain unsigned max, reduced with
-// shuffles and shared memory.  Many rows: one CTA per row.  Few long rows
-// (decode logits): a cluster of CTAs splits each row and combines the CTA
-// keys through distributed shared memory.
+// Design: each thread scans its elements in increasing index order keeping
+// (best value, index) and replacing only on a strictly greater value -- three
+// instructions per element, ties keep the earlier index, NaN never wins.
+// Thread results merge with shuffles and shared memory (larger value, then
+// lower index); few long rows (decode logits) are split over a thread-block
+// cluster whose CTAs merge through distributed shared memory.  A row whose
+// maximum is -inf (only -inf and NaN) finds no strictly greater element; for
+// it the CTA runs a second scan for the first non-NaN index (0 if none).
 #include <cooperative_groups.h>
 
 #include "oxide_common.cuh"
@@ -19,16 +21,50 @@ namespace cg = cooperative_groups;
 
 namespace oxide {
 
-__device__ __forceinline__ uint64_t amax_key(float v, uint32_t j) {
-    uint32_t k;
-    if (v != v) {
-        k = 0u;  // NaN: below -inf
-    } else {
-        if (v == 0.0f) v = 0.0f;  // -0 ranks equal to +0
-        const uint32_t u = __float_as_uint(v);
-        k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+constexpr uint32_t NONE = 0xffffffffu;
+
+struct Best {
+    float v;
+    uint32_t i;
+};
+
+__device__ __forceinline__ Best better(Best a, Best b) {
+    // b wins with a larger value, or an equal value at a lower index.
+    const bool take = (b.v > a.v) || (b.v == a.v && b.i < a.i);
+    return take ? b : a;
+}
+
+__device__ __forceinline__ Best warp_best(Best b) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Best c{__shfl_xor_sync(0xffffffffu, b.v, o), __shfl_xor_sync(0xffffffffu, b.i, o)};
+        b = better(b, c);
     }
-    return ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - j);
+    return b;
+}
+
+// Block-wide best (every thread receives it).  Contains __syncthreads().
+__device__ __forceinline__ Best block_best(Best b, Best* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    b = warp_best(b);
+    if (lane == 0) red[warp] = b;
+    __syncthreads();
+    Best r = red[0];
+    for (int w = 1; w < nw; ++w) r = better(r, red[w]);
+    __syncthreads();
+    return r;
+}
+
+__device__ __forceinline__ uint32_t block_min_u32(uint32_t v, uint32_t* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    uint32_t r = red[0];
+    for (int w = 1; w < nw; ++w) r = min(r, red[w]);
+    __syncthreads();
+    return r;
 }
 
 template <typename T, bool VEC>
@@ -36,8 +72,10 @@ __global__ void __launch_bounds__(256)
     argmax_kernel(const T* x, uint64_t rows, uint32_t cols, uint32_t* idx, int cl) {
     constexpr int V = VEC ? Vec<T>::N : 1;
     constexpr int UNROLL = 4;
-    __shared__ uint64_t red[8];
-    __shared__ uint64_t slot;
+    __shared__ Best red[8];
+    __shared__ uint32_t redi[8];
+    __shared__ Best slot;
+    __shared__ uint32_t slot_first;
     const uint32_t n = cols / V;  // units (vectors or elements) per row
     int rank = 0;
     if (cl > 1) rank = (int)cg::this_cluster().block_rank();
@@ -45,7 +83,8 @@ __global__ void __launch_bounds__(256)
     const uint32_t lo = rank * per, hi = min(n, lo + per);
     for (uint64_t row = blockIdx.x / cl; row < rows; row += gridDim.x / cl) {
         const T* xr = x + row * cols;
-        uint64_t best = 0;
+        float bv = -INFINITY;
+        uint32_t bi = NONE;
         for (uint32_t u0 = lo + threadIdx.x; u0 < hi; u0 += blockDim.x * UNROLL) {
             if (VEC) {
                 uint4 raw[UNROLL];
@@ -62,8 +101,10 @@ __global__ void __launch_bounds__(256)
                         Vec<T>::unpack(raw[k], f);
 #pragma unroll
                         for (int e = 0; e < Vec<T>::N; ++e) {
-                            const uint64_t key = amax_key(f[e], u * Vec<T>::N + e);
-                            best = key > best ? key : best;
+                            if (f[e] > bv) {
+                                bv = f[e];
+                                bi = u * Vec<T>::N + e;
+                            }
                         }
                     }
                 }
@@ -72,29 +113,48 @@ __global__ void __launch_bounds__(256)
                 for (int k = 0; k < UNROLL; ++k) {
                     const uint32_t u = u0 + k * blockDim.x;
                     if (u < hi) {
-                        const uint64_t key = amax_key(Vec<T>::load1(xr + u), u);
-                        best = key > best ? key : best;
+                        const float f = Vec<T>::load1(xr + u);
+                        if (f > bv) {
+                            bv = f;
+                            bi = u;
+                        }
                     }
                 }
             }
         }
-        best = group_reduce(best, red, (int)blockDim.x, OpMaxU64());
+        Best b = block_best(Best{bv, bi}, red);
         if (cl > 1) {
             cg::cluster_group cluster = cg::this_cluster();
-            if (threadIdx.x == 0) slot = best;
+            if (threadIdx.x == 0) slot = b;
             cluster.sync();
-            if (rank == 0 && threadIdx.x == 0) {
-                uint64_t b = 0;
-                for (int q = 0; q < cl; ++q) {
-                    const uint64_t v = *cluster.map_shared_rank(&slot, q);
-                    b = v > b ? v : b;
-                }
-                best = b;
-            }
-            cluster.sync();  // peers' slots stay valid until rank 0 has read them
+            Best m = *cluster.map_shared_rank(&slot, 0);
+            for (int q = 1; q < cl; ++q) m = better(m, *cluster.map_shared_rank(&slot, q));
+            b = m;
         }
-        if (rank == 0 && threadIdx.x == 0)
-            idx[row] = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+        uint32_t result = b.i;
+        if (b.i == NONE) {
+            // Maximum is -inf: the first non-NaN element wins (0 if all NaN).
+            // Uniform across the cluster: every CTA saw the same merged result.
+            uint32_t first = NONE;
+            for (uint32_t j = rank * per * V + threadIdx.x; j < min(cols, (rank * per + per) * V);
+                 j += blockDim.x) {
+                const float f = Vec<T>::load1(xr + j);
+                if (f == f) {
+                    first = j;
+                    break;
+                }
+            }
+            first = block_min_u32(first, redi);
+            if (cl > 1) {
+                cg::cluster_group cluster = cg::this_cluster();
+                if (threadIdx.x == 0) slot_first = first;
+                cluster.sync();
+                for (int q = 0; q < cl; ++q) first = min(first, *cluster.map_shared_rank(&slot_first, q));
+            }
+            result = first == NONE ? 0u : first;
+        }
+        if (cl > 1) cg::this_cluster().sync();  // peers' slots stay valid until read
+        if (rank == 0 && threadIdx.x == 0) idx[row] = result;
     }
 }
 

@@ -7,12 +7,14 @@
 //
 // Design: each row is owned by a group of `tpr` threads (a warp for short
 // rows, up to 1024 threads for long ones) that loads the whole row into
-// registers with 16-byte streaming reads, so the row crosses HBM exactly
-// once in and once out.  The sum of squares is reduced with a fixed
-// shuffle/shared-memory tree; the normalisation keeps the reference's IEEE
-// divide and separate multiply.  Rows too long for the register budget, or
-// with unaligned/odd lengths, take a two-pass kernel that re-reads the row
-// (the second read is served by L2).
+// registers with 16-byte streaming reads issued back to back, so the row
+// crosses HBM exactly once in and once out.  Each thread holds 16 row
+// elements (32 for rows beyond 16K elements), which keeps every instance
+// inside its register budget without spills.  The sum of squares is reduced
+// with a fixed shuffle/shared-memory tree; the normalisation keeps the
+// reference's IEEE divide and separate multiply.  Rows beyond the register
+// path, or with unaligned/odd lengths, take a two-pass kernel that re-reads
+// the row (the second read is served by L2).
 #include "oxide_common.cuh"
 
 namespace oxide {
@@ -20,12 +22,21 @@ namespace oxide {
 struct NormArgs {
     uint64_t rows;
     uint32_t cols;
-    int tpr;  // threads per row (multiple of 32)
+    int tpr;  // threads per row (multiple of 32; a power of 2 when < 256)
     float eps;
 };
 
+// Row elements held per thread: EPT = VPT * V.  Plain RMSNorm with EPT <= 16
+// fits a 64-register budget (blocks up to 1024 threads); the fused add (two
+// inputs in flight) and EPT = 32 use blocks of at most 512 threads so up to
+// 128 registers are available.
 template <typename T, int VPT, bool ADD>
-__global__ void __launch_bounds__(1024)
+constexpr int norm_block_cap() {
+    return (VPT * Vec<T>::N <= 16 && !ADD) ? 1024 : 512;
+}
+
+template <typename T, int VPT, bool ADD>
+__global__ void __launch_bounds__(norm_block_cap<T, VPT, ADD>())
     rmsnorm_vec_kernel(const T* x, const T* r, const T* w, T* h, T* y, NormArgs p) {
     constexpr int V = Vec<T>::N;
     __shared__ float red[32];
@@ -39,6 +50,7 @@ __global__ void __launch_bounds__(1024)
         const uint64_t off = row * p.cols;
         float v[VPT][V];
         uint4 raw[VPT], rawr[VPT];
+        // Issue every load of the row before using any of them.
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const uint32_t j = t + k * p.tpr;
@@ -115,39 +127,62 @@ static void launch_norm_vec(const T* x, const T* r, const T* w, T* h, T* y, Norm
                             cudaStream_t st) {
     const int rpc = p.tpr >= 256 ? 1 : 256 / p.tpr;
     const int threads = p.tpr * rpc;
-    auto kern = rmsnorm_vec_kernel<T, VPT, ADD>;
-    uint64_t want = (p.rows + rpc - 1) / rpc;
+    const uint64_t want = (p.rows + rpc - 1) / rpc;
     const uint64_t cap = (uint64_t)1 << 30;
-    kern<<<(unsigned)(want < cap ? want : cap), threads, 0, st>>>(x, r, w, h, y, p);
+    rmsnorm_vec_kernel<T, VPT, ADD>
+        <<<(unsigned)(want < cap ? want : cap), threads, 0, st>>>(x, r, w, h, y, p);
+}
+
+// Kernel shape for a row of nvec 16-byte vectors: returns VPT (0 = fallback)
+// and the threads per row.
+template <typename T, bool ADD>
+static int norm_shape(uint64_t nvec, uint64_t* tpr_out) {
+    constexpr int VPT16 = 16 / Vec<T>::N;  // vectors per thread for 16 elements
+    constexpr uint64_t MAX16 = ADD ? 512 : 1024;  // block cap of the EPT-16 instance
+    int vpt = 0;
+    uint64_t tpr = 32;
+    if (nvec <= 32ull * VPT16) {  // short rows: a warp per row, 8 rows per CTA
+        vpt = 1;
+        while ((uint64_t)vpt * 32 < nvec) vpt *= 2;
+    } else if (nvec <= MAX16 * VPT16) {
+        vpt = VPT16;
+        tpr = (nvec + vpt - 1) / vpt;
+    } else if (nvec <= 512ull * 2 * VPT16) {
+        vpt = 2 * VPT16;
+        tpr = (nvec + vpt - 1) / vpt;
+    }
+    if (tpr < 256) {  // sub-CTA groups must tile a 256-thread CTA: a power of 2
+        uint64_t t2 = 32;
+        while (t2 < tpr) t2 *= 2;
+        tpr = t2;
+    } else {
+        tpr = (tpr + 31) / 32 * 32;
+    }
+    *tpr_out = tpr;
+    return vpt;
 }
 
 template <typename T, bool ADD>
 static int norm_dispatch(const char* name, const T* x, const T* r, const T* w, T* h, T* y,
                          uint64_t rows, uint64_t cols, float eps, cudaStream_t st) {
     constexpr int V = Vec<T>::N;
-    constexpr int VPT_MAX = 64 / V;  // at most 64 row elements in registers per thread
     NormArgs p{rows, (uint32_t)cols, 32, eps};
     const bool vec = cols % V == 0 && aligned16(x) && aligned16(w) && aligned16(y) &&
                      (!ADD || (aligned16(r) && aligned16(h)));
-    const uint64_t nvec = cols / V;
-    if (vec && nvec <= (uint64_t)1024 * VPT_MAX) {
-        // Smallest VPT whose group fits in 1024 threads, but at least 4 vectors
-        // per thread for long rows so each thread has several loads in flight.
-        int vpt = 1;
-        while ((uint64_t)vpt * 1024 < nvec) vpt *= 2;
-        if (nvec >= 512 && vpt < 4) vpt = 4;
-        if (vpt > VPT_MAX) vpt = VPT_MAX;
-        uint64_t tpr = (nvec + vpt - 1) / vpt;
-        tpr = (tpr + 31) / 32 * 32;
-        p.tpr = (int)tpr;
-        switch (vpt) {
-            case 1: launch_norm_vec<T, 1, ADD>(x, r, w, h, y, p, st); break;
-            case 2: launch_norm_vec<T, 2, ADD>(x, r, w, h, y, p, st); break;
-            case 4: launch_norm_vec<T, 4, ADD>(x, r, w, h, y, p, st); break;
-            case 8: launch_norm_vec<T, 8, ADD>(x, r, w, h, y, p, st); break;
-            default: launch_norm_vec<T, VPT_MAX, ADD>(x, r, w, h, y, p, st); break;
-        }
+    uint64_t tpr = 32;
+    const int vpt = vec ? norm_shape<T, ADD>(cols / V, &tpr) : 0;
+    p.tpr = (int)tpr;
+    bool launched = true;
+    if (vpt == 1) launch_norm_vec<T, 1, ADD>(x, r, w, h, y, p, st);
+    else if (vpt == 2) launch_norm_vec<T, 2, ADD>(x, r, w, h, y, p, st);
+    else if (vpt == 4) launch_norm_vec<T, 4, ADD>(x, r, w, h, y, p, st);
+    else if constexpr (V == 4) {
+        if (vpt == 8) launch_norm_vec<T, 8, ADD>(x, r, w, h, y, p, st);
+        else launched = false;
     } else {
+        launched = false;
+    }
+    if (!launched) {
         const uint64_t cap = (uint64_t)1 << 30;
         rmsnorm_scalar_kernel<T, ADD>
             <<<(unsigned)(rows < cap ? rows : cap), 256, 0, st>>>(x, r, w, h, y, p);

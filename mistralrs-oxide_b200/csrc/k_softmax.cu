@@ -59,8 +59,18 @@ __device__ __forceinline__ float score(const SmaxArgs& p, float x, uint32_t j) {
     return s;
 }
 
+// 16 row elements per thread run 4 CTAs of 256 threads per SM (<= 64
+// registers); 32 elements per thread run 2 (<= 128 registers); the short-row
+// warp instances (< 16 elements) run 3, whose unrolled exp/divide sequences
+// need a little more than 64 registers.
 template <typename T, int VPT>
-__global__ void __launch_bounds__(256) smax_rows_kernel(const T* x, T* out, SmaxArgs p) {
+constexpr int smax_min_blocks() {
+    return VPT * Vec<T>::N == 16 ? 4 : (VPT * Vec<T>::N < 16 ? 3 : 2);
+}
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(256, smax_min_blocks<T, VPT>())
+    smax_rows_kernel(const T* x, T* out, SmaxArgs p) {
     constexpr int V = Vec<T>::N;
     __shared__ float red[8];
     __shared__ float cl_slot[2];
@@ -231,52 +241,53 @@ static cudaError_t launch_rows(const T* x, T* out, SmaxArgs p, cudaStream_t st) 
     return cudaSuccess;
 }
 
+// Kernel shape for rows of nvec 16-byte vectors.  Every thread holds 16 row
+// elements (32 for rows beyond 8 x 4096 elements); returns VPT (0 = the
+// multi-pass fallback) and sets the threads per row and the cluster size.
+template <typename T>
+static int smax_shape(uint64_t nvec, SmaxArgs& p) {
+    constexpr int VPT16 = 16 / Vec<T>::N;
+    p.cl = 1;
+    if (nvec <= 32ull * VPT16) {  // a warp per row, 8 rows per CTA
+        p.tpr = 32;
+        int vpt = 1;
+        while ((uint64_t)vpt * 32 < nvec) vpt *= 2;
+        return vpt;
+    }
+    if (nvec <= 256ull * VPT16) {  // 64..256 threads per row, 256 / tpr rows per CTA
+        uint64_t tpr = 64;
+        while (tpr * VPT16 < nvec) tpr *= 2;
+        p.tpr = (int)tpr;
+        return VPT16;
+    }
+    p.tpr = 256;  // a cluster of up to 8 CTAs x 256 threads per row (DSMEM exchange)
+    int vpt = VPT16;
+    uint64_t cl = (nvec + 256ull * VPT16 - 1) / (256ull * VPT16);
+    if (cl > 8) {
+        vpt = 2 * VPT16;
+        cl = (nvec + 256ull * vpt - 1) / (256ull * vpt);
+        if (cl > 8) return 0;
+    }
+    int c2 = 1;
+    while ((uint64_t)c2 < cl) c2 *= 2;
+    p.cl = c2;
+    return vpt;
+}
+
 template <typename T>
 static int rows_dispatch(const char* name, const T* x, T* out, SmaxArgs p, cudaStream_t st) {
     constexpr int V = Vec<T>::N;
-    constexpr int VPT_MAX = 64 / V;
-    const uint64_t nvec = p.cols / V;
     const bool vec = p.cols % V == 0 && aligned16(x) && aligned16(out);
+    const int vpt = vec ? smax_shape<T>(p.cols / V, p) : 0;
     const uint64_t cap = (uint64_t)1 << 30;
-    if (!vec || nvec > (uint64_t)8 * 256 * VPT_MAX) {
-        smax_rows_scalar_kernel<T><<<(unsigned)(p.rows < cap ? p.rows : cap), 256, 0, st>>>(x, out, p);
-        return check_launch(name);
-    }
-    int vpt;
-    if (nvec <= 32 * (uint64_t)VPT_MAX) {  // a warp per row, 8 rows per CTA
-        p.tpr = 32;
-        p.cl = 1;
-        vpt = 1;
-        while ((uint64_t)vpt * 32 < nvec) vpt *= 2;
-    } else if (nvec <= 256 * 4) {  // one CTA per row
-        vpt = 4;
-        uint64_t tpr = (nvec + vpt - 1) / vpt;
-        p.tpr = (int)((tpr + 31) / 32 * 32);
-        if (p.tpr > 128) p.tpr = 256;  // keep 256 % tpr == 0
-        else if (p.tpr > 64) p.tpr = 128;
-        p.cl = 1;
-    } else {  // a cluster of up to 8 CTAs x 256 threads per row
-        p.tpr = 256;
-        vpt = 4;
-        uint64_t cl = (nvec + 256 * 4 - 1) / (256 * 4);
-        if (cl > 8) {
-            cl = 8;
-            vpt = (int)((nvec + 8 * 256 - 1) / (8 * 256));
-            int v2 = 1;
-            while (v2 < vpt) v2 *= 2;
-            vpt = v2;
-        }
-        int c2 = 1;
-        while ((uint64_t)c2 < cl) c2 *= 2;
-        p.cl = c2;
-    }
     cudaError_t e = cudaSuccess;
-    switch (vpt) {
-        case 1: e = launch_rows<T, 1>(x, out, p, st); break;
-        case 2: e = launch_rows<T, 2>(x, out, p, st); break;
-        case 4: e = launch_rows<T, 4>(x, out, p, st); break;
-        case 8: e = launch_rows<T, 8>(x, out, p, st); break;
-        default: e = launch_rows<T, VPT_MAX>(x, out, p, st); break;
+    if (vpt == 1) e = launch_rows<T, 1>(x, out, p, st);
+    else if (vpt == 2) e = launch_rows<T, 2>(x, out, p, st);
+    else if (vpt == 4) e = launch_rows<T, 4>(x, out, p, st);
+    else if (vpt == 8) {
+        if constexpr (V == 4) e = launch_rows<T, 8>(x, out, p, st);
+    } else {
+        smax_rows_scalar_kernel<T><<<(unsigned)(p.rows < cap ? p.rows : cap), 256, 0, st>>>(x, out, p);
     }
     if (e != cudaSuccess) {
         cudaGetLastError();

@@ -67,6 +67,47 @@ def assert_close_rel(got: np.ndarray, ref: np.ndarray, rel: float):
     assert worst <= 1.0, f"max error {worst:.3g}x the {rel} relative tolerance"
 
 
+def assert_parity_rel(got: np.ndarray, ref: np.ndarray, exact: np.ndarray, rel: float):
+    """Parity for f32 results whose reference accumulates long sums
+    sequentially in f32: the reference itself is off the exact value by
+    |ref - exact| (a sequential f32 sum of n terms drifts by ~sqrt(n) ulps),
+    so the kernel must be within `rel` of the exact value and within
+    rel + that drift of the reference."""
+    got = np.asarray(got, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    exact = np.asarray(exact, np.float64).reshape(-1)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    m = ~np.isnan(ref)
+    g, r, e = got[m], ref[m], exact[m]
+    lim = rel * np.abs(e) + 1e-38
+    acc = np.max(np.abs(g - e) / lim, initial=0.0)
+    assert acc <= 1.0, f"kernel error vs exact is {acc:.3g}x the {rel} relative tolerance"
+    par = np.max(np.abs(g - r) / (lim + np.abs(r - e)), initial=0.0)
+    assert par <= 1.0, f"kernel vs reference exceeds rel + reference drift ({par:.3g}x)"
+
+
+def softmax_exact(s: np.ndarray, lens=None) -> np.ndarray:
+    """Softmax of f32 score rows with exp and the sum in f64; keys at or
+    beyond lens[row] are 0 (rows with length 0 are all 0)."""
+    s = np.asarray(s, np.float64)
+    rows, cols = s.shape
+    out = np.zeros_like(s)
+    for r in range(rows):
+        n = cols if lens is None else int(lens[r])
+        if n <= 0:
+            continue
+        v = s[r, :n]
+        e = np.exp(v - np.max(v))
+        out[r, :n] = e / np.sum(e)
+    return out
+
+
+def rms_norm_exact(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    x = np.asarray(x, np.float64)
+    rms = np.sqrt(np.sum(x * x, axis=-1, keepdims=True) / x.shape[-1] + np.float64(np.float32(eps)))
+    return x / rms * np.asarray(w, np.float64)
+
+
 def assert_ulp(got: np.ndarray, ref: np.ndarray, max_ulp: int):
     d = ulp_bf16(got, ref) if got.dtype == np.uint16 else ulp_f32(got, ref)
     assert d.max(initial=0) <= max_ulp, f"max {d.max()} ulp (> {max_ulp}) at {np.argmax(d)}"
