@@ -65,6 +65,11 @@ const char* oxide_status_string(int status);
 const char* oxide_last_error(void);
 /* Library version string. */
 const char* oxide_version(void);
+/* Synchronises the current device and reports (in *flags) the device-side
+ * error bits raised by kernels since the last clear: bit 0 = a bounded wait
+ * on a bulk copy timed out (the kernel stopped instead of hanging).  Zero
+ * means none.  clear != 0 resets the bits.  A diagnostic call: it blocks. */
+int oxide_device_errors(unsigned* flags, int clear);
 /* Host-side fault injection for tests: the next call of entry point `op`
  * (e.g. "oxide_rms_norm_f32"; "*" = any) made by any thread returns
  * OXIDE_ERR_INJECTED before launching anything.  NULL clears. */

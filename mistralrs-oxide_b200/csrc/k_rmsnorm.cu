@@ -15,7 +15,7 @@
 // reference's IEEE divide and separate multiply.  Rows beyond the register
 // path, or with unaligned/odd lengths, take a two-pass kernel that re-reads
 // the row (the second read is served by L2).
-#include "oxide_common.cuh"
+#include "oxide_rowstream.cuh"
 
 namespace oxide {
 
@@ -166,6 +166,9 @@ template <typename T, bool ADD>
 static int norm_dispatch(const char* name, const T* x, const T* r, const T* w, T* h, T* y,
                          uint64_t rows, uint64_t cols, float eps, cudaStream_t st) {
     constexpr int V = Vec<T>::N;
+    // Rows of 2-32 KiB stream through the shared-memory bulk-copy ring.
+    if (rms_stream_launch<T>(x, ADD ? r : nullptr, w, h, y, rows, (uint32_t)cols, eps, st))
+        return check_launch(name);
     NormArgs p{rows, (uint32_t)cols, 32, eps};
     const bool vec = cols % V == 0 && aligned16(x) && aligned16(w) && aligned16(y) &&
                      (!ADD || (aligned16(r) && aligned16(h)));

@@ -19,45 +19,11 @@
 // rows beyond the register budget take multi-pass kernels.
 #include <cooperative_groups.h>
 
-#include "oxide_common.cuh"
+#include "oxide_rowstream.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace oxide {
-
-struct SmaxArgs {
-    uint64_t rows;
-    uint32_t cols;
-    float scale;
-    const float* mask;  // additive mask, indexed j % mask_len (nullable)
-    uint32_t mask_len;
-    FastDiv mask_div;
-    const int32_t* lens;  // valid length per group of rows (nullable)
-    uint64_t rows_per_len;
-    uint64_t causal_q;  // 0 = no causal mask
-    int tpr;            // threads per row (per CTA when cl > 1)
-    int cl;             // CTAs per row (cluster size)
-};
-
-__device__ __forceinline__ uint32_t valid_len(const SmaxArgs& p, uint64_t row) {
-    uint64_t len = p.cols;
-    if (p.lens) {
-        int64_t l = p.lens[row / p.rows_per_len];
-        if (l < 0) l = 0;
-        if ((uint64_t)l < len) len = (uint64_t)l;
-    }
-    if (p.causal_q) {
-        uint64_t lim = row % p.causal_q + 1 + (p.cols - p.causal_q);
-        if (lim < len) len = lim;
-    }
-    return (uint32_t)len;
-}
-
-__device__ __forceinline__ float score(const SmaxArgs& p, float x, uint32_t j) {
-    float s = fmul(x, p.scale);
-    if (p.mask) s = fadd(s, __ldg(p.mask + p.mask_div.mod(j)));
-    return s;
-}
 
 // 16 row elements per thread run 4 CTAs of 256 threads per SM (<= 64
 // registers); 32 elements per thread run 2 (<= 128 registers); the short-row
@@ -277,6 +243,8 @@ static int smax_shape(uint64_t nvec, SmaxArgs& p) {
 template <typename T>
 static int rows_dispatch(const char* name, const T* x, T* out, SmaxArgs p, cudaStream_t st) {
     constexpr int V = Vec<T>::N;
+    // Rows of 1-32 KiB stream through the shared-memory bulk-copy ring.
+    if (smax_stream_launch<T>(x, out, p, st)) return check_launch(name);
     const bool vec = p.cols % V == 0 && aligned16(x) && aligned16(out);
     const int vpt = vec ? smax_shape<T>(p.cols / V, p) : 0;
     const uint64_t cap = (uint64_t)1 << 30;
