@@ -65,11 +65,13 @@ const char* oxide_status_string(int status);
 const char* oxide_last_error(void);
 /* Library version string. */
 const char* oxide_version(void);
-/* Synchronises the current device and reports (in *flags) the device-side
- * error bits raised by kernels since the last clear: bit 0 = a bounded wait
- * on a bulk copy timed out (the kernel stopped instead of hanging).  Zero
- * means none.  clear != 0 resets the bits.  A diagnostic call: it blocks. */
-int oxide_device_errors(unsigned* flags, int clear);
+/* Self-test of the row-shared division used by RMSNorm and softmax (a
+ * correctly rounded reciprocal plus FMA residual corrections): compares it
+ * with the IEEE quotient a[i] / b[j] for every pair.  out (device, 2 x u64)
+ * must hold {0, UINT64_MAX}; it receives the mismatch count and the smallest
+ * mismatching pair index i * nb + j.  Diagnostic; no reference counterpart. */
+int oxide_selftest_rowdiv(const float* a, uint64_t na, const float* b, uint64_t nb,
+                          unsigned long long* out, oxide_stream_t stream);
 /* Host-side fault injection for tests: the next call of entry point `op`
  * (e.g. "oxide_rms_norm_f32"; "*" = any) made by any thread returns
  * OXIDE_ERR_INJECTED before launching anything.  NULL clears. */

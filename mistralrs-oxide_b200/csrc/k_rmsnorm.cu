@@ -6,16 +6,18 @@
 // fusion intent src/kernels/normalization.rs:41-77).
 //
 // Design: each row is owned by a group of `tpr` threads (a warp for short
-// rows, up to 1024 threads for long ones) that loads the whole row into
-// registers with 16-byte streaming reads issued back to back, so the row
-// crosses HBM exactly once in and once out.  Each thread holds 16 row
-// elements (32 for rows beyond 16K elements), which keeps every instance
-// inside its register budget without spills.  The sum of squares is reduced
-// with a fixed shuffle/shared-memory tree; the normalisation keeps the
-// reference's IEEE divide and separate multiply.  Rows beyond the register
-// path, or with unaligned/odd lengths, take a two-pass kernel that re-reads
-// the row (the second read is served by L2).
-#include "oxide_rowstream.cuh"
+// rows, a power-of-two group with several rows per 256-thread CTA, or one CTA
+// of up to 1024 threads for long rows).  The group reads the whole row with
+// 16-byte streaming loads issued back to back and keeps it PACKED in
+// registers (bf16 stays 2 bytes per element), 32 elements per thread (16 for
+// the fused f32 add, which has two inputs in flight), so the row crosses HBM
+// once in and once out and many rows are in flight per SM.  The sum of
+// squares is reduced with a fixed shuffle/shared-memory tree; x / rms uses
+// the row-shared RowDiv (the correctly rounded quotient, as the reference's
+// IEEE divide) followed by a separate multiply by w.  Rows beyond the
+// register path, or with unaligned/odd lengths, take a two-pass kernel that
+// re-reads the row (the second read is served by L2).
+#include "oxide_common.cuh"
 
 namespace oxide {
 
@@ -26,17 +28,45 @@ struct NormArgs {
     float eps;
 };
 
-// Row elements held per thread: EPT = VPT * V.  Plain RMSNorm with EPT <= 16
-// fits a 64-register budget (blocks up to 1024 threads); the fused add (two
-// inputs in flight) and EPT = 32 use blocks of at most 512 threads so up to
-// 128 registers are available.
-template <typename T, int VPT, bool ADD>
-constexpr int norm_block_cap() {
-    return (VPT * Vec<T>::N <= 16 && !ADD) ? 1024 : 512;
+// Vectors per thread: 32 row elements, 16 for the fused f32 add.
+template <typename T, bool ADD>
+constexpr int norm_vpt() {
+    return (ADD && Vec<T>::N == 4) ? 4 : 32 / Vec<T>::N;
 }
 
-template <typename T, int VPT, bool ADD>
-__global__ void __launch_bounds__(norm_block_cap<T, VPT, ADD>())
+// y = (v / rms) * w for a thread's VPT packed vectors j = t + k * tpr < jhi.
+// RowDiv's fast path per vector; a vector with a numerator or quotient below
+// its range (or a row whose rms is outside it) is redone with the IEEE divide.
+template <typename T, int VPT>
+__device__ __forceinline__ void norm_store_rms(T* yrow, const T* w, const uint4 (&raw)[VPT],
+                                               uint32_t t, uint32_t tpr, uint32_t jhi, float rms) {
+    constexpr int V = Vec<T>::N;
+    const RowDiv div(rms);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const uint32_t j = t + k * tpr;
+        if (j < jhi) {
+            float v[V], wv[V], q[V], o[V];
+            Vec<T>::unpack(raw[k], v);
+            Vec<T>::unpack(ld_keep(w + (uint64_t)j * V), wv);
+            bool redo = div.ieee;
+#pragma unroll
+            for (int e = 0; e < V; ++e) q[e] = div.fast(v[e], redo);
+            if (redo) {
+#pragma unroll
+                for (int e = 0; e < V; ++e) q[e] = __fdiv_rn(v[e], rms);
+            }
+#pragma unroll
+            for (int e = 0; e < V; ++e) o[e] = fmul(q[e], wv[e]);
+            st_stream(yrow + (uint64_t)j * V, Vec<T>::pack(o));
+        }
+    }
+}
+
+// BIG: one row per CTA of up to 1024 threads; otherwise 256-thread CTAs with
+// a 64-register budget (4 CTAs per SM).
+template <typename T, int VPT, bool ADD, bool BIG>
+__global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : 4)
     rmsnorm_vec_kernel(const T* x, const T* r, const T* w, T* h, T* y, NormArgs p) {
     constexpr int V = Vec<T>::N;
     __shared__ float red[32];
@@ -48,8 +78,7 @@ __global__ void __launch_bounds__(norm_block_cap<T, VPT, ADD>())
         const uint64_t row = row0 + sub;
         const bool active = row < p.rows;
         const uint64_t off = row * p.cols;
-        float v[VPT][V];
-        uint4 raw[VPT], rawr[VPT];
+        uint4 raw[VPT], rawr[ADD ? VPT : 1];
         // Issue every load of the row before using any of them.
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
@@ -59,37 +88,93 @@ __global__ void __launch_bounds__(norm_block_cap<T, VPT, ADD>())
                 if (ADD) rawr[k] = ld_stream(r + off + (uint64_t)j * V);
             }
         }
+        // pass 1: h = x + r (stored, kept packed in raw) and the sum of squares
         float ss = 0.0f;
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const uint32_t j = t + k * p.tpr;
             if (active && j < nvec) {
-                Vec<T>::unpack(raw[k], v[k]);
+                float v[V];
+                Vec<T>::unpack(raw[k], v);
                 if (ADD) {
                     float rv[V];
-                    Vec<T>::unpack(rawr[k], rv);
+                    Vec<T>::unpack(rawr[ADD ? k : 0], rv);
 #pragma unroll
-                    for (int e = 0; e < V; ++e) v[k][e] = Vec<T>::rnd(fadd(v[k][e], rv[e]));
-                    st_stream(h + off + (uint64_t)j * V, Vec<T>::pack(v[k]));
+                    for (int e = 0; e < V; ++e) v[e] = Vec<T>::rnd(fadd(v[e], rv[e]));
+                    raw[k] = Vec<T>::pack(v);  // exact: v already holds T values
+                    st_stream(h + off + (uint64_t)j * V, raw[k]);
                 }
 #pragma unroll
-                for (int e = 0; e < V; ++e) ss = fadd(ss, fmul(v[k][e], v[k][e]));
+                for (int e = 0; e < V; ++e) ss = fadd(ss, fmul(v[e], v[e]));
             }
         }
         ss = group_reduce(ss, red, p.tpr, OpAddF());
-        const float rms = fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps));
+        // pass 2: y = (h / rms) * w
+        norm_store_rms<T, VPT>(y + off, w, raw, t, p.tpr, active ? nvec : 0,
+                               fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps)));
+    }
+}
+
+// Plain RMSNorm over tiled rows with prefetch: 256-thread CTAs own tiles of
+// 256 / tpr rows and loop over tiles blockIdx.x + i * gridDim.x; the next
+// NORM_PF - 1 tiles are copied into a shared-memory ring with per-thread
+// cp.async while the current tile is normalised, so rows are in flight from
+// HBM independently of the register budget.  Each thread copies exactly the
+// 16-byte vectors it later reads: cp.async.wait_group is the only sync.
+constexpr int NORM_PF = 4;
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(256, 3)
+    rmsnorm_pref_kernel(const T* x, const T* w, T* y, NormArgs p) {
+    constexpr int V = Vec<T>::N;
+    extern __shared__ __align__(16) uint4 ring[];  // [NORM_PF][VPT][256]
+    __shared__ float red[8];
+    const uint32_t nvec = p.cols / V;
+    const int rpc = 256 / p.tpr;
+    const int sub = threadIdx.x / p.tpr, t = threadIdx.x % p.tpr;
+    const uint64_t ntiles = (p.rows + rpc - 1) / rpc;
+    const uint64_t first = blockIdx.x, step = gridDim.x;
+    const uint64_t nmine = first < ntiles ? (ntiles - first + step - 1) / step : 0;
+    auto slot = [&](uint64_t i, int k) {
+        return ring + ((size_t)(i % NORM_PF) * VPT + k) * 256 + threadIdx.x;
+    };
+    auto prefetch = [&](uint64_t i) {
+        if (i < nmine) {
+            const uint64_t row = (first + i * step) * rpc + sub;
+            if (row < p.rows) {
+#pragma unroll
+                for (int k = 0; k < VPT; ++k) {
+                    const uint32_t j = t + k * p.tpr;
+                    if (j < nvec) cp_async16(slot(i, k), x + row * p.cols + (uint64_t)j * V);
+                }
+            }
+        }
+        cp_async_commit();  // one group per tile, possibly empty: uniform counting
+    };
+    for (int s = 0; s < NORM_PF - 1; ++s) prefetch(s);
+    for (uint64_t i = 0; i < nmine; ++i) {
+        prefetch(i + NORM_PF - 1);
+        cp_async_wait<NORM_PF - 1>();  // this thread's copies of tile i landed
+        const uint64_t row = (first + i * step) * rpc + sub;
+        const bool active = row < p.rows;
+        uint4 raw[VPT];
+        float ss = 0.0f;
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const uint32_t j = t + k * p.tpr;
             if (active && j < nvec) {
-                float wv[V], o[V];
-                Vec<T>::unpack(ld_keep(w + (uint64_t)j * V), wv);
+                raw[k] = lds16(slot(i, k));
+                float v[V];
+                Vec<T>::unpack(raw[k], v);
 #pragma unroll
-                for (int e = 0; e < V; ++e) o[e] = fmul(fdiv(v[k][e], rms), wv[e]);
-                st_stream(y + off + (uint64_t)j * V, Vec<T>::pack(o));
+                for (int e = 0; e < V; ++e) ss = fadd(ss, fmul(v[e], v[e]));
             }
         }
+        ss = group_reduce(ss, red, p.tpr, OpAddF());
+        norm_store_rms<T, VPT>(y + row * p.cols, w, raw, t, p.tpr, active ? nvec : 0,
+                               fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps)));
     }
+    cp_async_wait<0>();
 }
 
 // Two-pass fallback: any cols, any alignment.  One CTA per row.  Pass 2
@@ -110,82 +195,74 @@ __global__ void __launch_bounds__(256)
             ss = fadd(ss, fmul(v, v));
         }
         ss = group_reduce(ss, red, (int)blockDim.x, OpAddF());
-        const float rms = fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps));
+        const RowDiv div(fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps)));
         const T* src = ADD ? h : x;
         for (uint32_t i = threadIdx.x; i < p.cols; i += blockDim.x) {
             const T* q = src + off + i;
             float v;
             if (sizeof(T) == 4) v = *reinterpret_cast<const volatile float*>(q);
             else v = bf16_to_f32(*reinterpret_cast<const volatile uint16_t*>(q));
-            Vec<T>::store1(y + off + i, fmul(fdiv(v, rms), Vec<T>::load1(w + i)));
+            Vec<T>::store1(y + off + i, fmul(div(v), Vec<T>::load1(w + i)));
         }
     }
 }
 
-template <typename T, int VPT, bool ADD>
+template <typename T, int VPT, bool ADD, bool BIG>
 static void launch_norm_vec(const T* x, const T* r, const T* w, T* h, T* y, NormArgs p,
                             cudaStream_t st) {
     const int rpc = p.tpr >= 256 ? 1 : 256 / p.tpr;
     const int threads = p.tpr * rpc;
     const uint64_t want = (p.rows + rpc - 1) / rpc;
     const uint64_t cap = (uint64_t)1 << 30;
-    rmsnorm_vec_kernel<T, VPT, ADD>
+    rmsnorm_vec_kernel<T, VPT, ADD, BIG>
         <<<(unsigned)(want < cap ? want : cap), threads, 0, st>>>(x, r, w, h, y, p);
-}
-
-// Kernel shape for a row of nvec 16-byte vectors: returns VPT (0 = fallback)
-// and the threads per row.
-template <typename T, bool ADD>
-static int norm_shape(uint64_t nvec, uint64_t* tpr_out) {
-    constexpr int VPT16 = 16 / Vec<T>::N;  // vectors per thread for 16 elements
-    constexpr uint64_t MAX16 = ADD ? 512 : 1024;  // block cap of the EPT-16 instance
-    int vpt = 0;
-    uint64_t tpr = 32;
-    if (nvec <= 32ull * VPT16) {  // short rows: a warp per row, 8 rows per CTA
-        vpt = 1;
-        while ((uint64_t)vpt * 32 < nvec) vpt *= 2;
-    } else if (nvec <= MAX16 * VPT16) {
-        vpt = VPT16;
-        tpr = (nvec + vpt - 1) / vpt;
-    } else if (nvec <= 512ull * 2 * VPT16) {
-        vpt = 2 * VPT16;
-        tpr = (nvec + vpt - 1) / vpt;
-    }
-    if (tpr < 256) {  // sub-CTA groups must tile a 256-thread CTA: a power of 2
-        uint64_t t2 = 32;
-        while (t2 < tpr) t2 *= 2;
-        tpr = t2;
-    } else {
-        tpr = (tpr + 31) / 32 * 32;
-    }
-    *tpr_out = tpr;
-    return vpt;
 }
 
 template <typename T, bool ADD>
 static int norm_dispatch(const char* name, const T* x, const T* r, const T* w, T* h, T* y,
                          uint64_t rows, uint64_t cols, float eps, cudaStream_t st) {
     constexpr int V = Vec<T>::N;
-    // Rows of 2-32 KiB stream through the shared-memory bulk-copy ring.
-    if (rms_stream_launch<T>(x, ADD ? r : nullptr, w, h, y, rows, (uint32_t)cols, eps, st))
-        return check_launch(name);
+    constexpr int VT = norm_vpt<T, ADD>();
     NormArgs p{rows, (uint32_t)cols, 32, eps};
     const bool vec = cols % V == 0 && aligned16(x) && aligned16(w) && aligned16(y) &&
                      (!ADD || (aligned16(r) && aligned16(h)));
-    uint64_t tpr = 32;
-    const int vpt = vec ? norm_shape<T, ADD>(cols / V, &tpr) : 0;
-    p.tpr = (int)tpr;
-    bool launched = true;
-    if (vpt == 1) launch_norm_vec<T, 1, ADD>(x, r, w, h, y, p, st);
-    else if (vpt == 2) launch_norm_vec<T, 2, ADD>(x, r, w, h, y, p, st);
-    else if (vpt == 4) launch_norm_vec<T, 4, ADD>(x, r, w, h, y, p, st);
-    else if constexpr (V == 4) {
-        if (vpt == 8) launch_norm_vec<T, 8, ADD>(x, r, w, h, y, p, st);
-        else launched = false;
-    } else {
-        launched = false;
+    const uint64_t nvec = cols / V;
+    if constexpr (!ADD) {
+        // Plain RMSNorm on rows that tile a 256-thread CTA: prefetching kernel
+        // with 4 vectors per thread.
+        if (vec && nvec <= 256ull * 4) {
+            uint64_t tpr = 32;
+            while (tpr * 4 < nvec) tpr *= 2;
+            p.tpr = (int)tpr;
+            auto pk = rmsnorm_pref_kernel<T, 4>;
+            const size_t smem = (size_t)NORM_PF * 4 * 256 * 16;
+            const int resident = ensure_dyn_smem(reinterpret_cast<const void*>(pk), smem)
+                                     ? resident_blocks(reinterpret_cast<const void*>(pk), 256, smem)
+                                     : 0;
+            if (resident > 0) {
+                const uint64_t tiles = (rows + (256 / tpr) - 1) / (256 / tpr);
+                const unsigned grid = (unsigned)(tiles < (uint64_t)resident ? tiles : (uint64_t)resident);
+                pk<<<grid, 256, smem, st>>>(x, w, y, p);
+                return check_launch(name);
+            }
+        }
     }
-    if (!launched) {
+    if (vec && nvec <= 32ull * VT) {  // short rows: a warp per row, 8 rows per CTA
+        int vpt = 1;
+        while ((uint64_t)vpt * 32 < nvec) vpt *= 2;
+        if (vpt == VT) launch_norm_vec<T, VT, ADD, false>(x, r, w, h, y, p, st);
+        else if (vpt == 1) launch_norm_vec<T, 1, ADD, false>(x, r, w, h, y, p, st);
+        else if (vpt == 2) launch_norm_vec<T, 2, ADD, false>(x, r, w, h, y, p, st);
+        else launch_norm_vec<T, (VT >= 4 ? 4 : VT), ADD, false>(x, r, w, h, y, p, st);
+    } else if (vec && nvec <= 256ull * VT) {  // 64..256 threads per row
+        uint64_t tpr = 64;
+        while (tpr * VT < nvec) tpr *= 2;
+        p.tpr = (int)tpr;
+        launch_norm_vec<T, VT, ADD, false>(x, r, w, h, y, p, st);
+    } else if (vec && nvec <= 1024ull * VT) {  // one CTA of up to 1024 threads per row
+        p.tpr = (int)(((nvec + VT - 1) / VT + 31) / 32 * 32);
+        launch_norm_vec<T, VT, ADD, true>(x, r, w, h, y, p, st);
+    } else {
         const uint64_t cap = (uint64_t)1 << 30;
         rmsnorm_scalar_kernel<T, ADD>
             <<<(unsigned)(rows < cap ? rows : cap), 256, 0, st>>>(x, r, w, h, y, p);

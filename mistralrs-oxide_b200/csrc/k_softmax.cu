@@ -6,89 +6,227 @@
 // softmax over the key axis).
 //
 // Design (rows of a contiguous [rows, cols] tensor):
-//   * a row is owned by `tpr` threads of one CTA (a warp for rows of up to
-//     256 vectors, several rows per CTA) or, for long decode rows, by a
-//     thread-block cluster of `cl` CTAs that exchange the row max and the row
-//     sum through distributed shared memory;
-//   * the row is read once into registers with 16-byte streaming loads,
-//     max/sum are reduced with fixed trees (deterministic), and the
-//     probabilities are written once;
+//   * rows that tile a 256-thread CTA (a warp or a power-of-two group per
+//     row) run on persistent CTAs that prefetch the next tiles into a
+//     shared-memory ring with per-thread cp.async while computing the current
+//     one; long rows run one CTA of up to 512 threads per row, or, when there
+//     are too few rows to fill the GPU, a thread-block cluster of up to 8
+//     CTAs per row that exchange the row max and sum through distributed
+//     shared memory;
+//   * each thread holds its part of the row PACKED (bf16 stays 2 bytes per
+//     element), 32 elements for bf16 and 16 for f32; the kernels are
+//     instruction-bound, so fully valid 16-byte vectors take a path without
+//     per-element bounds checks and the additive mask is a template
+//     parameter; max and sum use fixed reduction trees (deterministic); the
+//     divide by the row sum is RowDiv (the correctly rounded quotient);
 //   * keys at or beyond a row's valid length (lens / causal) are written as 0
 //     and never read.
 // softmax over an inner (non-last) dim, odd lengths, unaligned pointers and
 // rows beyond the register budget take multi-pass kernels.
 #include <cooperative_groups.h>
 
-#include "oxide_rowstream.cuh"
+#include "oxide_softmax.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace oxide {
 
-// 16 row elements per thread run 4 CTAs of 256 threads per SM (<= 64
-// registers); 32 elements per thread run 2 (<= 128 registers); the short-row
-// warp instances (< 16 elements) run 3, whose unrolled exp/divide sequences
-// need a little more than 64 registers.
-template <typename T, int VPT>
-constexpr int smax_min_blocks() {
-    return VPT * Vec<T>::N == 16 ? 4 : (VPT * Vec<T>::N < 16 ? 3 : 2);
+// ---- per-thread row chunk: VPT packed vectors j = j0 + k * jstep ------------
+template <bool MASK>
+__device__ __forceinline__ float score_t(const SmaxArgs& p, float x, uint32_t c) {
+    float s = fmul(x, p.scale);
+    if (MASK) s = fadd(s, __ldg(p.mask + p.mask_div.mod(c)));
+    return s;
 }
 
-template <typename T, int VPT>
-__global__ void __launch_bounds__(256, smax_min_blocks<T, VPT>())
-    smax_rows_kernel(const T* x, T* out, SmaxArgs p) {
+// Max of the valid scores of the chunk (vectors j < jhi, keys c < len).
+template <typename T, int VPT, bool MASK>
+__device__ __forceinline__ float chunk_max(const uint4 (&raw)[VPT], const SmaxArgs& p, uint32_t j0,
+                                           uint32_t jstep, uint32_t jhi, uint32_t len) {
     constexpr int V = Vec<T>::N;
-    __shared__ float red[8];
-    __shared__ float cl_slot[2];
-    const uint32_t nvec = p.cols / V;
-    int rank = 0, rpc = 1, sub = 0, t = threadIdx.x;
-    uint64_t row_first, row_step;
-    uint32_t vlo = 0, vhi = nvec;
-    if (p.cl > 1) {
-        rank = (int)cg::this_cluster().block_rank();
-        const uint32_t per = (nvec + p.cl - 1) / p.cl;
-        vlo = rank * per;
-        vhi = min(nvec, vlo + per);
-        row_first = blockIdx.x / p.cl;
-        row_step = gridDim.x / p.cl;
-    } else {
-        rpc = blockDim.x / p.tpr;
-        sub = threadIdx.x / p.tpr;
-        t = threadIdx.x % p.tpr;
-        row_first = (uint64_t)blockIdx.x * rpc;
-        row_step = (uint64_t)gridDim.x * rpc;
-    }
-    for (uint64_t row0 = row_first; row0 < p.rows; row0 += row_step) {
-        const uint64_t row = row0 + sub;
-        const bool active = row < p.rows;
-        const uint32_t len = active ? valid_len(p, row) : 0;
-        const T* xr = x + row * p.cols;
-        T* orow = out + row * p.cols;
-        float s[VPT][V];
-        uint4 raw[VPT];
+    float m = -INFINITY;
 #pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            const uint32_t j = vlo + t + k * p.tpr;
-            if (active && j < vhi && j * V < len) raw[k] = ld_stream(xr + (uint64_t)j * V);
+    for (int k = 0; k < VPT; ++k) {
+        const uint32_t j = j0 + k * jstep;
+        if (j < jhi && j * V < len) {
+            float f[V];
+            Vec<T>::unpack(raw[k], f);
+            if (j * V + V <= len) {
+#pragma unroll
+                for (int e = 0; e < V; ++e) m = fmaxf(m, score_t<MASK>(p, f[e], j * V + e));
+            } else {
+#pragma unroll
+                for (int e = 0; e < V; ++e)
+                    if (j * V + e < len) m = fmaxf(m, score_t<MASK>(p, f[e], j * V + e));
+            }
         }
-        float m = -INFINITY;
+    }
+    return m;
+}
+
+// ev = exp(score - m) for valid keys (0 for masked keys of a partial vector);
+// returns the thread's sum in vector order.
+template <typename T, int VPT, bool MASK>
+__device__ __forceinline__ float chunk_exp(const uint4 (&raw)[VPT], float (&ev)[VPT][Vec<T>::N],
+                                           const SmaxArgs& p, uint32_t j0, uint32_t jstep,
+                                           uint32_t jhi, uint32_t len, float m) {
+    constexpr int V = Vec<T>::N;
+    float sum = 0.0f;
 #pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            const uint32_t j = vlo + t + k * p.tpr;
-            if (active && j < vhi && j * V < len) {
-                Vec<T>::unpack(raw[k], s[k]);
+    for (int k = 0; k < VPT; ++k) {
+        const uint32_t j = j0 + k * jstep;
+        if (j < jhi && j * V < len) {
+            float f[V];
+            Vec<T>::unpack(raw[k], f);
+            if (j * V + V <= len) {
 #pragma unroll
                 for (int e = 0; e < V; ++e) {
-                    const uint32_t c = j * V + e;
-                    s[k][e] = c < len ? score(p, s[k][e], c) : -INFINITY;
-                    m = fmaxf(m, s[k][e]);
+                    ev[k][e] = expf(fsub(score_t<MASK>(p, f[e], j * V + e), m));
+                    sum = fadd(sum, ev[k][e]);
                 }
             } else {
 #pragma unroll
-                for (int e = 0; e < V; ++e) s[k][e] = -INFINITY;
+                for (int e = 0; e < V; ++e) {
+                    ev[k][e] = j * V + e < len ? expf(fsub(score_t<MASK>(p, f[e], j * V + e), m))
+                                               : 0.0f;
+                    sum = fadd(sum, ev[k][e]);
+                }
             }
         }
-        m = group_reduce(m, red, p.tpr, OpMaxF());
+    }
+    return sum;
+}
+
+// Write p = ev / sum (0 beyond len) for every vector j < jhi of the chunk.
+// RowDiv's fast path per vector; a vector with a numerator or quotient below
+// its range (or a row whose sum is outside it) is redone with the IEEE divide.
+template <typename T, int VPT>
+__device__ __forceinline__ void chunk_store_div(T* orow, const float (&ev)[VPT][Vec<T>::N],
+                                                uint32_t j0, uint32_t jstep, uint32_t jhi,
+                                                uint32_t len, float sum) {
+    constexpr int V = Vec<T>::N;
+    const RowDiv div(sum);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const uint32_t j = j0 + k * jstep;
+        if (j < jhi) {
+            float o[V];
+            if (j * V < len) {
+                bool redo = div.ieee;
+#pragma unroll
+                for (int e = 0; e < V; ++e) o[e] = div.fast(ev[k][e], redo);
+                if (redo) {
+#pragma unroll
+                    for (int e = 0; e < V; ++e) o[e] = __fdiv_rn(ev[k][e], sum);
+                }
+                if (j * V + V > len) {
+#pragma unroll
+                    for (int e = 0; e < V; ++e)
+                        if (j * V + e >= len) o[e] = 0.0f;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < V; ++e) o[e] = 0.0f;
+            }
+            st_stream(orow + (uint64_t)j * V, Vec<T>::pack(o));
+        }
+    }
+}
+
+// Vectors per thread: 32 row elements for bf16 (2 bytes each in flight), 16
+// for f32, so the kept exp values fit the register budgets below.
+constexpr int SMAX_VPT = 4;
+
+// ---- tiled rows with prefetch ------------------------------------------------
+// 256-thread CTAs own tiles of 256 / tpr rows and loop over tiles
+// blockIdx.x + i * gridDim.x.  The next PF_STAGES - 1 tiles are copied into a
+// shared-memory ring with per-thread cp.async while the current tile is
+// computed.  Each thread copies exactly the 16-byte vectors it later reads, so
+// only cp.async.wait_group is needed.
+constexpr int PF_STAGES = 4;
+
+template <typename T, int VPT, bool MASK>
+__global__ void __launch_bounds__(256, 3) smax_pref_kernel(const T* x, T* out, SmaxArgs p) {
+    constexpr int V = Vec<T>::N;
+    extern __shared__ __align__(16) uint4 ring[];  // [PF_STAGES][VPT][256]
+    __shared__ float red[8];
+    const uint32_t nvec = p.cols / V;
+    const int rpc = 256 / p.tpr;
+    const int sub = threadIdx.x / p.tpr, t = threadIdx.x % p.tpr;
+    const uint64_t ntiles = (p.rows + rpc - 1) / rpc;
+    const uint64_t first = blockIdx.x, step = gridDim.x;
+    const uint64_t nmine = first < ntiles ? (ntiles - first + step - 1) / step : 0;
+    auto slot = [&](uint64_t i, int k) {
+        return ring + ((size_t)(i % PF_STAGES) * VPT + k) * 256 + threadIdx.x;
+    };
+    auto prefetch = [&](uint64_t i) {
+        if (i < nmine) {
+            const uint64_t row = (first + i * step) * rpc + sub;
+            if (row < p.rows) {
+                const uint32_t len = valid_len(p, row);
+                const T* xr = x + row * p.cols;
+#pragma unroll
+                for (int k = 0; k < VPT; ++k) {
+                    const uint32_t j = t + k * p.tpr;
+                    if (j < nvec && j * V < len) cp_async16(slot(i, k), xr + (uint64_t)j * V);
+                }
+            }
+        }
+        cp_async_commit();  // one group per tile, possibly empty: uniform counting
+    };
+    for (int s = 0; s < PF_STAGES - 1; ++s) prefetch(s);
+    for (uint64_t i = 0; i < nmine; ++i) {
+        prefetch(i + PF_STAGES - 1);
+        cp_async_wait<PF_STAGES - 1>();  // this thread's copies of tile i landed
+        const uint64_t row = (first + i * step) * rpc + sub;
+        const bool active = row < p.rows;
+        const uint32_t len = active ? valid_len(p, row) : 0;
+        const uint32_t jhi = active ? nvec : 0;
+        uint4 raw[VPT];
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const uint32_t j = t + k * p.tpr;
+            if (j < jhi && j * V < len) raw[k] = lds16(slot(i, k));
+        }
+        const float m = group_reduce(chunk_max<T, VPT, MASK>(raw, p, t, p.tpr, jhi, len), red,
+                                     p.tpr, OpMaxF());
+        float ev[VPT][V];
+        const float sum = group_reduce(chunk_exp<T, VPT, MASK>(raw, ev, p, t, p.tpr, jhi, len, m),
+                                       red, p.tpr, OpAddF());
+        chunk_store_div<T, VPT>(out + row * p.cols, ev, t, p.tpr, jhi, len, sum);
+    }
+    cp_async_wait<0>();
+}
+
+// ---- long rows: one CTA (BIG) or a cluster of CTAs per row --------------------
+// BIG: one row per CTA of up to 512 threads (128-register budget); otherwise
+// 256-thread CTAs of a cluster, one row split over the cluster.
+template <typename T, int VPT, bool BIG, bool MASK>
+__global__ void __launch_bounds__(BIG ? 512 : 256, BIG ? 1 : 3)
+    smax_rows_kernel(const T* x, T* out, SmaxArgs p) {
+    constexpr int V = Vec<T>::N;
+    __shared__ float red[32];
+    __shared__ float cl_slot[2];
+    const uint32_t nvec = p.cols / V;
+    uint32_t vlo = 0, vhi = nvec;
+    if (p.cl > 1) {
+        const int rank = (int)cg::this_cluster().block_rank();
+        const uint32_t per = (nvec + p.cl - 1) / p.cl;
+        vlo = rank * per;
+        vhi = min(nvec, vlo + per);
+    }
+    for (uint64_t row = blockIdx.x / p.cl; row < p.rows; row += gridDim.x / p.cl) {
+        const uint32_t len = valid_len(p, row);
+        const T* xr = x + row * p.cols;
+        const uint32_t j0 = vlo + threadIdx.x;
+        uint4 raw[VPT];
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const uint32_t j = j0 + k * p.tpr;
+            if (j < vhi && j * V < len) raw[k] = ld_stream(xr + (uint64_t)j * V);
+        }
+        float m = group_reduce(chunk_max<T, VPT, MASK>(raw, p, j0, p.tpr, vhi, len), red, p.tpr,
+                               OpMaxF());
         if (p.cl > 1) {
             cg::cluster_group cluster = cg::this_cluster();
             if (threadIdx.x == 0) cl_slot[0] = m;
@@ -97,16 +235,9 @@ __global__ void __launch_bounds__(256, smax_min_blocks<T, VPT>())
             for (int q = 0; q < p.cl; ++q) mm = fmaxf(mm, *cluster.map_shared_rank(&cl_slot[0], q));
             m = mm;
         }
-        float sum = 0.0f;
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-#pragma unroll
-            for (int e = 0; e < V; ++e) {
-                s[k][e] = expf(fsub(s[k][e], m));  // exp(-inf - m) = 0 for masked keys
-                sum = fadd(sum, s[k][e]);
-            }
-        }
-        sum = group_reduce(sum, red, p.tpr, OpAddF());
+        float ev[VPT][V];
+        float sum = group_reduce(chunk_exp<T, VPT, MASK>(raw, ev, p, j0, p.tpr, vhi, len, m), red,
+                                 p.tpr, OpAddF());
         if (p.cl > 1) {
             cg::cluster_group cluster = cg::this_cluster();
             if (threadIdx.x == 0) cl_slot[1] = sum;
@@ -116,25 +247,11 @@ __global__ void __launch_bounds__(256, smax_min_blocks<T, VPT>())
             sum = tot;
             cluster.sync();  // peers finished reading this CTA's slots
         }
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            const uint32_t j = vlo + t + k * p.tpr;
-            if (active && j < vhi) {
-                float o[V];
-                if (j * V < len) {
-#pragma unroll
-                    for (int e = 0; e < V; ++e)
-                        o[e] = (j * V + e < len) ? fdiv(s[k][e], sum) : 0.0f;
-                } else {
-#pragma unroll
-                    for (int e = 0; e < V; ++e) o[e] = 0.0f;
-                }
-                st_stream(orow + (uint64_t)j * V, Vec<T>::pack(o));
-            }
-        }
+        chunk_store_div<T, VPT>(out + row * p.cols, ev, j0, p.tpr, vhi, len, sum);
     }
 }
 
+// ---- fallbacks -----------------------------------------------------------------
 // Multi-pass row kernel: any cols, any alignment.  One CTA per row; reads the
 // unmasked part of the row three times (max, sum, write).
 template <typename T>
@@ -153,9 +270,10 @@ __global__ void __launch_bounds__(256) smax_rows_scalar_kernel(const T* x, T* ou
             sum = fadd(sum, expf(fsub(score(p, Vec<T>::load1(xr + j), j), m)));
         sum = group_reduce(sum, red, (int)blockDim.x, OpAddF());
         __syncthreads();  // every thread has read its inputs before any write (in place)
+        const RowDiv div(sum);
         for (uint32_t j = threadIdx.x; j < p.cols; j += blockDim.x) {
             float o = 0.0f;
-            if (j < len) o = fdiv(expf(fsub(score(p, Vec<T>::load1(xr + j), j), m)), sum);
+            if (j < len) o = div(expf(fsub(score(p, Vec<T>::load1(xr + j), j), m)));
             Vec<T>::store1(orow + j, o);
         }
     }
@@ -176,86 +294,108 @@ __global__ void __launch_bounds__(256)
         float sum = 0.0f;
         for (uint64_t d = 0; d < dim; ++d)
             sum = fadd(sum, expf(fsub(Vec<T>::load1(x + base + d * inner), m)));
+        const RowDiv div(sum);
         for (uint64_t d = 0; d < dim; ++d)
             Vec<T>::store1(out + base + d * inner,
-                           fdiv(expf(fsub(Vec<T>::load1(x + base + d * inner), m)), sum));
+                           div(expf(fsub(Vec<T>::load1(x + base + d * inner), m))));
     }
 }
 
-template <typename T, int VPT>
-static cudaError_t launch_rows(const T* x, T* out, SmaxArgs p, cudaStream_t st) {
+// ---- launchers -------------------------------------------------------------------
+static cudaError_t launch_cluster(const void* kern, void** args, SmaxArgs& p, cudaStream_t st) {
     const uint64_t cap = (uint64_t)1 << 30;
-    if (p.cl > 1) {
-        const uint64_t clusters = p.rows < cap / p.cl ? p.rows : cap / p.cl;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(clusters * p.cl), 1, 1);
-        cfg.blockDim = dim3(p.tpr, 1, 1);
-        cfg.dynamicSmemBytes = 0;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = p.cl;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, smax_rows_kernel<T, VPT>, x, out, p);
-    }
+    const uint64_t clusters = p.rows < cap / p.cl ? p.rows : cap / p.cl;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(clusters * p.cl), 1, 1);
+    cfg.blockDim = dim3(p.tpr, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = p.cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, kern, args);
+}
+
+template <typename T, int VPT, bool MASK>
+static cudaError_t launch_tiled(const T* x, T* out, SmaxArgs p, cudaStream_t st) {
+    auto pk = smax_pref_kernel<T, VPT, MASK>;
+    const size_t smem = (size_t)PF_STAGES * VPT * 256 * 16;
+    if (!ensure_dyn_smem(reinterpret_cast<const void*>(pk), smem)) return cudaErrorInvalidValue;
+    const int resident = resident_blocks(reinterpret_cast<const void*>(pk), 256, smem);
+    if (resident <= 0) return cudaErrorInvalidConfiguration;
     const int rpc = 256 / p.tpr;
-    const uint64_t want = (p.rows + rpc - 1) / rpc;
-    smax_rows_kernel<T, VPT><<<(unsigned)(want < cap ? want : cap), p.tpr * rpc, 0, st>>>(x, out, p);
+    const uint64_t tiles = (p.rows + rpc - 1) / rpc;
+    const unsigned grid = (unsigned)(tiles < (uint64_t)resident ? tiles : (uint64_t)resident);
+    pk<<<grid, 256, smem, st>>>(x, out, p);
     return cudaSuccess;
 }
 
-// Kernel shape for rows of nvec 16-byte vectors.  Every thread holds 16 row
-// elements (32 for rows beyond 8 x 4096 elements); returns VPT (0 = the
-// multi-pass fallback) and sets the threads per row and the cluster size.
-template <typename T>
-static int smax_shape(uint64_t nvec, SmaxArgs& p) {
-    constexpr int VPT16 = 16 / Vec<T>::N;
-    p.cl = 1;
-    if (nvec <= 32ull * VPT16) {  // a warp per row, 8 rows per CTA
-        p.tpr = 32;
-        int vpt = 1;
-        while ((uint64_t)vpt * 32 < nvec) vpt *= 2;
-        return vpt;
+template <typename T, bool BIG, bool MASK>
+static cudaError_t launch_long(const T* x, T* out, SmaxArgs p, cudaStream_t st) {
+    auto kern = smax_rows_kernel<T, SMAX_VPT, BIG, MASK>;
+    if (p.cl > 1) {
+        void* args[] = {(void*)&x, (void*)&out, (void*)&p};
+        return launch_cluster(reinterpret_cast<const void*>(kern), args, p, st);
     }
-    if (nvec <= 256ull * VPT16) {  // 64..256 threads per row, 256 / tpr rows per CTA
-        uint64_t tpr = 64;
-        while (tpr * VPT16 < nvec) tpr *= 2;
-        p.tpr = (int)tpr;
-        return VPT16;
-    }
-    p.tpr = 256;  // a cluster of up to 8 CTAs x 256 threads per row (DSMEM exchange)
-    int vpt = VPT16;
-    uint64_t cl = (nvec + 256ull * VPT16 - 1) / (256ull * VPT16);
-    if (cl > 8) {
-        vpt = 2 * VPT16;
-        cl = (nvec + 256ull * vpt - 1) / (256ull * vpt);
-        if (cl > 8) return 0;
-    }
-    int c2 = 1;
-    while ((uint64_t)c2 < cl) c2 *= 2;
-    p.cl = c2;
-    return vpt;
+    const uint64_t cap = (uint64_t)1 << 30;
+    kern<<<(unsigned)(p.rows < cap ? p.rows : cap), p.tpr, 0, st>>>(x, out, p);
+    return cudaSuccess;
+}
+
+template <typename T, bool MASK>
+static cudaError_t launch_vec(const T* x, T* out, SmaxArgs p, int vpt, bool tiled, bool big,
+                              cudaStream_t st) {
+    if (!tiled) return big ? launch_long<T, true, MASK>(x, out, p, st)
+                           : launch_long<T, false, MASK>(x, out, p, st);
+    if (vpt == 1) return launch_tiled<T, 1, MASK>(x, out, p, st);
+    if (vpt == 2) return launch_tiled<T, 2, MASK>(x, out, p, st);
+    return launch_tiled<T, SMAX_VPT, MASK>(x, out, p, st);
 }
 
 template <typename T>
 static int rows_dispatch(const char* name, const T* x, T* out, SmaxArgs p, cudaStream_t st) {
     constexpr int V = Vec<T>::N;
-    // Rows of 1-32 KiB stream through the shared-memory bulk-copy ring.
-    if (smax_stream_launch<T>(x, out, p, st)) return check_launch(name);
-    const bool vec = p.cols % V == 0 && aligned16(x) && aligned16(out);
-    const int vpt = vec ? smax_shape<T>(p.cols / V, p) : 0;
+    constexpr int VT = SMAX_VPT;
     const uint64_t cap = (uint64_t)1 << 30;
+    const uint64_t nvec = p.cols / V;
+    const bool vec = p.cols % V == 0 && aligned16(x) && aligned16(out);
+    int vpt = 0;
+    bool tiled = false, big = false;
+    p.cl = 1;
+    if (vec && nvec <= 32ull * VT) {  // a warp per row, 8 rows per tile
+        p.tpr = 32;
+        vpt = 1;
+        while ((uint64_t)vpt * 32 < nvec) vpt *= 2;
+        tiled = true;
+    } else if (vec && nvec <= 256ull * VT) {  // 64..256 threads per row
+        uint64_t tpr = 64;
+        while (tpr * VT < nvec) tpr *= 2;
+        p.tpr = (int)tpr;
+        vpt = VT;
+        tiled = true;
+    } else if (vec && nvec <= 512ull * VT && p.rows >= 2ull * sm_count()) {
+        p.tpr = (int)(((nvec + VT - 1) / VT + 31) / 32 * 32);  // one CTA per row
+        vpt = VT;
+        big = true;
+    } else if (vec && nvec <= 8ull * 256 * VT) {
+        p.tpr = 256;  // a cluster of up to 8 CTAs per row
+        const uint64_t cl = (nvec + 256ull * VT - 1) / (256ull * VT);
+        int c2 = 1;
+        while ((uint64_t)c2 < cl) c2 *= 2;
+        p.cl = c2;
+        vpt = VT;
+    }
     cudaError_t e = cudaSuccess;
-    if (vpt == 1) e = launch_rows<T, 1>(x, out, p, st);
-    else if (vpt == 2) e = launch_rows<T, 2>(x, out, p, st);
-    else if (vpt == 4) e = launch_rows<T, 4>(x, out, p, st);
-    else if (vpt == 8) {
-        if constexpr (V == 4) e = launch_rows<T, 8>(x, out, p, st);
-    } else {
+    if (vpt == 0) {
         smax_rows_scalar_kernel<T><<<(unsigned)(p.rows < cap ? p.rows : cap), 256, 0, st>>>(x, out, p);
+    } else if (p.mask) {
+        e = launch_vec<T, true>(x, out, p, vpt, tiled, big, st);
+    } else {
+        e = launch_vec<T, false>(x, out, p, vpt, tiled, big, st);
     }
     if (e != cudaSuccess) {
         cudaGetLastError();

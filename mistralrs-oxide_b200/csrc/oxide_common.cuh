@@ -68,6 +68,32 @@ __device__ __forceinline__ void st_stream(void* p, uint4 v) {
                  : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Per-thread asynchronous 16-byte copies global -> shared (cp.async, L1
+// bypass).  A thread that later reads only the vectors it copied itself needs
+// no barrier: cp.async.wait_group makes its own completed copies visible to it.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     (uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint4 lds16(const void* p) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+    return v;
+}
+
 // A 16-byte vector viewed as V floats (V = 4 for f32, 8 for bf16).
 template <typename T>
 struct Vec;
@@ -113,6 +139,51 @@ struct Vec<bf16_t> {
         return bf16_to_f32(__ldg(reinterpret_cast<const unsigned short*>(p)));
     }
     __device__ __forceinline__ static void store1(bf16_t* p, float f) { *p = f32_to_bf16(f); }
+};
+
+// ---------------------------------------------------------------------------
+// Division by a divisor shared by a whole row (RMSNorm's rms, softmax's sum),
+// rounded exactly like the IEEE quotient a / b.  Markstein's method: with
+// y = RN(1/b) (the correctly rounded reciprocal), q0 = RN(a*y) lies within a
+// few ulps of a/b; each correction q' = RN(q + RN(a - q*b) * y) (two FMAs)
+// shrinks the error, and once q is within one ulp of a/b the correction
+// returns RN(a/b) (P. Markstein, IBM J. Res. Dev. 34(1), 1990; the same
+// residual step as in the IA-64 division sequences).  Two corrections are
+// applied.  The residuals must stay normal numbers, so the fast path holds for
+// a positive divisor b in [2^-60, 2^60] (checked once per row; otherwise every
+// element takes the IEEE divide) and for numerators and quotients whose
+// magnitudes lie in [2^-100, 2^100] (or a zero numerator).  fast() raises
+// `redo` for any other numerator (tiny, huge, inf, NaN, or an overflowing
+// quotient); callers redo those few vectors with the IEEE divide -- the
+// callers' quotients are bounded (|x / rms| <= sqrt(cols), e / sum <= 1), so
+// in practice only underflowing exponentials get there.  A copysign restores
+// the sign of a zero quotient, so the fast path has no branch: one multiply,
+// four FMAs and a few compare/selects.  oxide_selftest_rowdiv checks
+// operator() against __fdiv_rn, all subnormal numerators included.
+// ---------------------------------------------------------------------------
+struct RowDiv {
+    float b, y;
+    bool ieee;  // divisor outside the fast path's range: IEEE divide
+    __device__ __forceinline__ explicit RowDiv(float bb) : b(bb) {
+        y = __frcp_rn(bb);
+        ieee = !(bb >= 0x1p-60f && bb <= 0x1p60f);
+    }
+    __device__ __forceinline__ float fast(float a, bool& redo) const {
+        const float q0 = __fmul_rn(a, y);
+        float r = __fmaf_rn(-q0, b, a);
+        float q = __fmaf_rn(r, y, q0);
+        r = __fmaf_rn(-q, b, a);
+        q = __fmaf_rn(r, y, q);
+        const float mq = fabsf(q0);
+        redo |= (a != 0.0f) & !((fminf(fabsf(a), mq) >= 0x1p-100f) & (mq <= 0x1p100f));
+        return copysignf(q, a);  // b > 0: the quotient has a's sign (also for 0)
+    }
+    __device__ __forceinline__ float operator()(float a) const {
+        if (ieee) return __fdiv_rn(a, b);
+        bool redo = false;
+        const float q = fast(a, redo);
+        return redo ? __fdiv_rn(a, b) : q;
+    }
 };
 
 // ---------------------------------------------------------------------------
@@ -200,6 +271,9 @@ int sm_count();                      // SMs of the current device (cached)
 // Resident CTAs of `kernel` across the whole current device (occupancy x SMs),
 // cached per (device, kernel, block size, dynamic smem).
 int resident_blocks(const void* kernel, int threads, size_t smem);
+// Opt `kernel` in to `smem` bytes of dynamic shared memory on the current
+// device (needed above 48 KiB); cached.  False if the device refuses.
+bool ensure_dyn_smem(const void* kernel, size_t smem);
 int set_error(int code, const char* fmt, ...);  // records message, returns code
 int check_launch(const char* op);    // cudaGetLastError -> status
 int injected_failure(const char* op);  // host-side fault injection hook

@@ -92,9 +92,61 @@ int resident_blocks(const void* kernel, int threads, size_t smem) {
     return blocks;
 }
 
+bool ensure_dyn_smem(const void* kernel, size_t smem) {
+    if (smem <= 48 * 1024) return true;
+    static std::mutex mu;
+    static std::map<std::pair<int, const void*>, size_t> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const auto key = std::make_pair(dev, kernel);
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= smem) return true;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    done[key] = smem;
+    return true;
+}
+
+// Self-test: RowDiv(b)(a) against the IEEE quotient for every pair (a_i, b_j).
+// out[0] counts the mismatching pairs, out[1] keeps the smallest mismatching
+// pair index (i * nb + j); the caller sets out = {0, UINT64_MAX} first.
+__global__ void __launch_bounds__(256)
+    selftest_rowdiv_kernel(const float* a, uint64_t na, const float* b, uint64_t nb,
+                           unsigned long long* out) {
+    const uint64_t total = na * nb;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t i = t / nb, j = t % nb;
+        const RowDiv d(b[j]);
+        const float q = d(a[i]);
+        const float ref = __fdiv_rn(a[i], b[j]);
+        const bool same = __float_as_uint(q) == __float_as_uint(ref) || (q != q && ref != ref);
+        if (!same) {
+            atomicAdd(&out[0], 1ull);
+            atomicMin(&out[1], (unsigned long long)t);
+        }
+    }
+}
+
 }  // namespace oxide
 
 extern "C" {
+
+int oxide_selftest_rowdiv(const float* a, uint64_t na, const float* b, uint64_t nb,
+                          unsigned long long* out, oxide_stream_t stream) {
+    const char* name = "oxide_selftest_rowdiv";
+    OXIDE_INJECT(name);
+    OXIDE_REQUIRE(out, name, "null output pointer");
+    if (na == 0 || nb == 0) return OXIDE_OK;
+    OXIDE_REQUIRE(a && b, name, "null pointer");
+    OXIDE_REQUIRE(na <= UINT64_MAX / nb, name, "na * nb overflows");
+    oxide::selftest_rowdiv_kernel<<<oxide::sm_count() * 8, 256, 0, stream>>>(a, na, b, nb, out);
+    return oxide::check_launch(name);
+}
 
 const char* oxide_status_string(int status) {
     switch (status) {

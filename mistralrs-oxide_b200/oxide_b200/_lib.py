@@ -22,7 +22,7 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_last_error": (C.c_char_p, []),
     "oxide_version": (C.c_char_p, []),
     "oxide_debug_fail_next": (None, [C.c_char_p]),
-    "oxide_device_errors": (i32, [C.POINTER(C.c_uint), i32]),
+    "oxide_selftest_rowdiv": (i32, [vp, u64, vp, u64, vp, vp]),
     "oxide_binary_f32": (i32, [i32, vp, u64, vp, u64, vp, u64, vp]),
     "oxide_binary_bf16": (i32, [i32, vp, u64, vp, u64, vp, u64, vp]),
     "oxide_add_f32": (i32, [vp, vp, vp, u64, vp]),

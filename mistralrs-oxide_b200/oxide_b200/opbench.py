@@ -1,0 +1,192 @@
+"""Op-level benchmark: one hot-path op at a benchmark-config shape.
+
+    python -m oxide_b200.opbench --op rms_norm_f32_c1 [--rows R] [--iters N] [--sets S]
+
+Runs the op `iters` times back to back over `sets` rotating input/output
+buffer sets (default: enough sets to exceed 2.5x the L2 size, so every launch
+reads from HBM), timed with CUDA events on the launching stream, and prints
+one JSON line: microseconds per launch and achieved GB/s of algorithmic bytes.
+--rows shrinks the row count (for profiler captures of a smaller case).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+if __package__ in (None, ""):
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from oxide_b200 import ops  # noqa: E402
+from oxide_b200._lib import call  # noqa: E402
+from oxide_b200.workloads import C1, C2, C3, C4, C5  # noqa: E402
+
+BF16 = torch.bfloat16
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def build(op: str, rows: int | None, dev):
+    """Returns (make_set, run, bytes_per_launch, shape) for the op."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+
+    def rn(*shape, dtype=torch.float32):
+        return torch.randn(shape, generator=g, device=dev, dtype=dtype)
+
+    if op == "rms_norm_f32_c1":
+        c = C1()
+        R = rows or c.rows
+        w = torch.rand(c.cols, generator=g, device=dev) + 0.5
+        mk = lambda: (rn(R, c.cols), torch.empty(R, c.cols, device=dev))  # noqa: E731
+        run = lambda s: ops.rms_norm(s[0], w, c.eps, out=s[1])  # noqa: E731
+        return mk, run, 2 * R * c.cols * 4 + c.cols * 4, [R, c.cols]
+    if op in ("add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2"):
+        c = C2()
+        R = rows or c.rows
+        if op == "silu_mul_f32_c2":
+            mk = lambda: (rn(R, c.inter), rn(R, c.inter), torch.empty(R, c.inter, device=dev))  # noqa: E731
+            run = lambda s: ops.silu_mul(s[0], s[1], out=s[2])  # noqa: E731
+            return mk, run, 3 * R * c.inter * 4, [R, c.inter]
+        if op == "add_f32_c2":
+            mk = lambda: (rn(R, c.cols), rn(R, c.cols), torch.empty(R, c.cols, device=dev))  # noqa: E731
+            run = lambda s: call("oxide_add_f32", s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(),  # noqa: E731
+                                 R * c.cols, _stream())
+            return mk, run, 3 * R * c.cols * 4, [R, c.cols]
+        sv = torch.rand(c.cols, generator=g, device=dev) + 0.5
+        mk = lambda: (rn(R, c.cols), torch.empty(R, c.cols, device=dev))  # noqa: E731
+        run = lambda s: call("oxide_mul_rowbcast_f32", s[0].data_ptr(), sv.data_ptr(),  # noqa: E731
+                             s[1].data_ptr(), R, c.cols, _stream())
+        return mk, run, 2 * R * c.cols * 4 + c.cols * 4, [R, c.cols]
+    if op == "softmax_f32_c3":
+        c = C3()
+        _, lens, _ = c.inputs()
+        R = rows or c.batch * c.heads
+        tl = torch.from_numpy(lens).to(dev)
+        mk = lambda: (rn(R, c.keys) * math.sqrt(c.head_dim), torch.empty(R, c.keys, device=dev))  # noqa: E731
+        run = lambda s: ops.scale_mask_softmax(s[0], c.scale, lens=tl, rows_per_len=c.heads,  # noqa: E731
+                                               out=s[1])
+        nb = int(sum(min(int(lens[r // c.heads]), c.keys) for r in range(R))) * 4 + R * c.keys * 4
+        return mk, run, nb, [R, c.keys]
+    if op == "argmax_f32_c3":
+        c = C3()
+        R = rows or c.logit_rows
+        idx = torch.empty(R, dtype=torch.int32, device=dev)
+        mk = lambda: (rn(R, c.vocab),)  # noqa: E731
+        run = lambda s: call("oxide_argmax_rows_f32", s[0].data_ptr(), R, c.vocab, idx.data_ptr(),  # noqa: E731
+                             _stream())
+        return mk, run, R * c.vocab * 4 + R * 4, [R, c.vocab]
+    if op == "rope_bf16_c4":
+        c = C4()
+        T = rows or c.tokens
+        cos, sin = ops.rope_table(c.theta, c.head_dim, T)
+        cos, sin = cos.to(dev), sin.to(dev)
+        mk = lambda: (rn(T, c.q_heads, c.head_dim, dtype=BF16), rn(T, c.k_heads, c.head_dim, dtype=BF16),  # noqa: E731
+                      torch.empty(T, c.q_heads, c.head_dim, dtype=BF16, device=dev),
+                      torch.empty(T, c.k_heads, c.head_dim, dtype=BF16, device=dev))
+        run = lambda s: ops.rope(s[0], s[1], cos, sin, q_out=s[2], k_out=s[3])  # noqa: E731
+        nb = 2 * T * (c.q_heads + c.k_heads) * c.head_dim * 2 + 2 * T * (c.head_dim // 2) * 4
+        return mk, run, nb, [T, c.q_heads + c.k_heads, c.head_dim]
+    c = C5()
+    if op in ("rms_norm_bf16_c5", "add_rms_norm_bf16_c5", "sumsq_bf16_c5"):
+        R = rows or c.rows
+        w = torch.ones(c.hidden, dtype=BF16, device=dev)
+        if op == "rms_norm_bf16_c5":
+            mk = lambda: (rn(R, c.hidden, dtype=BF16), torch.empty(R, c.hidden, dtype=BF16, device=dev))  # noqa: E731
+            run = lambda s: ops.rms_norm(s[0], w, c.eps, out=s[1])  # noqa: E731
+            return mk, run, 2 * R * c.hidden * 2 + c.hidden * 2, [R, c.hidden]
+        if op == "sumsq_bf16_c5":
+            ws = torch.empty(ops.workspace_bytes(R * c.hidden), dtype=torch.uint8, device=dev)
+            res = torch.empty((), dtype=torch.float64, device=dev)
+            mk = lambda: (rn(R, c.hidden, dtype=BF16),)  # noqa: E731
+            run = lambda s: ops.reduce(s[0], 2, workspace=ws, out=res)  # noqa: E731
+            return mk, run, R * c.hidden * 2 + 8, [R, c.hidden]
+        mk = lambda: (rn(R, c.hidden, dtype=BF16), rn(R, c.hidden, dtype=BF16),  # noqa: E731
+                      torch.empty(R, c.hidden, dtype=BF16, device=dev),
+                      torch.empty(R, c.hidden, dtype=BF16, device=dev))
+        run = lambda s: ops.add_rms_norm(s[0], s[1], w, c.eps, h=s[2], y=s[3])  # noqa: E731
+        return mk, run, 4 * R * c.hidden * 2 + c.hidden * 2, [R, c.hidden]
+    if op == "softmax_bf16_c5":
+        T = c.seq_len
+        R = rows or c.seqs * c.q_heads * T
+        R = max(T, R // T * T)
+        mk = lambda: (rn(R, T, dtype=BF16), torch.empty(R, T, dtype=BF16, device=dev))  # noqa: E731
+        run = lambda s: ops.scale_mask_softmax(s[0], 1.0 / math.sqrt(c.head_dim), causal_q_len=T,  # noqa: E731
+                                               out=s[1])
+        blocks = R // T
+        nb = blocks * (T * (T + 1) // 2) * 2 + R * T * 2
+        return mk, run, nb, [R, T]
+    if op == "silu_mul_bf16_c5":
+        R = rows or c.rows
+        mk = lambda: (rn(R, c.inter, dtype=BF16), rn(R, c.inter, dtype=BF16),  # noqa: E731
+                      torch.empty(R, c.inter, dtype=BF16, device=dev))
+        run = lambda s: ops.silu_mul(s[0], s[1], out=s[2])  # noqa: E731
+        return mk, run, 3 * R * c.inter * 2, [R, c.inter]
+    if op == "argmax_bf16_c5":
+        R = rows or c.rows
+        idx = torch.empty(R, dtype=torch.int32, device=dev)
+        mk = lambda: (rn(R, c.vocab, dtype=BF16),)  # noqa: E731
+        run = lambda s: call("oxide_argmax_rows_bf16", s[0].data_ptr(), R, c.vocab, idx.data_ptr(),  # noqa: E731
+                             _stream())
+        return mk, run, R * c.vocab * 2 + R * 4, [R, c.vocab]
+    raise SystemExit(f"unknown op {op}")
+
+
+OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softmax_f32_c3",
+       "argmax_f32_c3", "rope_bf16_c4", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
+       "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5"]
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", required=True, choices=OPS + ["all"])
+    ap.add_argument("--rows", type=int, default=None)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--sets", type=int, default=None)
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda")
+    l2 = getattr(torch.cuda.get_device_properties(dev), "L2_cache_size", 126 << 20)
+    for op in (OPS if a.op == "all" else [a.op]):
+        mk, run, nbytes, shape = build(op, a.rows, dev)
+        nsets = a.sets or max(1, min(16, math.ceil(2.5 * l2 / nbytes)))
+        sets = [mk() for _ in range(nsets)]
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for s in sets:  # warm-up: first-launch set-up of each kernel, outside capture
+                run(s)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        # The launches are captured in one CUDA graph so host launch overhead
+        # does not pace short kernels.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(a.iters):
+                run(sets[i % nsets])
+        graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (a.iters * reps)
+        del graph
+        print(json.dumps({"op": op, "shape": shape, "us_per_launch": round(us, 2),
+                          "gbs": round(nbytes / us / 1e3, 1), "bytes": nbytes, "sets": nsets,
+                          "iters": a.iters}), flush=True)
+        del sets
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()
