@@ -19,6 +19,9 @@ constexpr int EW_THREADS = 256;
 constexpr int EW_UNROLL = 4;
 
 // ---- per-element functors (f32 math, IEEE rounding per reference step) ----
+// operator() is one element; pair() is two elements on Blackwell's paired
+// f32 pipe (__fmul2_rn / __fadd2_rn: the same IEEE round-to-nearest per lane,
+// half the instructions).
 template <int OP>
 struct FBin {
     __device__ __forceinline__ float operator()(float x, float y) const {
@@ -27,13 +30,25 @@ struct FBin {
         if (OP == OXIDE_MUL) return fmul(x, y);
         return fdiv(x, y);
     }
+    __device__ __forceinline__ float2 pair(float2 x, float2 y) const {
+        if (OP == OXIDE_ADD) return fadd2(x, y);
+        if (OP == OXIDE_SUB) return fadd2(x, f2(-y.x, -y.y));  // x - y == x + (-y) exactly
+        if (OP == OXIDE_MUL) return fmul2(x, y);
+        return f2(fdiv(x.x, y.x), fdiv(x.y, y.y));
+    }
 };
 
-// silu(x) = x * (1 / (1 + exp(-x))), src/ops/activation.rs:30-33.
+// silu(x) = x * (1 / (1 + exp(-x))), src/ops/activation.rs:30-33.  The
+// reciprocal is __frcp_rn: the correctly rounded 1/d, i.e. the reference's
+// IEEE 1.0 / d.
 __device__ __forceinline__ float silu_f(float x) {
     float e = expf(-x);
-    float r = fdiv(1.0f, fadd(1.0f, e));
+    float r = __frcp_rn(fadd(1.0f, e));
     return fmul(x, r);
+}
+__device__ __forceinline__ float2 silu_f2(float2 x) {
+    const float2 d = fadd2(f2(1.0f, 1.0f), f2(expf(-x.x), expf(-x.y)));
+    return fmul2(x, f2(__frcp_rn(d.x), __frcp_rn(d.y)));
 }
 
 template <typename T>
@@ -41,15 +56,21 @@ struct FSiluMul {  // mul(silu(g), u); silu(g) rounded to T as the pair stores i
     __device__ __forceinline__ float operator()(float g, float u) const {
         return fmul(Vec<T>::rnd(silu_f(g)), u);
     }
+    __device__ __forceinline__ float2 pair(float2 g, float2 u) const {
+        const float2 s = silu_f2(g);
+        return fmul2(f2(Vec<T>::rnd(s.x), Vec<T>::rnd(s.y)), u);
+    }
 };
 
 struct FSilu {
     __device__ __forceinline__ float operator()(float x, float) const { return silu_f(x); }
+    __device__ __forceinline__ float2 pair(float2 x, float2) const { return silu_f2(x); }
 };
 
 struct FScale {
     float s;
     __device__ __forceinline__ float operator()(float x, float) const { return fmul(x, s); }
+    __device__ __forceinline__ float2 pair(float2 x, float2) const { return fmul2(x, f2(s, s)); }
 };
 
 // ---- vectorised kernel ------------------------------------------------------
@@ -84,7 +105,12 @@ __global__ void __launch_bounds__(EW_THREADS)
                 Vec<T>::unpack(va[k], x);
                 if (NIN == 2) Vec<T>::unpack(vb[k], y);
 #pragma unroll
-                for (int e = 0; e < V; ++e) o[e] = f(x[e], NIN == 2 ? y[e] : 0.0f);
+                for (int e = 0; e < V; e += 2) {
+                    const float2 r = f.pair(f2(x[e], x[e + 1]),
+                                            NIN == 2 ? f2(y[e], y[e + 1]) : f2(0.0f, 0.0f));
+                    o[e] = r.x;
+                    o[e + 1] = r.y;
+                }
                 st_stream(out + i * V, Vec<T>::pack(o));
             }
         }

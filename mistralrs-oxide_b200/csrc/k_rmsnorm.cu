@@ -34,8 +34,20 @@ constexpr int norm_vpt() {
     return (ADD && Vec<T>::N == 4) ? 4 : 32 / Vec<T>::N;
 }
 
+// Sum of squares of one unpacked vector into two lane accumulators (paired
+// f32: each product and each sum rounded separately, as the reference's
+// `ss += v * v`; the lanes are combined after the thread's last vector).
+template <int V>
+__device__ __forceinline__ void sumsq_add(float2& acc, const float (&v)[V]) {
+#pragma unroll
+    for (int e = 0; e < V; e += 2) {
+        const float2 p = f2(v[e], v[e + 1]);
+        acc = fadd2(acc, fmul2(p, p));
+    }
+}
+
 // y = (v / rms) * w for a thread's VPT packed vectors j = t + k * tpr < jhi.
-// RowDiv's fast path per vector; a vector with a numerator or quotient below
+// RowDiv's paired fast path per vector; a vector holding a numerator outside
 // its range (or a row whose rms is outside it) is redone with the IEEE divide.
 template <typename T, int VPT>
 __device__ __forceinline__ void norm_store_rms(T* yrow, const T* w, const uint4 (&raw)[VPT],
@@ -51,13 +63,21 @@ __device__ __forceinline__ void norm_store_rms(T* yrow, const T* w, const uint4 
             Vec<T>::unpack(ld_keep(w + (uint64_t)j * V), wv);
             bool redo = div.ieee;
 #pragma unroll
-            for (int e = 0; e < V; ++e) q[e] = div.fast(v[e], redo);
+            for (int e = 0; e < V; e += 2) {
+                const float2 qq = div.fast2(f2(v[e], v[e + 1]), redo);
+                q[e] = qq.x;
+                q[e + 1] = qq.y;
+            }
             if (redo) {
 #pragma unroll
                 for (int e = 0; e < V; ++e) q[e] = __fdiv_rn(v[e], rms);
             }
 #pragma unroll
-            for (int e = 0; e < V; ++e) o[e] = fmul(q[e], wv[e]);
+            for (int e = 0; e < V; e += 2) {
+                const float2 oo = fmul2(f2(q[e], q[e + 1]), f2(wv[e], wv[e + 1]));
+                o[e] = oo.x;
+                o[e + 1] = oo.y;
+            }
             st_stream(yrow + (uint64_t)j * V, Vec<T>::pack(o));
         }
     }
@@ -89,7 +109,7 @@ __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : 4)
             }
         }
         // pass 1: h = x + r (stored, kept packed in raw) and the sum of squares
-        float ss = 0.0f;
+        float2 acc = f2(0.0f, 0.0f);
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const uint32_t j = t + k * p.tpr;
@@ -100,15 +120,18 @@ __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : 4)
                     float rv[V];
                     Vec<T>::unpack(rawr[ADD ? k : 0], rv);
 #pragma unroll
-                    for (int e = 0; e < V; ++e) v[e] = Vec<T>::rnd(fadd(v[e], rv[e]));
+                    for (int e = 0; e < V; e += 2) {
+                        const float2 s = fadd2(f2(v[e], v[e + 1]), f2(rv[e], rv[e + 1]));
+                        v[e] = Vec<T>::rnd(s.x);
+                        v[e + 1] = Vec<T>::rnd(s.y);
+                    }
                     raw[k] = Vec<T>::pack(v);  // exact: v already holds T values
                     st_stream(h + off + (uint64_t)j * V, raw[k]);
                 }
-#pragma unroll
-                for (int e = 0; e < V; ++e) ss = fadd(ss, fmul(v[e], v[e]));
+                sumsq_add(acc, v);
             }
         }
-        ss = group_reduce(ss, red, p.tpr, OpAddF());
+        const float ss = group_reduce(fadd(acc.x, acc.y), red, p.tpr, OpAddF());
         // pass 2: y = (h / rms) * w
         norm_store_rms<T, VPT>(y + off, w, raw, t, p.tpr, active ? nvec : 0,
                                fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps)));
@@ -158,7 +181,7 @@ __global__ void __launch_bounds__(256, 3)
         const uint64_t row = (first + i * step) * rpc + sub;
         const bool active = row < p.rows;
         uint4 raw[VPT];
-        float ss = 0.0f;
+        float2 acc = f2(0.0f, 0.0f);
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const uint32_t j = t + k * p.tpr;
@@ -166,11 +189,10 @@ __global__ void __launch_bounds__(256, 3)
                 raw[k] = lds16(slot(i, k));
                 float v[V];
                 Vec<T>::unpack(raw[k], v);
-#pragma unroll
-                for (int e = 0; e < V; ++e) ss = fadd(ss, fmul(v[e], v[e]));
+                sumsq_add(acc, v);
             }
         }
-        ss = group_reduce(ss, red, p.tpr, OpAddF());
+        const float ss = group_reduce(fadd(acc.x, acc.y), red, p.tpr, OpAddF());
         norm_store_rms<T, VPT>(y + row * p.cols, w, raw, t, p.tpr, active ? nvec : 0,
                                fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps)));
     }

@@ -7,11 +7,10 @@
 //
 // Design (rows of a contiguous [rows, cols] tensor):
 //   * rows that tile a 256-thread CTA (a warp or a power-of-two group per
-//     row) run on persistent CTAs that prefetch the next tiles into a
-//     shared-memory ring with per-thread cp.async while computing the current
-//     one; long rows run one CTA of up to 512 threads per row, or, when there
-//     are too few rows to fill the GPU, a thread-block cluster of up to 8
-//     CTAs per row that exchange the row max and sum through distributed
+//     row, 256 / group rows per CTA) read straight from HBM, many CTAs per SM
+//     in flight; long rows run one CTA of up to 512 threads per row, or, when
+//     there are too few rows to fill the GPU, a thread-block cluster of up to
+//     8 CTAs per row that exchange the row max and sum through distributed
 //     shared memory;
 //   * each thread holds its part of the row PACKED (bf16 stays 2 bytes per
 //     element), 32 elements for bf16 and 16 for f32; the kernels are
@@ -39,6 +38,15 @@ __device__ __forceinline__ float score_t(const SmaxArgs& p, float x, uint32_t c)
     return s;
 }
 
+// Scores of keys c, c + 1 on the paired f32 pipe (same roundings as score_t).
+template <bool MASK>
+__device__ __forceinline__ float2 score2(const SmaxArgs& p, float x0, float x1, uint32_t c) {
+    float2 s = fmul2(f2(x0, x1), f2(p.scale, p.scale));
+    if (MASK)
+        s = fadd2(s, f2(__ldg(p.mask + p.mask_div.mod(c)), __ldg(p.mask + p.mask_div.mod(c + 1))));
+    return s;
+}
+
 // Max of the valid scores of the chunk (vectors j < jhi, keys c < len).
 template <typename T, int VPT, bool MASK>
 __device__ __forceinline__ float chunk_max(const uint4 (&raw)[VPT], const SmaxArgs& p, uint32_t j0,
@@ -53,7 +61,10 @@ __device__ __forceinline__ float chunk_max(const uint4 (&raw)[VPT], const SmaxAr
             Vec<T>::unpack(raw[k], f);
             if (j * V + V <= len) {
 #pragma unroll
-                for (int e = 0; e < V; ++e) m = fmaxf(m, score_t<MASK>(p, f[e], j * V + e));
+                for (int e = 0; e < V; e += 2) {
+                    const float2 s = score2<MASK>(p, f[e], f[e + 1], j * V + e);
+                    m = fmaxf(m, fmaxf(s.x, s.y));
+                }
             } else {
 #pragma unroll
                 for (int e = 0; e < V; ++e)
@@ -65,40 +76,44 @@ __device__ __forceinline__ float chunk_max(const uint4 (&raw)[VPT], const SmaxAr
 }
 
 // ev = exp(score - m) for valid keys (0 for masked keys of a partial vector);
-// returns the thread's sum in vector order.
+// returns the thread's sum (two lane accumulators, combined at the end).
 template <typename T, int VPT, bool MASK>
 __device__ __forceinline__ float chunk_exp(const uint4 (&raw)[VPT], float (&ev)[VPT][Vec<T>::N],
                                            const SmaxArgs& p, uint32_t j0, uint32_t jstep,
                                            uint32_t jhi, uint32_t len, float m) {
     constexpr int V = Vec<T>::N;
-    float sum = 0.0f;
+    const float2 nm = f2(-m, -m);
+    float2 acc = f2(0.0f, 0.0f);
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
         const uint32_t j = j0 + k * jstep;
         if (j < jhi && j * V < len) {
             float f[V];
             Vec<T>::unpack(raw[k], f);
-            if (j * V + V <= len) {
+            if (j * V + V <= len) {  // every key valid: no per-key checks
 #pragma unroll
-                for (int e = 0; e < V; ++e) {
-                    ev[k][e] = expf(fsub(score_t<MASK>(p, f[e], j * V + e), m));
-                    sum = fadd(sum, ev[k][e]);
+                for (int e = 0; e < V; e += 2) {
+                    const float2 d = fadd2(score2<MASK>(p, f[e], f[e + 1], j * V + e), nm);
+                    ev[k][e] = expf(d.x);
+                    ev[k][e + 1] = expf(d.y);
+                    acc = fadd2(acc, f2(ev[k][e], ev[k][e + 1]));
                 }
-            } else {
+            } else {  // the one vector of the row that straddles len
 #pragma unroll
-                for (int e = 0; e < V; ++e) {
-                    ev[k][e] = j * V + e < len ? expf(fsub(score_t<MASK>(p, f[e], j * V + e), m))
-                                               : 0.0f;
-                    sum = fadd(sum, ev[k][e]);
+                for (int e = 0; e < V; e += 2) {
+                    const float2 d = fadd2(score2<MASK>(p, f[e], f[e + 1], j * V + e), nm);
+                    ev[k][e] = j * V + e < len ? expf(d.x) : 0.0f;
+                    ev[k][e + 1] = j * V + e + 1 < len ? expf(d.y) : 0.0f;
+                    acc = fadd2(acc, f2(ev[k][e], ev[k][e + 1]));
                 }
             }
         }
     }
-    return sum;
+    return fadd(acc.x, acc.y);
 }
 
 // Write p = ev / sum (0 beyond len) for every vector j < jhi of the chunk.
-// RowDiv's fast path per vector; a vector with a numerator or quotient below
+// RowDiv's paired fast path per vector; a vector holding a numerator outside
 // its range (or a row whose sum is outside it) is redone with the IEEE divide.
 template <typename T, int VPT>
 __device__ __forceinline__ void chunk_store_div(T* orow, const float (&ev)[VPT][Vec<T>::N],
@@ -111,19 +126,21 @@ __device__ __forceinline__ void chunk_store_div(T* orow, const float (&ev)[VPT][
         const uint32_t j = j0 + k * jstep;
         if (j < jhi) {
             float o[V];
-            if (j * V < len) {
+            if (j * V + V <= len) {  // every key valid: RowDiv's paired fast path
                 bool redo = div.ieee;
 #pragma unroll
-                for (int e = 0; e < V; ++e) o[e] = div.fast(ev[k][e], redo);
+                for (int e = 0; e < V; e += 2) {
+                    const float2 q = div.fast2(f2(ev[k][e], ev[k][e + 1]), redo);
+                    o[e] = q.x;
+                    o[e + 1] = q.y;
+                }
                 if (redo) {
 #pragma unroll
                     for (int e = 0; e < V; ++e) o[e] = __fdiv_rn(ev[k][e], sum);
                 }
-                if (j * V + V > len) {
+            } else if (j * V < len) {  // the straddling vector: IEEE divide, 0 past len
 #pragma unroll
-                    for (int e = 0; e < V; ++e)
-                        if (j * V + e >= len) o[e] = 0.0f;
-                }
+                for (int e = 0; e < V; ++e) o[e] = j * V + e < len ? __fdiv_rn(ev[k][e], sum) : 0.0f;
             } else {
 #pragma unroll
                 for (int e = 0; e < V; ++e) o[e] = 0.0f;
@@ -137,70 +154,11 @@ __device__ __forceinline__ void chunk_store_div(T* orow, const float (&ev)[VPT][
 // for f32, so the kept exp values fit the register budgets below.
 constexpr int SMAX_VPT = 4;
 
-// ---- tiled rows with prefetch ------------------------------------------------
-// 256-thread CTAs own tiles of 256 / tpr rows and loop over tiles
-// blockIdx.x + i * gridDim.x.  The next PF_STAGES - 1 tiles are copied into a
-// shared-memory ring with per-thread cp.async while the current tile is
-// computed.  Each thread copies exactly the 16-byte vectors it later reads, so
-// only cp.async.wait_group is needed.
-constexpr int PF_STAGES = 4;
-
-template <typename T, int VPT, bool MASK>
-__global__ void __launch_bounds__(256, 3) smax_pref_kernel(const T* x, T* out, SmaxArgs p) {
-    constexpr int V = Vec<T>::N;
-    extern __shared__ __align__(16) uint4 ring[];  // [PF_STAGES][VPT][256]
-    __shared__ float red[8];
-    const uint32_t nvec = p.cols / V;
-    const int rpc = 256 / p.tpr;
-    const int sub = threadIdx.x / p.tpr, t = threadIdx.x % p.tpr;
-    const uint64_t ntiles = (p.rows + rpc - 1) / rpc;
-    const uint64_t first = blockIdx.x, step = gridDim.x;
-    const uint64_t nmine = first < ntiles ? (ntiles - first + step - 1) / step : 0;
-    auto slot = [&](uint64_t i, int k) {
-        return ring + ((size_t)(i % PF_STAGES) * VPT + k) * 256 + threadIdx.x;
-    };
-    auto prefetch = [&](uint64_t i) {
-        if (i < nmine) {
-            const uint64_t row = (first + i * step) * rpc + sub;
-            if (row < p.rows) {
-                const uint32_t len = valid_len(p, row);
-                const T* xr = x + row * p.cols;
-#pragma unroll
-                for (int k = 0; k < VPT; ++k) {
-                    const uint32_t j = t + k * p.tpr;
-                    if (j < nvec && j * V < len) cp_async16(slot(i, k), xr + (uint64_t)j * V);
-                }
-            }
-        }
-        cp_async_commit();  // one group per tile, possibly empty: uniform counting
-    };
-    for (int s = 0; s < PF_STAGES - 1; ++s) prefetch(s);
-    for (uint64_t i = 0; i < nmine; ++i) {
-        prefetch(i + PF_STAGES - 1);
-        cp_async_wait<PF_STAGES - 1>();  // this thread's copies of tile i landed
-        const uint64_t row = (first + i * step) * rpc + sub;
-        const bool active = row < p.rows;
-        const uint32_t len = active ? valid_len(p, row) : 0;
-        const uint32_t jhi = active ? nvec : 0;
-        uint4 raw[VPT];
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            const uint32_t j = t + k * p.tpr;
-            if (j < jhi && j * V < len) raw[k] = lds16(slot(i, k));
-        }
-        const float m = group_reduce(chunk_max<T, VPT, MASK>(raw, p, t, p.tpr, jhi, len), red,
-                                     p.tpr, OpMaxF());
-        float ev[VPT][V];
-        const float sum = group_reduce(chunk_exp<T, VPT, MASK>(raw, ev, p, t, p.tpr, jhi, len, m),
-                                       red, p.tpr, OpAddF());
-        chunk_store_div<T, VPT>(out + row * p.cols, ev, t, p.tpr, jhi, len, sum);
-    }
-    cp_async_wait<0>();
-}
-
-// ---- long rows: one CTA (BIG) or a cluster of CTAs per row --------------------
-// BIG: one row per CTA of up to 512 threads (128-register budget); otherwise
-// 256-thread CTAs of a cluster, one row split over the cluster.
+// ---- rows read straight from HBM: tiles of rows, one CTA per row (BIG), or a
+// cluster of CTAs per row --------------------------------------------------------
+// cl == 1: a CTA holds blockDim / tpr rows (tpr threads each); BIG: one row
+// per CTA of up to 512 threads (128-register budget); cl > 1: 256-thread CTAs
+// of a cluster split one row.
 template <typename T, int VPT, bool BIG, bool MASK>
 __global__ void __launch_bounds__(BIG ? 512 : 256, BIG ? 1 : 3)
     smax_rows_kernel(const T* x, T* out, SmaxArgs p) {
@@ -209,23 +167,32 @@ __global__ void __launch_bounds__(BIG ? 512 : 256, BIG ? 1 : 3)
     __shared__ float cl_slot[2];
     const uint32_t nvec = p.cols / V;
     uint32_t vlo = 0, vhi = nvec;
+    int rpc = 1, sub = 0, t = threadIdx.x;
     if (p.cl > 1) {
         const int rank = (int)cg::this_cluster().block_rank();
         const uint32_t per = (nvec + p.cl - 1) / p.cl;
         vlo = rank * per;
         vhi = min(nvec, vlo + per);
+    } else {
+        rpc = blockDim.x / p.tpr;
+        sub = threadIdx.x / p.tpr;
+        t = threadIdx.x % p.tpr;
     }
-    for (uint64_t row = blockIdx.x / p.cl; row < p.rows; row += gridDim.x / p.cl) {
-        const uint32_t len = valid_len(p, row);
+    for (uint64_t row0 = (uint64_t)(blockIdx.x / p.cl) * rpc; row0 < p.rows;
+         row0 += (uint64_t)(gridDim.x / p.cl) * rpc) {
+        const uint64_t row = row0 + sub;
+        const bool active = row < p.rows;
+        const uint32_t len = active ? valid_len(p, row) : 0;
+        const uint32_t jhi = active ? vhi : 0;
         const T* xr = x + row * p.cols;
-        const uint32_t j0 = vlo + threadIdx.x;
+        const uint32_t j0 = vlo + t;
         uint4 raw[VPT];
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const uint32_t j = j0 + k * p.tpr;
-            if (j < vhi && j * V < len) raw[k] = ld_stream(xr + (uint64_t)j * V);
+            if (j < jhi && j * V < len) raw[k] = ld_stream(xr + (uint64_t)j * V);
         }
-        float m = group_reduce(chunk_max<T, VPT, MASK>(raw, p, j0, p.tpr, vhi, len), red, p.tpr,
+        float m = group_reduce(chunk_max<T, VPT, MASK>(raw, p, j0, p.tpr, jhi, len), red, p.tpr,
                                OpMaxF());
         if (p.cl > 1) {
             cg::cluster_group cluster = cg::this_cluster();
@@ -236,7 +203,7 @@ __global__ void __launch_bounds__(BIG ? 512 : 256, BIG ? 1 : 3)
             m = mm;
         }
         float ev[VPT][V];
-        float sum = group_reduce(chunk_exp<T, VPT, MASK>(raw, ev, p, j0, p.tpr, vhi, len, m), red,
+        float sum = group_reduce(chunk_exp<T, VPT, MASK>(raw, ev, p, j0, p.tpr, jhi, len, m), red,
                                  p.tpr, OpAddF());
         if (p.cl > 1) {
             cg::cluster_group cluster = cg::this_cluster();
@@ -247,7 +214,7 @@ __global__ void __launch_bounds__(BIG ? 512 : 256, BIG ? 1 : 3)
             sum = tot;
             cluster.sync();  // peers finished reading this CTA's slots
         }
-        chunk_store_div<T, VPT>(out + row * p.cols, ev, j0, p.tpr, vhi, len, sum);
+        chunk_store_div<T, VPT>(out + row * p.cols, ev, j0, p.tpr, jhi, len, sum);
     }
 }
 
@@ -322,15 +289,12 @@ static cudaError_t launch_cluster(const void* kern, void** args, SmaxArgs& p, cu
 
 template <typename T, int VPT, bool MASK>
 static cudaError_t launch_tiled(const T* x, T* out, SmaxArgs p, cudaStream_t st) {
-    auto pk = smax_pref_kernel<T, VPT, MASK>;
-    const size_t smem = (size_t)PF_STAGES * VPT * 256 * 16;
-    if (!ensure_dyn_smem(reinterpret_cast<const void*>(pk), smem)) return cudaErrorInvalidValue;
-    const int resident = resident_blocks(reinterpret_cast<const void*>(pk), 256, smem);
-    if (resident <= 0) return cudaErrorInvalidConfiguration;
+    // One tile of 256 / tpr rows per 256-thread CTA; the hardware keeps the
+    // next CTAs' loads in flight while resident ones compute.
     const int rpc = 256 / p.tpr;
-    const uint64_t tiles = (p.rows + rpc - 1) / rpc;
-    const unsigned grid = (unsigned)(tiles < (uint64_t)resident ? tiles : (uint64_t)resident);
-    pk<<<grid, 256, smem, st>>>(x, out, p);
+    const uint64_t tiles = (p.rows + rpc - 1) / rpc, cap = (uint64_t)1 << 30;
+    smax_rows_kernel<T, VPT, false, MASK>
+        <<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, st>>>(x, out, p);
     return cudaSuccess;
 }
 
@@ -359,6 +323,10 @@ static cudaError_t launch_vec(const T* x, T* out, SmaxArgs p, int vpt, bool tile
 template <typename T>
 static int rows_dispatch(const char* name, const T* x, T* out, SmaxArgs p, cudaStream_t st) {
     constexpr int V = Vec<T>::N;
+    // 32-bit multiply-shift divisions for the per-row lens / causal lookups.
+    p.narrow = p.rows < 0xffffffffull;
+    p.len_div = FastDiv((uint32_t)(p.rows_per_len < 0xffffffffull ? p.rows_per_len : 0xffffffffull));
+    p.causal_div = FastDiv((uint32_t)(p.causal_q ? p.causal_q : 1));
     constexpr int VT = SMAX_VPT;
     const uint64_t cap = (uint64_t)1 << 30;
     const uint64_t nvec = p.cols / V;

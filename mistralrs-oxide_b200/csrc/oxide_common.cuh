@@ -151,40 +151,48 @@ struct Vec<bf16_t> {
 // residual step as in the IA-64 division sequences).  Two corrections are
 // applied.  The residuals must stay normal numbers, so the fast path holds for
 // a positive divisor b in [2^-60, 2^60] (checked once per row; otherwise every
-// element takes the IEEE divide) and for numerators and quotients whose
-// magnitudes lie in [2^-100, 2^100] (or a zero numerator).  fast() raises
-// `redo` for any other numerator (tiny, huge, inf, NaN, or an overflowing
-// quotient); callers redo those few vectors with the IEEE divide -- the
-// callers' quotients are bounded (|x / rms| <= sqrt(cols), e / sum <= 1), so
-// in practice only underflowing exponentials get there.  A copysign restores
-// the sign of a zero quotient, so the fast path has no branch: one multiply,
-// four FMAs and a few compare/selects.  oxide_selftest_rowdiv checks
-// operator() against __fdiv_rn, all subnormal numerators included.
+// element takes the IEEE divide) and for numerators with |a| in
+// [lo, hi] = [2^-100 max(1, b), 2^100 min(1, b)], which keeps |a|, the
+// quotient and the residuals normal.  fast2() raises `redo` for a pair with a
+// numerator outside (zero, tiny, huge, inf, NaN); callers redo that vector
+// with the IEEE divide -- the callers' quotients are bounded (|x / rms| <=
+// sqrt(cols), e / sum <= 1), so in practice only underflowing exponentials
+// and exact zeros get there.  Two quotients at a time on Blackwell's paired
+// f32 pipe (__fmul2_rn / __ffma2_rn: IEEE round-to-nearest per lane), so a
+// quotient costs 2.5 FMA-pipe instructions plus a compare.
+// oxide_selftest_rowdiv checks operator() against __fdiv_rn, all subnormal
+// numerators included.
 // ---------------------------------------------------------------------------
 struct RowDiv {
-    float b, y;
+    float b, y, lo, hi;
     bool ieee;  // divisor outside the fast path's range: IEEE divide
     __device__ __forceinline__ explicit RowDiv(float bb) : b(bb) {
         y = __frcp_rn(bb);
         ieee = !(bb >= 0x1p-60f && bb <= 0x1p60f);
+        lo = 0x1p-100f * fmaxf(1.0f, bb);
+        hi = 0x1p100f * fminf(1.0f, bb);
     }
-    __device__ __forceinline__ float fast(float a, bool& redo) const {
-        const float q0 = __fmul_rn(a, y);
-        float r = __fmaf_rn(-q0, b, a);
-        float q = __fmaf_rn(r, y, q0);
-        r = __fmaf_rn(-q, b, a);
-        q = __fmaf_rn(r, y, q);
-        const float mq = fabsf(q0);
-        redo |= (a != 0.0f) & !((fminf(fabsf(a), mq) >= 0x1p-100f) & (mq <= 0x1p100f));
-        return copysignf(q, a);  // b > 0: the quotient has a's sign (also for 0)
+    __device__ __forceinline__ float2 fast2(float2 a, bool& redo) const {
+        const float2 y2 = make_float2(y, y), nb = make_float2(-b, -b);
+        const float2 q0 = __fmul2_rn(a, y2);
+        float2 q = __ffma2_rn(__ffma2_rn(q0, nb, a), y2, q0);
+        q = __ffma2_rn(__ffma2_rn(q, nb, a), y2, q);
+        const float ax = fabsf(a.x), ay = fabsf(a.y);
+        redo |= !((fminf(ax, ay) >= lo) & (fmaxf(ax, ay) <= hi));
+        return q;
     }
     __device__ __forceinline__ float operator()(float a) const {
         if (ieee) return __fdiv_rn(a, b);
         bool redo = false;
-        const float q = fast(a, redo);
+        const float q = fast2(make_float2(a, a), redo).x;
         return redo ? __fdiv_rn(a, b) : q;
     }
 };
+
+// Paired f32 arithmetic (IEEE round-to-nearest per lane, no contraction).
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
 // ---------------------------------------------------------------------------
 // Unsigned 32-bit division by a run-time constant (multiply-high + shift).
