@@ -1,0 +1,82 @@
+"""Committed golden vectors (tests/golden/oracle_vectors.npz).
+
+CPU: the oracle still reproduces every stored output bit for bit.
+GPU: the kernels, fed the stored inputs, match the stored outputs within the
+parity tolerances (bit-exact where the contract says so).
+"""
+import os
+
+import numpy as np
+import pytest
+
+from _util import assert_bits_equal, assert_close_rel, assert_ulp, to_dev, to_np
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "oracle_vectors.npz")
+
+
+@pytest.fixture(scope="module")
+def golden():
+    return dict(np.load(GOLDEN))
+
+
+def test_oracle_reproduces_golden_vectors(orc, golden):
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location(
+        "make_golden", os.path.join(os.path.dirname(GOLDEN), "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    fresh = mg.build()
+    assert sorted(fresh) == sorted(golden)
+    for k, v in golden.items():
+        assert fresh[k].dtype == v.dtype and fresh[k].shape == v.shape, k
+        assert fresh[k].tobytes() == v.tobytes(), k
+
+
+@pytest.mark.gpu
+def test_kernels_match_golden_vectors(cuda, golden):
+    import torch
+
+    from oxide_b200 import ops
+
+    g = golden
+    d = lambda k: to_dev(g[k])  # noqa: E731
+    assert_bits_equal(to_np(ops.add(d("add_f32.a"), d("add_f32.b"))), g["add_f32.out"])
+    assert_bits_equal(to_np(ops.div(d("add_f32.a"), torch.abs(d("add_f32.b")) + 0.5)),
+                      g["div_f32.out"])
+    assert_bits_equal(to_np(ops.mul(d("mulb_f32.x"), d("mulb_f32.s"))).reshape(-1), g["mulb_f32.out"])
+    assert_bits_equal(to_np(ops.add(d("add_bf16.a"), d("add_bf16.b"))), g["add_bf16.out"])
+    assert_ulp(to_np(ops.silu_mul(d("silu_mul_f32.g"), d("silu_mul_f32.u"))), g["silu_mul_f32.out"], 8)
+    assert_ulp(to_np(ops.silu_mul(d("silu_mul_bf16.g"), d("silu_mul_bf16.u"))),
+               g["silu_mul_bf16.out"], 1)
+    assert_close_rel(to_np(ops.rms_norm(d("rms_f32.x"), d("rms_f32.w"), 1e-5)), g["rms_f32.out"], 1e-5)
+    assert_ulp(to_np(ops.rms_norm(d("rms_bf16.x"), d("rms_bf16.w"), 1e-5)), g["rms_bf16.out"], 1)
+    h, y = ops.add_rms_norm(d("rms_bf16.x"), d("addrms_bf16.r"), d("rms_bf16.w"), 1e-5)
+    assert_bits_equal(to_np(h), g["addrms_bf16.h"])
+    assert_ulp(to_np(y), g["addrms_bf16.y"], 1)
+    assert_close_rel(to_np(ops.softmax(d("smax_f32.x"), 1)), g["smax_f32.out"], 1e-5)
+    got = ops.scale_mask_softmax(d("smax_f32.x"), 0.125, lens=d("smax_lens.lens"), rows_per_len=2)
+    assert_close_rel(to_np(got), g["smax_lens_f32.out"], 1e-5)
+    got = ops.scale_mask_softmax(d("smax_f32.x"), 0.125, mask=d("smax_mask.mask"))
+    assert_close_rel(to_np(got), g["smax_mask_f32.out"], 1e-5)
+    got = ops.scale_mask_softmax(d("smax_causal_bf16.x"), 0.25, causal_q_len=4)
+    assert_ulp(to_np(got), g["smax_causal_bf16.out"], 1)
+    cos, sin, pos = d("rope.cos"), d("rope.sin"), d("rope.pos")
+    assert_bits_equal(to_np(ops.rope(d("rope_f32.x"), None, cos, sin, pos)), g["rope_f32.out"])
+    assert_bits_equal(to_np(ops.rope(d("rope_bf16.x"), None, cos, sin, pos)), g["rope_bf16.out"])
+    assert_bits_equal(to_np(ops.rope(d("rope_head_f32.x"), None, cos, sin, pos, layout="head")),
+                      g["rope_head_f32.out"])
+    assert np.array_equal(to_np(ops.argmax(d("argmax_f32.x"))).astype(np.uint32), g["argmax_f32.out"])
+    assert np.array_equal(to_np(ops.argmax(d("argmax_bf16.x"))).astype(np.uint32), g["argmax_bf16.out"])
+    x = d("red.x")
+    for op, name in ((0, "sum"), (1, "max"), (2, "sumsq")):
+        rows = to_np(ops.reduce_rows(x, op))
+        ref = g[f"red_rows_{name}.out"]
+        if op == 1:
+            assert_bits_equal(rows, ref)
+        else:
+            tol = 1e-5 * np.sum(np.abs(g["red.x"].astype(np.float64)) ** (1 + (op == 2)), axis=1)
+            assert np.all(np.abs(rows.astype(np.float64) - ref) <= tol)
+        total = float(ops.reduce(x, op).item())
+        want = float(g[f"red_all_{name}.out"])
+        assert abs(total - want) <= (0 if op == 1 else 1e-5 * np.sum(np.abs(g["red.x"].astype(np.float64)) ** (1 + (op == 2))))
