@@ -556,7 +556,7 @@ def run_oxide(args):
         line["cpu_baseline"] = cpu_baseline()
     if not args.no_extras:
         try:
-            line["per_op"] = per_op_lines(peak) if rank == 0 or True else {}
+            line["per_op"] = per_op_lines(peak)  # every rank: keeps the ranks in step for chain_c5
         except Exception as e:  # keep the headline line; report the failure
             line["per_op"] = {"error": repr(e)}
         try:
