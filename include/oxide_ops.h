@@ -233,6 +233,33 @@ int oxide_reduce_f32(int op, const float* x, uint64_t n, double* out, void* work
 int oxide_reduce_bf16(int op, const oxide_bf16* x, uint64_t n, double* out, void* workspace,
                       uint64_t workspace_bytes, oxide_stream_t stream);
 
+/* Whole-tensor reduction that allocates nothing and takes no workspace.
+ * No counterpart in the reference: an addition for callers that cannot hand
+ * over scratch memory, such as a launcher that receives only its input and
+ * output buffers (the shape of KernelManager::launch_*), or a decode loop that
+ * must not call cudaMalloc/cudaFree mid-step because they synchronise the
+ * device.  Same result, bit for bit, as oxide_reduce_* for the same x and n.
+ *
+ * Scratch: a fixed array of OXIDE_REDUCE_STATIC_SLOTS f64 partials (8 KiB) in
+ * the library's own device memory, one per device.  Every slot a call reads is
+ * written earlier in the same call, so no slot has to start at zero and the
+ * contents left by an earlier call do not matter.
+ * Limit: n <= OXIDE_REDUCE_STATIC_MAX_N elements (2^24 per slot); larger n
+ * returns OXIDE_ERR_INVALID_ARG without launching anything.
+ * First call on a device: looks up the array's device address with the
+ * calling thread's current device (cudaGetSymbolAddress), which may load the
+ * library's device code; make that first call outside any stream capture.
+ * Concurrency: all calls on one device share the one array, so two calls
+ * that can overlap on the GPU (different streams without an ordering event
+ * between them) race and return wrong results.  Order them on one stream, or
+ * use oxide_reduce_* with separate workspaces. */
+#define OXIDE_REDUCE_STATIC_SLOTS 1024
+#define OXIDE_REDUCE_STATIC_MAX_N (((uint64_t)OXIDE_REDUCE_STATIC_SLOTS) << 24)
+int oxide_reduce_static_f32(int op, const float* x, uint64_t n, double* out,
+                            oxide_stream_t stream);
+int oxide_reduce_static_bf16(int op, const oxide_bf16* x, uint64_t n, double* out,
+                             oxide_stream_t stream);
+
 /* ---- host-buffer pipeline ----------------------------------------------------
  * The reference's ops take host tensors and return host tensors
  * (src/ops/*: Tensor::zeros + as_f32_slice) and its GPU path copies through

@@ -14,6 +14,9 @@
 // initialised state: the workspace is only ever written before it is read.
 #include "oxide_common.cuh"
 
+#include <atomic>
+#include <mutex>
+
 namespace oxide {
 
 constexpr int RED_BLOCKS = 1024;
@@ -199,6 +202,65 @@ static int reduce_entry(const char* name, int op, const T* x, uint64_t n, double
     return check_launch(name);
 }
 
+// ---- whole-tensor reduction with library-owned scratch ----------------------------
+// oxide_reduce_static_* run the same two kernels as oxide_reduce_*, with the
+// stage-1 partials in this fixed array instead of a caller workspace.  Stage 1
+// writes every slot that stage 2 of the same call reads, so the array needs no
+// clearing and what an earlier call left in it is never read.
+static_assert(RED_BLOCKS <= OXIDE_REDUCE_STATIC_SLOTS, "stage 1 may use every scratch slot");
+static __device__ __align__(256) double g_static_partials[OXIDE_REDUCE_STATIC_SLOTS];
+
+constexpr int kMaxDevices = 64;
+static std::atomic<double*> g_static_addr[kMaxDevices];
+static std::mutex g_static_mu;
+
+// Device address of g_static_partials on the calling thread's current device,
+// looked up once per device (the lookup may load this module's device code).
+static int static_partials(const char* name, double** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return set_error(OXIDE_ERR_CUDA, "%s: cudaGetDevice: %s", name, cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices)
+        return set_error(OXIDE_ERR_UNSUPPORTED, "%s: device ordinal %d >= %d", name, dev, kMaxDevices);
+    double* p = g_static_addr[dev].load(std::memory_order_acquire);
+    if (!p) {
+        std::lock_guard<std::mutex> lock(g_static_mu);
+        p = g_static_addr[dev].load(std::memory_order_relaxed);
+        if (!p) {
+            void* addr = nullptr;
+            e = cudaGetSymbolAddress(&addr, g_static_partials);
+            if (e != cudaSuccess || !addr)
+                return set_error(OXIDE_ERR_CUDA, "%s: cudaGetSymbolAddress of the scratch array: %s",
+                                 name, cudaGetErrorString(e));
+            p = static_cast<double*>(addr);
+            g_static_addr[dev].store(p, std::memory_order_release);
+        }
+    }
+    *out = p;
+    return OXIDE_OK;
+}
+
+template <typename T>
+static int reduce_static_entry(const char* name, int op, const T* x, uint64_t n, double* out,
+                               cudaStream_t st) {
+    OXIDE_INJECT(name);
+    OXIDE_REQUIRE(op >= OXIDE_RED_SUM && op <= OXIDE_RED_SUMSQ, name, "unknown reduction");
+    OXIDE_REQUIRE(out, name, "null output pointer");
+    OXIDE_REQUIRE(n == 0 || x, name, "null input pointer");
+    if (n > OXIDE_REDUCE_STATIC_MAX_N)
+        return set_error(OXIDE_ERR_INVALID_ARG,
+                         "%s: n = %llu exceeds the %llu elements its fixed scratch of %d partials "
+                         "covers; use the workspace form for larger inputs",
+                         name, (unsigned long long)n, (unsigned long long)OXIDE_REDUCE_STATIC_MAX_N,
+                         OXIDE_REDUCE_STATIC_SLOTS);
+    double* partial = nullptr;
+    const int rc = static_partials(name, &partial);
+    if (rc != OXIDE_OK) return rc;
+    return reduce_entry<T>(name, op, x, n, out, partial,
+                           (uint64_t)OXIDE_REDUCE_STATIC_SLOTS * sizeof(double), st);
+}
+
 template <typename T>
 static int reduce_rows_entry(const char* name, int op, const T* x, uint64_t rows, uint64_t cols,
                              float* out, cudaStream_t st) {
@@ -249,6 +311,14 @@ int oxide_reduce_bf16(int op, const oxide_bf16* x, uint64_t n, double* out, void
                       uint64_t workspace_bytes, oxide_stream_t stream) {
     return oxide::reduce_entry<bf16_t>("oxide_reduce_bf16", op, x, n, out, workspace,
                                        workspace_bytes, stream);
+}
+int oxide_reduce_static_f32(int op, const float* x, uint64_t n, double* out,
+                            oxide_stream_t stream) {
+    return oxide::reduce_static_entry<float>("oxide_reduce_static_f32", op, x, n, out, stream);
+}
+int oxide_reduce_static_bf16(int op, const oxide_bf16* x, uint64_t n, double* out,
+                             oxide_stream_t stream) {
+    return oxide::reduce_static_entry<bf16_t>("oxide_reduce_static_bf16", op, x, n, out, stream);
 }
 int oxide_reduce_rows_f32(int op, const float* x, uint64_t rows, uint64_t cols, float* out,
                           oxide_stream_t stream) {

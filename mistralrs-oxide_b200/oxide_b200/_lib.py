@@ -55,6 +55,8 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_reduce_workspace_bytes": (u64, [u64]),
     "oxide_reduce_f32": (i32, [i32, vp, u64, vp, vp, u64, vp]),
     "oxide_reduce_bf16": (i32, [i32, vp, u64, vp, vp, u64, vp]),
+    "oxide_reduce_static_f32": (i32, [i32, vp, u64, vp, vp]),
+    "oxide_reduce_static_bf16": (i32, [i32, vp, u64, vp, vp]),
     "oxide_pipe_create": (i32, [i32, u64, i32, C.POINTER(C.c_void_p)]),
     "oxide_pipe_destroy": (i32, [vp]),
     "oxide_pipe_binary_f32": (i32, [vp, i32, vp, u64, vp, u64, vp, u64]),
