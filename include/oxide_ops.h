@@ -262,7 +262,7 @@ int oxide_reduce_static_bf16(int op, const oxide_bf16* x, uint64_t n, double* ou
 
 /* ---- host-buffer pipeline ----------------------------------------------------
  * The reference's ops take host tensors and return host tensors
- * (src/ops/*: Tensor::zeros + as_f32_slice) and its GPU path copies through
+ * (src/ops: Tensor::zeros + as_f32_slice) and its GPU path copies through
  * CudaBackend::copy_host_to_device / copy_device_to_host
  * (src/cuda_backend/mod.rs:76-85).  A pipeline runs one op on host buffers:
  * it splits the rows into chunks and, on `depth` streams, overlaps the
