@@ -24,6 +24,8 @@
 // rows beyond the register budget take multi-pass kernels.
 #include <cooperative_groups.h>
 
+#include <type_traits>
+
 #include "oxide_softmax.cuh"
 
 namespace cg = cooperative_groups;
@@ -320,6 +322,142 @@ static cudaError_t launch_vec(const T* x, T* out, SmaxArgs p, int vpt, bool tile
     return launch_tiled<T, SMAX_VPT, MASK>(x, out, p, st);
 }
 
+// ---- bf16 rows of up to 32 * 8 * VPT keys, no additive mask ---------------------
+// One warp per row, lane l owning the 8-key vectors l, l + 32, ...; rows are
+// taken in a grid-stride loop by a persistent grid.  Only vectors holding a
+// valid key are read.  The output is bf16, so the f32 intermediate only has to
+// be accurate far below half a bf16 ulp (2^-9 relative) for every output to
+// be within one bf16 ulp of the reference; that allows:
+//   * the row max taken on the packed bf16 keys (max.bf16x2): for scale > 0,
+//     x -> RN(x * scale) is non-decreasing, so RN(max(x) * scale) is the max
+//     of the scaled scores; NaN keys are skipped like f32::max skips them;
+//   * exp(s - m) as ex2(x * (scale * log2 e) - m * log2 e): one paired FMA and
+//     one ex2.approx (relative error ~2^-22, subnormal results kept) per key,
+//     error ~|s - m| * 2^-24 relative, at most ~1e-5 for |s - m| <= 100;
+//   * p = e * RN(1 / sum): within 1.5 f32 ulp of e / sum.
+// e stays in registers between the sum and the scaling.
+__device__ __forceinline__ float ex2_approx(float t) {
+    float y;
+    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(t));
+    return y;
+}
+__device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+// Keys k >= keep (0 < keep < 8) of a vector of 8 bf16 set to `fill`.
+__device__ __forceinline__ uint4 bf16_tail(uint4 v, uint32_t keep, uint32_t fill) {
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (2u * i >= keep) w[i] = fill | (fill << 16);
+        else if (2u * i + 1 >= keep) w[i] = (w[i] & 0xffffu) | (fill << 16);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int VPT>
+__global__ void __launch_bounds__(256)
+    smax_bf16_warp_kernel(const bf16_t* __restrict__ x, bf16_t* __restrict__ out, SmaxArgs p) {
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint64_t warp0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    const uint32_t nvec = p.cols >> 3;
+    const float c1 = fmul(p.scale, kLog2e);
+    for (uint64_t row = warp0; row < p.rows; row += nwarps) {
+        const uint32_t len = valid_len(p, row);
+        const uint32_t nv = (len + 7u) >> 3;  // vectors holding a valid key
+        const uint32_t tail = len & 7u;       // valid keys of vector nv - 1 (0: all 8)
+        const uint4* xr = reinterpret_cast<const uint4*>(x + row * p.cols);
+        uint4* orow = reinterpret_cast<uint4*>(out + row * p.cols);
+        uint4 raw[VPT];
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const uint32_t v = lane + 32u * k;
+            if (v < nv) raw[k] = ld_stream(xr + v);
+        }
+        uint32_t mx = 0xff80ff80u;  // (-inf, -inf)
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const uint32_t v = lane + 32u * k;
+            if (v < nv) {
+                if (tail && v == nv - 1) raw[k] = bf16_tail(raw[k], tail, 0xff80u);
+                mx = bf16x2_max(mx, bf16x2_max(bf16x2_max(raw[k].x, raw[k].y),
+                                               bf16x2_max(raw[k].z, raw[k].w)));
+            }
+        }
+        const float m = warp_max(fmaxf(bf16_lo(mx), bf16_hi(mx)));
+        const float c2 = fmul(-fmul(m, p.scale), kLog2e);
+        float e[VPT][8];
+        float2 acc = f2(0.0f, 0.0f);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const uint32_t v = lane + 32u * k;
+            if (v < nv) {
+                const uint32_t w[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 t = __ffma2_rn(f2(bf16_lo(w[i]), bf16_hi(w[i])), f2(c1, c1), f2(c2, c2));
+                    e[k][2 * i] = ex2_approx(t.x);
+                    e[k][2 * i + 1] = ex2_approx(t.y);
+                    acc = fadd2(acc, f2(e[k][2 * i], e[k][2 * i + 1]));
+                }
+            }
+        }
+        const float inv = __frcp_rn(warp_sum(fadd(acc.x, acc.y)));
+        const float2 inv2 = f2(inv, inv);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const uint32_t v = lane + 32u * k;
+            if (v < nvec) {
+                uint4 o = make_uint4(0u, 0u, 0u, 0u);
+                if (v < nv) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 q = fmul2(f2(e[k][2 * i], e[k][2 * i + 1]), inv2);
+                        w[i] = pack_bf16x2(q.x, q.y);
+                    }
+                    o = make_uint4(w[0], w[1], w[2], w[3]);
+                    if (tail && v == nv - 1) o = bf16_tail(o, tail, 0u);
+                }
+                st_stream(orow + v, o);
+            }
+        }
+    }
+}
+
+template <int VPT>
+static cudaError_t launch_bf16_warp(const bf16_t* x, bf16_t* out, const SmaxArgs& p, cudaStream_t st) {
+    const auto kern = smax_bf16_warp_kernel<VPT>;
+    const uint64_t want = (p.rows + 7) / 8;
+    const uint64_t cap = (uint64_t)resident_blocks(reinterpret_cast<const void*>(kern), 256, 0) * sm_count();
+    const unsigned grid = (unsigned)(want < cap ? want : cap);
+    kern<<<grid, 256, 0, st>>>(x, out, p);
+    return cudaSuccess;
+}
+
+// The bf16 warp kernel serves rows of whole vectors up to 2048 keys when the
+// scores are x * scale with 0 < scale < inf and no additive mask.
+template <typename T>
+static bool try_bf16_warp(const T* x, T* out, const SmaxArgs& p, cudaStream_t st, cudaError_t& e) {
+    if constexpr (!std::is_same<T, bf16_t>::value) {
+        return false;
+    } else {
+        if (p.mask || !(p.scale > 0.0f && p.scale <= 3.4028235e38f)) return false;
+        if (p.cols % 8 != 0 || p.cols > 2048 || !aligned16(x) || !aligned16(out)) return false;
+        const uint32_t nvec = p.cols / 8;
+        if (nvec <= 32) e = launch_bf16_warp<1>(x, out, p, st);
+        else if (nvec <= 64) e = launch_bf16_warp<2>(x, out, p, st);
+        else if (nvec <= 128) e = launch_bf16_warp<4>(x, out, p, st);
+        else e = launch_bf16_warp<8>(x, out, p, st);
+        return true;
+    }
+}
+
 template <typename T>
 static int rows_dispatch(const char* name, const T* x, T* out, SmaxArgs p, cudaStream_t st) {
     constexpr int V = Vec<T>::N;
@@ -327,6 +465,16 @@ static int rows_dispatch(const char* name, const T* x, T* out, SmaxArgs p, cudaS
     p.narrow = p.rows < 0xffffffffull;
     p.len_div = FastDiv((uint32_t)(p.rows_per_len < 0xffffffffull ? p.rows_per_len : 0xffffffffull));
     p.causal_div = FastDiv((uint32_t)(p.causal_q ? p.causal_q : 1));
+    {
+        cudaError_t e = cudaSuccess;
+        if (try_bf16_warp(x, out, p, st, e)) {
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return set_error(OXIDE_ERR_LAUNCH, "%s: launch failed: %s", name, cudaGetErrorString(e));
+            }
+            return check_launch(name);
+        }
+    }
     constexpr int VT = SMAX_VPT;
     const uint64_t cap = (uint64_t)1 << 30;
     const uint64_t nvec = p.cols / V;

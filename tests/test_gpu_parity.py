@@ -336,6 +336,31 @@ def test_causal_softmax(cuda, orc, dtype, q_len, cols):
                cols, dtype, 0.0883883, causal_q=q_len)
 
 
+@pytest.mark.parametrize("cols", [8, 40, 256, 264, 1024, 2048])
+def test_bf16_softmax_short_rows_edge_cases(cuda, orc, cols):
+    """bf16 rows of whole 8-key vectors up to 2048 keys: scores spread so wide
+    that exp underflows to subnormals and zero, ragged lengths (0, 1, partial
+    vectors, full), and rows with NaN, +inf and all -inf keys."""
+    from oxide_b200 import ops
+    from _util import bf16_to_f32, ulp_bf16
+
+    rows = 64
+    x = rand((rows, cols), 40 + cols, "bf16", 30.0, orc)
+    x[5, 3 % cols] = 0x7FC0          # NaN key: the row is NaN
+    x[6, 7 % cols] = 0x7F80          # +inf key: NaN like the reference (inf - inf)
+    x[7, :] = 0xFF80                 # all -inf: NaN like the reference
+    lens = np.random.default_rng(cols).integers(0, cols + 1, rows // 2).astype(np.int32)
+    lens[:4] = [0, cols, 1, max(cols - 3, 1)]
+    for kw in ({"lens": lens, "rows_per_len": 2}, {"causal_q_len": min(cols, 16)}, {}):
+        dev_kw = {k: (to_dev(v) if isinstance(v, np.ndarray) else v) for k, v in kw.items()}
+        got = to_np(ops.scale_mask_softmax(to_dev(x), 1.0, **dev_kw))
+        ref = orc.scale_mask_softmax(x, cols, 1.0, **kw)
+        gn, rn = np.isnan(bf16_to_f32(got)), np.isnan(bf16_to_f32(ref))
+        assert np.array_equal(gn, rn), kw
+        d = ulp_bf16(got[~gn], ref[~rn])
+        assert d.max(initial=0) <= BF16_ULP, (kw, d.max())
+
+
 def test_softmax_rows_sum_to_one_and_deterministic(cuda, orc):
     from oxide_b200 import ops
 
