@@ -8,10 +8,10 @@
 // Design (rows of a contiguous [rows, cols] tensor):
 //   * rows that tile a 256-thread CTA (a warp or a power-of-two group per
 //     row, 256 / group rows per CTA) read straight from HBM, many CTAs per SM
-//     in flight; long rows run one CTA of up to 512 threads per row, or, when
-//     there are too few rows to fill the GPU, a thread-block cluster of up to
-//     8 CTAs per row that exchange the row max and sum through distributed
-//     shared memory;
+//     in flight, the row kept in registers; longer rows are streamed three
+//     times (max, sum, store) by one CTA or a thread-block cluster of up to 8
+//     CTAs per row, the second and third reads served by L2, the cluster
+//     exchanging slice maxima and sums through distributed shared memory;
 //   * each thread holds its part of the row PACKED (bf16 stays 2 bytes per
 //     element), 32 elements for bf16 and 16 for f32; the kernels are
 //     instruction-bound, so fully valid 16-byte vectors take a path without
@@ -24,8 +24,8 @@
 //     attention-probability shape) take a warp-per-row kernel whose f32
 //     intermediate is accurate to ~1e-5 relative, far inside the one-bf16-ulp
 //     output tolerance (see smax_bf16_warp_kernel).
-// softmax over an inner (non-last) dim, odd lengths, unaligned pointers and
-// rows beyond the register budget take multi-pass kernels.
+// softmax over an inner (non-last) dim, odd lengths and unaligned pointers take
+// scalar multi-pass kernels.
 #include <cooperative_groups.h>
 
 #include <type_traits>
@@ -160,69 +160,202 @@ __device__ __forceinline__ void chunk_store_div(T* orow, const float (&ev)[VPT][
 // for f32, so the kept exp values fit the register budgets below.
 constexpr int SMAX_VPT = 4;
 
-// ---- rows read straight from HBM: tiles of rows, one CTA per row (BIG), or a
-// cluster of CTAs per row --------------------------------------------------------
-// cl == 1: a CTA holds blockDim / tpr rows (tpr threads each); BIG: one row
-// per CTA of up to 512 threads (128-register budget); cl > 1: 256-thread CTAs
-// of a cluster split one row.
-template <typename T, int VPT, bool BIG, bool MASK>
-__global__ void __launch_bounds__(BIG ? 512 : 256, BIG ? 1 : 3)
-    smax_rows_kernel(const T* x, T* out, SmaxArgs p) {
+// ---- rows that tile a CTA, read straight from HBM --------------------------------
+// A 256-thread CTA holds 256 / tpr rows of tpr threads each; each thread keeps
+// VPT packed vectors of its row in registers between the max, exp and store.
+template <typename T, int VPT, bool MASK>
+__global__ void __launch_bounds__(256, 3) smax_rows_kernel(const T* x, T* out, SmaxArgs p) {
     constexpr int V = Vec<T>::N;
     __shared__ float red[32];
-    __shared__ float cl_slot[2];
     const uint32_t nvec = p.cols / V;
-    uint32_t vlo = 0, vhi = nvec;
-    int rpc = 1, sub = 0, t = threadIdx.x;
-    if (p.cl > 1) {
-        const int rank = (int)cg::this_cluster().block_rank();
-        const uint32_t per = (nvec + p.cl - 1) / p.cl;
-        vlo = rank * per;
-        vhi = min(nvec, vlo + per);
-    } else {
-        rpc = blockDim.x / p.tpr;
-        sub = threadIdx.x / p.tpr;
-        t = threadIdx.x % p.tpr;
-    }
-    for (uint64_t row0 = (uint64_t)(blockIdx.x / p.cl) * rpc; row0 < p.rows;
-         row0 += (uint64_t)(gridDim.x / p.cl) * rpc) {
+    const int rpc = blockDim.x / p.tpr, sub = threadIdx.x / p.tpr, t = threadIdx.x % p.tpr;
+    for (uint64_t row0 = (uint64_t)blockIdx.x * rpc; row0 < p.rows; row0 += (uint64_t)gridDim.x * rpc) {
         const uint64_t row = row0 + sub;
         const bool active = row < p.rows;
         const uint32_t len = active ? valid_len(p, row) : 0;
-        const uint32_t jhi = active ? vhi : 0;
+        const uint32_t jhi = active ? nvec : 0;
         const T* xr = x + row * p.cols;
-        const uint32_t j0 = vlo + t;
+        const uint32_t j0 = t;
         uint4 raw[VPT];
 #pragma unroll
         for (int k = 0; k < VPT; ++k) {
             const uint32_t j = j0 + k * p.tpr;
             if (j < jhi && j * V < len) raw[k] = ld_stream(xr + (uint64_t)j * V);
         }
-        float m = group_reduce(chunk_max<T, VPT, MASK>(raw, p, j0, p.tpr, jhi, len), red, p.tpr,
-                               OpMaxF());
-        if (p.cl > 1) {
-            cg::cluster_group cluster = cg::this_cluster();
-            if (threadIdx.x == 0) cl_slot[0] = m;
-            cluster.sync();
-            float mm = -INFINITY;
-            for (int q = 0; q < p.cl; ++q) mm = fmaxf(mm, *cluster.map_shared_rank(&cl_slot[0], q));
-            m = mm;
-        }
+        const float m = group_reduce(chunk_max<T, VPT, MASK>(raw, p, j0, p.tpr, jhi, len), red, p.tpr,
+                                     OpMaxF());
         float ev[VPT][V];
-        float sum = group_reduce(chunk_exp<T, VPT, MASK>(raw, ev, p, j0, p.tpr, jhi, len, m), red,
-                                 p.tpr, OpAddF());
-        if (p.cl > 1) {
-            cg::cluster_group cluster = cg::this_cluster();
-            if (threadIdx.x == 0) cl_slot[1] = sum;
-            cluster.sync();
-            float tot = 0.0f;
-            for (int q = 0; q < p.cl; ++q) tot = fadd(tot, *cluster.map_shared_rank(&cl_slot[1], q));
-            sum = tot;
-            cluster.sync();  // peers finished reading this CTA's slots
-        }
+        const float sum = group_reduce(chunk_exp<T, VPT, MASK>(raw, ev, p, j0, p.tpr, jhi, len, m), red,
+                                       p.tpr, OpAddF());
         chunk_store_div<T, VPT>(out + row * p.cols, ev, j0, p.tpr, jhi, len, sum);
     }
 }
+
+// ---- long rows: two streaming passes, the second served by L2 ---------------------
+// A row is split over a cluster of p.cl CTAs (p.cl = 1: one CTA per row).
+// Pass 1 streams the CTA's slice from HBM once, keeping per thread the
+// running max m and the sum s of exp(score - m) (s rescaled by exp(m_old - m)
+// when the max grows); the CTA and then the cluster (through distributed
+// shared memory, in rank order) combine the (m, s) pairs into the row's max M
+// and sum S.  Pass 2 re-reads the slice -- from L2, where pass 1 left it -- and
+// writes p = exp(score - M) / S, computed exactly as the tiled kernel does
+// (IEEE score, expf, RowDiv); only S carries the extra roundings of the
+// rescaling (a few ulp, far inside the f32 tolerance).  Nothing is held across
+// passes, so each thread keeps U vectors in flight with few registers and a
+// decode-sized batch of long rows runs in one wave.  In place (out == x) is
+// safe: a CTA writes only its own slice, after its own last read of it.
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Merge (m, s) into the running pair (M, S): both sums are taken relative to
+// their own max.
+__device__ __forceinline__ void online_merge(float& M, float& S, float m, float s) {
+    if (m > M) {
+        S = fadd(fmul(S, expf(fsub(M, m))), s);
+        M = m;
+    } else if (m == M || m != m) {
+        S = fadd(S, s);
+    } else {
+        S = fadd(S, fmul(s, expf(fsub(m, M))));
+    }
+}
+
+template <typename T, bool MASK, int NT, int U>
+__global__ void __launch_bounds__(NT, 2048 / NT / 2)
+    smax_stream_kernel(const T* x, T* out, SmaxArgs p) {
+    constexpr int V = Vec<T>::N;
+    __shared__ float red[32];
+    __shared__ float slot[2];
+    const uint32_t cl = (uint32_t)p.cl;
+    const uint32_t rank = cl > 1 ? cg::this_cluster().block_rank() : 0u;
+    const uint32_t nvec = p.cols / V;
+    const uint32_t per = (nvec + cl - 1) / cl;
+    const uint32_t lo = min(nvec, rank * per), hi = min(nvec, lo + per);
+    for (uint64_t row = blockIdx.x / cl; row < p.rows; row += gridDim.x / cl) {
+        const uint32_t len = valid_len(p, row);
+        const uint32_t vv = min(hi, (len + V - 1) / V);  // slice vectors [lo, vv) hold valid keys
+        const T* xr = x + row * p.cols;
+        // pass 1: running max and rescaled sum of exp
+        float m = -INFINITY, ssum = 0.0f;
+        for (uint32_t j0 = lo + threadIdx.x; j0 < vv; j0 += NT * U) {
+            uint4 r[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t j = j0 + u * NT;
+                if (j < vv) r[u] = ld_stream(xr + (uint64_t)j * V);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t j = j0 + u * NT;
+                if (j < vv) {
+                    float f[V];
+                    Vec<T>::unpack(r[u], f);
+                    const bool full = j * V + V <= len;
+                    float sc[V];
+                    float vm = -INFINITY;
+#pragma unroll
+                    for (int e = 0; e < V; e += 2) {
+                        const float2 s2 = score2<MASK>(p, f[e], f[e + 1], j * V + e);
+                        sc[e] = full || j * V + e < len ? s2.x : -INFINITY;
+                        sc[e + 1] = full || j * V + e + 1 < len ? s2.y : -INFINITY;
+                        vm = fmaxf(vm, fmaxf(sc[e], sc[e + 1]));
+                    }
+                    if (vm > m) {
+                        ssum = fmul(ssum, expf(fsub(m, vm)));
+                        m = vm;
+                    }
+                    // while every score so far is -inf, exp(score - 0) adds 0
+                    // (and NaN for a NaN key) instead of exp(-inf + inf)
+                    const float mr = m == -INFINITY ? 0.0f : m;
+                    const float2 nm = f2(-mr, -mr);
+                    float2 acc = f2(0.0f, 0.0f);
+#pragma unroll
+                    for (int e = 0; e < V; e += 2) {
+                        const float2 d = fadd2(f2(sc[e], sc[e + 1]), nm);
+                        acc = fadd2(acc, f2(expf(d.x), expf(d.y)));
+                    }
+                    ssum = fadd(ssum, fadd(acc.x, acc.y));
+                }
+            }
+        }
+        // combine (m, s) over the CTA: max, then the sums rescaled to it
+        const float mb = group_reduce(m, red, NT, OpMaxF());
+        const float sb = group_reduce(m == mb ? ssum : fmul(ssum, expf(fsub(m, mb))), red, NT, OpAddF());
+        float M = mb, S = sb;
+        if (cl > 1) {
+            cg::cluster_group cluster = cg::this_cluster();
+            if (threadIdx.x == 0) {
+                slot[0] = mb;
+                slot[1] = sb;
+            }
+            cluster.sync();
+            M = -INFINITY;
+            S = 0.0f;
+            for (uint32_t q = 0; q < cl; ++q)
+                online_merge(M, S, *cluster.map_shared_rank(&slot[0], q), *cluster.map_shared_rank(&slot[1], q));
+            cluster_arrive();  // this CTA is done reading its peers' slots
+        }
+        // pass 2: p = exp(s - M) / S for valid keys, 0 beyond the valid length
+        const RowDiv div(S);
+        const float2 nm = f2(-M, -M);
+        T* orow = out + row * p.cols;
+        for (uint32_t j0 = lo + threadIdx.x; j0 < hi; j0 += NT * U) {
+            uint4 r[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t j = j0 + u * NT;
+                if (j < vv) r[u] = ld_stream(xr + (uint64_t)j * V);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t j = j0 + u * NT;
+                if (j < hi) {
+                    float o[V];
+                    if (j < vv) {
+                        float f[V];
+                        Vec<T>::unpack(r[u], f);
+                        if (j * V + V <= len) {
+                            bool redo = div.ieee;
+#pragma unroll
+                            for (int e = 0; e < V; e += 2) {
+                                const float2 d = fadd2(score2<MASK>(p, f[e], f[e + 1], j * V + e), nm);
+                                const float2 q = div.fast2(f2(expf(d.x), expf(d.y)), redo);
+                                o[e] = q.x;
+                                o[e + 1] = q.y;
+                            }
+                            if (redo) {
+#pragma unroll
+                                for (int e = 0; e < V; ++e)
+                                    o[e] = __fdiv_rn(expf(fsub(score_t<MASK>(p, f[e], j * V + e), M)), S);
+                            }
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < V; ++e)
+                                o[e] = j * V + e < len
+                                           ? __fdiv_rn(expf(fsub(score_t<MASK>(p, f[e], j * V + e), M)), S)
+                                           : 0.0f;
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < V; ++e) o[e] = 0.0f;
+                    }
+                    st_stream(orow + (uint64_t)j * V, Vec<T>::pack(o));
+                }
+            }
+        }
+        if (cl > 1) cluster_wait();  // peers are done with this CTA's slots
+    }
+}
+
+// 512 threads, 2 CTAs per SM (64 registers); vectors in flight per thread:
+// 4, or 2 with the additive mask (whose loads need registers of their own).
+constexpr int STREAM_THREADS = 512;
+template <bool MASK>
+constexpr int stream_unroll() { return MASK ? 2 : 4; }
 
 // ---- fallbacks -----------------------------------------------------------------
 // Multi-pass row kernel: any cols, any alignment.  One CTA per row; reads the
@@ -299,28 +432,38 @@ static cudaError_t launch_tiled(const T* x, T* out, SmaxArgs p, cudaStream_t st)
     // next CTAs' loads in flight while resident ones compute.
     const int rpc = 256 / p.tpr;
     const uint64_t tiles = (p.rows + rpc - 1) / rpc, cap = (uint64_t)1 << 30;
-    smax_rows_kernel<T, VPT, false, MASK>
+    smax_rows_kernel<T, VPT, MASK>
         <<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, st>>>(x, out, p);
     return cudaSuccess;
 }
 
-template <typename T, bool BIG, bool MASK>
-static cudaError_t launch_long(const T* x, T* out, SmaxArgs p, cudaStream_t st) {
-    auto kern = smax_rows_kernel<T, SMAX_VPT, BIG, MASK>;
-    if (p.cl > 1) {
+// Long rows: clusters of up to 8 CTAs per row while all CTAs still fit one
+// wave and each keeps at least two vectors per thread.
+template <typename T, bool MASK>
+static cudaError_t launch_stream(const T* x, T* out, SmaxArgs p, cudaStream_t st) {
+    constexpr int V = Vec<T>::N;
+    auto kern = smax_stream_kernel<T, MASK, STREAM_THREADS, stream_unroll<MASK>()>;
+    const uint64_t slots =
+        (uint64_t)resident_blocks(reinterpret_cast<const void*>(kern), STREAM_THREADS, 0);
+    const uint64_t nvec = p.cols / V;
+    int cl = 1;
+    while (cl < 8 && p.rows * (uint64_t)(2 * cl) <= slots && nvec / (2 * cl) >= 2ull * STREAM_THREADS)
+        cl *= 2;
+    p.cl = cl;
+    p.tpr = STREAM_THREADS;
+    if (cl > 1) {
         void* args[] = {(void*)&x, (void*)&out, (void*)&p};
         return launch_cluster(reinterpret_cast<const void*>(kern), args, p, st);
     }
     const uint64_t cap = (uint64_t)1 << 30;
-    kern<<<(unsigned)(p.rows < cap ? p.rows : cap), p.tpr, 0, st>>>(x, out, p);
+    kern<<<(unsigned)(p.rows < cap ? p.rows : cap), STREAM_THREADS, 0, st>>>(x, out, p);
     return cudaSuccess;
 }
 
+// vpt > 0: tiled rows of vpt vectors per thread; vpt == 0: streamed long rows.
 template <typename T, bool MASK>
-static cudaError_t launch_vec(const T* x, T* out, SmaxArgs p, int vpt, bool tiled, bool big,
-                              cudaStream_t st) {
-    if (!tiled) return big ? launch_long<T, true, MASK>(x, out, p, st)
-                           : launch_long<T, false, MASK>(x, out, p, st);
+static cudaError_t launch_vec(const T* x, T* out, SmaxArgs p, int vpt, cudaStream_t st) {
+    if (vpt == 0) return launch_stream<T, MASK>(x, out, p, st);
     if (vpt == 1) return launch_tiled<T, 1, MASK>(x, out, p, st);
     if (vpt == 2) return launch_tiled<T, 2, MASK>(x, out, p, st);
     return launch_tiled<T, SMAX_VPT, MASK>(x, out, p, st);
@@ -444,7 +587,7 @@ static cudaError_t launch_bf16_warp(const bf16_t* x, bf16_t* out, const SmaxArgs
     const auto kern = smax_bf16_warp_kernel<VPT>;
     const uint64_t want = (p.rows + 7) / 8;
     // two CTAs per resident slot: measured ~2% faster than one
-    const uint64_t cap = 2ull * resident_blocks(reinterpret_cast<const void*>(kern), 256, 0) * sm_count();
+    const uint64_t cap = 2ull * resident_blocks(reinterpret_cast<const void*>(kern), 256, 0);
     const unsigned grid = (unsigned)(want < cap ? want : cap);
     kern<<<grid, 256, 0, st>>>(x, out, p);
     return cudaSuccess;
@@ -490,38 +633,24 @@ static int rows_dispatch(const char* name, const T* x, T* out, SmaxArgs p, cudaS
     const uint64_t nvec = p.cols / V;
     const bool vec = p.cols % V == 0 && aligned16(x) && aligned16(out);
     int vpt = 0;
-    bool tiled = false, big = false;
     p.cl = 1;
     if (vec && nvec <= 32ull * VT) {  // a warp per row, 8 rows per tile
         p.tpr = 32;
         vpt = 1;
         while ((uint64_t)vpt * 32 < nvec) vpt *= 2;
-        tiled = true;
     } else if (vec && nvec <= 256ull * VT) {  // 64..256 threads per row
         uint64_t tpr = 64;
         while (tpr * VT < nvec) tpr *= 2;
         p.tpr = (int)tpr;
         vpt = VT;
-        tiled = true;
-    } else if (vec && nvec <= 512ull * VT && p.rows >= 2ull * sm_count()) {
-        p.tpr = (int)(((nvec + VT - 1) / VT + 31) / 32 * 32);  // one CTA per row
-        vpt = VT;
-        big = true;
-    } else if (vec && nvec <= 8ull * 256 * VT) {
-        p.tpr = 256;  // a cluster of up to 8 CTAs per row
-        const uint64_t cl = (nvec + 256ull * VT - 1) / (256ull * VT);
-        int c2 = 1;
-        while ((uint64_t)c2 < cl) c2 *= 2;
-        p.cl = c2;
-        vpt = VT;
     }
     cudaError_t e = cudaSuccess;
-    if (vpt == 0) {
+    if (!vec) {
         smax_rows_scalar_kernel<T><<<(unsigned)(p.rows < cap ? p.rows : cap), 256, 0, st>>>(x, out, p);
     } else if (p.mask) {
-        e = launch_vec<T, true>(x, out, p, vpt, tiled, big, st);
+        e = launch_vec<T, true>(x, out, p, vpt, st);
     } else {
-        e = launch_vec<T, false>(x, out, p, vpt, tiled, big, st);
+        e = launch_vec<T, false>(x, out, p, vpt, st);
     }
     if (e != cudaSuccess) {
         cudaGetLastError();

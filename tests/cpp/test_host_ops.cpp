@@ -251,7 +251,7 @@ DEVICE_TEST(rms_norm_matches_oracle_and_checks_weight_shape) {
     std::vector<uint16_t> rb(x.size());
     orc_rms_norm_bf16(xb.data(), wb.data(), rb.data(), rows, cols, 1e-5f, kThreads);
     expect_ulp16(host16(unwrap(ops::rms_norm(dev16(xb, {rows, cols}), dev16(wb, {cols}), 1e-5f))), rb, 1);
-    const OxideError e = expect_err(ops::rms_norm(dev(x, {rows, cols}), dev(w, {cols / 2}), 1e-5f));
+    const OxideError e = expect_err(ops::rms_norm(dev(x, {rows, cols}), dev(uniform(cols / 2, 22, 0.5f, 1.5f), {cols / 2}), 1e-5f));
     EXPECT(e.kind == OxideError::Kind::InvalidArgument);
     EXPECT(e.message == "rms_norm weight shape [2048] doesn't match input last dim 4096");
 }

@@ -324,6 +324,44 @@ def test_additive_mask_softmax(cuda, orc, dtype):
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_long_row_softmax_masked_prefix_nan_and_inf(cuda, orc, dtype):
+    """Rows longer than a CTA's register tile (streamed in slices): an
+    additive mask whose first 5000 keys are -inf (slices that see only -inf
+    add nothing), a NaN key and a +inf key (their rows are all NaN, like the
+    reference's), a row of -inf scores (NaN), and lengths that end inside a
+    slice."""
+    from oxide_b200 import ops
+
+    rows, cols = 8, 20000
+    x = rand((rows, cols), 37, dtype, 4.0, orc)
+    nan, inf, ninf = (0x7FC0, 0x7F80, 0xFF80) if dtype == "bf16" else (np.nan, np.inf, -np.inf)
+    x[1, 12345] = nan
+    x[2, 7] = inf
+    x[3, :] = ninf
+    mask = np.full(cols, 0.5, F)
+    mask[:5000] = -np.inf
+    got = ops.scale_mask_softmax(to_dev(x), 0.125, mask=to_dev(mask))
+    ref = orc.scale_mask_softmax(x, cols, 0.125, mask=mask)
+    if dtype == "bf16":
+        from _util import ulp_bf16
+
+        gn, rn = np.isnan(bf16_to_f32(to_np(got))), np.isnan(bf16_to_f32(ref))
+        assert np.array_equal(gn, rn)
+        assert ulp_bf16(to_np(got)[~gn], ref[~rn]).max(initial=0) <= BF16_ULP
+    else:
+        smax_close(to_np(got), ref, x, cols, dtype, 0.125, mask=mask)
+    lens = np.array([20000, 5001, 4999, 1], np.int32)
+    got = ops.scale_mask_softmax(to_dev(x), 0.125, lens=to_dev(lens), rows_per_len=2)
+    ref = orc.scale_mask_softmax(x, cols, 0.125, lens=lens, rows_per_len=2)
+    if dtype == "bf16":
+        gn, rn = np.isnan(bf16_to_f32(to_np(got))), np.isnan(bf16_to_f32(ref))
+        assert np.array_equal(gn, rn)
+        assert ulp_bf16(to_np(got)[~gn], ref[~rn]).max(initial=0) <= BF16_ULP
+    else:
+        smax_close(to_np(got), ref, x, cols, dtype, 0.125, lens=lens, rows_per_len=2)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
 @pytest.mark.parametrize("q_len,cols", [(256, 256), (64, 300), (2048, 2048)])
 def test_causal_softmax(cuda, orc, dtype, q_len, cols):
     """C5 shape family: [seqs x heads x q_len x keys] with a causal mask."""
