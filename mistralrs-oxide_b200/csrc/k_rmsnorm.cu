@@ -9,12 +9,13 @@
 // rows, a power-of-two group with several rows per 256-thread CTA, or one CTA
 // of up to 1024 threads for long rows).  The group reads the whole row with
 // 16-byte streaming loads issued back to back and keeps it PACKED in
-// registers (bf16 stays 2 bytes per element), 32 elements per thread (16 for
-// the fused f32 add, which has two inputs in flight), so the row crosses HBM
-// once in and once out and many rows are in flight per SM.  The sum of
-// squares is reduced with a fixed shuffle/shared-memory tree; x / rms uses
-// the row-shared RowDiv (the correctly rounded quotient, as the reference's
-// IEEE divide) followed by a separate multiply by w.  Rows beyond the
+// registers (bf16 stays 2 bytes per element), four 16-byte vectors per thread
+// (32 bf16 or 16 f32 elements), so the row crosses HBM once in and once out
+// and many rows are in flight per SM.  The sum of
+// squares is reduced with a fixed shuffle/shared-memory tree; for f32 x / rms
+// uses the row-shared RowDiv (the correctly rounded quotient, as the
+// reference's IEEE divide), for bf16 a multiply by the rounded reciprocal (see
+// bf16_recip_ok), followed by a separate multiply by w.  Rows beyond the
 // register path, or with unaligned/odd lengths, take a two-pass kernel that
 // re-reads the row (the second read is served by L2).
 #include "oxide_common.cuh"
@@ -28,10 +29,23 @@ struct NormArgs {
     float eps;
 };
 
-// Vectors per thread: 32 row elements, 16 for the fused f32 add.
+// bf16 outputs compute x / rms as x * RN(1 / rms): the product is within 1.5
+// f32 ulp of the correctly rounded quotient, far inside half a bf16 ulp, so
+// the bf16 result differs from the reference's by at most one ulp -- the same
+// bar as the rounding of the f32 sum of squares -- and the per-element divide
+// (RowDiv's residual corrections and range checks) becomes one multiply.  A
+// row whose rms is outside [2^-126, 2^126] (1 / rms would leave the normal
+// range) keeps the division.  f32 outputs always divide.
+__device__ __forceinline__ bool bf16_recip_ok(float rms) {
+    return rms >= 0x1p-126f && rms <= 0x1p126f;
+}
+
+// Vectors per thread: 4 (32 bf16 or 16 f32 elements).  Measured on B200 at
+// 4096 columns: f32 rows run 10-20% faster with 16 elements per thread and
+// twice the threads per row than with 32, and bf16 rows fastest with 32.
 template <typename T, bool ADD>
 constexpr int norm_vpt() {
-    return (ADD && Vec<T>::N == 4) ? 4 : 32 / Vec<T>::N;
+    return 4;
 }
 
 // Sum of squares of one unpacked vector into two lane accumulators (paired
@@ -53,6 +67,28 @@ template <typename T, int VPT>
 __device__ __forceinline__ void norm_store_rms(T* yrow, const T* w, const uint4 (&raw)[VPT],
                                                uint32_t t, uint32_t tpr, uint32_t jhi, float rms) {
     constexpr int V = Vec<T>::N;
+    if (V == 8 && bf16_recip_ok(rms)) {
+        // bf16 output: (x * RN(1 / rms)) * w -- see bf16_recip_ok
+        const float inv = __frcp_rn(rms);
+        const float2 inv2 = f2(inv, inv);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const uint32_t j = t + k * tpr;
+            if (j < jhi) {
+                float v[V], wv[V], o[V];
+                Vec<T>::unpack(raw[k], v);
+                Vec<T>::unpack(ld_keep(w + (uint64_t)j * V), wv);
+#pragma unroll
+                for (int e = 0; e < V; e += 2) {
+                    const float2 oo = fmul2(fmul2(f2(v[e], v[e + 1]), inv2), f2(wv[e], wv[e + 1]));
+                    o[e] = oo.x;
+                    o[e + 1] = oo.y;
+                }
+                st_stream(yrow + (uint64_t)j * V, Vec<T>::pack(o));
+            }
+        }
+        return;
+    }
     const RowDiv div(rms);
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
@@ -138,67 +174,6 @@ __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : 4)
     }
 }
 
-// Plain RMSNorm over tiled rows with prefetch: 256-thread CTAs own tiles of
-// 256 / tpr rows and loop over tiles blockIdx.x + i * gridDim.x; the next
-// NORM_PF - 1 tiles are copied into a shared-memory ring with per-thread
-// cp.async while the current tile is normalised, so rows are in flight from
-// HBM independently of the register budget.  Each thread copies exactly the
-// 16-byte vectors it later reads: cp.async.wait_group is the only sync.
-constexpr int NORM_PF = 4;
-
-template <typename T, int VPT>
-__global__ void __launch_bounds__(256, 3)
-    rmsnorm_pref_kernel(const T* x, const T* w, T* y, NormArgs p) {
-    constexpr int V = Vec<T>::N;
-    extern __shared__ __align__(16) uint4 ring[];  // [NORM_PF][VPT][256]
-    __shared__ float red[8];
-    const uint32_t nvec = p.cols / V;
-    const int rpc = 256 / p.tpr;
-    const int sub = threadIdx.x / p.tpr, t = threadIdx.x % p.tpr;
-    const uint64_t ntiles = (p.rows + rpc - 1) / rpc;
-    const uint64_t first = blockIdx.x, step = gridDim.x;
-    const uint64_t nmine = first < ntiles ? (ntiles - first + step - 1) / step : 0;
-    auto slot = [&](uint64_t i, int k) {
-        return ring + ((size_t)(i % NORM_PF) * VPT + k) * 256 + threadIdx.x;
-    };
-    auto prefetch = [&](uint64_t i) {
-        if (i < nmine) {
-            const uint64_t row = (first + i * step) * rpc + sub;
-            if (row < p.rows) {
-#pragma unroll
-                for (int k = 0; k < VPT; ++k) {
-                    const uint32_t j = t + k * p.tpr;
-                    if (j < nvec) cp_async16(slot(i, k), x + row * p.cols + (uint64_t)j * V);
-                }
-            }
-        }
-        cp_async_commit();  // one group per tile, possibly empty: uniform counting
-    };
-    for (int s = 0; s < NORM_PF - 1; ++s) prefetch(s);
-    for (uint64_t i = 0; i < nmine; ++i) {
-        prefetch(i + NORM_PF - 1);
-        cp_async_wait<NORM_PF - 1>();  // this thread's copies of tile i landed
-        const uint64_t row = (first + i * step) * rpc + sub;
-        const bool active = row < p.rows;
-        uint4 raw[VPT];
-        float2 acc = f2(0.0f, 0.0f);
-#pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            const uint32_t j = t + k * p.tpr;
-            if (active && j < nvec) {
-                raw[k] = lds16(slot(i, k));
-                float v[V];
-                Vec<T>::unpack(raw[k], v);
-                sumsq_add(acc, v);
-            }
-        }
-        const float ss = group_reduce(fadd(acc.x, acc.y), red, p.tpr, OpAddF());
-        norm_store_rms<T, VPT>(y + row * p.cols, w, raw, t, p.tpr, active ? nvec : 0,
-                               fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps)));
-    }
-    cp_async_wait<0>();
-}
-
 // Two-pass fallback: any cols, any alignment.  One CTA per row.  Pass 2
 // re-reads x (or the stored h) with coherent loads, so in-place use is safe.
 template <typename T, bool ADD>
@@ -217,14 +192,17 @@ __global__ void __launch_bounds__(256)
             ss = fadd(ss, fmul(v, v));
         }
         ss = group_reduce(ss, red, (int)blockDim.x, OpAddF());
-        const RowDiv div(fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps)));
+        const float rms = fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps));
+        const RowDiv div(rms);
+        const bool recip = sizeof(T) == 2 && bf16_recip_ok(rms);
+        const float inv = __frcp_rn(rms);
         const T* src = ADD ? h : x;
         for (uint32_t i = threadIdx.x; i < p.cols; i += blockDim.x) {
             const T* q = src + off + i;
             float v;
             if (sizeof(T) == 4) v = *reinterpret_cast<const volatile float*>(q);
             else v = bf16_to_f32(*reinterpret_cast<const volatile uint16_t*>(q));
-            Vec<T>::store1(y + off + i, fmul(div(v), Vec<T>::load1(w + i)));
+            Vec<T>::store1(y + off + i, fmul(recip ? fmul(v, inv) : div(v), Vec<T>::load1(w + i)));
         }
     }
 }
@@ -249,26 +227,6 @@ static int norm_dispatch(const char* name, const T* x, const T* r, const T* w, T
     const bool vec = cols % V == 0 && aligned16(x) && aligned16(w) && aligned16(y) &&
                      (!ADD || (aligned16(r) && aligned16(h)));
     const uint64_t nvec = cols / V;
-    if constexpr (!ADD) {
-        // Plain RMSNorm on rows that tile a 256-thread CTA: prefetching kernel
-        // with 4 vectors per thread.
-        if (vec && nvec <= 256ull * 4) {
-            uint64_t tpr = 32;
-            while (tpr * 4 < nvec) tpr *= 2;
-            p.tpr = (int)tpr;
-            auto pk = rmsnorm_pref_kernel<T, 4>;
-            const size_t smem = (size_t)NORM_PF * 4 * 256 * 16;
-            const int resident = ensure_dyn_smem(reinterpret_cast<const void*>(pk), smem)
-                                     ? resident_blocks(reinterpret_cast<const void*>(pk), 256, smem)
-                                     : 0;
-            if (resident > 0) {
-                const uint64_t tiles = (rows + (256 / tpr) - 1) / (256 / tpr);
-                const unsigned grid = (unsigned)(tiles < (uint64_t)resident ? tiles : (uint64_t)resident);
-                pk<<<grid, 256, smem, st>>>(x, w, y, p);
-                return check_launch(name);
-            }
-        }
-    }
     if (vec && nvec <= 32ull * VT) {  // short rows: a warp per row, 8 rows per CTA
         int vpt = 1;
         while ((uint64_t)vpt * 32 < nvec) vpt *= 2;
