@@ -77,8 +77,10 @@ struct FScale {
 // NIN = 1 (b unused) or 2.  AMOD/BMOD: operand indexed modulo its length
 // (in vectors).  Requires 16-byte aligned pointers and, for modulo operands,
 // lengths that are multiples of the vector width.
+// 64 registers (4 CTAs of 256 threads per SM): measured 10% faster than the
+// unbounded allocation (70 registers, 3 CTAs) for bf16 silu * up.
 template <typename T, typename F, int NIN, bool AMOD, bool BMOD>
-__global__ void __launch_bounds__(EW_THREADS)
+__global__ void __launch_bounds__(EW_THREADS, 4)
     ew_vec_kernel(const T* a, const T* b, T* out, uint64_t nvec, uint64_t nav, uint64_t nbv,
                   FastDiv adiv, FastDiv bdiv, bool wide, uint64_t tail_lo, uint64_t n, F f) {
     constexpr int V = Vec<T>::N;
