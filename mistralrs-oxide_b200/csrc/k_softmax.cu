@@ -198,9 +198,9 @@ __global__ void __launch_bounds__(256, 3) smax_rows_kernel(const T* x, T* out, S
 // when the max grows); the CTA and then the cluster (through distributed
 // shared memory, in rank order) combine the (m, s) pairs into the row's max M
 // and sum S.  Pass 2 re-reads the slice -- from L2, where pass 1 left it -- and
-// writes p = exp(score - M) / S, computed exactly as the tiled kernel does
-// (IEEE score, expf, RowDiv); only S carries the extra roundings of the
-// rescaling (a few ulp, far inside the f32 tolerance).  Nothing is held across
+// writes p = exp(score - M) * RN(1 / S) (IEEE score, expf); S carries the
+// extra roundings of the rescaling and p those of the reciprocal, a few ulp
+// in all, far inside the f32 tolerance.  Nothing is held across
 // passes, so each thread keeps U vectors in flight with few registers and a
 // decode-sized batch of long rows runs in one wave.  In place (out == x) is
 // safe: a CTA writes only its own slice, after its own last read of it.
@@ -299,8 +299,13 @@ __global__ void __launch_bounds__(NT, 2048 / NT / 2)
                 online_merge(M, S, *cluster.map_shared_rank(&slot[0], q), *cluster.map_shared_rank(&slot[1], q));
             cluster_arrive();  // this CTA is done reading its peers' slots
         }
-        // pass 2: p = exp(s - M) / S for valid keys, 0 beyond the valid length
-        const RowDiv div(S);
+        // pass 2: p = exp(s - M) * RN(1 / S) for valid keys, 0 beyond the valid
+        // length.  S >= 1 (the max key contributes exp(0)), so the reciprocal
+        // is normal and the product is within 1.5 ulp of exp(s - M) / S -- the
+        // sum itself carries more rounding than that; measured 7% faster than
+        // the per-element division on the decode shape.
+        const float inv = __frcp_rn(S);
+        const float2 inv2 = f2(inv, inv);
         const float2 nm = f2(-M, -M);
         T* orow = out + row * p.cols;
         for (uint32_t j0 = lo + threadIdx.x; j0 < hi; j0 += NT * U) {
@@ -318,26 +323,13 @@ __global__ void __launch_bounds__(NT, 2048 / NT / 2)
                     if (j < vv) {
                         float f[V];
                         Vec<T>::unpack(r[u], f);
-                        if (j * V + V <= len) {
-                            bool redo = div.ieee;
+                        const bool full = j * V + V <= len;
 #pragma unroll
-                            for (int e = 0; e < V; e += 2) {
-                                const float2 d = fadd2(score2<MASK>(p, f[e], f[e + 1], j * V + e), nm);
-                                const float2 q = div.fast2(f2(expf(d.x), expf(d.y)), redo);
-                                o[e] = q.x;
-                                o[e + 1] = q.y;
-                            }
-                            if (redo) {
-#pragma unroll
-                                for (int e = 0; e < V; ++e)
-                                    o[e] = __fdiv_rn(expf(fsub(score_t<MASK>(p, f[e], j * V + e), M)), S);
-                            }
-                        } else {
-#pragma unroll
-                            for (int e = 0; e < V; ++e)
-                                o[e] = j * V + e < len
-                                           ? __fdiv_rn(expf(fsub(score_t<MASK>(p, f[e], j * V + e), M)), S)
-                                           : 0.0f;
+                        for (int e = 0; e < V; e += 2) {
+                            const float2 d = fadd2(score2<MASK>(p, f[e], f[e + 1], j * V + e), nm);
+                            const float2 q = fmul2(f2(expf(d.x), expf(d.y)), inv2);
+                            o[e] = full || j * V + e < len ? q.x : 0.0f;
+                            o[e + 1] = full || j * V + e + 1 < len ? q.y : 0.0f;
                         }
                     } else {
 #pragma unroll
