@@ -169,11 +169,13 @@ static int argmax_entry(const char* name, const T* x, uint64_t rows, uint64_t co
     constexpr int V = Vec<T>::N;
     const bool vec = cols % V == 0 && aligned16(x);
     const uint64_t units = vec ? cols / V : cols;
-    // Split a row over a cluster when there are too few rows to fill the GPU
-    // and each CTA would still get at least 4 units per thread.
+    // Split a row over a cluster of up to 8 CTAs while all CTAs still fit one
+    // wave and each keeps at least 4 units per thread (one round of loads).
     int cl = 1;
-    const uint64_t target = 2ull * sm_count();
-    while (cl < 8 && rows * cl < target && units / (2 * cl) >= 256 * 4) cl *= 2;
+    const uint64_t slots = (uint64_t)resident_blocks(
+        vec ? reinterpret_cast<const void*>(argmax_kernel<T, true>)
+            : reinterpret_cast<const void*>(argmax_kernel<T, false>), 256, 0);
+    while (cl < 8 && rows * (uint64_t)(2 * cl) <= slots && units / (2 * cl) >= 256 * 4) cl *= 2;
     const uint64_t cap = ((uint64_t)1 << 30) / cl;
     const uint64_t groups = rows < cap ? rows : cap;
     cudaLaunchConfig_t cfg = {};

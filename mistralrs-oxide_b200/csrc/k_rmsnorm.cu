@@ -48,15 +48,17 @@ constexpr int norm_vpt() {
     return 4;
 }
 
-// Sum of squares of one unpacked vector into two lane accumulators (paired
-// f32: each product and each sum rounded separately, as the reference's
-// `ss += v * v`; the lanes are combined after the thread's last vector).
+// Sum of squares of one unpacked vector into two lane accumulators, each term
+// added with a fused multiply-add (one rounding per term; the reference's
+// `ss += v * v` rounds the product first -- on sm_100a a paired multiply
+// feeding a paired add comes out fused anyway, so the fused form is explicit).
+// The lanes are combined after the thread's last vector.
 template <int V>
 __device__ __forceinline__ void sumsq_add(float2& acc, const float (&v)[V]) {
 #pragma unroll
     for (int e = 0; e < V; e += 2) {
         const float2 p = f2(v[e], v[e + 1]);
-        acc = fadd2(acc, fmul2(p, p));
+        acc = __ffma2_rn(p, p, acc);
     }
 }
 
@@ -189,7 +191,7 @@ __global__ void __launch_bounds__(256)
                 v = Vec<T>::rnd(fadd(v, Vec<T>::load1(r + off + i)));
                 Vec<T>::store1(h + off + i, v);
             }
-            ss = fadd(ss, fmul(v, v));
+            ss = __fmaf_rn(v, v, ss);  // one rounding per term, as sumsq_add
         }
         ss = group_reduce(ss, red, (int)blockDim.x, OpAddF());
         const float rms = fsqrt(fadd(fdiv(ss, (float)p.cols), p.eps));

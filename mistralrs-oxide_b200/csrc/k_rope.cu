@@ -23,7 +23,8 @@ struct RopeArgs {
     uint64_t tokens;
     uint64_t table_rows;
     uint32_t q_heads, k_heads, head_dim;
-    int layout;  // 0 token-major [T,H,D], 1 head-major [H,T,D]
+    int layout;      // 0 token-major [T,H,D], 1 head-major [H,T,D]
+    FastDiv cph_div;  // division by the 16-byte chunks per half head
 };
 
 __device__ __forceinline__ uint64_t rope_base(const RopeArgs& p, uint64_t t, uint32_t h,
@@ -35,7 +36,6 @@ __device__ __forceinline__ void rot(float x1, float x2, float c, float s, float&
     o1 = fsub(fmul(x1, c), fmul(x2, s));
     o2 = fadd(fmul(x1, s), fmul(x2, c));
 }
-
 template <typename T>
 __global__ void __launch_bounds__(512)
     rope_vec_kernel(const T* q, T* qo, const T* k, T* ko, const float* cos_t, const float* sin_t,
@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(512)
         const int64_t pr = pos ? (int64_t)pos[t] : (int64_t)t;
         const bool ok = pr >= 0 && (uint64_t)pr < p.table_rows;
         for (uint32_t it = threadIdx.x; it < items; it += blockDim.x) {
-            const uint32_t hh = it / cph, c = it - hh * cph;
+            const uint32_t hh = p.cph_div.div(it), c = it - hh * cph;
             const bool isq = hh < p.q_heads;
             const uint32_t h = isq ? hh : hh - p.q_heads;
             const uint64_t base = rope_base(p, t, h, isq ? p.q_heads : p.k_heads) + c * V;
@@ -68,6 +68,10 @@ __global__ void __launch_bounds__(512)
                     Vec<float>::unpack(cv, cs + e);
                     Vec<float>::unpack(sv, sn + e);
                 }
+                // Scalar on purpose: a paired multiply feeding a paired add was
+                // measured to come out fused (one rounding) on sm_100a, which
+                // would break the bit-exact match with the reference's
+                // separately rounded x1*c - x2*s.
 #pragma unroll
                 for (int e = 0; e < V; ++e) rot(x1[e], x2[e], cs[e], sn[e], o1[e], o2[e]);
             } else {
@@ -129,10 +133,12 @@ static int rope_entry(const char* name, const T* q, T* qo, uint64_t qh, const T*
     OXIDE_REQUIRE(pos || table_rows >= tokens, name, "table_rows < tokens without positions");
     OXIDE_REQUIRE(tokens <= UINT64_MAX / ((qh + kh) * head_dim), name, "tensor size overflows");
     RopeArgs p{tokens, table_rows, (uint32_t)qh, (uint32_t)(k ? kh : 0), (uint32_t)head_dim,
-               layout};
+               layout, FastDiv()};
     const uint64_t half = head_dim / 2;
     const bool vec = half % V == 0 && half % 4 == 0 && aligned16(q) && aligned16(qo) &&
-                     aligned16(cos_t) && aligned16(sin_t) && (!k || (aligned16(k) && aligned16(ko)));
+                     aligned16(cos_t) && aligned16(sin_t) && (!k || (aligned16(k) && aligned16(ko))) &&
+                     (qh + (k ? kh : 0)) * (half / V) < (1ull << 31);  // items per token fit 32 bits
+    p.cph_div = FastDiv((uint32_t)(half / V > 0 ? half / V : 1));
     const uint64_t cap = (uint64_t)1 << 30;
     if (vec) {
         const uint64_t items = (qh + (k ? kh : 0)) * (half / V);

@@ -36,23 +36,34 @@ namespace cg = cooperative_groups;
 
 namespace oxide {
 
-// ---- per-thread row chunk: VPT packed vectors j = j0 + k * jstep ------------
+// ---- scores and exp arguments ---------------------------------------------------
+// s = x * scale, plus mask[c] as fma(x, scale, mask[c]) (one rounding); the exp
+// argument is d = s - m, formed without a mask as fma(x, scale, -m) (one
+// rounding).  The reference rounds x * scale before adding; on sm_100a a paired
+// multiply feeding a paired add comes out fused anyway, so the fused forms are
+// written explicitly and the scalar and paired lanes of every kernel agree.
 template <bool MASK>
 __device__ __forceinline__ float score_t(const SmaxArgs& p, float x, uint32_t c) {
-    float s = fmul(x, p.scale);
-    if (MASK) s = fadd(s, __ldg(p.mask + p.mask_div.mod(c)));
-    return s;
+    return MASK ? __fmaf_rn(x, p.scale, __ldg(p.mask + p.mask_div.mod(c))) : fmul(x, p.scale);
 }
-
-// Scores of keys c, c + 1 on the paired f32 pipe (same roundings as score_t).
 template <bool MASK>
 __device__ __forceinline__ float2 score2(const SmaxArgs& p, float x0, float x1, uint32_t c) {
-    float2 s = fmul2(f2(x0, x1), f2(p.scale, p.scale));
+    const float2 sc = f2(p.scale, p.scale);
     if (MASK)
-        s = fadd2(s, f2(__ldg(p.mask + p.mask_div.mod(c)), __ldg(p.mask + p.mask_div.mod(c + 1))));
-    return s;
+        return __ffma2_rn(f2(x0, x1), sc,
+                          f2(__ldg(p.mask + p.mask_div.mod(c)), __ldg(p.mask + p.mask_div.mod(c + 1))));
+    return fmul2(f2(x0, x1), sc);
+}
+template <bool MASK>
+__device__ __forceinline__ float diff_t(const SmaxArgs& p, float x, uint32_t c, float m) {
+    return MASK ? fsub(score_t<MASK>(p, x, c), m) : __fmaf_rn(x, p.scale, -m);
+}
+template <bool MASK>
+__device__ __forceinline__ float2 diff2(const SmaxArgs& p, float x0, float x1, uint32_t c, float2 nm) {
+    return MASK ? fadd2(score2<MASK>(p, x0, x1, c), nm) : __ffma2_rn(f2(x0, x1), f2(p.scale, p.scale), nm);
 }
 
+// ---- per-thread row chunk: VPT packed vectors j = j0 + k * jstep ------------
 // Max of the valid scores of the chunk (vectors j < jhi, keys c < len).
 template <typename T, int VPT, bool MASK>
 __device__ __forceinline__ float chunk_max(const uint4 (&raw)[VPT], const SmaxArgs& p, uint32_t j0,
@@ -99,7 +110,7 @@ __device__ __forceinline__ float chunk_exp(const uint4 (&raw)[VPT], float (&ev)[
             if (j * V + V <= len) {  // every key valid: no per-key checks
 #pragma unroll
                 for (int e = 0; e < V; e += 2) {
-                    const float2 d = fadd2(score2<MASK>(p, f[e], f[e + 1], j * V + e), nm);
+                    const float2 d = diff2<MASK>(p, f[e], f[e + 1], j * V + e, nm);
                     ev[k][e] = expf(d.x);
                     ev[k][e + 1] = expf(d.y);
                     acc = fadd2(acc, f2(ev[k][e], ev[k][e + 1]));
@@ -107,7 +118,7 @@ __device__ __forceinline__ float chunk_exp(const uint4 (&raw)[VPT], float (&ev)[
             } else {  // the one vector of the row that straddles len
 #pragma unroll
                 for (int e = 0; e < V; e += 2) {
-                    const float2 d = fadd2(score2<MASK>(p, f[e], f[e + 1], j * V + e), nm);
+                    const float2 d = diff2<MASK>(p, f[e], f[e + 1], j * V + e, nm);
                     ev[k][e] = j * V + e < len ? expf(d.x) : 0.0f;
                     ev[k][e + 1] = j * V + e + 1 < len ? expf(d.y) : 0.0f;
                     acc = fadd2(acc, f2(ev[k][e], ev[k][e + 1]));
@@ -275,8 +286,10 @@ __global__ void __launch_bounds__(NT, 2048 / NT / 2)
                     float2 acc = f2(0.0f, 0.0f);
 #pragma unroll
                     for (int e = 0; e < V; e += 2) {
-                        const float2 d = fadd2(f2(sc[e], sc[e + 1]), nm);
-                        acc = fadd2(acc, f2(expf(d.x), expf(d.y)));
+                        const float2 d = diff2<MASK>(p, f[e], f[e + 1], j * V + e, nm);
+                        const float e0 = full || j * V + e < len ? expf(d.x) : 0.0f;
+                        const float e1 = full || j * V + e + 1 < len ? expf(d.y) : 0.0f;
+                        acc = fadd2(acc, f2(e0, e1));
                     }
                     ssum = fadd(ssum, fadd(acc.x, acc.y));
                 }
@@ -326,7 +339,7 @@ __global__ void __launch_bounds__(NT, 2048 / NT / 2)
                         const bool full = j * V + V <= len;
 #pragma unroll
                         for (int e = 0; e < V; e += 2) {
-                            const float2 d = fadd2(score2<MASK>(p, f[e], f[e + 1], j * V + e), nm);
+                            const float2 d = diff2<MASK>(p, f[e], f[e + 1], j * V + e, nm);
                             const float2 q = fmul2(f2(expf(d.x), expf(d.y)), inv2);
                             o[e] = full || j * V + e < len ? q.x : 0.0f;
                             o[e + 1] = full || j * V + e + 1 < len ? q.y : 0.0f;
@@ -365,13 +378,13 @@ __global__ void __launch_bounds__(256) smax_rows_scalar_kernel(const T* x, T* ou
         m = group_reduce(m, red, (int)blockDim.x, OpMaxF());
         float sum = 0.0f;
         for (uint32_t j = threadIdx.x; j < len; j += blockDim.x)
-            sum = fadd(sum, expf(fsub(score(p, Vec<T>::load1(xr + j), j), m)));
+            sum = fadd(sum, expf(score_diff(p, Vec<T>::load1(xr + j), j, m)));
         sum = group_reduce(sum, red, (int)blockDim.x, OpAddF());
         __syncthreads();  // every thread has read its inputs before any write (in place)
         const RowDiv div(sum);
         for (uint32_t j = threadIdx.x; j < p.cols; j += blockDim.x) {
             float o = 0.0f;
-            if (j < len) o = div(expf(fsub(score(p, Vec<T>::load1(xr + j), j), m)));
+            if (j < len) o = div(expf(score_diff(p, Vec<T>::load1(xr + j), j, m)));
             Vec<T>::store1(orow + j, o);
         }
     }

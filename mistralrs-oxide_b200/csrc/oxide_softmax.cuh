@@ -42,11 +42,15 @@ __device__ __forceinline__ uint32_t valid_len(const SmaxArgs& p, uint64_t row) {
     return len;
 }
 
-// s = x * scale, then + mask[j % mask_len]: src/ops/attention.rs:60,66-68.
+// s = x * scale, then + mask[j % mask_len] (src/ops/attention.rs:60,66-68),
+// with the mask added as fma(x, scale, mask) and the exp argument s - m formed
+// without a mask as fma(x, scale, -m): the same roundings as the vector
+// kernels (k_softmax.cu, score_t / diff_t).
 __device__ __forceinline__ float score(const SmaxArgs& p, float x, uint32_t j) {
-    float s = fmul(x, p.scale);
-    if (p.mask) s = fadd(s, __ldg(p.mask + p.mask_div.mod(j)));
-    return s;
+    return p.mask ? __fmaf_rn(x, p.scale, __ldg(p.mask + p.mask_div.mod(j))) : fmul(x, p.scale);
+}
+__device__ __forceinline__ float score_diff(const SmaxArgs& p, float x, uint32_t j, float m) {
+    return p.mask ? fsub(score(p, x, j), m) : __fmaf_rn(x, p.scale, -m);
 }
 
 }  // namespace oxide
