@@ -4,8 +4,11 @@
 //   oxide::OxideError / OxideResult      src/error.rs:3-47
 //   oxide::Shape, DType, Tensor          src/core/dtype.rs:9,70-181, src/core/tensor.rs:29
 //   oxide::ops::{add, sub, mul, div,     src/ops/matmul.rs:74-177
-//                silu, softmax,          src/ops/activation.rs:21-124
-//                rms_norm,               src/ops/norm.rs:4-51
+//                relu, silu, gelu, gelu_quick, softmax, sigmoid, tanh
+//                                        src/ops/activation.rs
+//                exp, log, sqrt, pow, clamp, neg, abs
+//                                        src/ops/math.rs
+//                rms_norm, layer_norm,   src/ops/norm.rs:4-117
 //                apply_rotary_emb}       src/ops/attention.rs:96-159
 //   oxide::precompute_rope_cache         src/models/mistral.rs:91-115
 //   oxide::CudaBackend                   src/cuda_backend/mod.rs:43-140
@@ -353,6 +356,33 @@ inline Result<Tensor> silu(const Tensor& x) {
     return out;
 }
 
+// Unary ops of src/ops/activation.rs (relu, gelu, gelu_quick, sigmoid, tanh)
+// and src/ops/math.rs (exp, log, sqrt, pow, clamp, neg, abs): op is an
+// oxide_unop; a = pow exponent or clamp minimum, b = clamp maximum.
+inline Result<Tensor> unary(int op, const Tensor& x, float a = 0.0f, float b = 0.0f) {
+    auto out = Tensor::empty(x.shape(), x.dtype(), x.device());
+    if (out.is_err()) return out;
+    const int rc = detail::bf16(x)
+        ? oxide_unary_bf16(op, x.as<oxide_bf16>(), out.value().as<oxide_bf16>(), x.elem_count(), a, b,
+                           current_stream())
+        : oxide_unary_f32(op, x.as<float>(), out.value().as<float>(), x.elem_count(), a, b,
+                          current_stream());
+    OXIDE_TRY(check_status(rc));
+    return out;
+}
+inline Result<Tensor> relu(const Tensor& x) { return unary(OXIDE_RELU, x); }
+inline Result<Tensor> gelu(const Tensor& x) { return unary(OXIDE_GELU, x); }
+inline Result<Tensor> gelu_quick(const Tensor& x) { return unary(OXIDE_GELU_QUICK, x); }
+inline Result<Tensor> sigmoid(const Tensor& x) { return unary(OXIDE_SIGMOID, x); }
+inline Result<Tensor> tanh(const Tensor& x) { return unary(OXIDE_TANH, x); }
+inline Result<Tensor> exp(const Tensor& x) { return unary(OXIDE_EXP, x); }
+inline Result<Tensor> log(const Tensor& x) { return unary(OXIDE_LOG, x); }
+inline Result<Tensor> sqrt(const Tensor& x) { return unary(OXIDE_SQRT, x); }
+inline Result<Tensor> pow(const Tensor& x, float n) { return unary(OXIDE_POW, x, n); }
+inline Result<Tensor> clamp(const Tensor& x, float lo, float hi) { return unary(OXIDE_CLAMP, x, lo, hi); }
+inline Result<Tensor> neg(const Tensor& x) { return unary(OXIDE_NEG, x); }
+inline Result<Tensor> abs(const Tensor& x) { return unary(OXIDE_ABS, x); }
+
 // mul(silu(gate), up) in one pass (MLP::forward, src/layers/attention.rs:144-145).
 inline Result<Tensor> silu_mul(const Tensor& gate, const Tensor& up) {
     OXIDE_TRY(detail::same_dtype(gate, up, "silu_mul"));
@@ -396,6 +426,30 @@ inline Result<Tensor> rms_norm(const Tensor& x, const Tensor& w, float eps) {
                               c, eps, current_stream())
         : oxide_rms_norm_f32(x.as<float>(), w.as<float>(), out.value().as<float>(), rows, c, eps,
                              current_stream());
+    OXIDE_TRY(check_status(rc));
+    return out;
+}
+
+// layer_norm (src/ops/norm.rs:53-117), with the reference's argument checks.
+inline Result<Tensor> layer_norm(const Tensor& x, const Tensor& w, const Tensor& b, float eps) {
+    if (x.rank() < 1) return OxideError::invalid("layer_norm requires at least 1D tensor");
+    const size_t last = x.dims().back();
+    if (w.rank() != 1 || w.dims()[0] != last)
+        return OxideError::invalid("layer_norm weight shape " + w.shape().to_string() +
+                                   " doesn't match input last dim " + std::to_string(last));
+    if (b.rank() != 1 || b.dims()[0] != last)
+        return OxideError::invalid("layer_norm bias shape " + b.shape().to_string() +
+                                   " doesn't match input last dim " + std::to_string(last));
+    OXIDE_TRY(detail::same_dtype(x, w, "layer_norm"));
+    OXIDE_TRY(detail::same_dtype(x, b, "layer_norm"));
+    auto out = Tensor::empty(x.shape(), x.dtype(), x.device());
+    if (out.is_err()) return out;
+    const size_t rows = last ? x.elem_count() / last : 0;
+    const int rc = detail::bf16(x)
+        ? oxide_layer_norm_bf16(x.as<oxide_bf16>(), w.as<oxide_bf16>(), b.as<oxide_bf16>(),
+                                out.value().as<oxide_bf16>(), rows, last, eps, current_stream())
+        : oxide_layer_norm_f32(x.as<float>(), w.as<float>(), b.as<float>(), out.value().as<float>(), rows,
+                               last, eps, current_stream());
     OXIDE_TRY(check_status(rc));
     return out;
 }
@@ -630,6 +684,23 @@ class KernelManager {
     }
     LaunchResult launch_silu(const float* input, float* output, size_t n) const {
         return wrap("silu", oxide_silu_f32(input, output, n, stream_));
+    }
+    LaunchResult launch_relu(const float* input, float* output, size_t n) const {
+        return wrap("relu", oxide_relu_f32(input, output, n, stream_));
+    }
+    LaunchResult launch_gelu(const float* input, float* output, size_t n) const {
+        return wrap("gelu", oxide_gelu_f32(input, output, n, stream_));
+    }
+    LaunchResult launch_sigmoid(const float* input, float* output, size_t n) const {
+        return wrap("sigmoid", oxide_sigmoid_f32(input, output, n, stream_));
+    }
+    LaunchResult launch_tanh(const float* input, float* output, size_t n) const {
+        return wrap("tanh", oxide_tanh_f32(input, output, n, stream_));
+    }
+    LaunchResult launch_layer_norm(const float* input, const float* weight, const float* bias,
+                                   float* output, size_t num_rows, size_t num_cols, float eps) const {
+        return wrap("layer_norm",
+                    oxide_layer_norm_f32(input, weight, bias, output, num_rows, num_cols, eps, stream_));
     }
     LaunchResult launch_rms_norm(const float* input, const float* weight, float* output,
                                  size_t num_rows, size_t num_cols, float eps) const {

@@ -57,6 +57,22 @@ typedef enum { OXIDE_ADD = 0, OXIDE_SUB = 1, OXIDE_MUL = 2, OXIDE_DIV = 3 } oxid
 /* Reduction selector for oxide_reduce_*. */
 typedef enum { OXIDE_RED_SUM = 0, OXIDE_RED_MAX = 1, OXIDE_RED_SUMSQ = 2 } oxide_redop;
 
+/* Unary operator selector for oxide_unary_*. */
+typedef enum {
+    OXIDE_RELU = 0,       /* max(x, 0); NaN -> 0 like f32::max          */
+    OXIDE_GELU = 1,       /* tanh form, src/ops/activation.rs:39-56     */
+    OXIDE_GELU_QUICK = 2, /* x * sigmoid(1.702 x), activation.rs:58-74  */
+    OXIDE_SIGMOID = 3,    /* 1 / (1 + exp(-x)), activation.rs:126-140   */
+    OXIDE_TANH = 4,       /* activation.rs:142-156                      */
+    OXIDE_EXP = 5,        /* src/ops/math.rs:4-19                       */
+    OXIDE_LOG = 6,        /* natural log, math.rs:21-36                 */
+    OXIDE_SQRT = 7,       /* math.rs:38-53                              */
+    OXIDE_POW = 8,        /* powf(x, a), math.rs:55-70                  */
+    OXIDE_CLAMP = 9,      /* clamp(x, a, b), a <= b, math.rs:72-87      */
+    OXIDE_NEG = 10,       /* math.rs:89-104                             */
+    OXIDE_ABS = 11        /* math.rs:106-121                            */
+} oxide_unop;
+
 /* ---- library / status --------------------------------------------------- */
 
 /* Human-readable name of a status code (never NULL). */
@@ -125,6 +141,24 @@ int oxide_silu_mul_f32(const float* gate, const float* up, float* out, uint64_t 
 int oxide_silu_mul_bf16(const oxide_bf16* gate, const oxide_bf16* up, oxide_bf16* out,
                         uint64_t n, oxide_stream_t stream);
 
+/* ---- unary ops -----------------------------------------------------------------
+ * out[i] = op(x[i]) for the oxide_unop selector, with the scalar parameters a
+ * (pow exponent, clamp minimum) and b (clamp maximum); each step rounded as the
+ * reference's f32 expression (transcendentals are CUDA's expf/logf/tanhf/powf).
+ * CLAMP with a > b (or a NaN bound) is OXIDE_ERR_INVALID_ARG, where the
+ * reference's f32::clamp panics.  Replaces src/ops/activation.rs relu / gelu /
+ * gelu_quick / sigmoid / tanh and src/ops/math.rs exp / log / sqrt / pow / clamp
+ * / neg / abs; the named f32 forms replace KernelManager::launch_relu, launch_gelu,
+ * launch_sigmoid and launch_tanh (src/cuda_backend/kernels.rs:211-309). */
+int oxide_unary_f32(int op, const float* x, float* out, uint64_t n, float a, float b,
+                    oxide_stream_t stream);
+int oxide_unary_bf16(int op, const oxide_bf16* x, oxide_bf16* out, uint64_t n, float a, float b,
+                     oxide_stream_t stream);
+int oxide_relu_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream);
+int oxide_gelu_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream);
+int oxide_sigmoid_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream);
+int oxide_tanh_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream);
+
 /* ---- normalisation ----------------------------------------------------------
  * Per row of x[rows, cols]: rms = sqrt(sum(x*x) / cols + eps);
  * out = (x / rms) * w.  Replaces ops::rms_norm (src/ops/norm.rs:4-51) and
@@ -144,6 +178,16 @@ int oxide_add_rms_norm_f32(const float* x, const float* r, const float* w, float
 int oxide_add_rms_norm_bf16(const oxide_bf16* x, const oxide_bf16* r, const oxide_bf16* w,
                             oxide_bf16* h, oxide_bf16* y, uint64_t rows, uint64_t cols,
                             float eps, oxide_stream_t stream);
+
+/* Per row of x[rows, cols]: mean = sum(x) / cols; var = sum((x - mean)^2) / cols;
+ * out = (x - mean) / sqrt(var + eps) * w + b.  Replaces ops::layer_norm
+ * (src/ops/norm.rs:53-117) and KernelManager::launch_layer_norm
+ * (src/cuda_backend/kernels.rs:334-356). */
+int oxide_layer_norm_f32(const float* x, const float* w, const float* b, float* out, uint64_t rows,
+                         uint64_t cols, float eps, oxide_stream_t stream);
+int oxide_layer_norm_bf16(const oxide_bf16* x, const oxide_bf16* w, const oxide_bf16* b,
+                          oxide_bf16* out, uint64_t rows, uint64_t cols, float eps,
+                          oxide_stream_t stream);
 
 /* ---- softmax ---------------------------------------------------------------
  * softmax(x, dim) of a tensor viewed as [outer, dim, inner] (inner = product

@@ -73,6 +73,45 @@ struct FScale {
     __device__ __forceinline__ float2 pair(float2 x, float2) const { return fmul2(x, f2(s, s)); }
 };
 
+// Unary ops of src/ops/activation.rs and src/ops/math.rs, each step rounded as
+// the reference's f32 expression (scalar __f*_rn: never fused).  a: the pow
+// exponent, the clamp minimum or gelu's sqrt(2 / pi) (computed on the host as
+// the reference's (2.0 / PI).sqrt() in f32); b: the clamp maximum.
+template <int OP>
+struct FUnary {
+    float a, b;
+    __device__ __forceinline__ float operator()(float x, float) const {
+        switch (OP) {
+            case OXIDE_RELU: return fmaxf(x, 0.0f);  // f32::max(x, 0.0): NaN -> 0
+            case OXIDE_GELU: {  // 0.5 * x * (1 + tanh(k * (x + 0.044715 * (x * x) * x)))
+                const float half_x = fmul(0.5f, x);
+                const float p = fmul(fmul(x, x), x);
+                const float u = fadd(x, fmul(0.044715f, p));
+                return fmul(half_x, fadd(1.0f, tanhf(fmul(a, u))));
+            }
+            case OXIDE_GELU_QUICK:  // x * (1 / (1 + exp(-1.702 * x)))
+                return fmul(x, __frcp_rn(fadd(1.0f, expf(fmul(-1.702f, x)))));
+            case OXIDE_SIGMOID: return __frcp_rn(fadd(1.0f, expf(-x)));
+            case OXIDE_TANH: return tanhf(x);
+            case OXIDE_EXP: return expf(x);
+            case OXIDE_LOG: return logf(x);
+            case OXIDE_SQRT: return fsqrt(x);
+            case OXIDE_POW: return powf(x, a);
+            case OXIDE_CLAMP: {  // f32::clamp: below min -> min, above max -> max, NaN stays
+                float r = x;
+                if (r < a) r = a;
+                if (r > b) r = b;
+                return r;
+            }
+            case OXIDE_NEG: return -x;
+            default: return fabsf(x);
+        }
+    }
+    __device__ __forceinline__ float2 pair(float2 x, float2 y) const {
+        return f2((*this)(x.x, y.x), (*this)(x.y, y.y));
+    }
+};
+
 // ---- vectorised kernel ------------------------------------------------------
 // NIN = 1 (b unused) or 2.  AMOD/BMOD: operand indexed modulo its length
 // (in vectors).  Requires 16-byte aligned pointers and, for modulo operands,
@@ -228,11 +267,76 @@ static int full_entry(const char* name, const T* a, const T* b, T* out, uint64_t
     return ew_dispatch<T, F, NIN>(name, a, n, NIN == 2 ? b : a, n, out, n, f, st);
 }
 
+// Elementwise op over whole tensors (no broadcast): only the aligned-vector and
+// the scalar kernel are instantiated.
+template <typename T, typename F>
+static int unary_dispatch(const char* name, const T* x, T* out, uint64_t n, F f, cudaStream_t st) {
+    if (aligned16(x) && aligned16(out)) {
+        launch_vec<T, F, 1, false, false>(x, n, x, n, out, n, f, st);
+    } else {
+        auto kern = ew_scalar_kernel<T, F, 1>;
+        kern<<<resident_grid(kern, n), EW_THREADS, 0, st>>>(x, n, x, n, out, n, f);
+    }
+    return check_launch(name);
+}
+
+template <typename T>
+static int unary_entry(const char* name, int op, const T* x, T* out, uint64_t n, float a, float b,
+                       cudaStream_t st) {
+    OXIDE_INJECT(name);
+    OXIDE_REQUIRE(op >= OXIDE_RELU && op <= OXIDE_ABS, name, "unknown unary operator");
+    // f32::clamp asserts min <= max (neither NaN)
+    OXIDE_REQUIRE(op != OXIDE_CLAMP || a <= b, name, "clamp requires min <= max");
+    if (n == 0) return OXIDE_OK;
+    OXIDE_REQUIRE(x && out, name, "null pointer");
+    if (op == OXIDE_GELU) a = sqrtf(2.0f / 3.14159265358979323846f);  // (2.0 / PI).sqrt() in f32
+    switch (op) {
+#define OXIDE_UNARY_CASE(OPV) \
+    case OPV: return unary_dispatch<T, FUnary<OPV>>(name, x, out, n, FUnary<OPV>{a, b}, st);
+        OXIDE_UNARY_CASE(OXIDE_RELU)
+        OXIDE_UNARY_CASE(OXIDE_GELU)
+        OXIDE_UNARY_CASE(OXIDE_GELU_QUICK)
+        OXIDE_UNARY_CASE(OXIDE_SIGMOID)
+        OXIDE_UNARY_CASE(OXIDE_TANH)
+        OXIDE_UNARY_CASE(OXIDE_EXP)
+        OXIDE_UNARY_CASE(OXIDE_LOG)
+        OXIDE_UNARY_CASE(OXIDE_SQRT)
+        OXIDE_UNARY_CASE(OXIDE_POW)
+        OXIDE_UNARY_CASE(OXIDE_CLAMP)
+        OXIDE_UNARY_CASE(OXIDE_NEG)
+        OXIDE_UNARY_CASE(OXIDE_ABS)
+#undef OXIDE_UNARY_CASE
+    }
+    return set_error(OXIDE_ERR_INVALID_ARG, "%s: unknown unary operator", name);
+}
+
 }  // namespace oxide
 
 using oxide::bf16_t;
 
 extern "C" {
+
+int oxide_unary_f32(int op, const float* x, float* out, uint64_t n, float a, float b,
+                    oxide_stream_t stream) {
+    return oxide::unary_entry<float>("oxide_unary_f32", op, x, out, n, a, b, stream);
+}
+int oxide_unary_bf16(int op, const oxide_bf16* x, oxide_bf16* out, uint64_t n, float a, float b,
+                     oxide_stream_t stream) {
+    return oxide::unary_entry<bf16_t>("oxide_unary_bf16", op, x, out, n, a, b, stream);
+}
+int oxide_relu_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::unary_entry<float>("oxide_relu_f32", OXIDE_RELU, x, out, n, 0.0f, 0.0f, stream);
+}
+int oxide_gelu_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::unary_entry<float>("oxide_gelu_f32", OXIDE_GELU, x, out, n, 0.0f, 0.0f, stream);
+}
+int oxide_sigmoid_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::unary_entry<float>("oxide_sigmoid_f32", OXIDE_SIGMOID, x, out, n, 0.0f, 0.0f,
+                                     stream);
+}
+int oxide_tanh_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream) {
+    return oxide::unary_entry<float>("oxide_tanh_f32", OXIDE_TANH, x, out, n, 0.0f, 0.0f, stream);
+}
 
 int oxide_binary_f32(int op, const float* a, uint64_t na, const float* b, uint64_t nb,
                      float* out, uint64_t n, oxide_stream_t stream) {

@@ -50,6 +50,14 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_rope_table_host_f32": (i32, [f32, u64, u64, vp, vp]),
     "oxide_argmax_rows_f32": (i32, [vp, u64, u64, vp, vp]),
     "oxide_argmax_rows_bf16": (i32, [vp, u64, u64, vp, vp]),
+    "oxide_unary_f32": (i32, [i32, vp, vp, u64, f32, f32, vp]),
+    "oxide_unary_bf16": (i32, [i32, vp, vp, u64, f32, f32, vp]),
+    "oxide_relu_f32": (i32, [vp, vp, u64, vp]),
+    "oxide_gelu_f32": (i32, [vp, vp, u64, vp]),
+    "oxide_sigmoid_f32": (i32, [vp, vp, u64, vp]),
+    "oxide_tanh_f32": (i32, [vp, vp, u64, vp]),
+    "oxide_layer_norm_f32": (i32, [vp, vp, vp, vp, u64, u64, f32, vp]),
+    "oxide_layer_norm_bf16": (i32, [vp, vp, vp, vp, u64, u64, f32, vp]),
     "oxide_reduce_rows_f32": (i32, [i32, vp, u64, u64, vp, vp]),
     "oxide_reduce_rows_bf16": (i32, [i32, vp, u64, u64, vp, vp]),
     "oxide_reduce_workspace_bytes": (u64, [u64]),
@@ -68,6 +76,7 @@ SIGNATURES: dict[str, tuple] = {
 OK, ERR_INVALID_ARG, ERR_LAUNCH, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_INJECTED, ERR_TIMEOUT = (
     0, -1, -2, -3, -4, -5, -6, -7)
 ADD, SUB, MUL, DIV = 0, 1, 2, 3
+RELU, GELU, GELU_QUICK, SIGMOID, TANH, EXP, LOG, SQRT, POW, CLAMP, NEG, ABS = range(12)
 RED_SUM, RED_MAX, RED_SUMSQ = 0, 1, 2
 
 _lock = threading.Lock()

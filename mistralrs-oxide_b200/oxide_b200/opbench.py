@@ -23,6 +23,7 @@ if __package__ in (None, ""):
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from oxide_b200 import ops  # noqa: E402
+from oxide_b200 import _lib  # noqa: E402
 from oxide_b200._lib import call  # noqa: E402
 from oxide_b200.workloads import C1, C2, C3, C4, C5  # noqa: E402
 
@@ -94,7 +95,31 @@ def build(op: str, rows: int | None, dev):
         run = lambda s: ops.rope(s[0], s[1], cos, sin, q_out=s[2], k_out=s[3])  # noqa: E731
         nb = 2 * T * (c.q_heads + c.k_heads) * c.head_dim * 2 + 2 * T * (c.head_dim // 2) * 4
         return mk, run, nb, [T, c.q_heads + c.k_heads, c.head_dim]
+    if op in ("gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2"):
+        # remaining activations (src/ops/activation.rs) at the C2 MLP shape
+        c = C2()
+        R = rows or c.rows
+        code = {"gelu_f32_c2": _lib.GELU, "tanh_f32_c2": _lib.TANH, "relu_f32_c2": _lib.RELU}[op]
+        mk = lambda: (rn(R, c.inter), torch.empty(R, c.inter, device=dev))  # noqa: E731
+        run = lambda s: ops.unary(code, s[0], out=s[1])  # noqa: E731
+        return mk, run, 2 * R * c.inter * 4, [R, c.inter]
+    if op == "layer_norm_f32_c1":
+        # layer_norm (src/ops/norm.rs:53-117) at the C1 shape
+        c = C1()
+        R = rows or c.rows
+        w = torch.rand(c.cols, generator=g, device=dev) + 0.5
+        bias = torch.rand(c.cols, generator=g, device=dev) - 0.5
+        mk = lambda: (rn(R, c.cols), torch.empty(R, c.cols, device=dev))  # noqa: E731
+        run = lambda s: ops.layer_norm(s[0], w, bias, c.eps, out=s[1])  # noqa: E731
+        return mk, run, 2 * R * c.cols * 4 + 2 * c.cols * 4, [R, c.cols]
     c = C5()
+    if op == "layer_norm_bf16_c5":
+        R = rows or c.rows
+        w = torch.ones(c.hidden, dtype=BF16, device=dev)
+        bias = torch.zeros(c.hidden, dtype=BF16, device=dev)
+        mk = lambda: (rn(R, c.hidden, dtype=BF16), torch.empty(R, c.hidden, dtype=BF16, device=dev))  # noqa: E731
+        run = lambda s: ops.layer_norm(s[0], w, bias, c.eps, out=s[1])  # noqa: E731
+        return mk, run, 2 * R * c.hidden * 2 + 2 * c.hidden * 2, [R, c.hidden]
     if op in ("rms_norm_bf16_c5", "add_rms_norm_bf16_c5", "sumsq_bf16_c5"):
         R = rows or c.rows
         w = torch.ones(c.hidden, dtype=BF16, device=dev)
@@ -141,7 +166,8 @@ def build(op: str, rows: int | None, dev):
 
 OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softmax_f32_c3",
        "argmax_f32_c3", "rope_bf16_c4", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
-       "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5"]
+       "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5",
+       "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5"]
 
 
 def main(argv=None):

@@ -119,6 +119,82 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] =
     return out
 
 
+def unary(op: int, x: torch.Tensor, a: float = 0.0, b: float = 0.0,
+          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = op(x) elementwise (oxide_unop: src/ops/activation.rs, src/ops/math.rs)."""
+    _check(x, out)
+    out = torch.empty_like(x) if out is None else out
+    call(f"oxide_unary_{_sfx(x)}", op, _p(x), _p(out), x.numel(), float(a), float(b), _stream())
+    return out
+
+
+def relu(x):  # src/ops/activation.rs:4-19
+    return unary(_lib.RELU, x)
+
+
+def gelu(x):  # src/ops/activation.rs:39-56 (tanh approximation)
+    return unary(_lib.GELU, x)
+
+
+def gelu_quick(x):  # src/ops/activation.rs:58-74
+    return unary(_lib.GELU_QUICK, x)
+
+
+def sigmoid(x):  # src/ops/activation.rs:126-140
+    return unary(_lib.SIGMOID, x)
+
+
+def tanh(x):  # src/ops/activation.rs:142-156
+    return unary(_lib.TANH, x)
+
+
+def exp(x):  # src/ops/math.rs:4-19
+    return unary(_lib.EXP, x)
+
+
+def log(x):  # src/ops/math.rs:21-36 (natural log)
+    return unary(_lib.LOG, x)
+
+
+def sqrt(x):  # src/ops/math.rs:38-53
+    return unary(_lib.SQRT, x)
+
+
+def pow(x, n: float):  # src/ops/math.rs:55-70
+    return unary(_lib.POW, x, n)
+
+
+def clamp(x, lo: float, hi: float):  # src/ops/math.rs:72-87
+    return unary(_lib.CLAMP, x, lo, hi)
+
+
+def neg(x):  # src/ops/math.rs:89-104
+    return unary(_lib.NEG, x)
+
+
+def abs(x):  # src/ops/math.rs:106-121
+    return unary(_lib.ABS, x)
+
+
+def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """src/ops/norm.rs:53-117."""
+    _check(x, w, b, out)
+    if x.dim() < 1:
+        raise OxideError(_lib.ERR_INVALID_ARG, "layer_norm", "layer_norm requires at least 1D tensor")
+    cols = x.shape[-1]
+    if w.dim() != 1 or w.shape[0] != cols:
+        raise OxideError(_lib.ERR_INVALID_ARG, "layer_norm",
+                         f"layer_norm weight shape {list(w.shape)} doesn't match input last dim {cols}")
+    if b.dim() != 1 or b.shape[0] != cols:
+        raise OxideError(_lib.ERR_INVALID_ARG, "layer_norm",
+                         f"layer_norm bias shape {list(b.shape)} doesn't match input last dim {cols}")
+    out = torch.empty_like(x) if out is None else out
+    call(f"oxide_layer_norm_{_sfx(x)}", _p(x), _p(w), _p(b), _p(out), x.numel() // cols, cols,
+         float(eps), _stream())
+    return out
+
+
 def _norm_check(x: torch.Tensor, w: torch.Tensor) -> int:
     if x.dim() < 1:
         raise OxideError(_lib.ERR_INVALID_ARG, "rms_norm", "rms_norm requires at least 1D tensor")

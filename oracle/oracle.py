@@ -61,6 +61,10 @@ def lib() -> C.CDLL:
             "orc_argmax_rows_bf16": [vp, u64, u64, vp, i32],
             "orc_reduce_rows_f32": [i32, vp, u64, u64, vp, i32],
             "orc_reduce_rows_bf16": [i32, vp, u64, u64, vp, i32],
+            "orc_unary_f32": [i32, vp, vp, u64, f32, f32, i32],
+            "orc_unary_bf16": [i32, vp, vp, u64, f32, f32, i32],
+            "orc_layer_norm_f32": [vp, vp, vp, vp, u64, u64, f32, i32],
+            "orc_layer_norm_bf16": [vp, vp, vp, vp, u64, u64, f32, i32],
         }
         for name, args in sig.items():
             fn = getattr(h, name)
@@ -141,6 +145,29 @@ def silu_mul(g, u, threads=1, out=None):
     g, u = _c(g), _c(u)
     out = np.empty_like(g) if out is None else out
     getattr(lib(), f"orc_silu_mul_{_sfx(g)}")(_p(g), _p(u), _p(out), g.size, threads)
+    return out
+
+
+# unary op codes (oxide_unop in include/oxide_ops.h)
+RELU, GELU, GELU_QUICK, SIGMOID, TANH, EXP, LOG, SQRT, POW, CLAMP, NEG, ABS = range(12)
+
+
+def unary(op, x, a=0.0, b=0.0, threads=1):
+    """src/ops/activation.rs / src/ops/math.rs unary ops; a = exponent (pow) or
+    min (clamp), b = max (clamp)."""
+    x = _c(x)
+    out = np.empty_like(x)
+    getattr(lib(), f"orc_unary_{_sfx(x)}")(op, _p(x), _p(out), x.size, float(a), float(b), threads)
+    return out
+
+
+def layer_norm(x, w, b, eps, threads=1):
+    """src/ops/norm.rs:53-117 over the last dim of x."""
+    x, w, b = _c(x), _c(w), _c(b)
+    cols = w.size
+    out = np.empty_like(x)
+    getattr(lib(), f"orc_layer_norm_{_sfx(x)}")(_p(x), _p(w), _p(b), _p(out), x.size // cols, cols,
+                                                float(eps), threads)
     return out
 
 

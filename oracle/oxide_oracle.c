@@ -476,3 +476,101 @@ float orc_reduce_seq_f32(int op, const float* x, uint64_t n) {
     for (uint64_t i = 0; i < n; ++i) acc = reduce_step(op, acc, x[i]);
     return acc;
 }
+
+/* ---- unary ops: src/ops/activation.rs (relu :4-19, gelu :39-56, gelu_quick
+ * :58-74, sigmoid :126-140, tanh :142-156) and src/ops/math.rs (exp :4, ln :21,
+ * sqrt :38, powf :55, clamp :72, neg :89, abs :106) --------------------------- */
+static inline float unary1(int op, float x, float a, float b) {
+    switch (op) {
+        case ORC_RELU: return fmaxf(x, 0.0f); /* f32::max(x, 0.0): NaN -> 0 */
+        case ORC_GELU: {
+            /* 0.5 * x * (1.0 + ((2.0 / PI).sqrt() * (x + 0.044715 * x.powi(3))).tanh());
+             * powi(3) evaluates (x * x) * x; every step rounded to f32. */
+            const float k = sqrtf(2.0f / 3.14159265358979323846f);
+            float half_x = 0.5f * x;
+            float p = x * x;
+            p = p * x;
+            float t = 0.044715f * p;
+            float u = x + t;
+            float v = k * u;
+            float th = tanhf(v);
+            float w = 1.0f + th;
+            return half_x * w;
+        }
+        case ORC_GELU_QUICK: {
+            float n = -1.702f * x;
+            float e = expf(n);
+            float d = 1.0f + e;
+            float r = 1.0f / d;
+            return x * r;
+        }
+        case ORC_SIGMOID: {
+            float e = expf(-x);
+            float d = 1.0f + e;
+            return 1.0f / d;
+        }
+        case ORC_TANH: return tanhf(x);
+        case ORC_EXP: return expf(x);
+        case ORC_LOG: return logf(x);
+        case ORC_SQRT: return sqrtf(x);
+        case ORC_POW: return powf(x, a);
+        case ORC_CLAMP: { /* f32::clamp: x < min -> min; x > max -> max; NaN stays */
+            float r = x;
+            if (r < a) r = a;
+            if (r > b) r = b;
+            return r;
+        }
+        case ORC_NEG: return -x;
+        default: return fabsf(x);
+    }
+}
+
+void orc_unary_f32(int op, const float* x, float* out, uint64_t n, float a, float b, int threads) {
+    OMP_FOR for (uint64_t i = 0; i < n; ++i) out[i] = unary1(op, x[i], a, b);
+}
+
+void orc_unary_bf16(int op, const uint16_t* x, uint16_t* out, uint64_t n, float a, float b,
+                    int threads) {
+    OMP_FOR for (uint64_t i = 0; i < n; ++i) out[i] = F2B(unary1(op, B2F(x[i]), a, b));
+}
+
+/* ---- LayerNorm: src/ops/norm.rs:92-113 -------------------------------------- */
+static inline void layer_norm_row(const float* xr, const float* w, const float* bias, float* orow,
+                                  uint64_t cols, float eps) {
+    float sum = 0.0f;
+    for (uint64_t i = 0; i < cols; ++i) sum += xr[i];
+    float mean = sum / (float)cols;
+    float sum_sq = 0.0f;
+    for (uint64_t i = 0; i < cols; ++i) {
+        float diff = xr[i] - mean;
+        sum_sq += diff * diff;
+    }
+    float var = sum_sq / (float)cols;
+    float sd = sqrtf(var + eps);
+    for (uint64_t i = 0; i < cols; ++i) {
+        float normalized = (xr[i] - mean) / sd;
+        orow[i] = normalized * w[i] + bias[i];
+    }
+}
+
+void orc_layer_norm_f32(const float* x, const float* w, const float* b, float* out, uint64_t rows,
+                        uint64_t cols, float eps, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r)
+        layer_norm_row(x + r * cols, w, b, out + r * cols, cols, eps);
+}
+
+void orc_layer_norm_bf16(const uint16_t* x, const uint16_t* w, const uint16_t* b, uint16_t* out,
+                         uint64_t rows, uint64_t cols, float eps, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        float* tmp = (float*)__builtin_malloc(4 * cols * sizeof(float));
+        float *xf = tmp, *wf = tmp + cols, *bf = tmp + 2 * cols, *of = tmp + 3 * cols;
+        for (uint64_t i = 0; i < cols; ++i) {
+            xf[i] = B2F(x[r * cols + i]);
+            wf[i] = B2F(w[i]);
+            bf[i] = B2F(b[i]);
+        }
+        layer_norm_row(xf, wf, bf, of, cols, eps);
+        for (uint64_t i = 0; i < cols; ++i) out[r * cols + i] = F2B(of[i]);
+        __builtin_free(tmp);
+    }
+}

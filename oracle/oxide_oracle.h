@@ -128,6 +128,23 @@ double orc_reduce_bf16(int op, const uint16_t* x, uint64_t n, int threads);
  * order; reported for information only (it stalls for n ~ 1e8). */
 float orc_reduce_seq_f32(int op, const float* x, uint64_t n);
 
+/* Unary ops (op codes equal the C ABI's oxide_unop): relu, gelu (tanh form),
+ * gelu_quick, sigmoid, tanh (src/ops/activation.rs) and exp, ln, sqrt, powf(a),
+ * clamp(a, b), neg, abs (src/ops/math.rs). */
+enum {
+    ORC_RELU = 0, ORC_GELU = 1, ORC_GELU_QUICK = 2, ORC_SIGMOID = 3, ORC_TANH = 4, ORC_EXP = 5,
+    ORC_LOG = 6, ORC_SQRT = 7, ORC_POW = 8, ORC_CLAMP = 9, ORC_NEG = 10, ORC_ABS = 11
+};
+void orc_unary_f32(int op, const float* x, float* out, uint64_t n, float a, float b, int threads);
+void orc_unary_bf16(int op, const uint16_t* x, uint16_t* out, uint64_t n, float a, float b,
+                    int threads);
+
+/* src/ops/norm.rs:53-117: mean, variance of x - mean, (x - mean) / sqrt(var + eps) * w + b */
+void orc_layer_norm_f32(const float* x, const float* w, const float* b, float* out, uint64_t rows,
+                        uint64_t cols, float eps, int threads);
+void orc_layer_norm_bf16(const uint16_t* x, const uint16_t* w, const uint16_t* b, uint16_t* out,
+                         uint64_t rows, uint64_t cols, float eps, int threads);
+
 int orc_max_threads(void);
 
 #ifdef __cplusplus

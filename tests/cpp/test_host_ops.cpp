@@ -382,6 +382,45 @@ DEVICE_TEST(kernel_manager_launchers_match_oracle) {
     EXPECT(backend.synchronize().is_ok());
 }
 
+DEVICE_TEST(unary_ops_and_layer_norm_match_oracle) {
+    const size_t n = 3001;
+    const auto x = randn(n, 23, 3.0f);
+    std::vector<float> ref(n);
+    const Tensor tx = dev(x, {n});
+    orc_unary_f32(ORC_RELU, x.data(), ref.data(), n, 0.0f, 0.0f, kThreads);
+    expect_bits_equal(host(unwrap(ops::relu(tx))), ref);
+    orc_unary_f32(ORC_TANH, x.data(), ref.data(), n, 0.0f, 0.0f, kThreads);
+    expect_ulp(host(unwrap(ops::tanh(tx))), ref, 4);
+    orc_unary_f32(ORC_GELU_QUICK, x.data(), ref.data(), n, 0.0f, 0.0f, kThreads);
+    expect_ulp(host(unwrap(ops::gelu_quick(tx))), ref, 8);
+    orc_unary_f32(ORC_CLAMP, x.data(), ref.data(), n, -1.0f, 2.0f, kThreads);
+    expect_bits_equal(host(unwrap(ops::clamp(tx, -1.0f, 2.0f))), ref);
+    EXPECT(expect_err(ops::clamp(tx, 2.0f, -1.0f)).kind == OxideError::Kind::InvalidArgument);
+    // KernelManager::launch_sigmoid on raw buffers
+    KernelManager km;
+    Tensor out = unwrap(Tensor::empty(Shape{n}, DType::F32));
+    EXPECT(km.launch_sigmoid(tx.as<float>(), out.as<float>(), n).is_ok());
+    orc_unary_f32(ORC_SIGMOID, x.data(), ref.data(), n, 0.0f, 0.0f, kThreads);
+    expect_ulp(host(out), ref, 8);
+    // layer_norm: constant rows give the bias; shape errors carry the reference's message
+    const size_t rows = 6, cols = 768;
+    const auto w = uniform(cols, 24, 0.5f, 1.5f), b = uniform(cols, 25, -0.5f, 0.5f);
+    const Tensor tw = dev(w, {cols}), tb = dev(b, {cols});
+    std::vector<float> c(rows * cols, 2.5f);
+    const auto y = host(unwrap(ops::layer_norm(dev(c, {rows, cols}), tw, tb, 1e-5f)));
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t i = 0; i < cols; ++i) EXPECT(bits(y[r * cols + i]) == bits(b[i]));
+    const OxideError e =
+        expect_err(ops::layer_norm(dev(c, {rows, cols}), tw, dev(uniform(10, 26, 0.0f, 1.0f), {10}), 1e-5f));
+    EXPECT(e.message == "layer_norm bias shape [10] doesn't match input last dim 768");
+    const auto xr = randn(rows * cols, 27, 2.0f);
+    std::vector<float> lref(xr.size());
+    orc_layer_norm_f32(xr.data(), w.data(), b.data(), lref.data(), rows, cols, 1e-5f, kThreads);
+    const auto lgot = host(unwrap(ops::layer_norm(dev(xr, {rows, cols}), tw, tb, 1e-5f)));
+    for (size_t i = 0; i < lref.size(); ++i)
+        EXPECT(std::fabs(lgot[i] - lref[i]) <= 1e-5f * (std::fabs(lref[i] - b[i % cols]) + std::fabs(b[i % cols])) + 1e-6f);
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {

@@ -88,6 +88,23 @@ def build() -> dict:
     g["argmax_f32.x"], g["argmax_f32.out"] = x, orc.argmax_rows(x, 500)
     g["argmax_bf16.x"] = bf(x)
     g["argmax_bf16.out"] = orc.argmax_rows(bf(x), 500)
+    # unary ops (src/ops/activation.rs, src/ops/math.rs) and layer_norm (src/ops/norm.rs:53-117)
+    x = rng.standard_normal(777, dtype=F) * F(3)
+    g["unary.x"] = x
+    g["unary.xpos"] = xpos = np.abs(x) + F(0.01)
+    for name, op, inp, a, b in (("relu", orc.RELU, x, 0, 0), ("gelu", orc.GELU, x, 0, 0),
+                                ("gelu_quick", orc.GELU_QUICK, x, 0, 0), ("sigmoid", orc.SIGMOID, x, 0, 0),
+                                ("tanh", orc.TANH, x, 0, 0), ("exp", orc.EXP, x, 0, 0),
+                                ("log", orc.LOG, xpos, 0, 0), ("sqrt", orc.SQRT, xpos, 0, 0),
+                                ("pow", orc.POW, xpos, 1.7, 0), ("clamp", orc.CLAMP, x, -1.5, 2.5),
+                                ("neg", orc.NEG, x, 0, 0), ("abs", orc.ABS, x, 0, 0)):
+        g[f"unary_{name}.out"] = orc.unary(op, inp, a, b)
+    x = rng.standard_normal((6, 320), dtype=F) * F(2) + F(0.5)
+    w = rng.uniform(0.5, 1.5, 320).astype(F)
+    b = rng.uniform(-0.5, 0.5, 320).astype(F)
+    g["ln.x"], g["ln.w"], g["ln.b"] = x, w, b
+    g["ln_f32.out"] = orc.layer_norm(x, w, b, 1e-5)
+    g["ln_bf16.out"] = orc.layer_norm(bf(x), bf(w), bf(b), 1e-5)
     # reductions
     x = rng.standard_normal((9, 333), dtype=F)
     g["red.x"] = x

@@ -9,7 +9,7 @@ import os
 import numpy as np
 import pytest
 
-from _util import assert_bits_equal, assert_close_rel, assert_ulp, to_dev, to_np
+from _util import assert_bits_equal, assert_close_rel, assert_ulp, to_dev, to_np, ulp_f32
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "oracle_vectors.npz")
 
@@ -68,6 +68,26 @@ def test_kernels_match_golden_vectors(cuda, golden):
                       g["rope_head_f32.out"])
     assert np.array_equal(to_np(ops.argmax(d("argmax_f32.x"))).astype(np.uint32), g["argmax_f32.out"])
     assert np.array_equal(to_np(ops.argmax(d("argmax_bf16.x"))).astype(np.uint32), g["argmax_bf16.out"])
+    ulp_bar = {"relu": 0, "neg": 0, "abs": 0, "clamp": 0, "sqrt": 0, "exp": 4, "log": 4, "tanh": 4,
+               "pow": 8, "sigmoid": 8, "gelu_quick": 8, "gelu": 8}
+    codes = {"relu": 0, "gelu": 1, "gelu_quick": 2, "sigmoid": 3, "tanh": 4, "exp": 5, "log": 6,
+             "sqrt": 7, "pow": 8, "clamp": 9, "neg": 10, "abs": 11}
+    for name, bar in ulp_bar.items():
+        inp = d("unary.xpos") if name in ("log", "sqrt", "pow") else d("unary.x")
+        a, b = {"pow": (1.7, 0.0), "clamp": (-1.5, 2.5)}.get(name, (0.0, 0.0))
+        got = to_np(ops.unary(codes[name], inp, a, b))
+        ref = g[f"unary_{name}.out"]
+        if bar == 0:
+            assert_bits_equal(got, ref)
+        elif name == "gelu":  # 1 + tanh(v) cancels for x << 0: absolute slack 2^-22 |x|
+            xs = g["unary.x"].astype(np.float64)
+            ok = (ulp_f32(got, ref) <= bar) | (np.abs(got.astype(np.float64) - ref) <= 2.0 ** -22 * np.abs(xs))
+            assert ok.all()
+        else:
+            assert_ulp(got, ref, bar)
+    y = to_np(ops.layer_norm(d("ln.x"), d("ln.w"), d("ln.b"), 1e-5))
+    sc = np.abs(g["ln_f32.out"] - g["ln.b"]) + np.abs(g["ln.b"])
+    assert np.all(np.abs(y - g["ln_f32.out"]) <= 1e-5 * sc + 1e-6)
     x = d("red.x")
     for op, name in ((0, "sum"), (1, "max"), (2, "sumsq")):
         rows = to_np(ops.reduce_rows(x, op))

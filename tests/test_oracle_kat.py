@@ -150,3 +150,49 @@ def test_bf16_rounding_round_to_nearest_even(orc):
     assert back.tolist() == [1.0, 1.0, 1.0 + 2**-6, 1.0, -2.5, 65536.0]
     # the C library's scalar rounding agrees with the numpy one
     assert [orc.lib().orc_f32_to_bf16(float(v)) for v in vals] == bits.tolist()
+
+
+def test_unary_known_values(orc):
+    o = orc
+    x = np.array([-2.0, -0.5, 0.0, 0.5, 2.0, np.nan], dtype=F)
+    relu = o.unary(o.RELU, x)
+    assert np.array_equal(relu[:5], np.array([0, 0, 0, 0.5, 2.0], F)) and relu[5] == 0.0  # f32::max(NaN, 0) = 0
+    assert o.unary(o.SIGMOID, np.array([0.0], F))[0] == F(0.5)  # 1 / (1 + exp(0)) = 1/2 exactly
+    assert o.unary(o.GELU, np.array([0.0], F))[0] == 0.0
+    assert o.unary(o.GELU_QUICK, np.array([0.0], F))[0] == 0.0
+    assert o.unary(o.TANH, np.array([0.0], F))[0] == 0.0
+    assert o.unary(o.EXP, np.array([0.0], F))[0] == 1.0
+    assert o.unary(o.LOG, np.array([1.0], F))[0] == 0.0
+    assert np.isneginf(o.unary(o.LOG, np.array([0.0], F))[0])
+    assert np.array_equal(o.unary(o.SQRT, np.array([4.0, 2.25], F)), np.array([2.0, 1.5], F))
+    assert np.array_equal(o.unary(o.POW, np.array([2.0, 3.0], F), 3.0), np.array([8.0, 27.0], F))
+    c = o.unary(o.CLAMP, x, -1.0, 1.0)
+    assert np.array_equal(c[:5], np.array([-1, -0.5, 0, 0.5, 1], F)) and np.isnan(c[5])  # NaN stays
+    assert np.array_equal(o.unary(o.NEG, x[:5]), -x[:5])
+    assert np.array_equal(o.unary(o.ABS, x[:5]), np.abs(x[:5]))
+    # large |x|: sigmoid saturates, gelu(x) -> x for x >> 0 and -> -0 / 0 for x << 0
+    big = np.array([30.0, -30.0], F)
+    assert np.array_equal(o.unary(o.SIGMOID, big), np.array([1.0, F(np.exp(np.float64(-30.0)))], F)) or \
+        o.unary(o.SIGMOID, big)[0] == 1.0
+    assert o.unary(o.GELU, np.array([10.0], F))[0] == F(10.0)
+
+
+def test_layer_norm_constant_row_gives_bias(orc):
+    # src/ops/norm.rs:92-113: a constant row has mean = c exactly (c * n / n), every
+    # deviation 0, so normalized = 0 and out = 0 * w + b = b.
+    cols = 768
+    x = np.full((4, cols), 1.75, F)
+    w = np.linspace(0.5, 1.5, cols, dtype=F)
+    b = np.linspace(-1.0, 1.0, cols, dtype=F)
+    assert np.array_equal(orc.layer_norm(x, w, b, 1e-5), np.broadcast_to(b, x.shape))
+
+
+def test_layer_norm_two_values_by_hand(orc):
+    # row [a, -a, a, -a]: mean 0, var a^2, std sqrt(a^2 + eps); out = +-a / std * w + b
+    a, eps = F(2.0), F(1e-5)
+    x = np.array([[a, -a, a, -a]], F)
+    w = np.array([1.0, 2.0, 0.5, 1.0], F)
+    b = np.array([0.0, 0.25, -0.5, 1.0], F)
+    sd = np.sqrt(F(F(a * a) + eps))
+    expect = (np.array([a, -a, a, -a], F) / sd) * w + b
+    assert np.array_equal(orc.layer_norm(x, w, b, eps)[0], expect.astype(F))

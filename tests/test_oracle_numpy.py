@@ -172,3 +172,56 @@ def test_row_reductions_bit_exact(orc):
                 acc = max(acc, v) if op == orc.RED_MAX else F(acc + (v if op == orc.RED_SUM else F(v * v)))
             ref.append(acc)
         assert np.array_equal(orc.reduce_rows(op, x, 333), np.array(ref, F))
+
+
+def test_unary_ops_match_numpy(orc):
+    rng = np.random.default_rng(77)
+    x = (rng.standard_normal(20000) * 3).astype(F)
+    pos = np.abs(x) + F(1e-3)
+    o = orc
+    exact_ops = [(o.RELU, x, np.maximum(x, F(0))), (o.NEG, x, -x), (o.ABS, x, np.abs(x)),
+                 (o.SQRT, pos, np.sqrt(pos)), (o.CLAMP, x, np.clip(x, F(-1.5), F(2.5)))]
+    for op, inp, want in exact_ops:
+        got = o.unary(op, inp, -1.5, 2.5)
+        assert np.array_equal(got, want.astype(F)), op
+    # transcendental ops: numpy's f32 exp/log/tanh/pow (its own SIMD routines)
+    # differ from glibc's by up to a few ulp
+    def close(got, want, n):
+        d = np.abs(got.view(np.int32).astype(np.int64) - want.astype(F).view(np.int32).astype(np.int64))
+        assert d.max() <= n, d.max()
+    close(o.unary(o.EXP, x), np.exp(x), 4)
+    close(o.unary(o.LOG, pos), np.log(pos), 4)
+    close(o.unary(o.TANH, x), np.tanh(x), 4)
+    close(o.unary(o.POW, pos, 1.7), np.power(pos, F(1.7)), 4)
+    # sigmoid / gelu_quick: the reference expression evaluated step by step in f32
+    e = np.exp(-x).astype(F)
+    close(o.unary(o.SIGMOID, x), (F(1) / (F(1) + e)).astype(F), 4)
+    n = (F(-1.702) * x).astype(F)
+    close(o.unary(o.GELU_QUICK, x), (x * (F(1) / (F(1) + np.exp(n).astype(F))).astype(F)).astype(F), 4)
+    # gelu against float64 (1 + tanh cancels for x << 0: compare absolutely there)
+    x64 = x.astype(np.float64)
+    g64 = 0.5 * x64 * (1 + np.tanh(np.sqrt(2 / np.pi) * (x64 + 0.044715 * x64 ** 3)))
+    got = o.unary(o.GELU, x).astype(np.float64)
+    assert np.all(np.abs(got - g64) <= 1e-6 * np.abs(g64) + 2e-7 * np.abs(x64))
+
+
+def test_layer_norm_matches_numpy(orc):
+    rng = np.random.default_rng(78)
+    rows, cols = 37, 1000
+    x = (rng.standard_normal((rows, cols)) * 2 + 0.5).astype(F)
+    w = rng.uniform(0.5, 1.5, cols).astype(F)
+    b = rng.uniform(-0.5, 0.5, cols).astype(F)
+    # the reference's loops, vectorised per row with the same sequential f32 sums
+    want = np.empty_like(x)
+    for r in range(rows):
+        s = F(0)
+        for v in x[r]:
+            s = F(s + v)
+        mean = F(s / F(cols))
+        ss = F(0)
+        for v in x[r]:
+            d = F(v - mean)
+            ss = F(ss + F(d * d))
+        sd = np.sqrt(F(F(ss / F(cols)) + F(1e-5)))
+        want[r] = (((x[r] - mean).astype(F) / sd).astype(F) * w).astype(F) + b
+    assert np.array_equal(orc.layer_norm(x, w, b, 1e-5), want)
