@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <algorithm>
 #include <cstring>
 #include <memory>
 #include <optional>
@@ -454,6 +455,23 @@ inline Result<Tensor> layer_norm(const Tensor& x, const Tensor& w, const Tensor&
     return out;
 }
 
+// repeat_kv (src/ops/attention.rs:161-201): [b, kv_heads, s, d] -> [b, kv_heads * n_rep, s, d].
+inline Result<Tensor> repeat_kv(const Tensor& x, size_t n_rep) {
+    if (x.rank() < 4)
+        return OxideError::invalid("repeat_kv requires 4D tensor (batch, heads, seq_len, head_dim)");
+    std::vector<size_t> d = x.dims();
+    const size_t b = d[0], h = d[1], s = d[2], hd = (b && h && s) ? x.elem_count() / (b * h * s) : 0;
+    d[1] *= n_rep;
+    auto out = Tensor::empty(Shape(d), x.dtype(), x.device());
+    if (out.is_err()) return out;
+    const int rc = detail::bf16(x)
+        ? oxide_repeat_kv_bf16(x.as<oxide_bf16>(), out.value().as<oxide_bf16>(), b, h, s, hd, n_rep,
+                               current_stream())
+        : oxide_repeat_kv_f32(x.as<float>(), out.value().as<float>(), b, h, s, hd, n_rep, current_stream());
+    OXIDE_TRY(check_status(rc));
+    return out;
+}
+
 // (h, y): h = x + r, y = rms_norm(h) (src/layers/transformer.rs:64-67).
 inline Result<std::pair<Tensor, Tensor>> add_rms_norm(const Tensor& x, const Tensor& r,
                                                       const Tensor& w, float eps) {
@@ -656,6 +674,74 @@ inline Result<std::pair<Tensor, Tensor>> precompute_rope_cache(float theta, size
     if (st.is_err()) return st.error();
     return std::make_pair(std::move(ct).value(), std::move(st).value());
 }
+
+// KVCache (src/cache/kv_cache.rs): per-layer device caches [batch, kv_heads,
+// max_seq_len, head_dim]; update() appends with one kernel at the layer's own
+// length (the reference's single counter, advanced by every layer's update,
+// would place layer 1's tokens after layer 0's).
+class KvCache {
+  public:
+    static Result<KvCache> create(size_t num_layers, size_t batch, size_t kv_heads, size_t head_dim,
+                                  size_t max_seq_len, DType dtype = DType::F32, int device = 0) {
+        KvCache c;
+        c.batch_ = batch;
+        c.heads_ = kv_heads;
+        c.head_dim_ = head_dim;
+        c.max_ = max_seq_len;
+        c.len_.assign(num_layers, 0);
+        for (size_t l = 0; l < num_layers; ++l) {
+            auto k = Tensor::zeros(Shape{batch, kv_heads, max_seq_len, head_dim}, dtype, device);
+            if (k.is_err()) return k.error();
+            auto v = Tensor::zeros(Shape{batch, kv_heads, max_seq_len, head_dim}, dtype, device);
+            if (v.is_err()) return v.error();
+            c.k_.push_back(std::move(k).value());
+            c.v_.push_back(std::move(v).value());
+        }
+        return c;
+    }
+    Status update(size_t layer, const Tensor& key, const Tensor& value) {
+        if (layer >= k_.size())
+            return OxideError::invalid("Layer index " + std::to_string(layer) + " out of range for " +
+                                       std::to_string(k_.size()) + " layers");
+        const Tensor& kc = k_[layer];
+        if (key.shape() != value.shape() || key.rank() != 4 || key.dims()[0] != batch_ ||
+            key.dims()[1] != heads_ || key.dims()[3] != head_dim_ || key.dtype() != kc.dtype() ||
+            value.dtype() != kc.dtype())
+            return OxideError::invalid("key/value " + key.shape().to_string() + " do not match the cache " +
+                                       kc.shape().to_string());
+        const size_t cur = len_[layer], add = key.dims()[2];
+        if (cur + add > max_)
+            return OxideError::invalid("KV cache overflow: " + std::to_string(cur + add) + " > " +
+                                       std::to_string(max_));
+        const int rc = detail_bf16(kc)
+            ? oxide_kv_cache_append_bf16(kc.as<oxide_bf16>(), v_[layer].as<oxide_bf16>(), key.as<oxide_bf16>(),
+                                         value.as<oxide_bf16>(), batch_, heads_, max_, head_dim_, cur, add,
+                                         current_stream())
+            : oxide_kv_cache_append_f32(kc.as<float>(), v_[layer].as<float>(), key.as<float>(), value.as<float>(),
+                                        batch_, heads_, max_, head_dim_, cur, add, current_stream());
+        OXIDE_TRY(check_status(rc));
+        len_[layer] = cur + add;
+        return Unit{};
+    }
+    const Tensor& k_cache(size_t layer) const { return k_[layer]; }
+    const Tensor& v_cache(size_t layer) const { return v_[layer]; }
+    size_t seq_len(size_t layer) const { return len_[layer]; }
+    size_t current_seq_len() const { return len_.empty() ? 0 : len_[0]; }
+    size_t max_seq_len() const { return max_; }
+    size_t num_layers() const { return k_.size(); }
+    void clear() { std::fill(len_.begin(), len_.end(), 0); }
+    bool is_full() const { return current_seq_len() >= max_; }
+    size_t get_cache_size() const {
+        return k_.empty() ? 0 : 2 * k_[0].nbytes() * k_.size();
+    }
+
+  private:
+    static bool detail_bf16(const Tensor& t) { return t.dtype() == DType::BF16; }
+    KvCache() = default;
+    std::vector<Tensor> k_, v_;
+    std::vector<size_t> len_;
+    size_t batch_ = 0, heads_ = 0, head_dim_ = 0, max_ = 0;
+};
 
 // ---- launcher-level interface (src/cuda_backend) ------------------------------------------------
 // KernelManager (src/cuda_backend/kernels.rs:75-376): launchers over caller-owned

@@ -245,6 +245,50 @@ int oxide_rope_bf16(const oxide_bf16* q, oxide_bf16* q_out, uint64_t q_heads,
 int oxide_rope_table_host_f32(float theta, uint64_t head_dim, uint64_t max_pos,
                               float* cos_host, float* sin_host);
 
+/* ---- KV cache and grouped-query heads -------------------------------------------
+ * repeat_kv (src/ops/attention.rs:161-201): x [batch, kv_heads, seq_len,
+ * head_dim] -> out [batch, kv_heads * n_rep, seq_len, head_dim],
+ * out[b, h * n_rep + r] = x[b, h] (bit-exact copy; out must not alias x). */
+int oxide_repeat_kv_f32(const float* x, float* out, uint64_t batch, uint64_t kv_heads, uint64_t seq_len,
+                        uint64_t head_dim, uint64_t n_rep, oxide_stream_t stream);
+int oxide_repeat_kv_bf16(const oxide_bf16* x, oxide_bf16* out, uint64_t batch, uint64_t kv_heads,
+                         uint64_t seq_len, uint64_t head_dim, uint64_t n_rep, oxide_stream_t stream);
+
+/* KVCache::update (src/cache/kv_cache.rs:55-85; kernel intent kv_cache_update_f32,
+ * src/kernels/attention.rs:121-158): k, v [batch, kv_heads, new_len, head_dim]
+ * are copied to positions [cur_len, cur_len + new_len) of the caches
+ * [batch, kv_heads, max_seq, head_dim], both in one launch.  cur_len + new_len
+ * > max_seq is OXIDE_ERR_INVALID_ARG ("KV cache overflow"), nothing written. */
+int oxide_kv_cache_append_f32(float* k_cache, float* v_cache, const float* k, const float* v, uint64_t batch,
+                              uint64_t kv_heads, uint64_t max_seq, uint64_t head_dim, uint64_t cur_len,
+                              uint64_t new_len, oxide_stream_t stream);
+int oxide_kv_cache_append_bf16(oxide_bf16* k_cache, oxide_bf16* v_cache, const oxide_bf16* k,
+                               const oxide_bf16* v, uint64_t batch, uint64_t kv_heads, uint64_t max_seq,
+                               uint64_t head_dim, uint64_t cur_len, uint64_t new_len, oxide_stream_t stream);
+
+/* ---- decode attention ---------------------------------------------------------
+ * One query token per (batch, head) against KV caches [batch, kv_heads,
+ * max_seq, head_dim]: the inline attention of scaled_dot_product_attention
+ * (src/ops/attention.rs:41-87) with q_len = 1 -- s_j = (q . k_j) * scale,
+ * softmax over j < lens[b] (lens NULL: every position), out = sum_j p_j v_j --
+ * where query head h reads kv head h / (q_heads / kv_heads) (repeat_kv's head
+ * map, attention.rs:161-201, without materialising it).  q, out [batch,
+ * q_heads, head_dim].  A sequence of length 0 gives zeros.  Pass the
+ * reference's scale, (head_dim as f32).sqrt().recip().  `workspace` is device
+ * memory of at least oxide_decode_attention_workspace_bytes(...) bytes,
+ * 16-byte aligned, for the split-K partials.  API addition (flash-decoding);
+ * the reference computes it through repeat_kv + matmul + softmax + matmul. */
+uint64_t oxide_decode_attention_workspace_bytes(uint64_t batch, uint64_t q_heads, uint64_t max_seq,
+                                                uint64_t head_dim);
+int oxide_decode_attention_f32(const float* q, const float* k_cache, const float* v_cache, const int32_t* lens,
+                               float* out, uint64_t batch, uint64_t q_heads, uint64_t kv_heads, uint64_t max_seq,
+                               uint64_t head_dim, float scale, void* workspace, uint64_t workspace_bytes,
+                               oxide_stream_t stream);
+int oxide_decode_attention_bf16(const oxide_bf16* q, const oxide_bf16* k_cache, const oxide_bf16* v_cache,
+                                const int32_t* lens, oxide_bf16* out, uint64_t batch, uint64_t q_heads,
+                                uint64_t kv_heads, uint64_t max_seq, uint64_t head_dim, float scale,
+                                void* workspace, uint64_t workspace_bytes, oxide_stream_t stream);
+
 /* ---- argmax ----------------------------------------------------------------
  * Index of the largest element of each row of x[rows, cols] (cols < 2^32):
  * the lowest index among equal maxima (+0 == -0), NaN ranks below every

@@ -58,6 +58,13 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_tanh_f32": (i32, [vp, vp, u64, vp]),
     "oxide_layer_norm_f32": (i32, [vp, vp, vp, vp, u64, u64, f32, vp]),
     "oxide_layer_norm_bf16": (i32, [vp, vp, vp, vp, u64, u64, f32, vp]),
+    "oxide_repeat_kv_f32": (i32, [vp, vp, u64, u64, u64, u64, u64, vp]),
+    "oxide_repeat_kv_bf16": (i32, [vp, vp, u64, u64, u64, u64, u64, vp]),
+    "oxide_kv_cache_append_f32": (i32, [vp, vp, vp, vp, u64, u64, u64, u64, u64, u64, vp]),
+    "oxide_kv_cache_append_bf16": (i32, [vp, vp, vp, vp, u64, u64, u64, u64, u64, u64, vp]),
+    "oxide_decode_attention_workspace_bytes": (u64, [u64, u64, u64, u64]),
+    "oxide_decode_attention_f32": (i32, [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, vp, u64, vp]),
+    "oxide_decode_attention_bf16": (i32, [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, vp, u64, vp]),
     "oxide_reduce_rows_f32": (i32, [i32, vp, u64, u64, vp, vp]),
     "oxide_reduce_rows_bf16": (i32, [i32, vp, u64, u64, vp, vp]),
     "oxide_reduce_workspace_bytes": (u64, [u64]),

@@ -25,7 +25,7 @@ if __package__ in (None, ""):
 from oxide_b200 import ops  # noqa: E402
 from oxide_b200 import _lib  # noqa: E402
 from oxide_b200._lib import call  # noqa: E402
-from oxide_b200.workloads import C1, C2, C3, C4, C5  # noqa: E402
+from oxide_b200.workloads import C1, C2, C3, C4, C5, NKV  # noqa: E402
 
 BF16 = torch.bfloat16
 
@@ -76,6 +76,23 @@ def build(op: str, rows: int | None, dev):
                                                out=s[1])
         nb = int(sum(min(int(lens[r // c.heads]), c.keys) for r in range(R))) * 4 + R * c.keys * 4
         return mk, run, nb, [R, c.keys]
+    if op in ("decode_attn_bf16_c3", "decode_attn_f32_c3"):
+        # one decode step of attention at the C3 batch: q [8, 32, 128], KV caches
+        # [8, 8, 32768, 128] with the C3 per-sequence lengths
+        c = C3()
+        _, lens, _ = c.inputs()
+        kvh = NKV
+        dt = BF16 if op == "decode_attn_bf16_c3" else torch.float32
+        es = 2 if dt == BF16 else 4
+        tl = torch.from_numpy(lens).to(dev)
+        ws = torch.empty(int(_lib.lib().oxide_decode_attention_workspace_bytes(c.batch, c.heads, c.keys, c.head_dim)),
+                         dtype=torch.uint8, device=dev)
+        mk = lambda: (rn(c.batch, c.heads, c.head_dim, dtype=dt), rn(c.batch, kvh, c.keys, c.head_dim, dtype=dt),  # noqa: E731
+                      rn(c.batch, kvh, c.keys, c.head_dim, dtype=dt),
+                      torch.empty(c.batch, c.heads, c.head_dim, dtype=dt, device=dev))
+        run = lambda s: ops.decode_attention(s[0], s[1], s[2], tl, workspace=ws, out=s[3])  # noqa: E731
+        nb = int(np.sum(np.minimum(lens, c.keys))) * kvh * c.head_dim * es * 2 + 2 * c.batch * c.heads * c.head_dim * es
+        return mk, run, nb, [c.batch, c.heads, kvh, c.keys, c.head_dim]
     if op == "argmax_f32_c3":
         c = C3()
         R = rows or c.logit_rows
@@ -120,6 +137,27 @@ def build(op: str, rows: int | None, dev):
         mk = lambda: (rn(R, c.hidden, dtype=BF16), torch.empty(R, c.hidden, dtype=BF16, device=dev))  # noqa: E731
         run = lambda s: ops.layer_norm(s[0], w, bias, c.eps, out=s[1])  # noqa: E731
         return mk, run, 2 * R * c.hidden * 2 + 2 * c.hidden * 2, [R, c.hidden]
+    if op == "repeat_kv_bf16_c5":
+        # GQA head repetition of the C5 key cache: [64, 8, 2048, 128] -> [64, 32, 2048, 128]
+        R = rows or c.seqs
+        rep = c.q_heads // c.k_heads
+        mk = lambda: (rn(R, c.k_heads, c.seq_len, c.head_dim, dtype=BF16),  # noqa: E731
+                      torch.empty(R, c.q_heads, c.seq_len, c.head_dim, dtype=BF16, device=dev))
+        run = lambda s: ops.repeat_kv(s[0], rep, out=s[1])  # noqa: E731
+        nb = R * c.k_heads * c.seq_len * c.head_dim * 2 * (1 + rep)
+        return mk, run, nb, [R, c.k_heads, c.seq_len, c.head_dim]
+    if op == "kv_append_bf16_c5":
+        # prefill append of the C5 keys and values into caches of 4096 positions
+        R = rows or c.seqs
+        M = 2 * c.seq_len
+        kc = torch.zeros(R, c.k_heads, M, c.head_dim, dtype=BF16, device=dev)
+        vc = torch.zeros_like(kc)
+        mk = lambda: (rn(R, c.k_heads, c.seq_len, c.head_dim, dtype=BF16),  # noqa: E731
+                      rn(R, c.k_heads, c.seq_len, c.head_dim, dtype=BF16))
+        run = lambda s: call("oxide_kv_cache_append_bf16", kc.data_ptr(), vc.data_ptr(), s[0].data_ptr(),  # noqa: E731
+                             s[1].data_ptr(), R, c.k_heads, M, c.head_dim, 0, c.seq_len, _stream())
+        nb = 4 * R * c.k_heads * c.seq_len * c.head_dim * 2
+        return mk, run, nb, [R, c.k_heads, c.seq_len, c.head_dim]
     if op in ("rms_norm_bf16_c5", "add_rms_norm_bf16_c5", "sumsq_bf16_c5"):
         R = rows or c.rows
         w = torch.ones(c.hidden, dtype=BF16, device=dev)
@@ -167,7 +205,8 @@ def build(op: str, rows: int | None, dev):
 OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softmax_f32_c3",
        "argmax_f32_c3", "rope_bf16_c4", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
        "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5",
-       "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5"]
+       "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5",
+       "repeat_kv_bf16_c5", "kv_append_bf16_c5", "decode_attn_bf16_c3", "decode_attn_f32_c3"]
 
 
 def main(argv=None):

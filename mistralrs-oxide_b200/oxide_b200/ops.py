@@ -362,3 +362,113 @@ def reduce_max(x):
 
 def reduce_sumsq(x):
     return reduce(x, RED_SUMSQ)
+
+
+def repeat_kv(x: torch.Tensor, n_rep: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """src/ops/attention.rs:161-201: x [batch, kv_heads, seq, head_dim] ->
+    [batch, kv_heads * n_rep, seq, head_dim] (head h * n_rep + r = head h)."""
+    _check(x, out)
+    if x.dim() < 4:
+        raise OxideError(_lib.ERR_INVALID_ARG, "repeat_kv",
+                         "repeat_kv requires 4D tensor (batch, heads, seq_len, head_dim)")
+    b, h, s, d = x.shape[0], x.shape[1], x.shape[2], x.numel() // (x.shape[0] * x.shape[1] * x.shape[2])
+    shape = list(x.shape)
+    shape[1] *= n_rep
+    out = torch.empty(shape, dtype=x.dtype, device=x.device) if out is None else out
+    call(f"oxide_repeat_kv_{_sfx(x)}", _p(x), _p(out), b, h, s, d, int(n_rep), _stream())
+    return out
+
+
+class KvCache:
+    """Per-layer key/value caches [batch, kv_heads, max_seq_len, head_dim] on
+    the device, mirroring src/cache/kv_cache.rs (KVCache::new / update / get /
+    clear / is_full / get_cache_size).  update() appends with one kernel
+    (oxide_kv_cache_append_*) at the layer's own length: the reference keeps a
+    single counter advanced by every layer's update, which would place layer
+    1's tokens after layer 0's; here each layer tracks its own length and
+    current_seq_len() is layer 0's."""
+
+    def __init__(self, num_layers: int, batch_size: int, num_kv_heads: int, head_dim: int,
+                 max_seq_len: int, dtype=torch.float32, device="cuda"):
+        if dtype not in _SFX:
+            raise OxideError(_lib.ERR_UNSUPPORTED, "KvCache", f"dtype {dtype} is not float32/bfloat16")
+        shape = (batch_size, num_kv_heads, max_seq_len, head_dim)
+        self.k_cache = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)]
+        self.v_cache = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)]
+        self._len = [0] * num_layers
+        self.max_seq_len, self.num_layers = max_seq_len, num_layers
+        self.num_kv_heads, self.head_dim, self.batch_size = num_kv_heads, head_dim, batch_size
+
+    def _layer(self, layer_idx: int) -> None:
+        if not 0 <= layer_idx < self.num_layers:
+            raise OxideError(_lib.ERR_INVALID_ARG, "KvCache",
+                             f"Layer index {layer_idx} out of range for {self.num_layers} layers")
+
+    def update(self, layer_idx: int, key: torch.Tensor, value: torch.Tensor) -> None:
+        """kv_cache.rs:55-85: append key/value [batch, kv_heads, new_len, head_dim]."""
+        self._layer(layer_idx)
+        _check(key, value)
+        kc, vc = self.k_cache[layer_idx], self.v_cache[layer_idx]
+        if key.shape != value.shape or key.shape[:2] != kc.shape[:2] or key.shape[3] != kc.shape[3] \
+                or key.dtype != kc.dtype or value.dtype != kc.dtype:
+            raise OxideError(_lib.ERR_INVALID_ARG, "KvCache",
+                             f"key/value {list(key.shape)} do not match the cache {list(kc.shape)}")
+        cur, new = self._len[layer_idx], key.shape[2]
+        if cur + new > self.max_seq_len:
+            raise OxideError(_lib.ERR_INVALID_ARG, "KvCache",
+                             f"KV cache overflow: {cur + new} > {self.max_seq_len}")
+        call(f"oxide_kv_cache_append_{_sfx(kc)}", _p(kc), _p(vc), _p(key), _p(value), self.batch_size,
+             self.num_kv_heads, self.max_seq_len, self.head_dim, cur, new, _stream())
+        self._len[layer_idx] = cur + new
+
+    def get(self, layer_idx: int, seq_len: Optional[int] = None):
+        """kv_cache.rs:87-110: views [batch, kv_heads, seq_len, head_dim] of the
+        first seq_len positions (default: the layer's length), None if 0."""
+        self._layer(layer_idx)
+        n = self._len[layer_idx] if seq_len is None else seq_len
+        if n == 0:
+            return None
+        return self.k_cache[layer_idx][:, :, :n], self.v_cache[layer_idx][:, :, :n]
+
+    def current_seq_len(self) -> int:
+        return self._len[0]
+
+    def clear(self) -> None:
+        self._len = [0] * self.num_layers
+
+    def is_full(self) -> bool:
+        return self._len[0] >= self.max_seq_len
+
+    def get_cache_size(self) -> int:
+        """Bytes held by all layers' k and v caches (kv_cache.rs:128-133)."""
+        es = self.k_cache[0].element_size() if self.k_cache else 4
+        return 2 * self.batch_size * self.num_kv_heads * self.max_seq_len * self.head_dim * es * self.num_layers
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     lens: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                     workspace: Optional[torch.Tensor] = None,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One query token per (batch, head) against KV caches: the attention of
+    src/ops/attention.rs:41-87 with q_len = 1, keys j < lens[b] (int32; None:
+    every position), query head h reading kv head h // (q_heads // kv_heads).
+    q [batch, q_heads, head_dim]; caches [batch, kv_heads, max_seq, head_dim].
+    scale defaults to the reference's (head_dim as f32).sqrt().recip()."""
+    _check(q, k_cache, v_cache, lens, workspace, out)
+    if q.dim() != 3 or k_cache.dim() != 4 or k_cache.shape != v_cache.shape or \
+            k_cache.shape[0] != q.shape[0] or k_cache.shape[3] != q.shape[2]:
+        raise OxideError(_lib.ERR_INVALID_ARG, "decode_attention",
+                         f"q {list(q.shape)} and caches {list(k_cache.shape)} do not match")
+    if lens is not None and lens.dtype != torch.int32:
+        raise OxideError(_lib.ERR_INVALID_ARG, "decode_attention", "lens must be int32")
+    b, hq, d = q.shape
+    hkv, m = k_cache.shape[1], k_cache.shape[2]
+    if scale is None:
+        scale = float(torch.tensor(float(d), dtype=torch.float32).sqrt().reciprocal())
+    need = int(_lib.lib().oxide_decode_attention_workspace_bytes(b, hq, m, d))
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    out = torch.empty_like(q) if out is None else out
+    call(f"oxide_decode_attention_{_sfx(q)}", _p(q), _p(k_cache), _p(v_cache), _p(lens), _p(out), b, hq, hkv,
+         m, d, float(scale), _p(workspace), workspace.numel(), _stream())
+    return out

@@ -65,6 +65,9 @@ def lib() -> C.CDLL:
             "orc_unary_bf16": [i32, vp, vp, u64, f32, f32, i32],
             "orc_layer_norm_f32": [vp, vp, vp, vp, u64, u64, f32, i32],
             "orc_layer_norm_bf16": [vp, vp, vp, vp, u64, u64, f32, i32],
+            "orc_repeat_kv": [vp, vp, u64, u64, u64, u64, u64, u64],
+            "orc_decode_attention_f32": [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, i32],
+            "orc_decode_attention_bf16": [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, i32],
         }
         for name, args in sig.items():
             fn = getattr(h, name)
@@ -77,6 +80,8 @@ def lib() -> C.CDLL:
         h.orc_reduce_seq_f32.argtypes = [i32, vp, u64]
         h.orc_reduce_seq_f32.restype = C.c_float
         h.orc_max_threads.restype = i32
+        h.orc_kv_append.argtypes = [vp, vp, vp, vp, u64, u64, u64, u64, u64, u64, u64]
+        h.orc_kv_append.restype = i32
         h.orc_f32_to_bf16.argtypes = [C.c_float]
         h.orc_f32_to_bf16.restype = C.c_uint16
         _lib = h
@@ -168,6 +173,37 @@ def layer_norm(x, w, b, eps, threads=1):
     out = np.empty_like(x)
     getattr(lib(), f"orc_layer_norm_{_sfx(x)}")(_p(x), _p(w), _p(b), _p(out), x.size // cols, cols,
                                                 float(eps), threads)
+    return out
+
+
+def repeat_kv(x, n_rep):
+    """src/ops/attention.rs:161-201: x [b, h, s, d] -> [b, h * n_rep, s, d]."""
+    x = _c(x)
+    b, h, s, d = x.shape
+    out = np.empty((b, h * n_rep, s, d), dtype=x.dtype)
+    lib().orc_repeat_kv(_p(x), _p(out), b, h, s, d, n_rep, x.itemsize)
+    return out
+
+
+def kv_append(kc, vc, k, v, cur):
+    """src/cache/kv_cache.rs:55-85 (in place); returns False on overflow."""
+    b, h, m, d = kc.shape
+    k, v = _c(k), _c(v)
+    return lib().orc_kv_append(_p(kc), _p(vc), _p(k), _p(v), b, h, m, d, cur, k.shape[2], kc.itemsize) == 0
+
+
+def decode_attention(q, kc, vc, lens=None, scale=None, threads=1):
+    """src/ops/attention.rs:41-87 for one query token: q [b, hq, d], caches
+    [b, hkv, max_seq, d], lens [b] int32 (None: every position)."""
+    q, kc, vc = _c(q), _c(kc), _c(vc)
+    b, hq, d = q.shape
+    hkv, m = kc.shape[1], kc.shape[2]
+    if scale is None:
+        scale = float(np.float32(1.0) / np.sqrt(np.float32(d)))
+    lp = None if lens is None else _c(np.asarray(lens, np.int32))
+    out = np.empty_like(q)
+    getattr(lib(), f"orc_decode_attention_{_sfx(q)}")(_p(q), _p(kc), _p(vc), None if lp is None else _p(lp),
+                                                      _p(out), b, hq, hkv, m, d, float(scale), threads)
     return out
 
 

@@ -574,3 +574,101 @@ void orc_layer_norm_bf16(const uint16_t* x, const uint16_t* w, const uint16_t* b
         __builtin_free(tmp);
     }
 }
+
+/* ---- repeat_kv: src/ops/attention.rs:184-198 (element size `es` bytes) --------- */
+void orc_repeat_kv(const void* x, void* out, uint64_t batch, uint64_t heads, uint64_t seq,
+                   uint64_t head_dim, uint64_t n_rep, uint64_t es) {
+    const uint64_t per = seq * head_dim * es;
+    for (uint64_t b = 0; b < batch; ++b)
+        for (uint64_t h = 0; h < heads; ++h)
+            for (uint64_t r = 0; r < n_rep; ++r) {
+                const uint64_t src = (b * heads + h) * per;
+                const uint64_t dst = (b * (heads * n_rep) + h * n_rep + r) * per;
+                memcpy((char*)out + dst, (const char*)x + src, per);
+            }
+}
+
+/* ---- KV-cache append: positions [cur, cur + new_len) of [batch, heads, max_seq, hd]
+ * (src/cache/kv_cache.rs:55-85).  Returns -1 on overflow ("KV cache overflow"). -- */
+int orc_kv_append(void* kc, void* vc, const void* k, const void* v, uint64_t batch, uint64_t heads,
+                  uint64_t max_seq, uint64_t head_dim, uint64_t cur, uint64_t new_len, uint64_t es) {
+    if (cur > max_seq || new_len > max_seq - cur) return -1;
+    const uint64_t row = head_dim * es;
+    for (uint64_t bh = 0; bh < batch * heads; ++bh) {
+        memcpy((char*)kc + (bh * max_seq + cur) * row, (const char*)k + bh * new_len * row, new_len * row);
+        memcpy((char*)vc + (bh * max_seq + cur) * row, (const char*)v + bh * new_len * row, new_len * row);
+    }
+    return 0;
+}
+
+/* ---- decode attention: the inline attention of scaled_dot_product_attention
+ * (src/ops/attention.rs:41-87) for one query token per (batch, head), with the
+ * keys of batch b limited to j < lens[b] (the decode KV length) and query head
+ * qh reading kv head qh / (q_heads / kv_heads) (repeat_kv, attention.rs:161-201).
+ * dot sequential in f32, * scale, max, exp(s - max) with a sequential sum, divide,
+ * then out[d] = sum_j p_j * v[j][d] sequentially.  A batch with length 0 gives
+ * zeros.  The caches are [batch, kv_heads, max_seq, head_dim]. ---------------- */
+static void decode_attn_one(const float* q, const float* kc, const float* vc, float* out, uint64_t len,
+                            uint64_t d, float scale, float* p) {
+    if (len == 0) {
+        for (uint64_t i = 0; i < d; ++i) out[i] = 0.0f;
+        return;
+    }
+    float mx = -INFINITY;
+    for (uint64_t j = 0; j < len; ++j) {
+        float dot = 0.0f;
+        for (uint64_t i = 0; i < d; ++i) dot += q[i] * kc[j * d + i];
+        p[j] = dot * scale;
+        mx = fmaxf(mx, p[j]);
+    }
+    float sum = 0.0f;
+    for (uint64_t j = 0; j < len; ++j) {
+        p[j] = expf(p[j] - mx);
+        sum += p[j];
+    }
+    for (uint64_t j = 0; j < len; ++j) p[j] /= sum;
+    for (uint64_t i = 0; i < d; ++i) {
+        float acc = 0.0f;
+        for (uint64_t j = 0; j < len; ++j) acc += p[j] * vc[j * d + i];
+        out[i] = acc;
+    }
+}
+
+void orc_decode_attention_f32(const float* q, const float* kc, const float* vc, const int32_t* lens,
+                              float* out, uint64_t batch, uint64_t q_heads, uint64_t kv_heads,
+                              uint64_t max_seq, uint64_t head_dim, float scale, int threads) {
+    const uint64_t rep = q_heads / kv_heads;
+    OMP_FOR for (uint64_t bh = 0; bh < batch * q_heads; ++bh) {
+        const uint64_t b = bh / q_heads, h = bh % q_heads, kvh = h / rep;
+        uint64_t len = max_seq;
+        if (lens) len = lens[b] < 0 ? 0 : ((uint64_t)lens[b] < max_seq ? (uint64_t)lens[b] : max_seq);
+        float* p = (float*)__builtin_malloc((max_seq ? max_seq : 1) * sizeof(float));
+        const uint64_t kv_off = (b * kv_heads + kvh) * max_seq * head_dim;
+        decode_attn_one(q + bh * head_dim, kc + kv_off, vc + kv_off, out + bh * head_dim, len, head_dim,
+                        scale, p);
+        __builtin_free(p);
+    }
+}
+
+void orc_decode_attention_bf16(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                               const int32_t* lens, uint16_t* out, uint64_t batch, uint64_t q_heads,
+                               uint64_t kv_heads, uint64_t max_seq, uint64_t head_dim, float scale,
+                               int threads) {
+    const uint64_t rep = q_heads / kv_heads;
+    OMP_FOR for (uint64_t bh = 0; bh < batch * q_heads; ++bh) {
+        const uint64_t b = bh / q_heads, h = bh % q_heads, kvh = h / rep;
+        uint64_t len = max_seq;
+        if (lens) len = lens[b] < 0 ? 0 : ((uint64_t)lens[b] < max_seq ? (uint64_t)lens[b] : max_seq);
+        const uint64_t n = len * head_dim, kv_off = (b * kv_heads + kvh) * max_seq * head_dim;
+        float* buf = (float*)__builtin_malloc((2 * n + 2 * head_dim + len + 1) * sizeof(float));
+        float *kf = buf, *vf = buf + n, *qf = buf + 2 * n, *of = qf + head_dim, *p = of + head_dim;
+        for (uint64_t i = 0; i < n; ++i) {
+            kf[i] = B2F(kc[kv_off + i]);
+            vf[i] = B2F(vc[kv_off + i]);
+        }
+        for (uint64_t i = 0; i < head_dim; ++i) qf[i] = B2F(q[bh * head_dim + i]);
+        decode_attn_one(qf, kf, vf, of, len, head_dim, scale, p);
+        for (uint64_t i = 0; i < head_dim; ++i) out[bh * head_dim + i] = F2B(of[i]);
+        __builtin_free(buf);
+    }
+}

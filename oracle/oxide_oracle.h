@@ -145,6 +145,23 @@ void orc_layer_norm_f32(const float* x, const float* w, const float* b, float* o
 void orc_layer_norm_bf16(const uint16_t* x, const uint16_t* w, const uint16_t* b, uint16_t* out,
                          uint64_t rows, uint64_t cols, float eps, int threads);
 
+/* src/ops/attention.rs:161-201 repeat_kv and src/cache/kv_cache.rs:55-85 append
+ * (byte copies; es = element size in bytes; append returns -1 on overflow). */
+void orc_repeat_kv(const void* x, void* out, uint64_t batch, uint64_t heads, uint64_t seq,
+                   uint64_t head_dim, uint64_t n_rep, uint64_t es);
+int orc_kv_append(void* kc, void* vc, const void* k, const void* v, uint64_t batch, uint64_t heads,
+                  uint64_t max_seq, uint64_t head_dim, uint64_t cur, uint64_t new_len, uint64_t es);
+
+/* One-token (decode) attention, src/ops/attention.rs:41-87 with per-batch KV
+ * lengths and grouped-query heads (kv head = q head / (q_heads / kv_heads)). */
+void orc_decode_attention_f32(const float* q, const float* kc, const float* vc, const int32_t* lens,
+                              float* out, uint64_t batch, uint64_t q_heads, uint64_t kv_heads,
+                              uint64_t max_seq, uint64_t head_dim, float scale, int threads);
+void orc_decode_attention_bf16(const uint16_t* q, const uint16_t* kc, const uint16_t* vc,
+                               const int32_t* lens, uint16_t* out, uint64_t batch, uint64_t q_heads,
+                               uint64_t kv_heads, uint64_t max_seq, uint64_t head_dim, float scale,
+                               int threads);
+
 int orc_max_threads(void);
 
 #ifdef __cplusplus

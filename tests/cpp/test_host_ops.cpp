@@ -421,6 +421,33 @@ DEVICE_TEST(unary_ops_and_layer_norm_match_oracle) {
         EXPECT(std::fabs(lgot[i] - lref[i]) <= 1e-5f * (std::fabs(lref[i] - b[i % cols]) + std::fabs(b[i % cols])) + 1e-6f);
 }
 
+DEVICE_TEST(repeat_kv_and_kv_cache_match_oracle) {
+    const size_t b = 2, h = 3, s = 5, d = 64, rep = 4;
+    const auto x = randn(b * h * s * d, 28);
+    std::vector<float> ref(x.size() * rep);
+    orc_repeat_kv(x.data(), ref.data(), b, h, s, d, rep, 4);
+    const Tensor out = unwrap(ops::repeat_kv(dev(x, {b, h, s, d}), rep));
+    EXPECT((out.dims() == std::vector<size_t>{b, h * rep, s, d}));
+    expect_bits_equal(host(out), ref);
+    // cache: two appends (prefill of 3 tokens, then 1) equal one append of 4
+    KvCache cache = unwrap(KvCache::create(2, b, h, d, 8));
+    const auto k1 = randn(b * h * 3 * d, 29), v1 = randn(b * h * 3 * d, 30);
+    const auto k2 = randn(b * h * 1 * d, 31), v2 = randn(b * h * 1 * d, 32);
+    EXPECT(cache.update(1, dev(k1, {b, h, 3, d}), dev(v1, {b, h, 3, d})).is_ok());
+    EXPECT(cache.update(1, dev(k2, {b, h, 1, d}), dev(v2, {b, h, 1, d})).is_ok());
+    EXPECT(cache.seq_len(1) == 4 && cache.seq_len(0) == 0);
+    std::vector<float> kref(b * h * 8 * d, 0.0f), vref(kref.size(), 0.0f);
+    EXPECT(orc_kv_append(kref.data(), vref.data(), k1.data(), v1.data(), b, h, 8, d, 0, 3, 4) == 0);
+    EXPECT(orc_kv_append(kref.data(), vref.data(), k2.data(), v2.data(), b, h, 8, d, 3, 1, 4) == 0);
+    expect_bits_equal(host(cache.k_cache(1)), kref);
+    expect_bits_equal(host(cache.v_cache(1)), vref);
+    const auto big = randn(b * h * 5 * d, 33);
+    const Status st = cache.update(1, dev(big, {b, h, 5, d}), dev(big, {b, h, 5, d}));
+    EXPECT(st.is_err() && st.error().message == "KV cache overflow: 9 > 8");
+    EXPECT(cache.update(2, dev(k2, {b, h, 1, d}), dev(v2, {b, h, 1, d})).error().message ==
+           "Layer index 2 out of range for 2 layers");
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {

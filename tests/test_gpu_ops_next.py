@@ -176,3 +176,168 @@ def test_layer_norm_constant_rows_and_shape_errors(cuda, orc):
         ops.layer_norm(x, w, b[:10], 1e-5)
     with pytest.raises(OxideError, match="weight shape"):
         ops.layer_norm(x, w[:10], b, 1e-5)
+
+
+# ---------------------------------------------------------------- KV cache / repeat_kv
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("b,h,s,d,rep", [(2, 8, 37, 128, 4), (1, 1, 1, 8, 1), (3, 2, 5, 6, 3)])
+def test_repeat_kv_bit_exact(cuda, orc, dtype, b, h, s, d, rep):
+    from oxide_b200 import ops
+
+    x = np.random.default_rng(b * 100 + d).standard_normal((b, h, s, d)).astype(F)
+    if dtype == "bf16":
+        x = orc.f32_to_bf16(x)
+    got = to_np(ops.repeat_kv(to_dev(x), rep))
+    assert got.shape == (b, h * rep, s, d)
+    assert np.array_equal(got, orc.repeat_kv(x, rep))
+
+
+@pytest.mark.gpu
+def test_repeat_kv_unaligned_and_errors(cuda, orc):
+    from oxide_b200 import OxideError, ops
+
+    x = np.random.default_rng(9).standard_normal((2, 4, 9, 16)).astype(F)
+    got = to_np(ops.repeat_kv(misaligned_copy(x), 2))  # scalar kernel
+    assert np.array_equal(got, orc.repeat_kv(x, 2))
+    with pytest.raises(OxideError, match="4D"):
+        ops.repeat_kv(to_dev(x[0]), 2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_kv_cache_decode_appends_equal_prefill(cuda, orc, dtype):
+    """A prefill of 7 tokens followed by 5 single-token decode steps leaves the
+    cache equal to the oracle's appends and to one 12-token prefill."""
+    import torch
+
+    from oxide_b200 import OxideError, ops
+
+    B, H, D, M = 2, 8, 128, 16
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    rng = np.random.default_rng(11)
+    ks = rng.standard_normal((B, H, 12, D)).astype(F)
+    vs = rng.standard_normal((B, H, 12, D)).astype(F)
+    if dtype == "bf16":
+        ks, vs = orc.f32_to_bf16(ks), orc.f32_to_bf16(vs)
+    cache = ops.KvCache(2, B, H, D, M, dtype=tdt)
+    cache.update(0, to_dev(np.ascontiguousarray(ks[:, :, :7])), to_dev(np.ascontiguousarray(vs[:, :, :7])))
+    for t in range(7, 12):
+        cache.update(0, to_dev(np.ascontiguousarray(ks[:, :, t:t + 1])),
+                     to_dev(np.ascontiguousarray(vs[:, :, t:t + 1])))
+    assert cache.current_seq_len() == 12 and not cache.is_full()
+    kc = np.zeros((B, H, M, D), ks.dtype)
+    vc = np.zeros_like(kc)
+    assert orc.kv_append(kc, vc, ks, vs, 0)
+    assert np.array_equal(to_np(cache.k_cache[0]), kc) and np.array_equal(to_np(cache.v_cache[0]), vc)
+    k, v = cache.get(0)
+    assert k.shape == (B, H, 12, D) and np.array_equal(to_np(k.contiguous()), ks)
+    assert cache.get(1) is None  # layer 1 untouched
+    with pytest.raises(OxideError, match="KV cache overflow: 17 > 16"):
+        cache.update(0, to_dev(np.ascontiguousarray(ks[:, :, :5])), to_dev(np.ascontiguousarray(vs[:, :, :5])))
+    with pytest.raises(OxideError, match="Layer index 2 out of range"):
+        cache.update(2, to_dev(ks), to_dev(vs))
+    assert cache.get_cache_size() == 2 * B * H * M * D * (4 if dtype == "f32" else 2) * 2
+    cache.clear()
+    assert cache.current_seq_len() == 0
+
+
+@pytest.mark.gpu
+def test_kv_append_abi_overflow_writes_nothing(cuda):
+    import torch
+
+    from oxide_b200 import _lib
+
+    kc = torch.zeros(1, 1, 4, 8, device=cuda)
+    vc = torch.zeros_like(kc)
+    k = torch.ones(1, 1, 3, 8, device=cuda)
+    st = torch.cuda.current_stream().cuda_stream
+    rc = _lib.raw("oxide_kv_cache_append_f32", kc.data_ptr(), vc.data_ptr(), k.data_ptr(), k.data_ptr(),
+                  1, 1, 4, 8, 2, 3, st)
+    assert rc == _lib.ERR_INVALID_ARG and "overflow" in _lib.last_error()
+    torch.cuda.synchronize()
+    assert not kc.any() and not vc.any()
+
+
+# ---------------------------------------------------------------- decode attention
+def _attn_exact(q, kc, vc, lens, scale):
+    q, kc, vc = (np.asarray(a, np.float64) for a in (q, kc, vc))
+    b, hq, d = q.shape
+    hkv = kc.shape[1]
+    rep = hq // hkv
+    out = np.zeros((b, hq, d))
+    mag = np.zeros((b, hq, d))
+    for bi in range(b):
+        n = kc.shape[2] if lens is None else max(0, min(int(lens[bi]), kc.shape[2]))
+        for h in range(hq):
+            if n == 0:
+                continue
+            k, v = kc[bi, h // rep, :n], vc[bi, h // rep, :n]
+            s = (k @ q[bi, h]) * np.float64(scale)
+            p = np.exp(s - s.max())
+            p /= p.sum()
+            out[bi, h] = p @ v
+            mag[bi, h] = p @ np.abs(v)
+    return out, mag
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("b,hq,hkv,m,d,lens", [
+    (2, 8, 2, 300, 128, [300, 77]),      # rep 4 (Mistral), a partial tile
+    (3, 4, 4, 1000, 128, [1000, 1, 0]),   # rep 1, a single key, an empty sequence
+    (1, 16, 2, 4500, 128, [4321]),        # rep 8, many splits
+    (2, 6, 3, 129, 128, None),            # rep 2, no lengths
+    (2, 4, 2, 50, 64, [50, 33]),          # head_dim 64: the generic kernel
+])
+def test_decode_attention_matches_oracle(cuda, orc, dtype, b, hq, hkv, m, d, lens):
+    from oxide_b200 import ops
+
+    rng = np.random.default_rng(b * 1000 + m)
+    q = rng.standard_normal((b, hq, d)).astype(F)
+    kc = rng.standard_normal((b, hkv, m, d)).astype(F)
+    vc = rng.standard_normal((b, hkv, m, d)).astype(F)
+    if dtype == "bf16":
+        q, kc, vc = orc.f32_to_bf16(q), orc.f32_to_bf16(kc), orc.f32_to_bf16(vc)
+    lz = None if lens is None else np.array(lens, np.int32)
+    got = to_np(ops.decode_attention(to_dev(q), to_dev(kc), to_dev(vc),
+                                     None if lz is None else to_dev(lz)))
+    ref = orc.decode_attention(q, kc, vc, lz)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(d)))
+    f = (lambda a: bf16_to_f32(a)) if dtype == "bf16" else (lambda a: a)
+    exact, mag = _attn_exact(f(q), f(kc), f(vc), lz, scale)
+    g = f(got).astype(np.float64)
+    r = f(ref).astype(np.float64)
+    if dtype == "f32":
+        lim = 1e-5 * mag + 1e-7
+        assert np.all(np.abs(g - exact) <= lim), "kernel vs exact"
+        assert np.all(np.abs(g - r) <= lim + np.abs(r - exact)), "kernel vs reference + its drift"
+    else:
+        d_ulp = ulp_bf16(got, ref)
+        ok = (d_ulp <= 1) | (np.abs(g - r) <= 2.0 ** -9 * mag + 1e-6)
+        assert ok.all(), f"max {d_ulp.max()} bf16 ulp"
+    if lz is not None:
+        for bi, n in enumerate(lz):
+            if n == 0:
+                assert np.all(g[bi] == 0)
+
+
+@pytest.mark.gpu
+def test_decode_attention_equals_repeat_kv_then_softmax(cuda):
+    """The GQA head map equals materialising repeat_kv and attending per head."""
+    import torch
+
+    from oxide_b200 import ops
+
+    g = torch.Generator(device=cuda).manual_seed(5)
+    q = torch.randn(2, 8, 128, device=cuda, generator=g)
+    kc = torch.randn(2, 2, 200, 128, device=cuda, generator=g)
+    vc = torch.randn(2, 2, 200, 128, device=cuda, generator=g)
+    lens = torch.tensor([200, 150], dtype=torch.int32, device=cuda)
+    got = ops.decode_attention(q, kc, vc, lens)
+    k4, v4 = ops.repeat_kv(kc, 4), ops.repeat_kv(vc, 4)
+    want = torch.empty_like(got)
+    for bi, n in enumerate((200, 150)):
+        s = torch.einsum("hd,hjd->hj", q[bi].double(), k4[bi, :, :n].double()) / np.sqrt(128.0)
+        want[bi] = torch.einsum("hj,hjd->hd", torch.softmax(s, -1), v4[bi, :, :n].double()).float()
+    assert torch.allclose(got, want, rtol=1e-4, atol=1e-5)
