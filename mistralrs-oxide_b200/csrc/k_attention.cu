@@ -19,11 +19,15 @@
 //      to the workspace;
 //   2. one CTA per (batch, q head) merges the splits in order:
 //      M = max m_s, L = sum l_s e^(m_s - M), out = sum o_s e^(m_s - M) / L.
-// Arithmetic is f32 (bf16 operands widened), dot products and P.V with fused
+// bf16 caches run the tile products on the tensor cores (decode_attn_mma_kernel);
+// f32 caches on the CUDA cores.  Arithmetic is f32 accumulation (bf16 operands
+// widened or multiplied exactly), dot products and P.V with fused
 // multiply-adds; the result differs from the reference's sequential f32 sums
 // by rounding only.  head_dim 128 with rep in {1, 2, 4, 8} takes this path;
 // other shapes take a one-CTA-per-(batch, head) kernel.  A sequence of length 0
 // yields zeros.
+#include <type_traits>
+
 #include "oxide_common.cuh"
 
 namespace oxide {
@@ -220,6 +224,218 @@ __global__ void __launch_bounds__(DA_THREADS)
     }
 }
 
+// ---- bf16 caches: the two tile products on the tensor cores --------------------
+// Same split-K structure and cp.async ring as decode_attn_split_kernel, with
+// S = Q K^T and O += P V as warp-level mma.sync m16n8k16 (bf16 operands, f32
+// accumulate).  The rep query heads of the group are rows 0..rep-1 of a
+// 16-row A operand (the rest zero); a memory-bound op, so the padding costs
+// nothing -- the tensor cores replace the per-element shared-memory loads
+// and FMAs that made the CUDA-core loop instruction-bound (tcgen05's smallest
+// tile, 64 rows, would be 94 % padding for 4 heads).  Q . K: bf16 x bf16
+// products are exact in the f32 accumulator.  P enters as the sum of two bf16
+// halves (p_hi = RN_bf16(p), p_lo = RN_bf16(p - p_hi): 16 significant bits)
+// multiplied by the bf16 V rows, so P V keeps f32-level accuracy.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+// d += a * b for one 16x8x16 tile; rows 8..15 of A are zero here (a1 = a3 = 0).
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+template <int NR>
+__global__ void __launch_bounds__(DA_THREADS)
+    decode_attn_mma_kernel(const bf16_t* q, const bf16_t* kc, const bf16_t* vc, float* part_ml, float* part_o,
+                           DecArgs p) {
+    using TL = DaTile<bf16_t>;
+    constexpr int TK = TL::TK, RS = TL::RS, RB = TL::RB, CPR = TL::CPR;  // 64 keys, 272-byte rows
+    constexpr int SS = TK + 4;                                         // S row stride (floats)
+    extern __shared__ __align__(16) unsigned char smem[];
+    unsigned char* kbuf = smem;
+    unsigned char* vbuf = smem + 2 * TK * RS;
+    float* S = reinterpret_cast<float*>(smem + 4 * TK * RS);  // [NR][SS]
+    float* m_run = S + NR * SS;
+    float* l_run = m_run + NR;
+    float* corr = l_run + NR;
+
+    const uint32_t split = blockIdx.x, kvh = blockIdx.y;
+    const uint64_t b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t4 = lane & 3;  // mma fragment row group / thread in group
+    const uint64_t len = seq_len_of(p, b);
+    const uint64_t s0 = (uint64_t)split * p.split_len;
+    const uint64_t s1 = s0 + p.split_len < len ? s0 + p.split_len : len;
+    const uint32_t qh0 = kvh * NR;
+
+    // Q fragments (rows g < NR), 8 k-steps of 16 dims: a0 = Q[g][16ks + 2t4 ..], a2 = Q[g][16ks + 8 + 2t4 ..]
+    uint32_t qa0[8], qa2[8];
+    {
+        const uint32_t* qrow = reinterpret_cast<const uint32_t*>(q + (b * p.q_heads + qh0 + (g < NR ? g : 0)) * DA_D);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            qa0[ks] = g < NR ? qrow[ks * 8 + t4] : 0u;
+            qa2[ks] = g < NR ? qrow[ks * 8 + 4 + t4] : 0u;
+        }
+    }
+    if (tid < NR) {
+        m_run[tid] = -INFINITY;
+        l_run[tid] = 0.0f;
+    }
+    float o[4][4];  // 4 n-tiles of 8 dims (dims warp*32 + nt*8 ..), fragment rows g / g + 8
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[nt][e] = 0.0f;
+
+    const uint64_t row0 = (b * p.kv_heads + kvh) * p.max_seq;
+    const char* kbase = reinterpret_cast<const char*>(kc + row0 * DA_D);
+    const char* vbase = reinterpret_cast<const char*>(vc + row0 * DA_D);
+    const uint32_t nkeys = s1 > s0 ? (uint32_t)(s1 - s0) : 0u;
+    const uint32_t ntiles = (nkeys + TK - 1) / TK;
+    auto issue = [&](uint32_t t) {
+        const uint32_t stage = t & 1u;
+        const uint64_t key0 = s0 + (uint64_t)t * TK;
+        const uint32_t nk = nkeys - t * TK < (uint32_t)TK ? nkeys - t * TK : (uint32_t)TK;
+        for (uint32_t c = tid; c < nk * CPR; c += DA_THREADS) {
+            const uint32_t row = c / CPR, col = c % CPR;
+            const uint64_t src = (key0 + row) * RB + col * 16;
+            cp_async16(kbuf + stage * TK * RS + row * RS + col * 16, kbase + src);
+            cp_async16(vbuf + stage * TK * RS + row * RS + col * 16, vbase + src);
+        }
+        cp_async_commit();
+    };
+    if (ntiles > 0) issue(0);
+    __syncthreads();
+    const uint32_t kbuf_s = (uint32_t)__cvta_generic_to_shared(kbuf);
+    const uint32_t vbuf_s = (uint32_t)__cvta_generic_to_shared(vbuf);
+    for (uint32_t t = 0; t < ntiles; ++t) {
+        if (t + 1 < ntiles) issue(t + 1);
+        else cp_async_commit();
+        cp_async_wait<1>();
+        const uint32_t stage = t & 1u;
+        const uint32_t nk = nkeys - t * TK < (uint32_t)TK ? nkeys - t * TK : (uint32_t)TK;
+        if (nk < (uint32_t)TK) {
+            // rows past the last key hold stale bytes; P V multiplies them by p = 0, so
+            // they must be finite: zero them
+            for (uint32_t c = nk * CPR + tid; c < (uint32_t)TK * CPR; c += DA_THREADS) {
+                const uint32_t row = c / CPR, col = c % CPR;
+                *reinterpret_cast<uint4*>(vbuf + stage * TK * RS + row * RS + col * 16) = make_uint4(0, 0, 0, 0);
+            }
+        }
+        __syncthreads();
+        // S = Q K^T: warp w computes keys 16w .. 16w + 15 (two n-tiles)
+        {
+            float s0f[4] = {0.f, 0.f, 0.f, 0.f}, s1f[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t key = warp * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+            const uint32_t base = kbuf_s + stage * TK * RS + key * RS + ((lane >> 3) & 1) * 16;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                uint32_t b00, b01, b10, b11;
+                ldsm_x4(base + ks * 32, b00, b01, b10, b11);
+                mma_bf16(s0f, qa0[ks], qa2[ks], b00, b01);
+                mma_bf16(s1f, qa0[ks], qa2[ks], b10, b11);
+            }
+            if (g < NR) {
+                const uint32_t j0 = warp * 16 + 2 * t4;
+                S[g * SS + j0] = j0 < nk ? fmul(s0f[0], p.scale) : -INFINITY;
+                S[g * SS + j0 + 1] = j0 + 1 < nk ? fmul(s0f[1], p.scale) : -INFINITY;
+                S[g * SS + j0 + 8] = j0 + 8 < nk ? fmul(s1f[0], p.scale) : -INFINITY;
+                S[g * SS + j0 + 9] = j0 + 9 < nk ? fmul(s1f[1], p.scale) : -INFINITY;
+            }
+        }
+        __syncthreads();
+        for (int r = warp; r < NR; r += DA_THREADS / 32) {
+            float* sr = S + r * SS;
+            float tmax = -INFINITY;
+            for (int j = lane; j < TK; j += 32) tmax = fmaxf(tmax, sr[j]);
+            tmax = warp_max(tmax);
+            const float m_old = m_run[r];
+            const float m_new = fmaxf(m_old, tmax);
+            float psum = 0.0f;
+            for (int j = lane; j < TK; j += 32) {
+                const float pj = m_new == -INFINITY ? 0.0f : expf(fsub(sr[j], m_new));
+                sr[j] = pj;
+                psum = fadd(psum, pj);
+            }
+            psum = warp_sum(psum);
+            if (lane == 0) {
+                const float c = m_old == -INFINITY ? 0.0f : expf(fsub(m_old, m_new));
+                corr[r] = c;
+                l_run[r] = __fmaf_rn(l_run[r], c, psum);
+                m_run[r] = m_new;
+            }
+        }
+        __syncthreads();
+        // O += P V: warp w owns dims 32w .. 32w + 31 (four n-tiles)
+        {
+            const float cg = g < NR ? corr[g] : 0.0f;
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                o[nt][0] = fmul(o[nt][0], cg);
+                o[nt][1] = fmul(o[nt][1], cg);
+            }
+            const uint32_t vkey = (lane & 7) + ((lane >> 3) & 1) * 8;   // key within the 16-key step
+            const uint32_t vdim = warp * 32 + ((lane >> 4) & 1) * 8;     // first dim of the n-tile pair
+#pragma unroll
+            for (int ks = 0; ks < TK / 16; ++ks) {
+                uint32_t ph0 = 0, ph2 = 0, pl0 = 0, pl2 = 0;
+                if (g < NR) {
+                    const float* pr = S + g * SS + ks * 16 + 2 * t4;
+                    const float p0 = pr[0], p1 = pr[1], p8 = pr[8], p9 = pr[9];
+                    const float h0 = round_bf16(p0), h1 = round_bf16(p1), h8 = round_bf16(p8), h9 = round_bf16(p9);
+                    ph0 = pack_bf16x2(h0, h1);
+                    ph2 = pack_bf16x2(h8, h9);
+                    pl0 = pack_bf16x2(fsub(p0, h0), fsub(p1, h1));
+                    pl2 = pack_bf16x2(fsub(p8, h8), fsub(p9, h9));
+                }
+#pragma unroll
+                for (int np = 0; np < 2; ++np) {  // n-tile pairs (16 dims each)
+                    uint32_t b00, b01, b10, b11;
+                    ldsm_x4_trans(vbuf_s + stage * TK * RS + (ks * 16 + vkey) * RS + (vdim + np * 16) * 2, b00, b01,
+                                  b10, b11);
+                    mma_bf16(o[2 * np], ph0, ph2, b00, b01);
+                    mma_bf16(o[2 * np], pl0, pl2, b00, b01);
+                    mma_bf16(o[2 * np + 1], ph0, ph2, b10, b11);
+                    mma_bf16(o[2 * np + 1], pl0, pl2, b10, b11);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    cp_async_wait<0>();
+    if (g < NR) {
+        const uint64_t slot = (b * p.q_heads + qh0 + g) * p.splits + split;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+            const uint32_t d = warp * 32 + nt * 8 + 2 * t4;
+            part_o[slot * DA_D + d] = o[nt][0];
+            part_o[slot * DA_D + d + 1] = o[nt][1];
+        }
+        if (warp == 0 && t4 == 0) {
+            part_ml[slot * 2] = m_run[g];
+            part_ml[slot * 2 + 1] = l_run[g];
+        }
+    }
+}
+
+template <int NR>
+constexpr size_t decode_mma_smem_bytes() {
+    return (size_t)4 * DaTile<bf16_t>::TK * DaTile<bf16_t>::RS + (size_t)NR * (DaTile<bf16_t>::TK + 4) * 4 +
+           (size_t)3 * NR * 4;
+}
+
 // Merge the splits of one (batch, q head); thread d writes out[d].
 template <typename T>
 __global__ void __launch_bounds__(DA_THREADS)
@@ -291,12 +507,20 @@ static uint32_t max_splits(uint64_t max_seq, uint64_t tk) {
 template <typename T, int NR>
 static cudaError_t launch_split(const T* q, const T* kc, const T* vc, T* out, float* ws, DecArgs p,
                                 cudaStream_t st) {
-    auto kern = decode_attn_split_kernel<T, NR>;
-    const size_t smem = decode_smem_bytes<T, NR>();
-    if (!ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem)) return cudaErrorInvalidConfiguration;
     float* part_ml = ws;
     float* part_o = ws + (size_t)2 * p.batch * p.q_heads * p.splits;
-    kern<<<dim3(p.splits, p.kv_heads, (unsigned)p.batch), DA_THREADS, smem, st>>>(q, kc, vc, part_ml, part_o, p);
+    const dim3 grid(p.splits, p.kv_heads, (unsigned)p.batch);
+    if constexpr (std::is_same<T, bf16_t>::value) {  // tensor-core tile products
+        auto kern = decode_attn_mma_kernel<NR>;
+        const size_t smem = decode_mma_smem_bytes<NR>();
+        if (!ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem)) return cudaErrorInvalidConfiguration;
+        kern<<<grid, DA_THREADS, smem, st>>>(q, kc, vc, part_ml, part_o, p);
+    } else {
+        auto kern = decode_attn_split_kernel<T, NR>;
+        const size_t smem = decode_smem_bytes<T, NR>();
+        if (!ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem)) return cudaErrorInvalidConfiguration;
+        kern<<<grid, DA_THREADS, smem, st>>>(q, kc, vc, part_ml, part_o, p);
+    }
     decode_attn_combine_kernel<T><<<(unsigned)(p.batch * p.q_heads), DA_THREADS, 0, st>>>(part_ml, part_o, out, p);
     return cudaSuccess;
 }
