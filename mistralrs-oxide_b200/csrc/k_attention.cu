@@ -8,24 +8,24 @@
 // keys j >= lens[b] (the sequence's KV length) are masked.
 //
 // Design (split-K, two launches):
-//   1. grid (splits, kv_heads, batch): a 128-thread CTA streams the keys
-//      [split * split_len, ...) of one (batch, kv head) through a two-stage
-//      cp.async ring of 16-byte copies into shared memory (K and V tiles of 64
-//      bf16 / 32 f32 rows, rows padded by 16 bytes against bank conflicts),
-//      computes the scores of all `rep` query heads of the group (each K row
-//      is read from HBM once for the group), keeps a running max / sum per
-//      head (online softmax) and accumulates the unnormalised output in
-//      registers (thread d owns output dim d); it writes (m, l, o[d]) per head
-//      to the workspace;
+//   1. grid (splits, kv_heads, batch): one CTA streams the keys
+//      [split * split_len, ...) of one (batch, kv head) into shared memory with
+//      16-byte cp.async copies (rows padded by 16 bytes against bank
+//      conflicts), computes the scores of all `rep` query heads of the group
+//      (each K row is read from HBM once for the group), keeps a running max /
+//      sum per head (online softmax) and accumulates the unnormalised output;
+//      it writes (m, l, o[d]) per head to the workspace.  bf16 caches: four
+//      warps stream interleaved 16-key tiles independently and run both tile
+//      products on the tensor cores (decode_attn_warp_kernel); f32 caches: a
+//      two-stage block ring on the CUDA cores, thread d owning output dim d
+//      (decode_attn_split_kernel);
 //   2. one CTA per (batch, q head) merges the splits in order:
 //      M = max m_s, L = sum l_s e^(m_s - M), out = sum o_s e^(m_s - M) / L.
-// bf16 caches run the tile products on the tensor cores (decode_attn_mma_kernel);
-// f32 caches on the CUDA cores.  Arithmetic is f32 accumulation (bf16 operands
-// widened or multiplied exactly), dot products and P.V with fused
-// multiply-adds; the result differs from the reference's sequential f32 sums
-// by rounding only.  head_dim 128 with rep in {1, 2, 4, 8} takes this path;
-// other shapes take a one-CTA-per-(batch, head) kernel.  A sequence of length 0
-// yields zeros.
+// Arithmetic is f32 accumulation (bf16 operands multiplied exactly), dot
+// products and P.V with fused multiply-adds; the result differs from the
+// reference's sequential f32 sums by rounding only.  head_dim 128 with rep in
+// {1, 2, 4, 8} takes this path; other shapes take a one-CTA-per-(batch, head)
+// kernel.  A sequence of length 0 yields zeros.
 #include <type_traits>
 
 #include "oxide_common.cuh"
@@ -224,17 +224,23 @@ __global__ void __launch_bounds__(DA_THREADS)
     }
 }
 
-// ---- bf16 caches: the two tile products on the tensor cores --------------------
-// Same split-K structure and cp.async ring as decode_attn_split_kernel, with
-// S = Q K^T and O += P V as warp-level mma.sync m16n8k16 (bf16 operands, f32
-// accumulate).  The rep query heads of the group are rows 0..rep-1 of a
-// 16-row A operand (the rest zero); a memory-bound op, so the padding costs
-// nothing -- the tensor cores replace the per-element shared-memory loads
-// and FMAs that made the CUDA-core loop instruction-bound (tcgen05's smallest
-// tile, 64 rows, would be 94 % padding for 4 heads).  Q . K: bf16 x bf16
-// products are exact in the f32 accumulator.  P enters as the sum of two bf16
-// halves (p_hi = RN_bf16(p), p_lo = RN_bf16(p - p_hi): 16 significant bits)
-// multiplied by the bf16 V rows, so P V keeps f32-level accuracy.
+// ---- bf16 caches: per-warp key streams on the tensor cores -------------------
+// Each warp of a 4-warp CTA streams every 4th 16-key tile of the split through
+// its own 3-stage cp.async ring and keeps its own online-softmax state, so the
+// key loop has no block barrier; the four warp states are merged once at the
+// end.  The tile products run transposed on warp-level mma.sync m16n8k16
+// (bf16 operands, f32 accumulate) so that the rep <= 8 query heads of the
+// group are the n = 8 side:
+//   S^T[16 keys x 8 heads]  = K[16 x 128] . Q^T       (A = K rows, ldmatrix)
+//   O^T[128 dims x 8 heads] += V^T[128 x 16] . P^T    (A = V rows, ldmatrix.trans)
+// The score fragment (key g / g + 8, heads 2t4, 2t4 + 1) becomes the P^T
+// operand fragment (keys 2t4.., head g) by one movmatrix.trans per 8x8 block,
+// without a round trip through shared memory.  Q . K: bf16 x bf16 products
+// are exact in the f32 accumulator.  P enters as the sum of two bf16 halves
+// (p_hi = RN_bf16(p), p_lo = RN_bf16(p - p_hi): 16 significant bits), so P V
+// keeps f32-level accuracy.  Scores are kept in the base-2 domain,
+// t = (q . k) * (scale * log2 e), and p = ex2.approx(t - m): relative error
+// ~2^-22 per probability, far below the bf16 output rounding (2^-9).
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -246,194 +252,216 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint3
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(addr));
 }
-// d += a * b for one 16x8x16 tile; rows 8..15 of A are zero here (a1 = a3 = 0).
-__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+// d += a * b for one 16x8x16 tile (A row-major 16x16, B column-major 16x8).
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Transpose an 8x8 b16 matrix held as one fragment register per lane
+// (lane g * 4 + t holds row g, columns 2t and 2t + 1).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
 }
 
-template <int NR>
-__global__ void __launch_bounds__(DA_THREADS)
-    decode_attn_mma_kernel(const bf16_t* q, const bf16_t* kc, const bf16_t* vc, float* part_ml, float* part_o,
-                           DecArgs p) {
-    using TL = DaTile<bf16_t>;
-    constexpr int TK = TL::TK, RS = TL::RS, RB = TL::RB, CPR = TL::CPR;  // 64 keys, 272-byte rows
-    constexpr int SS = TK + 4;                                         // S row stride (floats)
-    extern __shared__ __align__(16) unsigned char smem[];
-    unsigned char* kbuf = smem;
-    unsigned char* vbuf = smem + 2 * TK * RS;
-    float* S = reinterpret_cast<float*>(smem + 4 * TK * RS);  // [NR][SS]
-    float* m_run = S + NR * SS;
-    float* l_run = m_run + NR;
-    float* corr = l_run + NR;
+constexpr int DW_WARPS = 4;                                     // warps per CTA
+constexpr int DW_TK = 16;                                       // keys per warp tile
+constexpr int DW_STAGES = 3;                                    // cp.async ring depth per warp
+constexpr int DW_RS = DA_D * 2 + 16;                            // 272-byte rows: conflict-free ldmatrix
+constexpr int DW_STAGE = 2 * DW_TK * DW_RS;                     // K and V tile of one stage
+constexpr size_t DW_SMEM = (size_t)DW_WARPS * DW_STAGES * DW_STAGE;  // 104,448 B: 2 CTAs per SM
+constexpr float DW_LOG2E = 1.4426950408889634f;
+constexpr float DW_LN2 = 0.6931471805599453f;
 
+template <int NR>
+__global__ void __launch_bounds__(DW_WARPS * 32, 2)
+    decode_attn_warp_kernel(const bf16_t* q, const bf16_t* kc, const bf16_t* vc, float* part_ml, float* part_o,
+                            DecArgs p) {
+    static_assert(DW_WARPS * 32 == DA_D, "the merge maps one thread to one output dim");
+    extern __shared__ __align__(16) unsigned char smem[];
     const uint32_t split = blockIdx.x, kvh = blockIdx.y;
     const uint64_t b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = lane >> 2, t4 = lane & 3;  // mma fragment row group / thread in group
+    const int g = lane >> 2, t4 = lane & 3;  // fragment row group / thread in group
     const uint64_t len = seq_len_of(p, b);
     const uint64_t s0 = (uint64_t)split * p.split_len;
     const uint64_t s1 = s0 + p.split_len < len ? s0 + p.split_len : len;
+    const uint32_t nkeys = s1 > s0 ? (uint32_t)(s1 - s0) : 0u;
+    const uint32_t ntiles = (nkeys + DW_TK - 1) / DW_TK;
     const uint32_t qh0 = kvh * NR;
 
-    // Q fragments (rows g < NR), 8 k-steps of 16 dims: a0 = Q[g][16ks + 2t4 ..], a2 = Q[g][16ks + 8 + 2t4 ..]
-    uint32_t qa0[8], qa2[8];
+    // Q^T as the B operand: b0 = Q[head g][16 ks + 2 t4, +1], b1 = Q[head g][16 ks + 8 + 2 t4, +1]
+    uint32_t qb0[8], qb1[8];
     {
         const uint32_t* qrow = reinterpret_cast<const uint32_t*>(q + (b * p.q_heads + qh0 + (g < NR ? g : 0)) * DA_D);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
-            qa0[ks] = g < NR ? qrow[ks * 8 + t4] : 0u;
-            qa2[ks] = g < NR ? qrow[ks * 8 + 4 + t4] : 0u;
+            qb0[ks] = g < NR ? qrow[ks * 8 + t4] : 0u;
+            qb1[ks] = g < NR ? qrow[ks * 8 + 4 + t4] : 0u;
         }
     }
-    if (tid < NR) {
-        m_run[tid] = -INFINITY;
-        l_run[tid] = 0.0f;
-    }
-    float o[4][4];  // 4 n-tiles of 8 dims (dims warp*32 + nt*8 ..), fragment rows g / g + 8
+    // O^T m-tile mt: o[mt][0] (dim 16 mt + g, head 2 t4), [1] (same dim, head 2 t4 + 1),
+    // [2] / [3] the same heads at dim 16 mt + g + 8
+    float o[8][4];
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o[nt][e] = 0.0f;
+        for (int e = 0; e < 4; ++e) o[mt][e] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY;  // running max of heads 2 t4, 2 t4 + 1 (base 2)
+    float l0 = 0.0f, l1 = 0.0f;            // this lane's share of the running sums
+    const float c1 = fmul(p.scale, DW_LOG2E);
 
-    const uint64_t row0 = (b * p.kv_heads + kvh) * p.max_seq;
+    unsigned char* wbuf = smem + (size_t)warp * DW_STAGES * DW_STAGE;
+    const uint64_t row0 = (b * p.kv_heads + kvh) * p.max_seq + s0;
     const char* kbase = reinterpret_cast<const char*>(kc + row0 * DA_D);
     const char* vbase = reinterpret_cast<const char*>(vc + row0 * DA_D);
-    const uint32_t nkeys = s1 > s0 ? (uint32_t)(s1 - s0) : 0u;
-    const uint32_t ntiles = (nkeys + TK - 1) / TK;
-    auto issue = [&](uint32_t t) {
-        const uint32_t stage = t & 1u;
-        const uint64_t key0 = s0 + (uint64_t)t * TK;
-        const uint32_t nk = nkeys - t * TK < (uint32_t)TK ? nkeys - t * TK : (uint32_t)TK;
-        for (uint32_t c = tid; c < nk * CPR; c += DA_THREADS) {
-            const uint32_t row = c / CPR, col = c % CPR;
-            const uint64_t src = (key0 + row) * RB + col * 16;
-            cp_async16(kbuf + stage * TK * RS + row * RS + col * 16, kbase + src);
-            cp_async16(vbuf + stage * TK * RS + row * RS + col * 16, vbase + src);
+    // copy slots of this lane: rows 2 i + (lane >> 4), 16-byte column lane & 15
+    const uint32_t crow = lane >> 4, ccol = (lane & 15) * 16;
+    const uint32_t my_tiles = ntiles > (uint32_t)warp ? (ntiles - warp + DW_WARPS - 1) / DW_WARPS : 0u;
+    auto issue = [&](uint32_t it) {
+        unsigned char* kd = wbuf + (it % DW_STAGES) * DW_STAGE;
+        unsigned char* vd = kd + DW_TK * DW_RS;
+        const uint32_t key0 = (warp + it * DW_WARPS) * DW_TK;
+        const uint32_t nk = nkeys - key0 < (uint32_t)DW_TK ? nkeys - key0 : (uint32_t)DW_TK;
+#pragma unroll
+        for (int i = 0; i < DW_TK / 2; ++i) {
+            const uint32_t row = 2 * i + crow;
+            // rows past the last key repeat the last key: finite data that p = 0 multiplies
+            const uint32_t src = row < nk ? row : nk - 1;
+            const uint64_t off = (uint64_t)(key0 + src) * (DA_D * 2) + ccol;
+            cp_async16(kd + row * DW_RS + ccol, kbase + off);
+            cp_async16(vd + row * DW_RS + ccol, vbase + off);
         }
-        cp_async_commit();
     };
-    if (ntiles > 0) issue(0);
-    __syncthreads();
-    const uint32_t kbuf_s = (uint32_t)__cvta_generic_to_shared(kbuf);
-    const uint32_t vbuf_s = (uint32_t)__cvta_generic_to_shared(vbuf);
-    for (uint32_t t = 0; t < ntiles; ++t) {
-        if (t + 1 < ntiles) issue(t + 1);
-        else cp_async_commit();
-        cp_async_wait<1>();
-        const uint32_t stage = t & 1u;
-        const uint32_t nk = nkeys - t * TK < (uint32_t)TK ? nkeys - t * TK : (uint32_t)TK;
-        if (nk < (uint32_t)TK) {
-            // rows past the last key hold stale bytes; P V multiplies them by p = 0, so
-            // they must be finite: zero them
-            for (uint32_t c = nk * CPR + tid; c < (uint32_t)TK * CPR; c += DA_THREADS) {
-                const uint32_t row = c / CPR, col = c % CPR;
-                *reinterpret_cast<uint4*>(vbuf + stage * TK * RS + row * RS + col * 16) = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int s = 0; s < DW_STAGES - 1; ++s) {
+        if ((uint32_t)s < my_tiles) issue(s);
+        cp_async_commit();
+    }
+    const uint32_t wbuf_s = (uint32_t)__cvta_generic_to_shared(wbuf);
+    // ldmatrix row addresses: K as A (keys x dims), V as A^T (dims x keys)
+    const uint32_t k_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * DW_RS + (lane >> 4) * 16;
+    const uint32_t v_lane = DW_TK * DW_RS + ((lane & 7) + (lane >> 4) * 8) * DW_RS + ((lane >> 3) & 1) * 16;
+    for (uint32_t it = 0; it < my_tiles; ++it) {
+        if (it + DW_STAGES - 1 < my_tiles) issue(it + DW_STAGES - 1);
+        cp_async_commit();
+        cp_async_wait<DW_STAGES - 1>();
+        __syncwarp();  // every lane's copies of this tile are visible to the warp
+        const uint32_t base = wbuf_s + (it % DW_STAGES) * DW_STAGE;
+        const uint32_t key0 = (warp + it * DW_WARPS) * DW_TK;
+        const uint32_t nk = nkeys - key0 < (uint32_t)DW_TK ? nkeys - key0 : (uint32_t)DW_TK;
+        float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4(base + k_lane + ks * 32, a0, a1, a2, a3);
+            mma_bf16(s, a0, a1, a2, a3, qb0[ks], qb1[ks]);
+        }
+        // s: (key g, head 2t4), (key g, head 2t4+1), (key g+8, head 2t4), (key g+8, head 2t4+1)
+        const float t0 = (uint32_t)g < nk ? fmul(s[0], c1) : -INFINITY;
+        const float t1 = (uint32_t)g < nk ? fmul(s[1], c1) : -INFINITY;
+        const float t2 = (uint32_t)g + 8 < nk ? fmul(s[2], c1) : -INFINITY;
+        const float t3 = (uint32_t)g + 8 < nk ? fmul(s[3], c1) : -INFINITY;
+        float x0 = fmaxf(t0, t2), x1 = fmaxf(t1, t3);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            x0 = fmaxf(x0, __shfl_xor_sync(0xffffffffu, x0, off));
+            x1 = fmaxf(x1, __shfl_xor_sync(0xffffffffu, x1, off));
+        }
+        const float mn0 = fmaxf(m0, x0), mn1 = fmaxf(m1, x1);
+        const float cr0 = m0 == -INFINITY ? 0.0f : ex2_approx(fsub(m0, mn0));
+        const float cr1 = m1 == -INFINITY ? 0.0f : ex2_approx(fsub(m1, mn1));
+        m0 = mn0;
+        m1 = mn1;
+        const float p0 = mn0 == -INFINITY ? 0.0f : ex2_approx(fsub(t0, mn0));
+        const float p2 = mn0 == -INFINITY ? 0.0f : ex2_approx(fsub(t2, mn0));
+        const float p1 = mn1 == -INFINITY ? 0.0f : ex2_approx(fsub(t1, mn1));
+        const float p3 = mn1 == -INFINITY ? 0.0f : ex2_approx(fsub(t3, mn1));
+        l0 = __fmaf_rn(l0, cr0, fadd(p0, p2));
+        l1 = __fmaf_rn(l1, cr1, fadd(p1, p3));
+        if (__any_sync(0xffffffffu, cr0 != 1.0f || cr1 != 1.0f)) {
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                o[mt][0] = fmul(o[mt][0], cr0);
+                o[mt][1] = fmul(o[mt][1], cr1);
+                o[mt][2] = fmul(o[mt][2], cr0);
+                o[mt][3] = fmul(o[mt][3], cr1);
             }
         }
-        __syncthreads();
-        // S = Q K^T: warp w computes keys 16w .. 16w + 15 (two n-tiles)
-        {
-            float s0f[4] = {0.f, 0.f, 0.f, 0.f}, s1f[4] = {0.f, 0.f, 0.f, 0.f};
-            const uint32_t key = warp * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
-            const uint32_t base = kbuf_s + stage * TK * RS + key * RS + ((lane >> 3) & 1) * 16;
+        // P^T operand: the 8x8 blocks P[keys 0-7 | 8-15][heads] transposed
+        const float h0 = round_bf16(p0), h1 = round_bf16(p1), h2 = round_bf16(p2), h3 = round_bf16(p3);
+        const uint32_t bh0 = movmatrix_trans(pack_bf16x2(h0, h1));
+        const uint32_t bh1 = movmatrix_trans(pack_bf16x2(h2, h3));
+        const uint32_t bl0 = movmatrix_trans(pack_bf16x2(fsub(p0, h0), fsub(p1, h1)));
+        const uint32_t bl1 = movmatrix_trans(pack_bf16x2(fsub(p2, h2), fsub(p3, h3)));
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-                uint32_t b00, b01, b10, b11;
-                ldsm_x4(base + ks * 32, b00, b01, b10, b11);
-                mma_bf16(s0f, qa0[ks], qa2[ks], b00, b01);
-                mma_bf16(s1f, qa0[ks], qa2[ks], b10, b11);
-            }
-            if (g < NR) {
-                const uint32_t j0 = warp * 16 + 2 * t4;
-                S[g * SS + j0] = j0 < nk ? fmul(s0f[0], p.scale) : -INFINITY;
-                S[g * SS + j0 + 1] = j0 + 1 < nk ? fmul(s0f[1], p.scale) : -INFINITY;
-                S[g * SS + j0 + 8] = j0 + 8 < nk ? fmul(s1f[0], p.scale) : -INFINITY;
-                S[g * SS + j0 + 9] = j0 + 9 < nk ? fmul(s1f[1], p.scale) : -INFINITY;
-            }
+        for (int mt = 0; mt < 8; ++mt) {
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_trans(base + v_lane + mt * 32, a0, a1, a2, a3);
+            mma_bf16(o[mt], a0, a1, a2, a3, bh0, bh1);
+            mma_bf16(o[mt], a0, a1, a2, a3, bl0, bl1);
         }
-        __syncthreads();
-        for (int r = warp; r < NR; r += DA_THREADS / 32) {
-            float* sr = S + r * SS;
-            float tmax = -INFINITY;
-            for (int j = lane; j < TK; j += 32) tmax = fmaxf(tmax, sr[j]);
-            tmax = warp_max(tmax);
-            const float m_old = m_run[r];
-            const float m_new = fmaxf(m_old, tmax);
-            float psum = 0.0f;
-            for (int j = lane; j < TK; j += 32) {
-                const float pj = m_new == -INFINITY ? 0.0f : expf(fsub(sr[j], m_new));
-                sr[j] = pj;
-                psum = fadd(psum, pj);
-            }
-            psum = warp_sum(psum);
-            if (lane == 0) {
-                const float c = m_old == -INFINITY ? 0.0f : expf(fsub(m_old, m_new));
-                corr[r] = c;
-                l_run[r] = __fmaf_rn(l_run[r], c, psum);
-                m_run[r] = m_new;
-            }
-        }
-        __syncthreads();
-        // O += P V: warp w owns dims 32w .. 32w + 31 (four n-tiles)
-        {
-            const float cg = g < NR ? corr[g] : 0.0f;
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                o[nt][0] = fmul(o[nt][0], cg);
-                o[nt][1] = fmul(o[nt][1], cg);
-            }
-            const uint32_t vkey = (lane & 7) + ((lane >> 3) & 1) * 8;   // key within the 16-key step
-            const uint32_t vdim = warp * 32 + ((lane >> 4) & 1) * 8;     // first dim of the n-tile pair
-#pragma unroll
-            for (int ks = 0; ks < TK / 16; ++ks) {
-                uint32_t ph0 = 0, ph2 = 0, pl0 = 0, pl2 = 0;
-                if (g < NR) {
-                    const float* pr = S + g * SS + ks * 16 + 2 * t4;
-                    const float p0 = pr[0], p1 = pr[1], p8 = pr[8], p9 = pr[9];
-                    const float h0 = round_bf16(p0), h1 = round_bf16(p1), h8 = round_bf16(p8), h9 = round_bf16(p9);
-                    ph0 = pack_bf16x2(h0, h1);
-                    ph2 = pack_bf16x2(h8, h9);
-                    pl0 = pack_bf16x2(fsub(p0, h0), fsub(p1, h1));
-                    pl2 = pack_bf16x2(fsub(p8, h8), fsub(p9, h9));
-                }
-#pragma unroll
-                for (int np = 0; np < 2; ++np) {  // n-tile pairs (16 dims each)
-                    uint32_t b00, b01, b10, b11;
-                    ldsm_x4_trans(vbuf_s + stage * TK * RS + (ks * 16 + vkey) * RS + (vdim + np * 16) * 2, b00, b01,
-                                  b10, b11);
-                    mma_bf16(o[2 * np], ph0, ph2, b00, b01);
-                    mma_bf16(o[2 * np], pl0, pl2, b00, b01);
-                    mma_bf16(o[2 * np + 1], ph0, ph2, b10, b11);
-                    mma_bf16(o[2 * np + 1], pl0, pl2, b10, b11);
-                }
-            }
-        }
-        __syncthreads();
+        __syncwarp();  // the whole warp is done with this stage before it is refilled
     }
     cp_async_wait<0>();
-    if (g < NR) {
-        const uint64_t slot = (b * p.q_heads + qh0 + g) * p.splits + split;
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            const uint32_t d = warp * 32 + nt * 8 + 2 * t4;
-            part_o[slot * DA_D + d] = o[nt][0];
-            part_o[slot * DA_D + d + 1] = o[nt][1];
+    for (int off = 4; off < 32; off <<= 1) {
+        l0 = fadd(l0, __shfl_xor_sync(0xffffffffu, l0, off));
+        l1 = fadd(l1, __shfl_xor_sync(0xffffffffu, l1, off));
+    }
+    // merge the four warp states: [W][8] max, [W][8] sum, [W][NR][D] output
+    __syncthreads();  // every warp is done with its ring: the buffers are reused
+    float* wm = reinterpret_cast<float*>(smem);
+    float* wl = wm + DW_WARPS * 8;
+    float* wo = wl + DW_WARPS * 8;
+    if (g == 0) {
+        wm[warp * 8 + 2 * t4] = m0;
+        wm[warp * 8 + 2 * t4 + 1] = m1;
+        wl[warp * 8 + 2 * t4] = l0;
+        wl[warp * 8 + 2 * t4 + 1] = l1;
+    }
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+        const int d0 = mt * 16 + g;
+        if (2 * t4 < NR) {
+            wo[(warp * NR + 2 * t4) * DA_D + d0] = o[mt][0];
+            wo[(warp * NR + 2 * t4) * DA_D + d0 + 8] = o[mt][2];
         }
-        if (warp == 0 && t4 == 0) {
-            part_ml[slot * 2] = m_run[g];
-            part_ml[slot * 2 + 1] = l_run[g];
+        if (2 * t4 + 1 < NR) {
+            wo[(warp * NR + 2 * t4 + 1) * DA_D + d0] = o[mt][1];
+            wo[(warp * NR + 2 * t4 + 1) * DA_D + d0 + 8] = o[mt][3];
         }
     }
-}
-
-template <int NR>
-constexpr size_t decode_mma_smem_bytes() {
-    return (size_t)4 * DaTile<bf16_t>::TK * DaTile<bf16_t>::RS + (size_t)NR * (DaTile<bf16_t>::TK + 4) * 4 +
-           (size_t)3 * NR * 4;
+    __syncthreads();
+    const int d = tid;
+#pragma unroll
+    for (int h = 0; h < NR; ++h) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < DW_WARPS; ++w) M = fmaxf(M, wm[w * 8 + h]);
+        float L = 0.0f, acc = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < DW_WARPS; ++w) {
+                const float mw = wm[w * 8 + h];
+                if (mw == -INFINITY) continue;
+                const float sc = ex2_approx(fsub(mw, M));
+                L = __fmaf_rn(wl[w * 8 + h], sc, L);
+                acc = __fmaf_rn(wo[(w * NR + h) * DA_D + d], sc, acc);
+            }
+        }
+        const uint64_t slot = (b * p.q_heads + qh0 + h) * p.splits + split;
+        part_o[slot * DA_D + d] = acc;
+        if (d == 0) {
+            part_ml[slot * 2] = M == -INFINITY ? M : fmul(M, DW_LN2);  // natural-log domain for the merge
+            part_ml[slot * 2 + 1] = L;
+        }
+    }
 }
 
 // Merge the splits of one (batch, q head); thread d writes out[d].
@@ -511,10 +539,9 @@ static cudaError_t launch_split(const T* q, const T* kc, const T* vc, T* out, fl
     float* part_o = ws + (size_t)2 * p.batch * p.q_heads * p.splits;
     const dim3 grid(p.splits, p.kv_heads, (unsigned)p.batch);
     if constexpr (std::is_same<T, bf16_t>::value) {  // tensor-core tile products
-        auto kern = decode_attn_mma_kernel<NR>;
-        const size_t smem = decode_mma_smem_bytes<NR>();
-        if (!ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem)) return cudaErrorInvalidConfiguration;
-        kern<<<grid, DA_THREADS, smem, st>>>(q, kc, vc, part_ml, part_o, p);
+        auto kern = decode_attn_warp_kernel<NR>;
+        if (!ensure_dyn_smem(reinterpret_cast<const void*>(kern), DW_SMEM)) return cudaErrorInvalidConfiguration;
+        kern<<<grid, DW_WARPS * 32, DW_SMEM, st>>>(q, kc, vc, part_ml, part_o, p);
     } else {
         auto kern = decode_attn_split_kernel<T, NR>;
         const size_t smem = decode_smem_bytes<T, NR>();

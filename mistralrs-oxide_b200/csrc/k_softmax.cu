@@ -491,16 +491,6 @@ static cudaError_t launch_vec(const T* x, T* out, SmaxArgs p, int vpt, cudaStrea
 //     holds only its packed keys (64 registers, 4 CTAs of 256 threads per SM:
 //     measured 10% faster than keeping e at 2 CTAs per SM); lg2.approx adds
 //     ~2^-22 absolute to the exponent, ~1.7e-7 relative to p.
-__device__ __forceinline__ float ex2_approx(float t) {
-    float y;
-    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(t));
-    return y;
-}
-__device__ __forceinline__ float lg2_approx(float t) {
-    float y;
-    asm("lg2.approx.f32 %0, %1;" : "=f"(y) : "f"(t));
-    return y;
-}
 __device__ __forceinline__ uint32_t bf16x2_max(uint32_t a, uint32_t b) {
     uint32_t r;
     asm("max.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));

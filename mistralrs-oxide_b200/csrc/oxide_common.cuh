@@ -215,6 +215,22 @@ struct FastDiv {
 };
 
 // ---------------------------------------------------------------------------
+// Special-function unit approximations (relative error ~2^-22; subnormal
+// results kept).  Used only where the result is rounded to bf16 afterwards or
+// the tolerance is stated beside the caller.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float ex2_approx(float t) {
+    float y;
+    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(t));
+    return y;
+}
+__device__ __forceinline__ float lg2_approx(float t) {
+    float y;
+    asm("lg2.approx.f32 %0, %1;" : "=f"(y) : "f"(t));
+    return y;
+}
+
+// ---------------------------------------------------------------------------
 // Warp / block reductions (fixed shuffle trees: deterministic)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {
