@@ -39,6 +39,7 @@
 #include <string>
 #include <utility>
 #include <variant>
+#include <cmath>
 #include <vector>
 
 #include "oxide_ops.h"
@@ -659,7 +660,100 @@ inline Result<Tensor> reduce_rows(const Tensor& x, int op) {
     OXIDE_TRY(check_status(rc));
     return out;
 }
+
+// One decode step of attention over a KV cache (src/layers/attention.rs:96-99
+// for one query token): q [batch, q_heads, head_dim], caches
+// [batch, kv_heads, max_seq, head_dim], lens (device int32 [batch], may be
+// null: every position) -> out [batch, q_heads, head_dim].  The GQA head map
+// of repeat_kv is applied without materialising it.
+inline Result<Tensor> decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache,
+                                       const int32_t* lens = nullptr) {
+    if (q.rank() != 3 || k_cache.rank() != 4 || k_cache.shape() != v_cache.shape() ||
+        q.dims()[0] != k_cache.dims()[0] || q.dims()[2] != k_cache.dims()[3])
+        return OxideError::invalid("decode_attention: q " + q.shape().to_string() + " and caches " +
+                                   k_cache.shape().to_string() + " must be [b, hq, d] and [b, hkv, max_seq, d]");
+    OXIDE_TRY(detail::same_dtype(q, k_cache, "decode_attention"));
+    OXIDE_TRY(detail::same_dtype(q, v_cache, "decode_attention"));
+    const size_t b = q.dims()[0], hq = q.dims()[1], d = q.dims()[2];
+    const size_t hkv = k_cache.dims()[1], max_seq = k_cache.dims()[2];
+    auto out = Tensor::empty(q.shape(), q.dtype(), q.device());
+    if (out.is_err()) return out;
+    const uint64_t wb = oxide_decode_attention_workspace_bytes(b, hq, max_seq, d);
+    auto ws = DeviceBuffer::allocate(wb ? wb : 16, q.device());
+    if (ws.is_err()) return ws.error();
+    const float scale = 1.0f / std::sqrt((float)d);
+    const int rc = detail::bf16(q)
+        ? oxide_decode_attention_bf16(q.as<oxide_bf16>(), k_cache.as<oxide_bf16>(), v_cache.as<oxide_bf16>(),
+                                      lens, out.value().as<oxide_bf16>(), b, hq, hkv, max_seq, d, scale,
+                                      ws.value()->ptr(), wb, current_stream())
+        : oxide_decode_attention_f32(q.as<float>(), k_cache.as<float>(), v_cache.as<float>(), lens,
+                                     out.value().as<float>(), b, hq, hkv, max_seq, d, scale, ws.value()->ptr(), wb,
+                                     current_stream());
+    OXIDE_TRY(check_status(rc));
+    OXIDE_TRY(check_cuda(cudaStreamSynchronize(current_stream()), "cudaStreamSynchronize"));  // ws lifetime
+    return out;
+}
+
+// softmax_with_temperature (src/tokenizer.rs:166-180) over the last dim ->
+// f32 probabilities of the same shape.
+inline Result<Tensor> softmax_with_temperature(const Tensor& logits, float temperature) {
+    if (logits.rank() < 1) return OxideError::invalid("softmax_with_temperature requires at least 1D tensor");
+    const size_t vocab = logits.dims().back(), rows = vocab ? logits.elem_count() / vocab : 0;
+    auto out = Tensor::empty(logits.shape(), DType::F32, logits.device());
+    if (out.is_err()) return out;
+    const int rc = detail::bf16(logits)
+        ? oxide_softmax_with_temperature_bf16(logits.as<oxide_bf16>(), out.value().as<float>(), rows, vocab,
+                                              temperature, current_stream())
+        : oxide_softmax_with_temperature_f32(logits.as<float>(), out.value().as<float>(), rows, vocab,
+                                             temperature, current_stream());
+    OXIDE_TRY(check_status(rc));
+    return out;
+}
 }  // namespace ops
+
+// InferenceParams (src/tokenizer.rs:145-162) with the reference's defaults.
+struct InferenceParams {
+    size_t max_new_tokens = 100;
+    float temperature = 1.0f;
+    float top_p = 1.0f;
+    size_t top_k = 50;
+    float repetition_penalty = 1.0f;
+};
+
+// The token step of the generation loop (src/pipeline.rs:181-205) for every
+// row of logits [..., vocab]: softmax_with_temperature, then sample_top_p when
+// top_p < 1, else sample_top_k.  uniforms holds one draw in [0, 1) per row --
+// the reference's fastrand::f32() -- so the caller keeps the generator.  A
+// row whose probabilities hold a NaN gives OXIDE_SAMPLE_INVALID (the
+// reference's sort panics there).
+inline Result<std::vector<uint32_t>> sample_next_token(const Tensor& logits, const std::vector<float>& uniforms,
+                                                       const InferenceParams& params = {}) {
+    if (logits.rank() < 1) return OxideError::invalid("sample_next_token requires at least 1D tensor");
+    const size_t vocab = logits.dims().back();
+    size_t rows = 1;
+    for (size_t i = 0; i + 1 < logits.rank(); ++i) rows *= logits.dims()[i];
+    if (uniforms.size() != rows)
+        return OxideError::invalid("sample_next_token: " + std::to_string(uniforms.size()) +
+                                   " uniforms for " + std::to_string(rows) + " rows");
+    auto buf = DeviceBuffer::allocate(rows * (sizeof(float) + sizeof(uint32_t)) + 16, logits.device());
+    if (buf.is_err()) return buf.error();
+    float* u = static_cast<float*>(buf.value()->ptr());
+    uint32_t* tok = reinterpret_cast<uint32_t*>(u + rows);
+    std::vector<uint32_t> host(rows);
+    if (rows == 0) return host;
+    OXIDE_TRY(check_cuda(cudaMemcpyAsync(u, uniforms.data(), rows * sizeof(float), cudaMemcpyHostToDevice,
+                                         current_stream()), "cudaMemcpyAsync"));
+    const int rc = logits.dtype() == DType::BF16
+        ? oxide_sample_bf16(logits.as<oxide_bf16>(), rows, vocab, params.temperature, params.top_k, params.top_p,
+                            u, tok, nullptr, current_stream())
+        : oxide_sample_f32(logits.as<float>(), rows, vocab, params.temperature, params.top_k, params.top_p, u,
+                           tok, nullptr, current_stream());
+    OXIDE_TRY(check_status(rc));
+    OXIDE_TRY(check_cuda(cudaMemcpyAsync(host.data(), tok, rows * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                         current_stream()), "cudaMemcpyAsync"));
+    OXIDE_TRY(check_cuda(cudaStreamSynchronize(current_stream()), "cudaStreamSynchronize"));
+    return host;
+}
 
 // precompute_rope_cache (src/models/mistral.rs:91-115): f32 (cos, sin)
 // tables [max_pos, head_dim/2] built on the host, then uploaded.

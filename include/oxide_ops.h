@@ -289,6 +289,37 @@ int oxide_decode_attention_bf16(const oxide_bf16* q, const oxide_bf16* k_cache, 
                                 uint64_t kv_heads, uint64_t max_seq, uint64_t head_dim, float scale,
                                 void* workspace, uint64_t workspace_bytes, oxide_stream_t stream);
 
+/* ---- token sampling ----------------------------------------------------------
+ * sample_next_token (src/pipeline.rs:181-205) for each row of logits
+ * [rows, vocab] (vocab <= 262144): probs = softmax_with_temperature(row,
+ * temperature) (src/tokenizer.rs:166-180: x / T, max, sum of exp(s - max),
+ * exp(s - max) / sum); then, if top_p < 1, sample_top_p (:182-211: the
+ * shortest prefix of the probabilities sorted in descending order whose
+ * running sum reaches top_p), else sample_top_k (:213-232: the first
+ * min(top_k, vocab)); r = uniforms[r] * (the prefix's sum), and tokens[row] =
+ * the first index of the prefix whose running sum reaches r.  Equal
+ * probabilities keep ascending index order (the reference's stable sort).
+ * uniforms[rows] (device, f32 in [0, 1)) are the draws the reference takes
+ * from fastrand::f32(), so the caller keeps the reference's generator.
+ * tokens[row] = OXIDE_SAMPLE_INVALID when the row's probabilities hold a NaN
+ * (a NaN logit, a scaled logit of +-inf, an all -inf row; the reference's
+ * sort panics there); vocab == 1 gives 0; top_k == 0 gives 0 (the reference's
+ * empty prefix).  probs (device f32 [rows, vocab]) may be NULL; tokens may be
+ * NULL when probs is not (softmax_with_temperature alone).  Running sums are
+ * f64 sums of per-thread f32 sums, so an index can differ from the
+ * reference's sequential f32 walk only when r falls within that walk's
+ * rounding drift of a boundary between two running sums. */
+#define OXIDE_SAMPLE_INVALID 0xFFFFFFFFu
+int oxide_sample_f32(const float* logits, uint64_t rows, uint64_t vocab, float temperature, uint64_t top_k,
+                     float top_p, const float* uniforms, uint32_t* tokens, float* probs, oxide_stream_t stream);
+int oxide_sample_bf16(const oxide_bf16* logits, uint64_t rows, uint64_t vocab, float temperature, uint64_t top_k,
+                      float top_p, const float* uniforms, uint32_t* tokens, float* probs, oxide_stream_t stream);
+/* softmax_with_temperature (src/tokenizer.rs:166-180) alone: probs [rows, vocab] f32. */
+int oxide_softmax_with_temperature_f32(const float* logits, float* probs, uint64_t rows, uint64_t vocab,
+                                       float temperature, oxide_stream_t stream);
+int oxide_softmax_with_temperature_bf16(const oxide_bf16* logits, float* probs, uint64_t rows, uint64_t vocab,
+                                        float temperature, oxide_stream_t stream);
+
 /* ---- argmax ----------------------------------------------------------------
  * Index of the largest element of each row of x[rows, cols] (cols < 2^32):
  * the lowest index among equal maxima (+0 == -0), NaN ranks below every

@@ -1,0 +1,670 @@
+// k_sample.cu -- token sampling: softmax_with_temperature and the top-k / top-p
+// selection of the reference's sample_next_token, on the GPU.
+//
+// Reference: src/pipeline.rs:181-205 takes the last row of logits, computes
+// probs = softmax_with_temperature(row, T) (src/tokenizer.rs:166-180:
+// s = x / T, m = fold(-inf, f32::max), sum = sum exp(s - m), p = exp(s - m) / sum)
+// and then, when top_p < 1, sample_top_p (:182-211), else sample_top_k
+// (:213-232).  Both sort the probabilities in descending order (a stable sort:
+// equal probabilities keep ascending index order), keep a prefix (the first k,
+// or the shortest prefix whose running sum reaches top_p), draw
+// r = u * total with u = fastrand::f32() and total the prefix's sum, and
+// return the first index of the prefix whose running sum reaches r.  Here the
+// uniform draw is an input (one per row), so the caller keeps the reference's
+// generator; everything after it runs on the device.
+//
+// Design: one CTA per row of up to 32768 logits, or a thread-block cluster of
+// 2-8 CTAs (up to 262144), each CTA holding its contiguous 32768-element
+// segment of the row in shared memory (128 KB, natural order; thread t owns
+// the float4 groups t, t + 512, ...).  No full sort:
+//   1. softmax_with_temperature with three passes over shared memory and two
+//      block reductions (max, then sum); x / T and e / sum are IEEE quotients;
+//   2. a threshold v whose candidates (every probability >= v) hold the kept
+//      prefix and number at most 2048, by bisection on the probability bits
+//      (non-negative floats order like their bit patterns): for a pivot x the
+//      count / sum of the probabilities >= x is one block reduction, and the
+//      search stops at the first pivot that is both far enough down and
+//      selective enough (usually after ~10 halvings);
+//   3. the candidates are gathered into the first CTA as 64-bit keys
+//      (probability bits << 32 | ~index: descending key order is descending
+//      probability, then ascending index -- the stable sort's order), sorted
+//      by a bitonic network, and one thread runs the reference's sequential
+//      f32 loops over them, so the token equals the reference's for the same
+//      probabilities, bit for bit.
+// When the kept prefix is longer than 2048 (top-p over a flat row, top-k >
+// 2048), step 3 is replaced by the bisection carried to the crossing element
+// itself, with f64 running sums (sums of per-thread f32 sums in a fixed
+// order): the token then equals the reference's unless r lies within the
+// reference's own sequential-sum drift of a boundary.  Equal probabilities
+// cut by the prefix are ordered by index with a bisection on the index.
+//
+// A row whose probabilities are not all numbers (a NaN logit, a scaled logit
+// of +-inf, or all -inf) yields OXIDE_SAMPLE_INVALID: the reference's sort
+// panics on NaN there.  vocab == 1 yields 0, as the reference does.  All loops
+// are bounded (bisections halve an interval, the sort has fixed stages), and
+// every branch before a barrier depends only on reduced values, which are
+// bit-identical in every thread and CTA of the cluster.
+#include <cooperative_groups.h>
+
+#include "oxide_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace oxide {
+
+constexpr int SMP_THREADS = 512;
+constexpr int SMP_WARPS = SMP_THREADS / 32;
+constexpr uint32_t SMP_SPAN = 32768;                      // logits per CTA
+constexpr uint32_t SMP_GROUPS = SMP_SPAN / 4;             // float4 groups per CTA
+constexpr int SMP_GATHER = 2048;                          // candidates walked exactly
+constexpr uint32_t SMP_FALLBACK = 0xFFFFFFFEu;            // the walk needs more than was gathered
+constexpr size_t SMP_SMEM = (size_t)SMP_SPAN * 4 + (size_t)SMP_GATHER * 8;  // 147,456 B
+
+struct SmpArgs {
+    const void* logits;
+    uint64_t rows;
+    uint32_t vocab;
+    float temperature;
+    uint64_t top_k;
+    float top_p;
+    const float* uniforms;
+    uint32_t* tokens;  // null: probabilities only
+    float* probs;      // null: not stored
+};
+
+enum { RSUM = 0, RMAX = 1, RMIN = 2 };
+
+template <int OP>
+__device__ __forceinline__ double rop(double a, double b) {
+    if (OP == RSUM) return a + b;
+    if (OP == RMAX) return a > b ? a : b;
+    return a < b ? a : b;
+}
+template <int OP>
+__device__ __forceinline__ double rident() {
+    return OP == RSUM ? 0.0 : (OP == RMAX ? -INFINITY : INFINITY);
+}
+
+// Block (and cluster) reduction of two doubles with ops OA / OB.  The warp
+// partials are double-buffered by `phase`, so one barrier per call suffices:
+// a slot is rewritten two calls later, after every reader has passed the
+// barrier of the call in between.
+template <int CL>
+struct Reducer {
+    double2* red;   // [2][SMP_WARPS] warp partials
+    double2* cred;  // [2] CTA partials (cluster only)
+    uint32_t phase;
+
+    template <int OA, int OB>
+    __device__ __forceinline__ double2 run(double a, double b) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            a = rop<OA>(a, __shfl_xor_sync(0xffffffffu, a, o));
+            b = rop<OB>(b, __shfl_xor_sync(0xffffffffu, b, o));
+        }
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        double2* slot = red + phase * SMP_WARPS;
+        if (lane == 0) slot[warp] = make_double2(a, b);
+        __syncthreads();
+        double2 r;
+        if (CL == 1) {
+            r = slot[0];
+#pragma unroll
+            for (int w = 1; w < SMP_WARPS; ++w) {
+                const double2 v = slot[w];
+                r.x = rop<OA>(r.x, v.x);
+                r.y = rop<OB>(r.y, v.y);
+            }
+        } else {
+            if (warp == 0) {
+                double2 v = lane < SMP_WARPS ? slot[lane] : make_double2(rident<OA>(), rident<OB>());
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    v.x = rop<OA>(v.x, __shfl_xor_sync(0xffffffffu, v.x, o));
+                    v.y = rop<OB>(v.y, __shfl_xor_sync(0xffffffffu, v.y, o));
+                }
+                if (lane == 0) cred[phase] = v;
+            }
+            cg::cluster_group cluster = cg::this_cluster();
+            cluster.sync();
+            r = *cluster.map_shared_rank(cred + phase, 0);
+#pragma unroll
+            for (int q = 1; q < CL; ++q) {
+                const double2 v = *cluster.map_shared_rank(cred + phase, q);
+                r.x = rop<OA>(r.x, v.x);
+                r.y = rop<OB>(r.y, v.y);
+            }
+        }
+        phase ^= 1u;
+        return r;
+    }
+};
+
+// The element at which the running measure, in (probability desc, index asc)
+// order, first reaches t.
+struct Cross {
+    float v;          // its probability
+    uint32_t idx;     // its index (when asked for)
+    double cum_sum;   // sum of the probabilities up to and including it
+    double j;         // its rank among the elements equal to v (1-based)
+    double ties;      // number of probabilities == v
+};
+
+// A threshold whose candidates hold the kept prefix (see coarse()).
+struct Coarse {
+    float v;
+    bool ok;
+    double count, c_gt, s_gt, ties;
+};
+
+// One CTA's segment of a row of probabilities in shared memory; slots past
+// the row hold -1, which no pivot >= 0 counts.
+template <int CL>
+struct Row {
+    const float4* sp;  // this CTA's segment, natural order
+    uint32_t base;     // row index of sp[0]
+    uint32_t vocab;
+    Reducer<CL>* rd;
+
+    // (sum, count) of the probabilities >= x; f32 per thread in a fixed order
+    // (monotone in the set), f64 across threads.
+    __device__ double2 measure(float x) {
+        float s = 0.0f;
+        uint32_t c = 0;
+#pragma unroll 4
+        for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+            const float4 v = sp[q];
+            if (v.x >= x) { s = fadd(s, v.x); ++c; }
+            if (v.y >= x) { s = fadd(s, v.y); ++c; }
+            if (v.z >= x) { s = fadd(s, v.z); ++c; }
+            if (v.w >= x) { s = fadd(s, v.w); ++c; }
+        }
+        return rd->template run<RSUM, RSUM>((double)s, (double)c);
+    }
+
+    // The j-th (1-based) index holding exactly v, in ascending index order.
+    __device__ uint32_t tie_index(float v, double ties, double j) {
+        if (ties == 1.0) {
+            double mi = 4294967296.0;
+            for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+                const float4 w = sp[q];
+                const double i0 = (double)(base + 4 * q);
+                if (w.x == v) mi = fmin(mi, i0);
+                if (w.y == v) mi = fmin(mi, i0 + 1.0);
+                if (w.z == v) mi = fmin(mi, i0 + 2.0);
+                if (w.w == v) mi = fmin(mi, i0 + 3.0);
+            }
+            return (uint32_t)rd->template run<RMIN, RMIN>(mi, 0.0).x;
+        }
+        // smallest I with count(p == v, index <= I) >= j
+        uint32_t lo = 0, hi = vocab - 1;
+        while (lo < hi) {
+            const uint32_t mid = lo + (hi - lo) / 2;
+            uint32_t c = 0;
+            for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+                const float4 w = sp[q];
+                const uint32_t i0 = base + 4 * q;
+                c += (w.x == v && i0 <= mid) + (w.y == v && i0 + 1 <= mid) + (w.z == v && i0 + 2 <= mid) +
+                     (w.w == v && i0 + 3 <= mid);
+            }
+            const double n = rd->template run<RSUM, RSUM>((double)c, 0.0).x;
+            if (n >= j) hi = mid;
+            else lo = mid + 1;
+        }
+        return lo;
+    }
+
+    // A value v with M(v) >= t and at most `cap` probabilities >= v, by
+    // bisection that stops at the first such pivot (the crossing value itself
+    // is not needed: the candidates >= v are sorted afterwards).  On entry
+    // M(lo) >= t > M(hi) = 0.  When the crossing value alone has more than
+    // `cap` elements >= it (a long run of equal probabilities), ok is false and
+    // v is that value, with the count and sum of the elements above it.
+    template <bool SUM>
+    __device__ Coarse coarse(double t, uint32_t lo, uint32_t hi, double c_lo, uint32_t cap) {
+        Coarse g{__uint_as_float(lo), true, c_lo, 0.0, 0.0, 0.0};
+        if (c_lo <= (double)cap) return g;
+        double c_hi = 0.0, s_hi = 0.0;
+        while (hi - lo > 1) {
+            const uint32_t mid = lo + (hi - lo) / 2;
+            const double2 m = measure(__uint_as_float(mid));
+            if ((SUM ? m.x : m.y) >= t) {
+                lo = mid;
+                c_lo = m.y;
+                if (m.y <= (double)cap) {
+                    g.v = __uint_as_float(mid);
+                    g.count = m.y;
+                    return g;
+                }
+            } else {
+                hi = mid;
+                c_hi = m.y;
+                s_hi = m.x;
+            }
+        }
+        g.ok = false;
+        g.v = __uint_as_float(lo);
+        g.count = c_lo;
+        g.c_gt = c_hi;
+        g.s_gt = s_hi;
+        g.ties = c_lo - c_hi;
+        return g;
+    }
+
+    // The crossing element itself: bisection over probability bits in
+    // [lo, hi) with M(lo) >= t > M(hi) on entry, c_lo the count of
+    // measure(lo) and (s_hi, c_hi) = measure(hi).  SUM: t is a probability
+    // mass, else a count.  j_cap (> 0) bounds the rank among ties of cap_v (a
+    // kept prefix that ends inside a run of equal probabilities).
+    template <bool SUM>
+    __device__ Cross bisect(double t, uint32_t lo, uint32_t hi, double c_lo, double s_hi, double c_hi,
+                            float cap_v, double j_cap, bool want_idx) {
+        while (hi - lo > 1) {
+            const uint32_t mid = lo + (hi - lo) / 2;
+            const double2 m = measure(__uint_as_float(mid));
+            if ((SUM ? m.x : m.y) >= t) {
+                lo = mid;
+                c_lo = m.y;
+            } else {
+                hi = mid;
+                s_hi = m.x;
+                c_hi = m.y;
+            }
+        }
+        const float v = __uint_as_float(lo);
+        const double ties = c_lo - c_hi;
+        const double vd = (double)v;
+        double j;
+        if (SUM) {
+            if (vd > 0.0) {
+                j = ceil((t - s_hi) / vd);
+                if (j < 1.0) j = 1.0;
+                if (j > ties) j = ties;
+                while (j > 1.0 && s_hi + (j - 1.0) * vd >= t) j -= 1.0;
+                while (j < ties && s_hi + j * vd < t) j += 1.0;
+            } else {
+                j = ties;
+            }
+        } else {
+            j = t - c_hi;
+            if (j < 1.0) j = 1.0;
+            if (j > ties) j = ties;
+        }
+        if (v == cap_v && j > j_cap) j = j_cap;
+        Cross x;
+        x.v = v;
+        x.j = j;
+        x.ties = ties;
+        x.cum_sum = s_hi + j * vd;
+        x.idx = want_idx ? tie_index(v, ties, j) : 0u;
+        return x;
+    }
+};
+
+__device__ __forceinline__ void bitonic_desc(unsigned long long* buf, uint32_t n) {
+    for (uint32_t k = 2; k <= n; k <<= 1) {
+        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
+            for (uint32_t i = threadIdx.x; i < n; i += SMP_THREADS) {
+                const uint32_t ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long x = buf[i], y = buf[ixj];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? x < y : x > y) {
+                        buf[i] = y;
+                        buf[ixj] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// sample_top_k / sample_top_p on the sorted keys (src/tokenizer.rs:182-232).
+__device__ uint32_t walk_sorted(const unsigned long long* buf, uint32_t n, bool whole_row, bool topp,
+                                uint64_t top_k, float top_p, float u) {
+    auto pr = [&](uint32_t i) { return __uint_as_float((uint32_t)(buf[i] >> 32)); };
+    auto ix = [&](uint32_t i) { return ~(uint32_t)buf[i]; };
+    uint32_t keep;
+    if (topp) {
+        float cumsum = 0.0f;
+        keep = 0;
+        for (uint32_t i = 0; i < n; ++i) {
+            cumsum = fadd(cumsum, pr(i));
+            if (cumsum >= top_p) {
+                keep = i + 1;
+                break;
+            }
+        }
+        if (keep == 0) {
+            if (!whole_row) return SMP_FALLBACK;
+            keep = n;
+        }
+    } else {
+        keep = (uint32_t)(top_k < n ? top_k : n);
+    }
+    float total = 0.0f;
+    for (uint32_t i = 0; i < keep; ++i) total = fadd(total, pr(i));
+    const float r = fmul(u, total);
+    float cum = 0.0f;
+    for (uint32_t i = 0; i < keep; ++i) {
+        cum = fadd(cum, pr(i));
+        if (cum >= r) return ix(i);
+    }
+    return ix(keep - 1);
+}
+
+__device__ __forceinline__ float load_logit(const float* x, uint64_t i) { return __ldg(x + i); }
+__device__ __forceinline__ float load_logit(const bf16_t* x, uint64_t i) { return bf16_to_f32(__ldg(x + i)); }
+
+template <typename T, int CL>
+__global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* sp = reinterpret_cast<float*>(smem);                                           // [SMP_SPAN]
+    unsigned long long* gbuf = reinterpret_cast<unsigned long long*>(smem + SMP_SPAN * 4);  // [SMP_GATHER]
+    float4* sp4 = reinterpret_cast<float4*>(sp);
+    __shared__ double2 red[2 * SMP_WARPS];
+    __shared__ double2 cred[2];
+    __shared__ uint32_t gcount, gresult;
+    Reducer<CL> rd{red, cred, 0u};
+    const uint32_t crank = CL == 1 ? 0u : (uint32_t)cg::this_cluster().block_rank();
+    if (threadIdx.x == 0) gcount = 0;  // visible to the cluster after the first reduction's barrier
+    unsigned long long* gbuf0 = gbuf;
+    uint32_t* gcount0 = &gcount;
+    uint32_t* gresult0 = &gresult;
+    if (CL > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        gbuf0 = cluster.map_shared_rank(gbuf, 0);
+        gcount0 = cluster.map_shared_rank(&gcount, 0);
+        gresult0 = cluster.map_shared_rank(&gresult, 0);
+    }
+    auto group_sync = [&]() {
+        if (CL > 1) cg::this_cluster().sync();
+        else __syncthreads();
+    };
+    Row<CL> row;
+    row.sp = sp4;
+    row.base = crank * SMP_SPAN;
+    row.vocab = a.vocab;
+    row.rd = &rd;
+    const uint32_t seg = a.vocab > row.base ? min(a.vocab - row.base, SMP_SPAN) : 0u;  // valid slots
+    const RowDiv div_t(a.temperature);
+    const uint64_t groups = gridDim.x / CL;
+    for (uint64_t r = blockIdx.x / CL; r < a.rows; r += groups) {
+        const T* x = static_cast<const T*>(a.logits) + r * a.vocab + row.base;
+        // s = x / T (the IEEE quotient: RowDiv for the row-constant divisor);
+        // row max (NaN skipped, as f32::max does) and a NaN flag
+        float mx = -INFINITY;
+        bool nan = false;
+#pragma unroll 4
+        for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+            float v[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) v[c] = 4 * q + c < seg ? load_logit(x, 4 * q + c) : 0.0f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (4 * q + c < seg) {
+                    v[c] = div_t(v[c]);
+                    nan |= v[c] != v[c];
+                    mx = fmaxf(mx, v[c]);
+                } else {
+                    v[c] = -INFINITY;
+                }
+            }
+            sp4[q] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        const double2 mr = rd.template run<RMAX, RMAX>((double)mx, nan ? 1.0 : 0.0);
+        const float m = (float)mr.x;
+        const bool invalid = mr.y != 0.0 || isinf(m);  // exp(inf - inf) / exp(-inf + inf) is NaN
+        float ls = 0.0f;
+#pragma unroll 4
+        for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+            float4 w = sp4[q];
+            float* v = reinterpret_cast<float*>(&w);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (4 * q + c < seg) {
+                    v[c] = expf(fsub(v[c], m));
+                    ls = fadd(ls, v[c]);
+                }
+            }
+            sp4[q] = w;
+        }
+        const float S = (float)rd.template run<RSUM, RSUM>((double)ls, 0.0).x;
+        const RowDiv div_s(S);
+        float* prow = a.probs ? a.probs + r * a.vocab + row.base : nullptr;
+#pragma unroll 4
+        for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+            float4 w = sp4[q];
+            float* v = reinterpret_cast<float*>(&w);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (4 * q + c < seg) {
+                    v[c] = div_s(v[c]);
+                    if (prow) prow[4 * q + c] = v[c];
+                } else {
+                    v[c] = -1.0f;
+                }
+            }
+            sp4[q] = w;
+        }
+        __syncthreads();  // the probabilities are in place for every thread
+        if (!a.tokens) continue;
+        // Every probability is <= 1, so M(bits(1) + 1) = 0.  A threshold t <= 0
+        // is reached by the first element, as is the smallest positive double:
+        // t is raised to that.
+        constexpr uint32_t top = 0x3F800001u;
+        constexpr double tiny = 4.9406564584124654e-324;
+        const bool topp = a.top_p < 1.0f;
+        const uint64_t k_top = a.top_k < a.vocab ? a.top_k : a.vocab;
+        uint32_t tok = 0;
+        bool done = true;
+        if (a.vocab == 1) {
+            tok = 0;
+        } else if (invalid) {
+            tok = OXIDE_SAMPLE_INVALID;
+        } else if (!topp && k_top == 0) {
+            tok = 0;  // the reference's empty prefix returns 0
+        } else {
+            // the set to walk exactly: the probabilities > gv and those == gv
+            // at indices <= gidx, at most SMP_GATHER of them
+            uint32_t gidx = 0xFFFFFFFFu;
+            bool short_prefix;
+            double tq = 0.0;
+            Coarse g;
+            if (topp) {
+                // a sequential f32 running sum of n terms is within
+                // gam = n 2^-24 / (1 - n 2^-24) of the exact one, so the reference
+                // reaches top_p no later than the exact sum reaches top_p (1 + 2 gam)
+                const double nu = (double)a.vocab * 5.9604644775390625e-8;
+                const double gam = nu / (1.0 - nu);
+                tq = fmax((double)a.top_p, tiny) * (1.0 + 2.0 * gam);
+                const double2 all = row.measure(0.0f);
+                if (tq >= all.x) {  // the whole row
+                    g = Coarse{0.0f, true, all.y, 0.0, 0.0, 0.0};
+                    short_prefix = all.y <= (double)SMP_GATHER;
+                } else {
+                    g = row.template coarse<true>(tq, 0u, top, all.y, SMP_GATHER);
+                    short_prefix = g.ok;
+                }
+            } else {
+                g = row.template coarse<false>((double)k_top, 0u, top, (double)a.vocab, SMP_GATHER);
+                short_prefix = g.ok;
+            }
+            const float gv = g.v;
+            if (!g.ok) {
+                // the prefix ends inside a run of equal probabilities gv longer
+                // than SMP_GATHER: keep the elements above gv and the first m
+                // of the run in index order (the stable sort's order)
+                double mm = topp ? (gv > 0.0f ? ceil((tq - g.s_gt) / (double)gv) + 1.0 : g.ties)
+                                 : (double)k_top - g.c_gt;
+                mm = fmin(fmax(mm, 1.0), g.ties);
+                if (g.c_gt + mm <= (double)SMP_GATHER) {
+                    gidx = row.tie_index(gv, g.ties, mm);
+                    short_prefix = true;
+                }
+            }
+            done = false;
+            if (short_prefix) {
+                for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+                    const float4 w = sp4[q];
+                    const float v[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint32_t i = row.base + 4 * q + c;
+                        if (v[c] > gv || (v[c] == gv && i <= gidx)) {
+                            const uint32_t pos = atomicAdd(gcount0, 1u);
+                            if (pos < (uint32_t)SMP_GATHER)
+                                gbuf0[pos] = ((unsigned long long)__float_as_uint(v[c]) << 32) |
+                                             (unsigned long long)(~i);
+                        }
+                    }
+                }
+                group_sync();
+                if (crank == 0) {
+                    const uint32_t n = gcount < (uint32_t)SMP_GATHER ? gcount : (uint32_t)SMP_GATHER;
+                    uint32_t np2 = 1;
+                    while (np2 < n) np2 <<= 1;
+                    for (uint32_t i = n + threadIdx.x; i < np2; i += SMP_THREADS) gbuf[i] = 0ull;
+                    __syncthreads();
+                    bitonic_desc(gbuf, np2);
+                    if (threadIdx.x == 0) {
+                        gresult = walk_sorted(gbuf, n, n == a.vocab, topp, a.top_k, a.top_p, a.uniforms[r]);
+                        gcount = 0;
+                    }
+                }
+                group_sync();
+                tok = *gresult0;
+                done = tok != SMP_FALLBACK;
+            }
+        }
+        if (!done) {
+            // Long prefixes: the f64 running sums of the bisection stand in for
+            // the sequential walk.  The kept prefix ends at (kv, kj-th tie);
+            // kv < 0: the whole row.
+            float kv = -1.0f;
+            double kj = 0.0, kties = 0.0, total = 0.0;
+            if (topp) {  // sample_top_p: shortest prefix whose sum reaches top_p
+                const double t = fmax((double)a.top_p, tiny);
+                const double2 all = row.measure(0.0f);
+                total = all.x;
+                if (all.x >= t) {
+                    const Cross c = row.template bisect<true>(t, 0u, top, all.y, 0.0, 0.0, -1.0f, 0.0, false);
+                    kv = c.v;
+                    kj = c.j;
+                    kties = c.ties;
+                    total = c.cum_sum;
+                }
+            } else {  // sample_top_k: the first min(k, vocab) elements
+                const Cross c = row.template bisect<false>((double)k_top, 0u, top, (double)a.vocab, 0.0, 0.0,
+                                                           -1.0f, 0.0, false);
+                kv = c.v;
+                kj = c.j;
+                kties = c.ties;
+                total = c.cum_sum;
+            }
+            // r = u * total in f32, as the reference computes it; the walk
+            // never passes the prefix's last element
+            double t = (double)fmul(a.uniforms[r], (float)total);
+            t = fmax(fmin(t, total), tiny);
+            const uint32_t lo = kv >= 0.0f ? __float_as_uint(kv) : 0u;
+            const double2 at = row.measure(__uint_as_float(lo));
+            if (at.x >= t || kv < 0.0f)
+                tok = row.template bisect<true>(fmin(t, at.x), lo, top, at.y, 0.0, 0.0, kv, kj, true).idx;
+            else  // rounding left r above the prefix's measure: its last element
+                tok = row.tie_index(kv, kties, kj);
+        }
+        if (crank == 0 && threadIdx.x == 0) a.tokens[r] = tok;
+        __syncthreads();  // the segment is rewritten by the next row
+    }
+    if (CL > 1) cg::this_cluster().sync();  // peers' slots stay valid until read
+}
+
+template <typename T>
+static int sample_entry(const char* name, const T* logits, uint64_t rows, uint64_t vocab, float temperature,
+                        uint64_t top_k, float top_p, const float* uniforms, uint32_t* tokens, float* probs,
+                        cudaStream_t st) {
+    OXIDE_INJECT(name);
+    if (rows == 0) return OXIDE_OK;
+    OXIDE_REQUIRE(tokens || probs, name, "null pointer");
+    OXIDE_REQUIRE(!tokens || uniforms, name, "uniforms must be given when tokens are sampled");
+    if (vocab == 0) {  // empty rows: the reference's empty prefix returns 0
+        const cudaError_t e = tokens ? cudaMemsetAsync(tokens, 0, rows * sizeof(uint32_t), st) : cudaSuccess;
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(OXIDE_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+        }
+        return OXIDE_OK;
+    }
+    OXIDE_REQUIRE(logits, name, "null pointer");
+    OXIDE_REQUIRE(vocab <= 8ull * SMP_SPAN, name, "vocab must be <= 262144");
+    OXIDE_REQUIRE(rows <= UINT64_MAX / vocab, name, "logits size overflows");
+    int cl = 1;
+    while ((uint64_t)cl * SMP_SPAN < vocab) cl *= 2;
+    const uint64_t cap = ((uint64_t)1 << 30) / (uint64_t)cl;
+    const uint64_t groups = rows < cap ? rows : cap;
+    SmpArgs a{logits, rows, (uint32_t)vocab, temperature, top_k, top_p, uniforms, tokens, probs};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(groups * cl), 1, 1);
+    cfg.blockDim = dim3(SMP_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMP_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const void* kern;
+    switch (cl) {
+        case 1: kern = reinterpret_cast<const void*>(sample_kernel<T, 1>); break;
+        case 2: kern = reinterpret_cast<const void*>(sample_kernel<T, 2>); break;
+        case 4: kern = reinterpret_cast<const void*>(sample_kernel<T, 4>); break;
+        default: kern = reinterpret_cast<const void*>(sample_kernel<T, 8>); break;
+    }
+    if (!ensure_dyn_smem(kern, SMP_SMEM))
+        return set_error(OXIDE_ERR_LAUNCH, "%s: cannot reserve %zu bytes of shared memory", name, SMP_SMEM);
+    cudaError_t e;
+    switch (cl) {
+        case 1: e = cudaLaunchKernelEx(&cfg, sample_kernel<T, 1>, a); break;
+        case 2: e = cudaLaunchKernelEx(&cfg, sample_kernel<T, 2>, a); break;
+        case 4: e = cudaLaunchKernelEx(&cfg, sample_kernel<T, 4>, a); break;
+        default: e = cudaLaunchKernelEx(&cfg, sample_kernel<T, 8>, a); break;
+    }
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(OXIDE_ERR_LAUNCH, "%s: launch failed: %s", name, cudaGetErrorString(e));
+    }
+    return check_launch(name);
+}
+
+}  // namespace oxide
+
+using oxide::bf16_t;
+
+extern "C" {
+
+int oxide_sample_f32(const float* logits, uint64_t rows, uint64_t vocab, float temperature, uint64_t top_k,
+                     float top_p, const float* uniforms, uint32_t* tokens, float* probs, oxide_stream_t stream) {
+    return oxide::sample_entry<float>("oxide_sample_f32", logits, rows, vocab, temperature, top_k, top_p, uniforms,
+                                      tokens, probs, stream);
+}
+int oxide_sample_bf16(const oxide_bf16* logits, uint64_t rows, uint64_t vocab, float temperature, uint64_t top_k,
+                      float top_p, const float* uniforms, uint32_t* tokens, float* probs, oxide_stream_t stream) {
+    return oxide::sample_entry<bf16_t>("oxide_sample_bf16", reinterpret_cast<const bf16_t*>(logits), rows, vocab,
+                                       temperature, top_k, top_p, uniforms, tokens, probs, stream);
+}
+int oxide_softmax_with_temperature_f32(const float* logits, float* probs, uint64_t rows, uint64_t vocab,
+                                       float temperature, oxide_stream_t stream) {
+    return oxide::sample_entry<float>("oxide_softmax_with_temperature_f32", logits, rows, vocab, temperature, 0,
+                                      1.0f, nullptr, nullptr, probs, stream);
+}
+int oxide_softmax_with_temperature_bf16(const oxide_bf16* logits, float* probs, uint64_t rows, uint64_t vocab,
+                                        float temperature, oxide_stream_t stream) {
+    return oxide::sample_entry<bf16_t>("oxide_softmax_with_temperature_bf16",
+                                       reinterpret_cast<const bf16_t*>(logits), rows, vocab, temperature, 0, 1.0f,
+                                       nullptr, nullptr, probs, stream);
+}
+
+}  // extern "C"

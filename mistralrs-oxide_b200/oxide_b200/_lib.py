@@ -65,6 +65,10 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_decode_attention_workspace_bytes": (u64, [u64, u64, u64, u64]),
     "oxide_decode_attention_f32": (i32, [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, vp, u64, vp]),
     "oxide_decode_attention_bf16": (i32, [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, vp, u64, vp]),
+    "oxide_sample_f32": (i32, [vp, u64, u64, f32, u64, f32, vp, vp, vp, vp]),
+    "oxide_sample_bf16": (i32, [vp, u64, u64, f32, u64, f32, vp, vp, vp, vp]),
+    "oxide_softmax_with_temperature_f32": (i32, [vp, vp, u64, u64, f32, vp]),
+    "oxide_softmax_with_temperature_bf16": (i32, [vp, vp, u64, u64, f32, vp]),
     "oxide_reduce_rows_f32": (i32, [i32, vp, u64, u64, vp, vp]),
     "oxide_reduce_rows_bf16": (i32, [i32, vp, u64, u64, vp, vp]),
     "oxide_reduce_workspace_bytes": (u64, [u64]),
@@ -85,6 +89,7 @@ OK, ERR_INVALID_ARG, ERR_LAUNCH, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE, ERR_I
 ADD, SUB, MUL, DIV = 0, 1, 2, 3
 RELU, GELU, GELU_QUICK, SIGMOID, TANH, EXP, LOG, SQRT, POW, CLAMP, NEG, ABS = range(12)
 RED_SUM, RED_MAX, RED_SUMSQ = 0, 1, 2
+SAMPLE_INVALID = 0xFFFFFFFF
 
 _lock = threading.Lock()
 _lib: C.CDLL | None = None

@@ -93,6 +93,25 @@ def build(op: str, rows: int | None, dev):
         run = lambda s: ops.decode_attention(s[0], s[1], s[2], tl, workspace=ws, out=s[3])  # noqa: E731
         nb = int(np.sum(np.minimum(lens, c.keys))) * kvh * c.head_dim * es * 2 + 2 * c.batch * c.heads * c.head_dim * es
         return mk, run, nb, [c.batch, c.heads, kvh, c.keys, c.head_dim]
+    if op == "softmax_temperature_f32_c3":
+        # softmax_with_temperature alone over the C3 logits [64, 32000]
+        c = C3()
+        R = rows or c.logit_rows
+        out = torch.empty(R, c.vocab, dtype=torch.float32, device=dev)
+        mk = lambda: (rn(R, c.vocab) * 3,)  # noqa: E731
+        run = lambda s: ops.softmax_with_temperature(s[0], 0.7, out=out)  # noqa: E731
+        return mk, run, 2 * R * c.vocab * 4, [R, c.vocab]
+    if op in ("sample_topk_f32_c3", "sample_topp_f32_c3"):
+        # token sampling over the C3 logits [64, 32000]: the reference's defaults
+        # (T = 1, top-k 50), and top-p 0.9 at T = 0.7
+        c = C3()
+        R = rows or c.logit_rows
+        topk = op == "sample_topk_f32_c3"
+        u = torch.rand(R, generator=g, device=dev)
+        mk = lambda: (rn(R, c.vocab) * 3,)  # noqa: E731
+        run = lambda s: ops.sample_next_token(s[0], u, 1.0 if topk else 0.7, 50,  # noqa: E731
+                                              1.0 if topk else 0.9)
+        return mk, run, R * c.vocab * 4 + R * 8, [R, c.vocab]
     if op == "argmax_f32_c3":
         c = C3()
         R = rows or c.logit_rows
@@ -206,7 +225,8 @@ OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softma
        "argmax_f32_c3", "rope_bf16_c4", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
        "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5",
        "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5",
-       "repeat_kv_bf16_c5", "kv_append_bf16_c5", "decode_attn_bf16_c3", "decode_attn_f32_c3"]
+       "repeat_kv_bf16_c5", "kv_append_bf16_c5", "decode_attn_bf16_c3", "decode_attn_f32_c3",
+       "softmax_temperature_f32_c3", "sample_topk_f32_c3", "sample_topp_f32_c3"]
 
 
 def main(argv=None):

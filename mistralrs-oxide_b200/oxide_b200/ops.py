@@ -10,6 +10,7 @@ op is one call into liboxide_b200.so.
 """
 from __future__ import annotations
 
+import math
 from typing import Optional, Sequence
 
 import torch
@@ -472,3 +473,42 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     call(f"oxide_decode_attention_{_sfx(q)}", _p(q), _p(k_cache), _p(v_cache), _p(lens), _p(out), b, hq, hkv,
          m, d, float(scale), _p(workspace), workspace.numel(), _stream())
     return out
+
+
+# ---- token sampling (src/tokenizer.rs:166-232, src/pipeline.rs:181-205) ----
+SAMPLE_INVALID = -1  # OXIDE_SAMPLE_INVALID seen through an int32 tensor
+
+
+def softmax_with_temperature(logits: torch.Tensor, temperature: float,
+                             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """src/tokenizer.rs:166-180 over the last dim -> f32 probabilities."""
+    _check(logits, out)
+    vocab = logits.shape[-1]
+    if out is None:
+        out = torch.empty(logits.shape, dtype=torch.float32, device=logits.device)
+    call(f"oxide_softmax_with_temperature_{_sfx(logits)}", _p(logits), _p(out),
+         math.prod(logits.shape[:-1]), vocab, float(temperature), _stream())
+    return out
+
+
+def sample_next_token(logits: torch.Tensor, uniforms: torch.Tensor, temperature: float = 1.0,
+                      top_k: int = 50, top_p: float = 1.0,
+                      probs_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """sample_next_token (src/pipeline.rs:181-205) for every row of logits
+    [..., vocab]: softmax_with_temperature, then sample_top_p when top_p < 1,
+    else sample_top_k, with uniforms[row] (f32 in [0, 1), on the device) as
+    the reference's fastrand::f32() draw.  Returns int32 token ids;
+    SAMPLE_INVALID (-1) marks a row whose probabilities hold a NaN (the
+    reference's sort panics there).  The defaults are InferenceParams::default's
+    (src/tokenizer.rs:153-162)."""
+    _check(logits, uniforms, probs_out)
+    vocab = logits.shape[-1]
+    rows = math.prod(logits.shape[:-1])
+    if probs_out is not None and (probs_out.dtype != torch.float32 or probs_out.numel() != rows * vocab):
+        raise ValueError("probs_out must be f32 with the logits' element count")
+    if uniforms.dtype != torch.float32 or uniforms.numel() != rows:
+        raise ValueError(f"uniforms must be f32 with one value per row ({rows})")
+    tokens = torch.empty(logits.shape[:-1], dtype=torch.int32, device=logits.device)
+    call(f"oxide_sample_{_sfx(logits)}", _p(logits), rows, vocab, float(temperature), int(top_k),
+         float(top_p), _p(uniforms), _p(tokens), _p(probs_out), _stream())
+    return tokens

@@ -68,6 +68,10 @@ def lib() -> C.CDLL:
             "orc_repeat_kv": [vp, vp, u64, u64, u64, u64, u64, u64],
             "orc_decode_attention_f32": [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, i32],
             "orc_decode_attention_bf16": [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, i32],
+            "orc_softmax_temperature_f32": [vp, u64, u64, f32, vp, i32],
+            "orc_softmax_temperature_bf16": [vp, u64, u64, f32, vp, i32],
+            "orc_sample_f32": [vp, u64, u64, f32, u64, f32, vp, vp, vp, i32],
+            "orc_sample_bf16": [vp, u64, u64, f32, u64, f32, vp, vp, vp, i32],
         }
         for name, args in sig.items():
             fn = getattr(h, name)
@@ -80,6 +84,8 @@ def lib() -> C.CDLL:
         h.orc_reduce_seq_f32.argtypes = [i32, vp, u64]
         h.orc_reduce_seq_f32.restype = C.c_float
         h.orc_max_threads.restype = i32
+        h.orc_sample_probs.argtypes = [vp, u64, u64, f32, f32]
+        h.orc_sample_probs.restype = C.c_uint32
         h.orc_kv_append.argtypes = [vp, vp, vp, vp, u64, u64, u64, u64, u64, u64, u64]
         h.orc_kv_append.restype = i32
         h.orc_f32_to_bf16.argtypes = [C.c_float]
@@ -205,6 +211,41 @@ def decode_attention(q, kc, vc, lens=None, scale=None, threads=1):
     getattr(lib(), f"orc_decode_attention_{_sfx(q)}")(_p(q), _p(kc), _p(vc), None if lp is None else _p(lp),
                                                       _p(out), b, hq, hkv, m, d, float(scale), threads)
     return out
+
+
+SAMPLE_INVALID = 0xFFFFFFFF
+
+
+def softmax_with_temperature(logits, temperature, threads=1):
+    """src/tokenizer.rs:166-180 on each row of logits [rows, vocab] (f32 or
+    bf16 bits); returns f32 probabilities."""
+    x = _c(logits)
+    vocab = x.shape[-1]
+    out = np.empty(x.shape, np.float32)
+    getattr(lib(), f"orc_softmax_temperature_{_sfx(x)}")(_p(x), x.size // max(vocab, 1), vocab,
+                                                          float(temperature), _p(out), threads)
+    return out
+
+
+def sample_probs(probs, top_k, top_p, u):
+    """sample_top_p / sample_top_k (src/tokenizer.rs:182-232) on one row of
+    probabilities with the uniform draw u."""
+    p = _c(np.asarray(probs, np.float32))
+    return int(lib().orc_sample_probs(_p(p), p.size, int(top_k), float(top_p), float(u)))
+
+
+def sample(logits, temperature, top_k, top_p, uniforms, threads=1):
+    """sample_next_token (src/pipeline.rs:181-205) per row of logits
+    [rows, vocab]; returns (tokens uint32 [rows], probs f32 [rows, vocab])."""
+    x = _c(logits)
+    vocab = x.shape[-1]
+    rows = x.size // max(vocab, 1)
+    u = _c(np.asarray(uniforms, np.float32).reshape(rows))
+    tok = np.empty(rows, np.uint32)
+    probs = np.empty((rows, vocab), np.float32)
+    getattr(lib(), f"orc_sample_{_sfx(x)}")(_p(x), rows, vocab, float(temperature), int(top_k), float(top_p),
+                                             _p(u), _p(tok), _p(probs), threads)
+    return tok, probs
 
 
 def rms_norm(x, w, eps, threads=1):

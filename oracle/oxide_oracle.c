@@ -13,6 +13,7 @@
 #include "oxide_oracle.h"
 
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
 #include <omp.h>
@@ -670,5 +671,107 @@ void orc_decode_attention_bf16(const uint16_t* q, const uint16_t* kc, const uint
         decode_attn_one(qf, kf, vf, of, len, head_dim, scale, p);
         for (uint64_t i = 0; i < head_dim; ++i) out[bh * head_dim + i] = F2B(of[i]);
         __builtin_free(buf);
+    }
+}
+
+/* ---- token sampling (src/tokenizer.rs:166-232, src/pipeline.rs:181-205) ---- */
+/* softmax_with_temperature, src/tokenizer.rs:166-180 */
+static void softmax_temperature_row(const float* x, uint64_t n, float t, float* p) {
+    float m = -INFINITY;
+    for (uint64_t i = 0; i < n; ++i) m = fmaxf(m, x[i] / t); /* fold(NEG_INFINITY, f32::max) */
+    float sum = 0.0f;
+    for (uint64_t i = 0; i < n; ++i) sum += expf(x[i] / t - m);
+    for (uint64_t i = 0; i < n; ++i) p[i] = expf(x[i] / t - m) / sum;
+}
+
+void orc_softmax_temperature_f32(const float* x, uint64_t rows, uint64_t vocab, float temperature,
+                                 float* probs, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r)
+        softmax_temperature_row(x + r * vocab, vocab, temperature, probs + r * vocab);
+}
+
+void orc_softmax_temperature_bf16(const uint16_t* x, uint64_t rows, uint64_t vocab, float temperature,
+                                  float* probs, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        float* row = probs + r * vocab;
+        for (uint64_t i = 0; i < vocab; ++i) row[i] = B2F(x[r * vocab + i]); /* to_f32_vec */
+        softmax_temperature_row(row, vocab, temperature, row);
+    }
+}
+
+typedef struct {
+    uint32_t idx;
+    float p;
+} orc_prob_t;
+
+/* sort_by(|a, b| b.1.partial_cmp(&a.1)) is a stable sort: descending by
+ * probability, equal probabilities keep ascending index order. */
+static int prob_desc_cmp(const void* a, const void* b) {
+    const orc_prob_t* x = (const orc_prob_t*)a;
+    const orc_prob_t* y = (const orc_prob_t*)b;
+    if (x->p > y->p) return -1;
+    if (x->p < y->p) return 1;
+    return x->idx < y->idx ? -1 : (x->idx > y->idx ? 1 : 0);
+}
+
+uint32_t orc_sample_probs(const float* probs, uint64_t vocab, uint64_t top_k, float top_p, float u) {
+    if (vocab >= 2)
+        for (uint64_t i = 0; i < vocab; ++i)
+            if (isnan(probs[i])) return ORC_SAMPLE_INVALID; /* partial_cmp(..).unwrap() panics */
+    orc_prob_t* s = (orc_prob_t*)malloc((vocab ? vocab : 1) * sizeof(orc_prob_t));
+    for (uint64_t i = 0; i < vocab; ++i) {
+        s[i].idx = (uint32_t)i;
+        s[i].p = probs[i];
+    }
+    qsort(s, vocab, sizeof(orc_prob_t), prob_desc_cmp);
+    uint64_t keep;
+    if (top_p < 1.0f) { /* sample_top_p, src/tokenizer.rs:182-211 */
+        float cumsum = 0.0f;
+        keep = vocab;
+        for (uint64_t i = 0; i < vocab; ++i) {
+            cumsum += s[i].p;
+            if (cumsum >= top_p) {
+                keep = i + 1;
+                break;
+            }
+        }
+    } else { /* sample_top_k, src/tokenizer.rs:213-232 */
+        keep = top_k < vocab ? top_k : vocab;
+    }
+    float total = 0.0f;
+    for (uint64_t i = 0; i < keep; ++i) total += s[i].p;
+    const float r = u * total;
+    uint32_t tok = keep ? s[keep - 1].idx : 0u; /* last().map(..).unwrap_or(0) */
+    float cum = 0.0f;
+    for (uint64_t i = 0; i < keep; ++i) {
+        cum += s[i].p;
+        if (cum >= r) {
+            tok = s[i].idx;
+            break;
+        }
+    }
+    free(s);
+    return tok;
+}
+
+void orc_sample_f32(const float* logits, uint64_t rows, uint64_t vocab, float temperature, uint64_t top_k,
+                    float top_p, const float* uniforms, uint32_t* tokens, float* probs, int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        float* p = probs ? probs + r * vocab : (float*)malloc((vocab ? vocab : 1) * sizeof(float));
+        softmax_temperature_row(logits + r * vocab, vocab, temperature, p);
+        tokens[r] = orc_sample_probs(p, vocab, top_k, top_p, uniforms[r]);
+        if (!probs) free(p);
+    }
+}
+
+void orc_sample_bf16(const uint16_t* logits, uint64_t rows, uint64_t vocab, float temperature,
+                     uint64_t top_k, float top_p, const float* uniforms, uint32_t* tokens, float* probs,
+                     int threads) {
+    OMP_FOR for (uint64_t r = 0; r < rows; ++r) {
+        float* p = probs ? probs + r * vocab : (float*)malloc((vocab ? vocab : 1) * sizeof(float));
+        for (uint64_t i = 0; i < vocab; ++i) p[i] = B2F(logits[r * vocab + i]);
+        softmax_temperature_row(p, vocab, temperature, p);
+        tokens[r] = orc_sample_probs(p, vocab, top_k, top_p, uniforms[r]);
+        if (!probs) free(p);
     }
 }

@@ -162,6 +162,27 @@ void orc_decode_attention_bf16(const uint16_t* q, const uint16_t* kc, const uint
                                uint64_t kv_heads, uint64_t max_seq, uint64_t head_dim, float scale,
                                int threads);
 
+/* Token sampling, src/pipeline.rs:181-205 (sample_next_token) on one row of
+ * logits: probs = softmax_with_temperature(row, T) (src/tokenizer.rs:166-180:
+ * s = x / T, m = fold(-inf, f32::max), sum = sequential sum of exp(s - m),
+ * p = exp(s - m) / sum), then top_p < 1 ? sample_top_p (:182-211) :
+ * sample_top_k (:213-232): a stable descending sort by probability, the kept
+ * prefix, total = its sequential f32 sum, r = u * total, and the first index
+ * whose sequential cumulative sum reaches r.  u is the uniform draw the
+ * reference takes from fastrand::f32().  A row whose probabilities hold a NaN
+ * (vocab >= 2) yields ORC_SAMPLE_INVALID: the reference's sort panics there. */
+#define ORC_SAMPLE_INVALID 0xFFFFFFFFu
+void orc_softmax_temperature_f32(const float* x, uint64_t rows, uint64_t vocab, float temperature,
+                                 float* probs, int threads);
+void orc_softmax_temperature_bf16(const uint16_t* x, uint64_t rows, uint64_t vocab, float temperature,
+                                  float* probs, int threads);
+uint32_t orc_sample_probs(const float* probs, uint64_t vocab, uint64_t top_k, float top_p, float u);
+void orc_sample_f32(const float* logits, uint64_t rows, uint64_t vocab, float temperature, uint64_t top_k,
+                    float top_p, const float* uniforms, uint32_t* tokens, float* probs, int threads);
+void orc_sample_bf16(const uint16_t* logits, uint64_t rows, uint64_t vocab, float temperature,
+                     uint64_t top_k, float top_p, const float* uniforms, uint32_t* tokens, float* probs,
+                     int threads);
+
 int orc_max_threads(void);
 
 #ifdef __cplusplus

@@ -111,3 +111,56 @@ def rms_norm_exact(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
 def assert_ulp(got: np.ndarray, ref: np.ndarray, max_ulp: int):
     d = ulp_bf16(got, ref) if got.dtype == np.uint16 else ulp_f32(got, ref)
     assert d.max(initial=0) <= max_ulp, f"max {d.max()} ulp (> {max_ulp}) at {np.argmax(d)}"
+
+
+SAMPLE_INVALID = 0xFFFFFFFF
+
+
+def sample_exact(p, top_k, top_p, u):
+    """The reference's selection (sample_top_p / sample_top_k,
+    src/tokenizer.rs:182-232) in exact (f64) arithmetic on one row of f32
+    probabilities.  Returns (token, margin): margin is the distance, relative
+    to the row's total, between a deciding threshold (top_p for the prefix, r
+    for the walk) and the nearest running sum -- a result computed with
+    rounded sums can differ only when the margin is within that rounding."""
+    p = np.asarray(p, np.float32).ravel()
+    n = p.size
+    if n == 0:
+        return 0, np.inf
+    if n >= 2 and np.isnan(p).any():
+        return SAMPLE_INVALID, np.inf
+    order = np.argsort(-p.astype(np.float64), kind="stable")
+    c = np.cumsum(p[order].astype(np.float64))
+    scale = max(float(c[-1]), 1e-300)
+    margin = np.inf
+    if np.float32(top_p) < np.float32(1.0):
+        tp = float(np.float32(top_p))
+        i = int(np.searchsorted(c, tp, side="left"))
+        keep = n if i >= n else i + 1
+        near = [c[j] for j in (i - 1, i) if 0 <= j < n]
+        margin = min(margin, min(abs(tp - x) for x in near) / scale)
+    else:
+        keep = min(int(top_k), n)
+    if keep == 0:
+        return 0, margin
+    total = float(c[keep - 1])
+    r = min(float(np.float32(np.float32(u) * np.float32(total))), total)
+    j = min(int(np.searchsorted(c[:keep], r, side="left")), keep - 1)
+    near = [c[x] for x in (j - 1, j) if 0 <= x < keep]
+    margin = min(margin, min(abs(r - x) for x in near) / scale)
+    return int(order[j]), margin
+
+
+def in_drift_band(tok, ref, p_ref):
+    """The two tokens are at most one sorted position apart, or the mass
+    strictly between them lies within the rounding drift of the reference's
+    sequential f32 running sums (n 2^-24 of the total, doubled for the kept
+    prefix's total and the walk, and doubled again for the other side)."""
+    p_ref = np.asarray(p_ref, np.float32)
+    n = p_ref.size
+    order = np.argsort(-p_ref.astype(np.float64), kind="stable")
+    pos = np.empty(n, np.int64)
+    pos[order] = np.arange(n)
+    c = np.cumsum(p_ref[order].astype(np.float64))
+    lo, hi = sorted((int(pos[tok]), int(pos[ref])))
+    return hi - lo <= 1 or c[hi - 1] - c[lo] <= 4 * n * 2.0 ** -24 * c[-1]

@@ -448,6 +448,44 @@ DEVICE_TEST(repeat_kv_and_kv_cache_match_oracle) {
            "Layer index 2 out of range for 2 layers");
 }
 
+DEVICE_TEST(decode_attention_and_sampling_match_oracle) {
+    // one decode step over a cache of 40 positions, 8 query heads on 2 kv heads
+    const size_t b = 2, hq = 8, hkv = 2, m = 40, d = 128;
+    const auto q = randn(b * hq * d, 40), kc = randn(b * hkv * m * d, 41), vc = randn(b * hkv * m * d, 42);
+    const std::vector<int32_t> lens = {40, 17};
+    int32_t* dl = nullptr;
+    EXPECT(cudaMalloc(&dl, sizeof(int32_t) * b) == cudaSuccess);
+    EXPECT(cudaMemcpy(dl, lens.data(), sizeof(int32_t) * b, cudaMemcpyHostToDevice) == cudaSuccess);
+    const Tensor out = unwrap(ops::decode_attention(dev(q, {b, hq, d}), dev(kc, {b, hkv, m, d}),
+                                                    dev(vc, {b, hkv, m, d}), dl));
+    std::vector<float> ref(q.size());
+    orc_decode_attention_f32(q.data(), kc.data(), vc.data(), lens.data(), ref.data(), b, hq, hkv, m, d,
+                             1.0f / std::sqrt((float)d), 1);
+    const auto got = host(out);
+    for (size_t i = 0; i < got.size(); ++i) EXPECT(std::fabs(got[i] - ref[i]) <= 1e-5f * (1.0f + std::fabs(ref[i])));
+    cudaFree(dl);
+    // sampling: the reference's defaults (top-k 50) and a top-p nucleus
+    const size_t rows = 4, vocab = 5000;
+    auto logits = randn(rows * vocab, 43);
+    for (auto& v : logits) v *= 3.0f;
+    const std::vector<float> u = {0.1f, 0.5f, 0.0f, 0.97f};
+    const Tensor lt = dev(logits, {rows, vocab});
+    // the kernel's own probabilities, walked by the reference's loops (the oracle)
+    const auto gp = host(unwrap(ops::softmax_with_temperature(lt, 1.0f)));
+    for (const auto& [k, p] : std::vector<std::pair<size_t, float>>{{50, 1.0f}, {1, 1.0f}, {50, 0.8f}}) {
+        InferenceParams params;
+        params.top_k = k;
+        params.top_p = p;
+        const auto tok = unwrap(sample_next_token(lt, u, params));
+        for (size_t r = 0; r < rows; ++r) EXPECT(tok[r] == orc_sample_probs(gp.data() + r * vocab, vocab, k, p, u[r]));
+    }
+    const auto probs = host(unwrap(ops::softmax_with_temperature(lt, 0.7f)));
+    std::vector<float> pref(logits.size());
+    orc_softmax_temperature_f32(logits.data(), rows, vocab, 0.7f, pref.data(), 1);
+    for (size_t i = 0; i < probs.size(); ++i) EXPECT(std::fabs(probs[i] - pref[i]) <= 2e-5f * pref[i] + 1e-12f);
+    EXPECT(sample_next_token(lt, {0.5f}).error().message == "sample_next_token: 1 uniforms for 4 rows");
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
