@@ -16,10 +16,10 @@
 //      sum per head (online softmax) and accumulates the unnormalised output;
 //      it writes (m, l, o[d]) per head to the workspace.  bf16 caches: four
 //      warps stream interleaved 16-key tiles independently and run both tile
-//      products on the tensor cores (decode_attn_warp_kernel); f32 caches: a
-//      two-stage block ring on the CUDA cores, thread d owning output dim d
-//      (decode_attn_split_kernel);
-//   2. one CTA per (batch, q head) merges the splits in order:
+//      products on the tensor cores (decode_attn_warp_kernel); f32 caches:
+//      the same warp streams with 8-key tiles on the CUDA cores
+//      (decode_attn_warp_f32_kernel);
+//   2. one CTA per (batch, q head) merges the splits:
 //      M = max m_s, L = sum l_s e^(m_s - M), out = sum o_s e^(m_s - M) / L.
 // Arithmetic is f32 accumulation (bf16 operands multiplied exactly), dot
 // products and P.V with fused multiply-adds; the result differs from the
@@ -49,180 +49,10 @@ __device__ __forceinline__ uint64_t seq_len_of(const DecArgs& p, uint64_t b) {
     return l < 0 ? 0 : ((uint64_t)l < p.max_seq ? (uint64_t)l : p.max_seq);
 }
 
+// Split lengths are whole multiples of one CTA's key granule: 4 warps x 16
+// keys (bf16) or 4 warps x 8 keys (f32).
 template <typename T>
-struct DaTile {
-    static constexpr int RB = DA_D * (int)sizeof(T);  // bytes per cached row
-    static constexpr int RS = RB + 16;                // shared-memory row stride
-    static constexpr int TK = sizeof(T) == 2 ? 64 : 32;  // keys per tile
-    static constexpr int CPR = RB / 16;               // 16-byte chunks per row
-    static constexpr int TPK = DA_THREADS / TK;       // threads per key in the score pass
-    static constexpr int DPT = DA_D / TPK;            // dims per thread in the score pass
-};
-
-template <typename T, int NR>
-constexpr size_t decode_smem_bytes() {
-    return (size_t)4 * DaTile<T>::TK * DaTile<T>::RS + (size_t)NR * DA_D * 4 + (size_t)NR * DaTile<T>::TK * 4 +
-           (size_t)4 * NR * 4;
-}
-
-template <typename T, int NR>
-__global__ void __launch_bounds__(DA_THREADS)
-    decode_attn_split_kernel(const T* q, const T* kc, const T* vc, float* part_ml, float* part_o, DecArgs p) {
-    using TL = DaTile<T>;
-    constexpr int TK = TL::TK, RS = TL::RS, RB = TL::RB, CPR = TL::CPR, TPK = TL::TPK, DPT = TL::DPT;
-    constexpr int V = 16 / (int)sizeof(T);
-    extern __shared__ __align__(16) unsigned char smem[];
-    unsigned char* kbuf = smem;
-    unsigned char* vbuf = smem + 2 * TK * RS;
-    float* qs = reinterpret_cast<float*>(smem + 4 * TK * RS);  // [NR][D]
-    float* S = qs + NR * DA_D;                                 // [NR][TK]
-    float* m_run = S + NR * TK;                                // [NR]
-    float* l_run = m_run + NR;
-    float* corr = l_run + NR;
-
-    const uint32_t split = blockIdx.x, kvh = blockIdx.y;
-    const uint64_t b = blockIdx.z;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint64_t len = seq_len_of(p, b);
-    const uint64_t s0 = (uint64_t)split * p.split_len;
-    const uint64_t s1 = s0 + p.split_len < len ? s0 + p.split_len : len;
-    const uint32_t qh0 = kvh * NR;
-
-    for (int i = tid; i < NR * DA_D; i += DA_THREADS)
-        qs[i] = Vec<T>::load1(q + (b * p.q_heads + qh0 + i / DA_D) * DA_D + (i % DA_D));
-    if (tid < NR) {
-        m_run[tid] = -INFINITY;
-        l_run[tid] = 0.0f;
-    }
-    float o[NR];
-#pragma unroll
-    for (int r = 0; r < NR; ++r) o[r] = 0.0f;
-
-    const uint64_t row0 = (b * p.kv_heads + kvh) * p.max_seq;
-    const char* kbase = reinterpret_cast<const char*>(kc + row0 * DA_D);
-    const char* vbase = reinterpret_cast<const char*>(vc + row0 * DA_D);
-    const uint32_t nkeys = s1 > s0 ? (uint32_t)(s1 - s0) : 0u;
-    const uint32_t ntiles = (nkeys + TK - 1) / TK;
-    auto issue = [&](uint32_t t) {
-        const uint32_t stage = t & 1u;
-        const uint64_t key0 = s0 + (uint64_t)t * TK;
-        const uint32_t nk = nkeys - t * TK < (uint32_t)TK ? nkeys - t * TK : (uint32_t)TK;
-        for (uint32_t c = tid; c < nk * CPR; c += DA_THREADS) {
-            const uint32_t row = c / CPR, col = c % CPR;
-            const uint64_t src = (key0 + row) * RB + col * 16;
-            cp_async16(kbuf + stage * TK * RS + row * RS + col * 16, kbase + src);
-            cp_async16(vbuf + stage * TK * RS + row * RS + col * 16, vbase + src);
-        }
-        cp_async_commit();
-    };
-    if (ntiles > 0) issue(0);
-    __syncthreads();  // qs, m_run, l_run visible
-    for (uint32_t t = 0; t < ntiles; ++t) {
-        if (t + 1 < ntiles) issue(t + 1);
-        else cp_async_commit();  // empty group: the wait below counts uniformly
-        cp_async_wait<1>();
-        __syncthreads();  // tile t is in shared memory for every thread
-        const uint32_t stage = t & 1u;
-        const uint32_t nk = nkeys - t * TK < (uint32_t)TK ? nkeys - t * TK : (uint32_t)TK;
-        // scores: TPK threads per key, DPT dims each
-        {
-            const int jj = tid / TPK, part = tid % TPK;
-            float acc[NR];
-#pragma unroll
-            for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
-            if ((uint32_t)jj < nk) {
-                const unsigned char* krow = kbuf + stage * TK * RS + jj * RS + part * DPT * (int)sizeof(T);
-#pragma unroll
-                for (int c = 0; c < DPT / V; ++c) {
-                    float kf[V];
-                    Vec<T>::unpack(lds16(krow + c * 16), kf);
-#pragma unroll
-                    for (int r = 0; r < NR; ++r) {
-                        const float4* qv = reinterpret_cast<const float4*>(qs + r * DA_D + part * DPT + c * V);
-#pragma unroll
-                        for (int e4 = 0; e4 < V / 4; ++e4) {
-                            const float4 qq = qv[e4];
-                            acc[r] = __fmaf_rn(qq.x, kf[4 * e4], acc[r]);
-                            acc[r] = __fmaf_rn(qq.y, kf[4 * e4 + 1], acc[r]);
-                            acc[r] = __fmaf_rn(qq.z, kf[4 * e4 + 2], acc[r]);
-                            acc[r] = __fmaf_rn(qq.w, kf[4 * e4 + 3], acc[r]);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < NR; ++r) {
-#pragma unroll
-                for (int o2 = 1; o2 < TPK; o2 <<= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], o2));
-                if (part == 0) S[r * TK + jj] = (uint32_t)jj < nk ? fmul(acc[r], p.scale) : -INFINITY;
-            }
-        }
-        __syncthreads();
-        // online softmax per head: warp w handles heads w, w + 4, ...
-        for (int r = warp; r < NR; r += DA_THREADS / 32) {
-            float* sr = S + r * TK;
-            float tmax = -INFINITY;
-            for (int j = lane; j < TK; j += 32) tmax = fmaxf(tmax, sr[j]);
-            tmax = warp_max(tmax);
-            const float m_old = m_run[r];
-            const float m_new = fmaxf(m_old, tmax);
-            float psum = 0.0f;
-            for (int j = lane; j < TK; j += 32) {
-                const float pj = m_new == -INFINITY ? 0.0f : expf(fsub(sr[j], m_new));
-                sr[j] = pj;
-                psum = fadd(psum, pj);
-            }
-            psum = warp_sum(psum);
-            if (lane == 0) {
-                const float c = m_old == -INFINITY ? 0.0f : expf(fsub(m_old, m_new));
-                corr[r] = c;
-                l_run[r] = __fmaf_rn(l_run[r], c, psum);
-                m_run[r] = m_new;
-            }
-        }
-        __syncthreads();
-        // P.V: thread d accumulates o[r] += p[r][j] * v[j][d]
-        {
-            const int d = tid;
-#pragma unroll
-            for (int r = 0; r < NR; ++r) o[r] = fmul(o[r], corr[r]);
-            const unsigned char* vcol = vbuf + stage * TK * RS + d * (int)sizeof(T);
-            auto vat = [&](uint32_t j) {
-                if (sizeof(T) == 4) return *reinterpret_cast<const float*>(vcol + j * RS);
-                return bf16_to_f32(*reinterpret_cast<const bf16_t*>(vcol + j * RS));
-            };
-            uint32_t j = 0;
-            for (; j + 4 <= nk; j += 4) {  // probabilities 4 at a time (one 16-byte load per head)
-                const float v0 = vat(j), v1 = vat(j + 1), v2 = vat(j + 2), v3 = vat(j + 3);
-#pragma unroll
-                for (int r = 0; r < NR; ++r) {
-                    const float4 pp = *reinterpret_cast<const float4*>(S + r * TK + j);
-                    o[r] = __fmaf_rn(pp.x, v0, o[r]);
-                    o[r] = __fmaf_rn(pp.y, v1, o[r]);
-                    o[r] = __fmaf_rn(pp.z, v2, o[r]);
-                    o[r] = __fmaf_rn(pp.w, v3, o[r]);
-                }
-            }
-            for (; j < nk; ++j) {  // rows past nk hold stale data: never read
-                const float v = vat(j);
-#pragma unroll
-                for (int r = 0; r < NR; ++r) o[r] = __fmaf_rn(S[r * TK + j], v, o[r]);
-            }
-        }
-        __syncthreads();  // every thread is done with this stage before it is refilled
-    }
-    cp_async_wait<0>();
-    // partial results of this split
-#pragma unroll
-    for (int r = 0; r < NR; ++r) {
-        const uint64_t slot = ((b * p.q_heads + qh0 + r) * p.splits + split);
-        part_o[slot * DA_D + tid] = o[r];
-        if (tid == 0) {
-            part_ml[slot * 2] = m_run[r];
-            part_ml[slot * 2 + 1] = l_run[r];
-        }
-    }
-}
+constexpr uint64_t split_granule() { return sizeof(T) == 2 ? 64 : 32; }
 
 // ---- bf16 caches: per-warp key streams on the tensor cores -------------------
 // Each warp of a 4-warp CTA streams every 4th 16-key tile of the split through
@@ -275,6 +105,14 @@ constexpr int DW_STAGES = 3;                                    // cp.async ring
 constexpr int DW_RS = DA_D * 2 + 16;                            // 272-byte rows: conflict-free ldmatrix
 constexpr int DW_STAGE = 2 * DW_TK * DW_RS;                     // K and V tile of one stage
 constexpr size_t DW_SMEM = (size_t)DW_WARPS * DW_STAGES * DW_STAGE;  // 104,448 B: 2 CTAs per SM
+// 16-byte copy into shared memory with an L2 prefetch-size hint: each warp
+// tile reads whole 256-byte cache rows, so the hint lets L2 fetch them whole.
+__device__ __forceinline__ void cp_async16_l2(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(
+                     (uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(gsrc)
+                 : "memory");
+}
 constexpr float DW_LOG2E = 1.4426950408889634f;
 constexpr float DW_LN2 = 0.6931471805599453f;
 
@@ -334,8 +172,8 @@ __global__ void __launch_bounds__(DW_WARPS * 32, 2)
             // rows past the last key repeat the last key: finite data that p = 0 multiplies
             const uint32_t src = row < nk ? row : nk - 1;
             const uint64_t off = (uint64_t)(key0 + src) * (DA_D * 2) + ccol;
-            cp_async16(kd + row * DW_RS + ccol, kbase + off);
-            cp_async16(vd + row * DW_RS + ccol, vbase + off);
+            cp_async16_l2(kd + row * DW_RS + ccol, kbase + off);
+            cp_async16_l2(vd + row * DW_RS + ccol, vbase + off);
         }
     };
 #pragma unroll
@@ -355,13 +193,18 @@ __global__ void __launch_bounds__(DW_WARPS * 32, 2)
         const uint32_t base = wbuf_s + (it % DW_STAGES) * DW_STAGE;
         const uint32_t key0 = (warp + it * DW_WARPS) * DW_TK;
         const uint32_t nk = nkeys - key0 < (uint32_t)DW_TK ? nkeys - key0 : (uint32_t)DW_TK;
-        float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        // two accumulators (even / odd 16-dim steps) halve the dependent mma chain
+        float s[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-            uint32_t a0, a1, a2, a3;
+        for (int ks = 0; ks < 8; ks += 2) {
+            uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
             ldsm_x4(base + k_lane + ks * 32, a0, a1, a2, a3);
+            ldsm_x4(base + k_lane + ks * 32 + 32, c0, c1, c2, c3);
             mma_bf16(s, a0, a1, a2, a3, qb0[ks], qb1[ks]);
+            mma_bf16(s2, c0, c1, c2, c3, qb0[ks + 1], qb1[ks + 1]);
         }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[e] = fadd(s[e], s2[e]);
         // s: (key g, head 2t4), (key g, head 2t4+1), (key g+8, head 2t4), (key g+8, head 2t4+1)
         const float t0 = (uint32_t)g < nk ? fmul(s[0], c1) : -INFINITY;
         const float t1 = (uint32_t)g < nk ? fmul(s[1], c1) : -INFINITY;
@@ -464,28 +307,217 @@ __global__ void __launch_bounds__(DW_WARPS * 32, 2)
     }
 }
 
-// Merge the splits of one (batch, q head); thread d writes out[d].
+// ---- f32 caches: per-warp key streams on the CUDA cores ---------------------
+// The split-K and warp-stream structure of the bf16 kernel, with 8-key tiles of
+// f32 rows (512 B, padded to 528 B: conflict-free 16-byte reads) through a
+// private 3-stage cp.async ring per warp.  Scores: lane l holds key l & 7 and
+// dims 32 (l >> 3) .. + 31, reading the group's query heads from shared memory
+// (a broadcast within each 8-lane phase), and the four dim quarters are summed
+// by shuffles.  P V: lane l owns dims 4 l .. 4 l + 3 of every head's output,
+// each key's probabilities broadcast from its lane by shuffle.  f32 throughout,
+// expf for the exponentials, FMAs for the dot products and P V.
+constexpr int DF_TK = 8;                                         // keys per warp tile
+constexpr int DF_STAGES = 3;
+constexpr int DF_RS = DA_D * 4 + 16;                             // 528-byte rows
+constexpr int DF_RSF = DF_RS / 4;                                // the same in floats
+constexpr int DF_STAGE = 2 * DF_TK * DF_RS;                      // 8448 B: K and V tile
+constexpr size_t DF_RING = (size_t)DW_WARPS * DF_STAGES * DF_STAGE;  // 101,376 B
+template <int NR>
+constexpr size_t df_smem() {
+    return DF_RING + (size_t)NR * DA_D * 4;  // + the group's query heads
+}
+
+template <int NR>
+__global__ void __launch_bounds__(DW_WARPS * 32, 2)
+    decode_attn_warp_f32_kernel(const float* q, const float* kc, const float* vc, float* part_ml, float* part_o,
+                                DecArgs p) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    float* qs = reinterpret_cast<float*>(smem + DF_RING);  // [NR][D]
+    const uint32_t split = blockIdx.x, kvh = blockIdx.y;
+    const uint64_t b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int kk = lane & 7, qq = lane >> 3;  // score pass: key in tile, dim quarter
+    const uint64_t len = seq_len_of(p, b);
+    const uint64_t s0 = (uint64_t)split * p.split_len;
+    const uint64_t s1 = s0 + p.split_len < len ? s0 + p.split_len : len;
+    const uint32_t nkeys = s1 > s0 ? (uint32_t)(s1 - s0) : 0u;
+    const uint32_t ntiles = (nkeys + DF_TK - 1) / DF_TK;
+    const uint32_t qh0 = kvh * NR;
+    {
+        const float4* qsrc = reinterpret_cast<const float4*>(q + (b * p.q_heads + qh0) * DA_D);
+        for (int i = tid; i < NR * DA_D / 4; i += DW_WARPS * 32) reinterpret_cast<float4*>(qs)[i] = qsrc[i];
+    }
+    float acc[NR][4];
+    float m[NR], l[NR];
+#pragma unroll
+    for (int h = 0; h < NR; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[h][c] = 0.0f;
+    }
+    unsigned char* wbuf = smem + (size_t)warp * DF_STAGES * DF_STAGE;
+    const uint64_t row0 = (b * p.kv_heads + kvh) * p.max_seq + s0;
+    const char* kbase = reinterpret_cast<const char*>(kc + row0 * DA_D);
+    const char* vbase = reinterpret_cast<const char*>(vc + row0 * DA_D);
+    const uint32_t my_tiles = ntiles > (uint32_t)warp ? (ntiles - warp + DW_WARPS - 1) / DW_WARPS : 0u;
+    auto issue = [&](uint32_t it) {
+        unsigned char* kd = wbuf + (it % DF_STAGES) * DF_STAGE;
+        unsigned char* vd = kd + DF_TK * DF_RS;
+        const uint32_t key0 = (warp + it * DW_WARPS) * DF_TK;
+        const uint32_t nk = nkeys - key0 < (uint32_t)DF_TK ? nkeys - key0 : (uint32_t)DF_TK;
+#pragma unroll
+        for (int row = 0; row < DF_TK; ++row) {  // lane copies 16-byte column `lane` of each row
+            // rows past the last key repeat the last key: finite data that p = 0 multiplies
+            const uint32_t src = (uint32_t)row < nk ? (uint32_t)row : nk - 1;
+            const uint64_t off = (uint64_t)(key0 + src) * (DA_D * 4) + lane * 16;
+            cp_async16(kd + row * DF_RS + lane * 16, kbase + off);
+            cp_async16(vd + row * DF_RS + lane * 16, vbase + off);
+        }
+    };
+#pragma unroll
+    for (int st = 0; st < DF_STAGES - 1; ++st) {
+        if ((uint32_t)st < my_tiles) issue(st);
+        cp_async_commit();
+    }
+    __syncthreads();  // the query heads are in shared memory
+    for (uint32_t it = 0; it < my_tiles; ++it) {
+        if (it + DF_STAGES - 1 < my_tiles) issue(it + DF_STAGES - 1);
+        cp_async_commit();
+        cp_async_wait<DF_STAGES - 1>();
+        __syncwarp();  // every lane's copies of this tile are visible to the warp
+        const float* kt = reinterpret_cast<const float*>(wbuf + (it % DF_STAGES) * DF_STAGE);
+        const float* vt = kt + DF_TK * DF_RSF;
+        const uint32_t key0 = (warp + it * DW_WARPS) * DF_TK;
+        const uint32_t nk = nkeys - key0 < (uint32_t)DF_TK ? nkeys - key0 : (uint32_t)DF_TK;
+        float dot[NR];
+#pragma unroll
+        for (int h = 0; h < NR; ++h) dot[h] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float4 kv = *reinterpret_cast<const float4*>(kt + kk * DF_RSF + qq * 32 + c * 4);
+#pragma unroll
+            for (int h = 0; h < NR; ++h) {
+                const float4 qv = *reinterpret_cast<const float4*>(qs + h * DA_D + qq * 32 + c * 4);
+                dot[h] = __fmaf_rn(kv.x, qv.x, dot[h]);
+                dot[h] = __fmaf_rn(kv.y, qv.y, dot[h]);
+                dot[h] = __fmaf_rn(kv.z, qv.z, dot[h]);
+                dot[h] = __fmaf_rn(kv.w, qv.w, dot[h]);
+            }
+        }
+        bool rescale = false;
+        float pr[NR], corr[NR];
+#pragma unroll
+        for (int h = 0; h < NR; ++h) {
+            dot[h] = fadd(dot[h], __shfl_xor_sync(0xffffffffu, dot[h], 8));
+            dot[h] = fadd(dot[h], __shfl_xor_sync(0xffffffffu, dot[h], 16));
+            const float sc = (uint32_t)kk < nk ? fmul(dot[h], p.scale) : -INFINITY;
+            float x = sc;
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
+            const float mn = fmaxf(m[h], x);
+            corr[h] = m[h] == -INFINITY ? 0.0f : expf(fsub(m[h], mn));
+            rescale |= corr[h] != 1.0f;
+            m[h] = mn;
+            pr[h] = mn == -INFINITY ? 0.0f : expf(fsub(sc, mn));
+            float ps = pr[h];
+#pragma unroll
+            for (int off = 1; off < 8; off <<= 1) ps = fadd(ps, __shfl_xor_sync(0xffffffffu, ps, off));
+            l[h] = __fmaf_rn(l[h], corr[h], ps);
+        }
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+            for (int h = 0; h < NR; ++h)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) acc[h][c] = fmul(acc[h][c], corr[h]);
+        }
+#pragma unroll
+        for (int j = 0; j < DF_TK; ++j) {
+            const float4 vv = *reinterpret_cast<const float4*>(vt + j * DF_RSF + lane * 4);
+#pragma unroll
+            for (int h = 0; h < NR; ++h) {
+                const float pj = __shfl_sync(0xffffffffu, pr[h], j);  // lane j holds key j
+                acc[h][0] = __fmaf_rn(pj, vv.x, acc[h][0]);
+                acc[h][1] = __fmaf_rn(pj, vv.y, acc[h][1]);
+                acc[h][2] = __fmaf_rn(pj, vv.z, acc[h][2]);
+                acc[h][3] = __fmaf_rn(pj, vv.w, acc[h][3]);
+            }
+        }
+        __syncwarp();  // the whole warp is done with this stage before it is refilled
+    }
+    cp_async_wait<0>();
+    // merge the four warp states: [W][8] max, [W][8] sum, [W][NR][D] output
+    __syncthreads();  // every warp is done with its ring: the buffers are reused
+    float* wm = reinterpret_cast<float*>(smem);
+    float* wl = wm + DW_WARPS * 8;
+    float* wo = wl + DW_WARPS * 8;
+    if (lane == 0) {
+#pragma unroll
+        for (int h = 0; h < NR; ++h) {
+            wm[warp * 8 + h] = m[h];
+            wl[warp * 8 + h] = l[h];
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < NR; ++h)
+        *reinterpret_cast<float4*>(wo + (warp * NR + h) * DA_D + lane * 4) =
+            make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    __syncthreads();
+    const int d = tid;
+#pragma unroll
+    for (int h = 0; h < NR; ++h) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < DW_WARPS; ++w) M = fmaxf(M, wm[w * 8 + h]);
+        float L = 0.0f, o = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < DW_WARPS; ++w) {
+                const float mw = wm[w * 8 + h];
+                if (mw == -INFINITY) continue;
+                const float sc = expf(fsub(mw, M));
+                L = __fmaf_rn(wl[w * 8 + h], sc, L);
+                o = __fmaf_rn(wo[(w * NR + h) * DA_D + d], sc, o);
+            }
+        }
+        const uint64_t slot = (b * p.q_heads + qh0 + h) * p.splits + split;
+        part_o[slot * DA_D + d] = o;
+        if (d == 0) {
+            part_ml[slot * 2] = M;
+            part_ml[slot * 2 + 1] = L;
+        }
+    }
+}
+
+// Merge the splits of one (batch, q head); thread d writes out[d].  The
+// splits' weights e^(m_s - M) and the sum L are found cooperatively (block
+// reductions), the weights kept in shared memory, so the loop over the
+// splits' outputs is a run of independent loads.
+constexpr int DA_MAX_SPLITS = 1024;
 template <typename T>
 __global__ void __launch_bounds__(DA_THREADS)
     decode_attn_combine_kernel(const float* part_ml, const float* part_o, T* out, DecArgs p) {
+    __shared__ float wts[DA_MAX_SPLITS];
+    __shared__ float red[32];
     const uint64_t bh = blockIdx.x;
     const int d = threadIdx.x;
     const uint64_t base = bh * p.splits;
     float M = -INFINITY;
-    for (uint32_t s = 0; s < p.splits; ++s) M = fmaxf(M, part_ml[(base + s) * 2]);
-    float res = 0.0f;
-    if (M != -INFINITY) {
-        float L = 0.0f, acc = 0.0f;
-        for (uint32_t s = 0; s < p.splits; ++s) {
-            const float ms = part_ml[(base + s) * 2];
-            if (ms == -INFINITY) continue;
-            const float w = expf(fsub(ms, M));
-            L = __fmaf_rn(part_ml[(base + s) * 2 + 1], w, L);
-            acc = __fmaf_rn(part_o[(base + s) * DA_D + d], w, acc);
-        }
-        res = fdiv(acc, L);
+    for (uint32_t s = d; s < p.splits; s += DA_THREADS) M = fmaxf(M, part_ml[(base + s) * 2]);
+    M = group_reduce(M, red, DA_THREADS, OpMaxF());
+    float lp = 0.0f;
+    for (uint32_t s = d; s < p.splits; s += DA_THREADS) {
+        const float ms = part_ml[(base + s) * 2];
+        const float w = (M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(fsub(ms, M));
+        wts[s] = w;
+        lp = __fmaf_rn(part_ml[(base + s) * 2 + 1], w, lp);
     }
-    Vec<T>::store1(out + bh * DA_D + d, res);
+    const float L = group_reduce(lp, red, DA_THREADS, OpAddF());  // its barrier also publishes wts
+    float acc = 0.0f;
+    const float* po = part_o + base * DA_D + d;
+#pragma unroll 8
+    for (uint32_t s = 0; s < p.splits; ++s) acc = __fmaf_rn(po[(uint64_t)s * DA_D], wts[s], acc);
+    Vec<T>::store1(out + bh * DA_D + d, M == -INFINITY ? 0.0f : fdiv(acc, L));
 }
 
 // General shapes: one CTA per (batch, q head), three passes over the keys
@@ -542,11 +574,11 @@ static cudaError_t launch_split(const T* q, const T* kc, const T* vc, T* out, fl
         auto kern = decode_attn_warp_kernel<NR>;
         if (!ensure_dyn_smem(reinterpret_cast<const void*>(kern), DW_SMEM)) return cudaErrorInvalidConfiguration;
         kern<<<grid, DW_WARPS * 32, DW_SMEM, st>>>(q, kc, vc, part_ml, part_o, p);
-    } else {
-        auto kern = decode_attn_split_kernel<T, NR>;
-        const size_t smem = decode_smem_bytes<T, NR>();
+    } else {  // f32: CUDA-core tile products
+        auto kern = decode_attn_warp_f32_kernel<NR>;
+        const size_t smem = df_smem<NR>();
         if (!ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem)) return cudaErrorInvalidConfiguration;
-        kern<<<grid, DA_THREADS, smem, st>>>(q, kc, vc, part_ml, part_o, p);
+        kern<<<grid, DW_WARPS * 32, smem, st>>>(q, kc, vc, part_ml, part_o, p);
     }
     decode_attn_combine_kernel<T><<<(unsigned)(p.batch * p.q_heads), DA_THREADS, 0, st>>>(part_ml, part_o, out, p);
     return cudaSuccess;
@@ -583,7 +615,7 @@ static int decode_entry(const char* name, const T* q, const T* kc, const T* vc, 
     cudaError_t e = cudaSuccess;
     if (fast) {
         // splits: enough CTAs for ~4 waves, whole tiles per split
-        const uint64_t tk = DaTile<T>::TK;
+        const uint64_t tk = split_granule<T>();
         const uint64_t groups = batch * kv_heads;
         const uint64_t target = 4ull * 3 * sm_count();
         uint64_t splits = (target + groups - 1) / groups;
