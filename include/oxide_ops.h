@@ -245,6 +245,18 @@ int oxide_rope_bf16(const oxide_bf16* q, oxide_bf16* q_out, uint64_t q_heads,
 int oxide_rope_table_host_f32(float theta, uint64_t head_dim, uint64_t max_pos,
                               float* cos_host, float* sin_host);
 
+/* ---- weight decoding (safetensors element bytes) ---------------------------------
+ * SafetensorsLoader::load_tensor_from_view (src/loading/safetensors.rs:48-82)
+ * on the device: n little-endian elements of src_dtype (device memory, aligned
+ * to the element size) -> out.  F32 is copied; F16 is converted exactly as the
+ * half crate does (NaN: quiet bit set, payload kept); BF16 is decoded as the
+ * high half of an f32 -- the reference decodes BF16 bytes as f16, a bug this
+ * entry point fixes.  The bf16 form rounds the decoded value to nearest-even
+ * bf16 (exact for BF16 sources; a NaN becomes the canonical bf16 NaN). */
+enum oxide_wdtype { OXIDE_WDT_F32 = 0, OXIDE_WDT_F16 = 1, OXIDE_WDT_BF16 = 2 };
+int oxide_decode_weights_f32(const void* src, uint64_t n, int src_dtype, float* out, oxide_stream_t stream);
+int oxide_decode_weights_bf16(const void* src, uint64_t n, int src_dtype, oxide_bf16* out, oxide_stream_t stream);
+
 /* ---- KV cache and grouped-query heads -------------------------------------------
  * repeat_kv (src/ops/attention.rs:161-201): x [batch, kv_heads, seq_len,
  * head_dim] -> out [batch, kv_heads * n_rep, seq_len, head_dim],

@@ -58,6 +58,8 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_tanh_f32": (i32, [vp, vp, u64, vp]),
     "oxide_layer_norm_f32": (i32, [vp, vp, vp, vp, u64, u64, f32, vp]),
     "oxide_layer_norm_bf16": (i32, [vp, vp, vp, vp, u64, u64, f32, vp]),
+    "oxide_decode_weights_f32": (i32, [vp, u64, i32, vp, vp]),
+    "oxide_decode_weights_bf16": (i32, [vp, u64, i32, vp, vp]),
     "oxide_repeat_kv_f32": (i32, [vp, vp, u64, u64, u64, u64, u64, vp]),
     "oxide_repeat_kv_bf16": (i32, [vp, vp, u64, u64, u64, u64, u64, vp]),
     "oxide_kv_cache_append_f32": (i32, [vp, vp, vp, vp, u64, u64, u64, u64, u64, u64, vp]),
@@ -90,6 +92,7 @@ ADD, SUB, MUL, DIV = 0, 1, 2, 3
 RELU, GELU, GELU_QUICK, SIGMOID, TANH, EXP, LOG, SQRT, POW, CLAMP, NEG, ABS = range(12)
 RED_SUM, RED_MAX, RED_SUMSQ = 0, 1, 2
 SAMPLE_INVALID = 0xFFFFFFFF
+WDT_F32, WDT_F16, WDT_BF16 = 0, 1, 2
 
 _lock = threading.Lock()
 _lib: C.CDLL | None = None

@@ -93,6 +93,15 @@ def build(op: str, rows: int | None, dev):
         run = lambda s: ops.decode_attention(s[0], s[1], s[2], tl, workspace=ws, out=s[3])  # noqa: E731
         nb = int(np.sum(np.minimum(lens, c.keys))) * kvh * c.head_dim * es * 2 + 2 * c.batch * c.heads * c.head_dim * es
         return mk, run, nb, [c.batch, c.heads, kvh, c.keys, c.head_dim]
+    if op in ("decode_weights_bf16_f32", "decode_weights_f16_f32"):
+        # safetensors element decode of one Mistral MLP matrix [14336, 4096] to f32
+        n = (rows or 14336) * 4096
+        code = _lib.WDT_BF16 if op == "decode_weights_bf16_f32" else _lib.WDT_F16
+        out = torch.empty(n, dtype=torch.float32, device=dev)
+        mk = lambda: (torch.randint(0, 2**15, (n,), dtype=torch.int16, device=dev, generator=g),)  # noqa: E731
+        run = lambda s: call("oxide_decode_weights_f32", s[0].data_ptr(), n, code, out.data_ptr(),  # noqa: E731
+                             _stream())
+        return mk, run, n * 6, [n]
     if op == "softmax_temperature_f32_c3":
         # softmax_with_temperature alone over the C3 logits [64, 32000]
         c = C3()
@@ -226,7 +235,8 @@ OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softma
        "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5",
        "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5",
        "repeat_kv_bf16_c5", "kv_append_bf16_c5", "decode_attn_bf16_c3", "decode_attn_f32_c3",
-       "softmax_temperature_f32_c3", "sample_topk_f32_c3", "sample_topp_f32_c3"]
+       "softmax_temperature_f32_c3", "sample_topk_f32_c3", "sample_topp_f32_c3",
+       "decode_weights_bf16_f32", "decode_weights_f16_f32"]
 
 
 def main(argv=None):

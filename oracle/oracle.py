@@ -68,6 +68,8 @@ def lib() -> C.CDLL:
             "orc_repeat_kv": [vp, vp, u64, u64, u64, u64, u64, u64],
             "orc_decode_attention_f32": [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, i32],
             "orc_decode_attention_bf16": [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, i32],
+            "orc_decode_weights_f32": [vp, u64, i32, vp],
+            "orc_decode_weights_bf16": [vp, u64, i32, vp],
             "orc_softmax_temperature_f32": [vp, u64, u64, f32, vp, i32],
             "orc_softmax_temperature_bf16": [vp, u64, u64, f32, vp, i32],
             "orc_sample_f32": [vp, u64, u64, f32, u64, f32, vp, vp, vp, i32],
@@ -84,6 +86,8 @@ def lib() -> C.CDLL:
         h.orc_reduce_seq_f32.argtypes = [i32, vp, u64]
         h.orc_reduce_seq_f32.restype = C.c_float
         h.orc_max_threads.restype = i32
+        h.orc_decode_f16_bits_f32.argtypes = [C.c_uint16]
+        h.orc_decode_f16_bits_f32.restype = C.c_float
         h.orc_sample_probs.argtypes = [vp, u64, u64, f32, f32]
         h.orc_sample_probs.restype = C.c_uint32
         h.orc_kv_append.argtypes = [vp, vp, vp, vp, u64, u64, u64, u64, u64, u64, u64]
@@ -214,6 +218,21 @@ def decode_attention(q, kc, vc, lens=None, scale=None, threads=1):
 
 
 SAMPLE_INVALID = 0xFFFFFFFF
+WDT_F32, WDT_F16, WDT_BF16 = 0, 1, 2
+
+
+def decode_weights(raw, dtype_code, out_bf16=False):
+    """src/loading/safetensors.rs:48-82 element decode of little-endian bytes
+    (a numpy uint8 array) -> f32 values (or bf16 bits with out_bf16)."""
+    raw = _c(np.frombuffer(bytes(raw), np.uint8) if not isinstance(raw, np.ndarray) else raw)
+    n = raw.size // (4 if dtype_code == WDT_F32 else 2)
+    if out_bf16:
+        out = np.empty(n, np.uint16)
+        lib().orc_decode_weights_bf16(_p(raw), n, int(dtype_code), _p(out))
+    else:
+        out = np.empty(n, np.float32)
+        lib().orc_decode_weights_f32(_p(raw), n, int(dtype_code), _p(out))
+    return out
 
 
 def softmax_with_temperature(logits, temperature, threads=1):

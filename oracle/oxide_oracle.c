@@ -775,3 +775,46 @@ void orc_sample_bf16(const uint16_t* logits, uint64_t rows, uint64_t vocab, floa
         if (!probs) free(p);
     }
 }
+
+/* ---- weight decoding (src/loading/safetensors.rs:48-82) -------------------- */
+/* half::f16 -> f32: exact; NaN keeps its payload with the quiet bit set */
+float orc_decode_f16_bits_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, exp = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+    uint32_t bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {
+            float v = (float)man * 0x1p-24f; /* subnormal half: exact in f32 */
+            memcpy(&bits, &v, 4);
+            bits |= sign;
+        }
+    } else if (exp == 31) {
+        bits = man == 0 ? (sign | 0x7F800000u) : (sign | 0x7FC00000u | (man << 13));
+    } else {
+        bits = sign | ((exp + 112u) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+static float decode_elem(const unsigned char* s, uint64_t i, int dtype) {
+    if (dtype == ORC_WDT_F32) {
+        float f;
+        memcpy(&f, s + 4 * i, 4); /* f32::from_le_bytes on a little-endian host */
+        return f;
+    }
+    uint16_t h;
+    memcpy(&h, s + 2 * i, 2);
+    if (dtype == ORC_WDT_F16) return orc_decode_f16_bits_f32(h);
+    return B2F(h);
+}
+
+void orc_decode_weights_f32(const void* src, uint64_t n, int dtype, float* out) {
+    for (uint64_t i = 0; i < n; ++i) out[i] = decode_elem((const unsigned char*)src, i, dtype);
+}
+
+void orc_decode_weights_bf16(const void* src, uint64_t n, int dtype, uint16_t* out) {
+    for (uint64_t i = 0; i < n; ++i) out[i] = orc_f32_to_bf16(decode_elem((const unsigned char*)src, i, dtype));
+}

@@ -183,6 +183,15 @@ void orc_sample_bf16(const uint16_t* logits, uint64_t rows, uint64_t vocab, floa
                      uint64_t top_k, float top_p, const float* uniforms, uint32_t* tokens, float* probs,
                      int threads);
 
+/* src/loading/safetensors.rs:48-82 element decode: F32 copy, F16 through the
+ * half crate's exact f16 -> f32 conversion, BF16 as the high half of an f32
+ * (the reference runs BF16 bytes through the f16 conversion, a bug not
+ * restated here; orc_decode_f16_bits_f32 gives what it computes). */
+enum { ORC_WDT_F32 = 0, ORC_WDT_F16 = 1, ORC_WDT_BF16 = 2 };
+void orc_decode_weights_f32(const void* src, uint64_t n, int dtype, float* out);
+void orc_decode_weights_bf16(const void* src, uint64_t n, int dtype, uint16_t* out);
+float orc_decode_f16_bits_f32(uint16_t h);
+
 int orc_max_threads(void);
 
 #ifdef __cplusplus
