@@ -330,6 +330,32 @@ def per_op_lines(peak):
            for i in range(nset)]
     rec("rope_bf16[C4]", c4.bytes(), graph_time_per_launch(fns), "q[4096,32,128] k[4096,8,128]")
     del qs, ks, qo, ko
+
+    # C3 decode step of attention over bf16 KV caches (q [8,32,128], caches
+    # [8,8,32768,128], the C3 lengths) and token sampling over the C3 logits
+    from oxide_b200.workloads import NKV
+
+    g = torch.Generator(device=dev).manual_seed(3)
+    nb = int(np.sum(np.minimum(lens, c3.keys))) * NKV * c3.head_dim * 2 * 2 + 2 * c3.batch * c3.heads * c3.head_dim * 2
+    nset = rotating_sets(nb)
+    kvs = [(torch.randn(c3.batch, NKV, c3.keys, c3.head_dim, generator=g, device=dev).to(torch.bfloat16),
+            torch.randn(c3.batch, NKV, c3.keys, c3.head_dim, generator=g, device=dev).to(torch.bfloat16))
+           for _ in range(nset)]
+    qd = torch.randn(c3.batch, c3.heads, c3.head_dim, generator=g, device=dev).to(torch.bfloat16)
+    od = torch.empty_like(qd)
+    ws = torch.empty(int(ops._lib.lib().oxide_decode_attention_workspace_bytes(c3.batch, c3.heads, c3.keys,
+                                                                                c3.head_dim)),
+                     dtype=torch.uint8, device=dev)
+    fns = [(lambda i=i: ops.decode_attention(qd, kvs[i][0], kvs[i][1], tl, workspace=ws, out=od))
+           for i in range(nset)]
+    rec("decode_attention_bf16[C3]", nb, graph_time_per_launch(fns), "q[8,32,128] kv[8,8,32768,128] lens")
+    del kvs
+    nset = rotating_sets(c3.bytes_argmax())
+    ls = [torch.from_numpy(logits).to(dev) * 3 for _ in range(nset)]
+    u = torch.rand(c3.logit_rows, generator=g, device=dev)
+    fns = [(lambda i=i: ops.sample_next_token(ls[i], u, 1.0, 50, 1.0)) for i in range(nset)]
+    rec("sample_topk50_f32[C3]", c3.bytes_argmax(), graph_time_per_launch(fns), "[64,32000] T=1 top-k 50")
+    del ls
     torch.cuda.empty_cache()
     return res
 

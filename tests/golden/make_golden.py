@@ -105,6 +105,40 @@ def build() -> dict:
     g["ln.x"], g["ln.w"], g["ln.b"] = x, w, b
     g["ln_f32.out"] = orc.layer_norm(x, w, b, 1e-5)
     g["ln_bf16.out"] = orc.layer_norm(bf(x), bf(w), bf(b), 1e-5)
+    # repeat_kv (src/ops/attention.rs:161-201) and the KV-cache append (src/cache/kv_cache.rs:55-85)
+    x = rng.standard_normal((2, 2, 5, 16), dtype=F)
+    g["repeat_kv.x"], g["repeat_kv.out"] = x, orc.repeat_kv(x, 3)
+    kc = np.zeros((2, 2, 8, 16), F)
+    vc = np.zeros((2, 2, 8, 16), F)
+    k = rng.standard_normal((2, 2, 3, 16), dtype=F)
+    v = rng.standard_normal((2, 2, 3, 16), dtype=F)
+    assert orc.kv_append(kc, vc, k, v, 2)
+    g["kv_append.k"], g["kv_append.v"], g["kv_append.kc"], g["kv_append.vc"] = k, v, kc, vc
+    # one-token attention over a cache (src/ops/attention.rs:41-87, GQA head map of repeat_kv)
+    q = rng.standard_normal((2, 8, 128), dtype=F)
+    kc = rng.standard_normal((2, 2, 40, 128), dtype=F)
+    vc = rng.standard_normal((2, 2, 40, 128), dtype=F)
+    lens = np.array([40, 13], np.int32)
+    g["dec.q"], g["dec.kc"], g["dec.vc"], g["dec.lens"] = q, kc, vc, lens
+    g["dec_f32.out"] = orc.decode_attention(q, kc, vc, lens)
+    g["dec_bf16.q"], g["dec_bf16.kc"], g["dec_bf16.vc"] = bf(q), bf(kc), bf(vc)
+    g["dec_bf16.out"] = orc.decode_attention(bf(q), bf(kc), bf(vc), lens)
+    # token sampling (src/tokenizer.rs:166-232, src/pipeline.rs:181-205)
+    x = rng.standard_normal((6, 500), dtype=F) * F(3)
+    u = rng.random(6).astype(F)
+    g["smp.x"], g["smp.u"] = x, u
+    for name, tk, tp in (("topk", 50, 1.0), ("topp", 50, 0.9), ("greedy", 1, 1.0)):
+        tok, probs = orc.sample(x, 0.8, tk, tp, u)
+        g[f"smp_{name}.tok"] = tok
+    g["smp.probs"] = orc.softmax_with_temperature(x, 0.8)
+    g["smp_bf16.x"] = bf(x)
+    g["smp_bf16_topk.tok"] = orc.sample(bf(x), 0.8, 50, 1.0, u)[0]
+    # weight decode (src/loading/safetensors.rs:48-82; BF16 read as bf16)
+    h = rng.integers(0, 65536, 300).astype(np.uint16)
+    h[:8] = [0x0000, 0x8000, 0x0001, 0x03FF, 0x7C00, 0xFC00, 0x7E01, 0x7C01]
+    g["wdec.bits"] = h
+    g["wdec_f16.out"] = orc.decode_weights(h.view(np.uint8), orc.WDT_F16)
+    g["wdec_bf16.out"] = orc.decode_weights(h.view(np.uint8), orc.WDT_BF16)
     # reductions
     x = rng.standard_normal((9, 333), dtype=F)
     g["red.x"] = x

@@ -100,3 +100,36 @@ def test_kernels_match_golden_vectors(cuda, golden):
         total = float(ops.reduce(x, op).item())
         want = float(g[f"red_all_{name}.out"])
         assert abs(total - want) <= (0 if op == 1 else 1e-5 * np.sum(np.abs(g["red.x"].astype(np.float64)) ** (1 + (op == 2))))
+    # repeat_kv and the KV-cache append: bit-exact copies
+    assert_bits_equal(to_np(ops.repeat_kv(d("repeat_kv.x"), 3)), g["repeat_kv.out"])
+    cache = ops.KvCache(1, 2, 2, 16, 8, dtype=torch.float32)
+    cache.update(0, torch.zeros(2, 2, 2, 16, device=cuda), torch.zeros(2, 2, 2, 16, device=cuda))
+    cache.update(0, d("kv_append.k"), d("kv_append.v"))
+    assert_bits_equal(to_np(cache.k_cache[0]), g["kv_append.kc"])
+    assert_bits_equal(to_np(cache.v_cache[0]), g["kv_append.vc"])
+    # one-token attention: f32 within 2e-5 of the row's scale, bf16 within one bf16 ulp
+    q, kc, vc, lens = d("dec.q"), d("dec.kc"), d("dec.vc"), d("dec.lens")
+    out = to_np(ops.decode_attention(q, kc, vc, lens))
+    ref = g["dec_f32.out"]
+    assert np.all(np.abs(out - ref) <= 2e-5 * np.abs(ref).max(axis=-1, keepdims=True) + 1e-7)
+    out = ops.decode_attention(d("dec_bf16.q"), d("dec_bf16.kc"), d("dec_bf16.vc"), lens)
+    assert_ulp(to_np(out), g["dec_bf16.out"], 1)
+    # sampling: probabilities within 1e-5 of the row max; tokens equal (short prefixes
+    # walk the reference's loops; these rows sit far from any running-sum boundary)
+    x, u = d("smp.x"), d("smp.u")
+    probs = torch.empty(6, 500, device=cuda)
+    for name, tk, tp in (("topk", 50, 1.0), ("topp", 50, 0.9), ("greedy", 1, 1.0)):
+        tok = to_np(ops.sample_next_token(x, u, 0.8, tk, tp, probs_out=probs)).astype(np.uint32)
+        assert np.array_equal(tok, g[f"smp_{name}.tok"]), name
+    pref = g["smp.probs"]
+    assert np.all(np.abs(to_np(probs) - pref) <= 1e-5 * pref.max(axis=-1, keepdims=True))
+    assert np.array_equal(to_np(ops.sample_next_token(d("smp_bf16.x"), u, 0.8, 50, 1.0)).astype(np.uint32),
+                          g["smp_bf16_topk.tok"])
+    # weight decode: bit-exact
+    from oxide_b200 import _lib
+
+    bits = d("wdec.bits")
+    for code, key in ((1, "wdec_f16.out"), (2, "wdec_bf16.out")):
+        out = torch.empty(bits.numel(), dtype=torch.float32, device=cuda)
+        _lib.call("oxide_decode_weights_f32", bits.data_ptr(), bits.numel(), code, out.data_ptr(), 0)
+        assert np.array_equal(to_np(out).view(np.uint32), g[key].view(np.uint32)), key
