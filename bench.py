@@ -179,6 +179,20 @@ def cpu_step_sample(rows: int, threads: int):
     return time.perf_counter() - t0, cfg.bytes()
 
 
+def host_cpu() -> dict:
+    """The box's host: logical CPUs (nproc) and the CPU model."""
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "cpu_model": model}
+
+
 def cpu_baseline(budget_s: float = 12.0):
     """Single-thread oracle port (the reference is single-threaded) on a
     bounded sample of the C2 step, repeated for about `budget_s` seconds."""
@@ -190,7 +204,8 @@ def cpu_baseline(budget_s: float = 12.0):
         times.append(dt)
     gbs = nbytes / statistics.median(times) / 1e9
     return {"value": round(gbs, 3), "unit": UNIT, "cores": 1, "kind": "port",
-            "sample": f"C2 step on {rows} of 8192 rows, single thread, {len(times)} reps, median"}
+            "sample": f"C2 step on {rows} of 8192 rows, single thread, {len(times)} reps, median",
+            "host": host_cpu()}
 
 
 def run_reference(args):
@@ -221,7 +236,8 @@ def run_reference(args):
         "config": {"workload": WORKLOAD, "sample_rows": rows},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
                          "kind": "port",
-                         "sample": f"C2 step on {rows} of 8192 rows per step, {threads} OpenMP threads"},
+                         "sample": f"C2 step on {rows} of 8192 rows per step, {threads} OpenMP threads",
+                         "host": host_cpu()},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
