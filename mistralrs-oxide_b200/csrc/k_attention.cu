@@ -105,14 +105,6 @@ constexpr int DW_STAGES = 3;                                    // cp.async ring
 constexpr int DW_RS = DA_D * 2 + 16;                            // 272-byte rows: conflict-free ldmatrix
 constexpr int DW_STAGE = 2 * DW_TK * DW_RS;                     // K and V tile of one stage
 constexpr size_t DW_SMEM = (size_t)DW_WARPS * DW_STAGES * DW_STAGE;  // 104,448 B: 2 CTAs per SM
-// 16-byte copy into shared memory with an L2 prefetch-size hint: each warp
-// tile reads whole 256-byte cache rows, so the hint lets L2 fetch them whole.
-__device__ __forceinline__ void cp_async16_l2(void* smem_dst, const void* gsrc) {
-    asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(
-                     (uint32_t)__cvta_generic_to_shared(smem_dst)),
-                 "l"(gsrc)
-                 : "memory");
-}
 constexpr float DW_LOG2E = 1.4426950408889634f;
 constexpr float DW_LN2 = 0.6931471805599453f;
 
@@ -172,8 +164,8 @@ __global__ void __launch_bounds__(DW_WARPS * 32, 2)
             // rows past the last key repeat the last key: finite data that p = 0 multiplies
             const uint32_t src = row < nk ? row : nk - 1;
             const uint64_t off = (uint64_t)(key0 + src) * (DA_D * 2) + ccol;
-            cp_async16_l2(kd + row * DW_RS + ccol, kbase + off);
-            cp_async16_l2(vd + row * DW_RS + ccol, vbase + off);
+            cp_async16(kd + row * DW_RS + ccol, kbase + off);
+            cp_async16(vd + row * DW_RS + ccol, vbase + off);
         }
     };
 #pragma unroll
