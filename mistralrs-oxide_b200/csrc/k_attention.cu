@@ -302,25 +302,25 @@ __global__ void __launch_bounds__(DW_WARPS * 32, 2)
 // ---- f32 caches: per-warp key streams on the CUDA cores ---------------------
 // The split-K and warp-stream structure of the bf16 kernel, with 8-key tiles of
 // f32 rows (512 B, padded to 528 B: conflict-free 16-byte reads) through a
-// private 3-stage cp.async ring per warp.  Scores: lane l holds key l & 7 and
+// private 2-stage cp.async ring per warp (3 CTAs per SM).  Scores: lane l holds key l & 7 and
 // dims 32 (l >> 3) .. + 31, reading the group's query heads from shared memory
 // (a broadcast within each 8-lane phase), and the four dim quarters are summed
 // by shuffles.  P V: lane l owns dims 4 l .. 4 l + 3 of every head's output,
 // each key's probabilities broadcast from its lane by shuffle.  f32 throughout,
 // expf for the exponentials, FMAs for the dot products and P V.
 constexpr int DF_TK = 8;                                         // keys per warp tile
-constexpr int DF_STAGES = 3;
+constexpr int DF_STAGES = 2;
 constexpr int DF_RS = DA_D * 4 + 16;                             // 528-byte rows
 constexpr int DF_RSF = DF_RS / 4;                                // the same in floats
 constexpr int DF_STAGE = 2 * DF_TK * DF_RS;                      // 8448 B: K and V tile
-constexpr size_t DF_RING = (size_t)DW_WARPS * DF_STAGES * DF_STAGE;  // 101,376 B
+constexpr size_t DF_RING = (size_t)DW_WARPS * DF_STAGES * DF_STAGE;  // 67,584 B
 template <int NR>
 constexpr size_t df_smem() {
     return DF_RING + (size_t)NR * DA_D * 4;  // + the group's query heads
 }
 
 template <int NR>
-__global__ void __launch_bounds__(DW_WARPS * 32, 2)
+__global__ void __launch_bounds__(DW_WARPS * 32, 3)
     decode_attn_warp_f32_kernel(const float* q, const float* kc, const float* vc, float* part_ml, float* part_o,
                                 DecArgs p) {
     extern __shared__ __align__(16) unsigned char smem[];
