@@ -121,10 +121,13 @@ __device__ __forceinline__ void norm_store_rms(T* yrow, const T* w, const uint4 
     }
 }
 
-// BIG: one row per CTA of up to 1024 threads; otherwise 256-thread CTAs with
-// a 64-register budget (4 CTAs per SM).
+// BIG: one row per CTA of up to 1024 threads; otherwise 256-thread CTAs with a
+// register budget of 6 CTAs per SM (40 registers) for RMSNorm and 4 (64) for
+// add + RMSNorm, which holds both inputs.  Measured on the C5 rows: RMSNorm bf16
+// 341.8 / 327.0 / 314.6 us at 4 / 5 / 6 CTAs per SM (the few registers spilled
+// at 6 cost less than the rows gained in flight); add + RMSNorm 621 / 660 / 745.
 template <typename T, int VPT, bool ADD, bool BIG>
-__global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : 4)
+__global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : (ADD ? 4 : 6))
     rmsnorm_vec_kernel(const T* x, const T* r, const T* w, T* h, T* y, NormArgs p) {
     constexpr int V = Vec<T>::N;
     __shared__ float red[32];
