@@ -135,7 +135,10 @@ int oxide_silu_bf16(const oxide_bf16* x, oxide_bf16* out, uint64_t n, oxide_stre
 /* out = silu(gate) * up in one pass.  Replaces the pair
  * silu(&gate) then ops::mul(&gated, &up) of MLP::forward
  * (src/layers/attention.rs:144-145).  The bf16 form rounds silu(gate) to
- * bf16 before the multiply, exactly as the composed pair would. */
+ * bf16 before the multiply, as the composed pair would, and rounds the exact
+ * product of the two bf16 values once; the pair's f32 multiply rounds it
+ * twice where that product is an f32 subnormal (|p| < 2^-126), so the two
+ * can differ there by one bf16 ulp. */
 int oxide_silu_mul_f32(const float* gate, const float* up, float* out, uint64_t n,
                        oxide_stream_t stream);
 int oxide_silu_mul_bf16(const oxide_bf16* gate, const oxide_bf16* up, oxide_bf16* out,

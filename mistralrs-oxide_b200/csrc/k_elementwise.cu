@@ -11,6 +11,8 @@
 // so the only traffic is one read of each input and one write of the output.
 // A broadcast operand (e.g. a [cols] row vector) is addressed by a fast
 // modulo on the vector index and stays resident in L1/L2.
+#include <type_traits>
+
 #include "oxide_common.cuh"
 
 namespace oxide {
@@ -63,8 +65,22 @@ __device__ __forceinline__ float2 silu_f2(float2 x) {
     return fmul2(x, f2(__frcp_rn(d.x), __frcp_rn(d.y)));
 }
 
+// bf16x2 product rounded once to bf16 (subnormals kept).
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 template <typename T>
 struct FSiluMul {  // mul(silu(g), u); silu(g) rounded to T as the pair stores it
+    // bf16 words are processed packed: silu of the two gate halves rounded to
+    // bf16 by one paired conversion, then the product with the two up halves
+    // rounded once by mul.rn.bf16x2.  The f32 product of two bf16 values is
+    // exact, so this is the f32 multiply rounded to bf16, except where the
+    // f32 product is subnormal and its own rounding would come first (a
+    // double rounding the single one avoids): within 1 bf16 ulp there.
+    static constexpr bool PACKED = sizeof(T) == 2;
     __device__ __forceinline__ float operator()(float g, float u) const {
         return fmul(Vec<T>::rnd(silu_f(g)), u);
     }
@@ -72,6 +88,20 @@ struct FSiluMul {  // mul(silu(g), u); silu(g) rounded to T as the pair stores i
         const float2 s = silu_f2(g);
         return fmul2(f2(Vec<T>::rnd(s.x), Vec<T>::rnd(s.y)), u);
     }
+    __device__ __forceinline__ uint32_t packed(uint32_t g, uint32_t u) const {
+        const float2 s = silu_f2(f2(__uint_as_float(g << 16), __uint_as_float(g & 0xFFFF0000u)));
+        return mul_bf16x2(pack_bf16x2(s.x, s.y), u);
+    }
+};
+
+// Functors with a packed bf16 form declare PACKED = true.
+template <typename F, typename = void>
+struct HasPacked {
+    static constexpr bool value = false;
+};
+template <typename F>
+struct HasPacked<F, std::void_t<decltype(F::PACKED)>> {
+    static constexpr bool value = F::PACKED;
 };
 
 struct FSilu {
@@ -154,7 +184,11 @@ __global__ void __launch_bounds__(EW_THREADS, ew_min_blocks<T>())
 #pragma unroll
         for (int k = 0; k < EW_UNROLL; ++k) {
             const uint64_t i = base + k * stride;
-            if (i < nvec) {
+            if constexpr (HasPacked<F>::value && NIN == 2) {
+                if (i < nvec)
+                    st_stream(out + i * V, make_uint4(f.packed(va[k].x, vb[k].x), f.packed(va[k].y, vb[k].y),
+                                                      f.packed(va[k].z, vb[k].z), f.packed(va[k].w, vb[k].w)));
+            } else if (i < nvec) {
                 float x[V], y[V], o[V];
                 Vec<T>::unpack(va[k], x);
                 if (NIN == 2) Vec<T>::unpack(vb[k], y);

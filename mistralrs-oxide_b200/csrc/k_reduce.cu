@@ -6,10 +6,10 @@
 // whole-tensor result is f64, because a sequential f32 sum over ~10^8-10^9
 // terms stalls once the running sum's ulp exceeds the terms.
 //
-// Whole-tensor design (deterministic for a given n): stage 1 splits x into
-// at most RED_BLOCKS contiguous slices of whole 16-byte vectors, one CTA per
-// slice; each thread keeps per-lane f32 partials, the CTA combines them in
-// f64 with a fixed tree and writes one f64 partial to the workspace.  Stage 2,
+// Whole-tensor design (deterministic for a given n): stage 1 deals the whole
+// 16-byte vectors of x to at most RED_BLOCKS CTAs in grid-stride order; each
+// thread keeps per-lane f32 partials, the CTA combines them in f64 with a
+// fixed tree and writes one f64 partial to the workspace.  Stage 2,
 // one CTA, combines the partials in a fixed order.  No atomics, no
 // initialised state: the workspace is only ever written before it is read.
 #include "oxide_common.cuh"
@@ -79,29 +79,30 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---- whole-tensor, stage 1 ------------------------------------------------------
+// The grid sweeps the tensor together (vector u to thread u mod the grid's
+// threads), so all CTAs stream neighbouring addresses at any moment; the
+// scalar path below, for unaligned bases, keeps contiguous slices.
 template <typename T, int OP>
 __global__ void __launch_bounds__(RED_THREADS)
-    reduce_stage1_kernel(const T* x, uint64_t n, uint64_t nvec, uint64_t per_block,
-                         double* partial) {
+    reduce_stage1_kernel(const T* x, uint64_t n, uint64_t nvec, double* partial) {
     constexpr int V = Vec<T>::N;
     __shared__ double red[RED_THREADS / 32];
-    const uint64_t lo = (uint64_t)blockIdx.x * per_block;
-    const uint64_t hi = lo + per_block < nvec ? lo + per_block : nvec;
+    const uint64_t stride = (uint64_t)gridDim.x * RED_THREADS;
     float lane[V];
 #pragma unroll
     for (int e = 0; e < V; ++e) lane[e] = red_init<OP>();
     constexpr int UNROLL = 4;
-    for (uint64_t u0 = lo + threadIdx.x; u0 < hi; u0 += RED_THREADS * UNROLL) {
+    for (uint64_t u0 = (uint64_t)blockIdx.x * RED_THREADS + threadIdx.x; u0 < nvec; u0 += stride * UNROLL) {
         uint4 raw[UNROLL];
 #pragma unroll
         for (int k = 0; k < UNROLL; ++k) {
-            const uint64_t u = u0 + (uint64_t)k * RED_THREADS;
-            if (u < hi) raw[k] = ld_stream(x + u * V);
+            const uint64_t u = u0 + (uint64_t)k * stride;
+            if (u < nvec) raw[k] = ld_stream(x + u * V);
         }
 #pragma unroll
         for (int k = 0; k < UNROLL; ++k) {
-            const uint64_t u = u0 + (uint64_t)k * RED_THREADS;
-            if (u < hi) {
+            const uint64_t u = u0 + (uint64_t)k * stride;
+            if (u < nvec) {
                 float f[V];
                 Vec<T>::unpack(raw[k], f);
 #pragma unroll
@@ -163,8 +164,7 @@ static void launch_reduce(const T* x, uint64_t n, double* out, double* partial, 
     if (aligned16(x)) {
         const uint64_t nvec = n / V;
         const uint64_t blocks = stage1_blocks(nvec);
-        const uint64_t per = (nvec + blocks - 1) / blocks;
-        reduce_stage1_kernel<T, OP><<<(unsigned)blocks, RED_THREADS, 0, st>>>(x, n, nvec, per, partial);
+        reduce_stage1_kernel<T, OP><<<(unsigned)blocks, RED_THREADS, 0, st>>>(x, n, nvec, partial);
         reduce_stage2_kernel<OP><<<1, RED_THREADS, 0, st>>>(partial, (int)blocks, out);
     } else {
         const uint64_t blocks = stage1_blocks(n);

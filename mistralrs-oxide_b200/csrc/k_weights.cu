@@ -9,9 +9,11 @@
 // including NaN payloads (quiet bit set, payload kept).  The bf16 entry point
 // stores the decoded values rounded to nearest-even bf16 (exact for BF16).
 //
-// An HBM-bound elementwise pass: 16-byte loads of the source (8 halves or 4
-// floats) when the pointers and the element count allow it, element loads
-// otherwise (safetensors data offsets need not be 16-byte aligned).
+// An HBM-bound elementwise pass: vector loads and stores when the pointers and
+// the element count allow it, element loads otherwise (safetensors data
+// offsets need not be 16-byte aligned).
+#include <cuda_fp16.h>
+
 #include <type_traits>
 
 #include "oxide_common.cuh"
@@ -20,15 +22,14 @@ namespace oxide {
 
 constexpr int WD_THREADS = 256;
 
-// binary16 bits -> f32, exactly as the half crate converts them
+// binary16 bits -> f32, exactly as the half crate converts them: the
+// hardware conversion (exact for every number and infinity, subnormals
+// included), with NaNs rebuilt as the crate builds them (quiet bit set,
+// payload kept) rather than left to the hardware's NaN output.
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
-    const uint32_t sign = (h & 0x8000u) << 16, exp = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
-    if (exp == 0) {
-        if (man == 0) return __uint_as_float(sign);
-        return __uint_as_float(sign | __float_as_uint((float)man * 0x1p-24f));  // subnormal, exact
-    }
-    if (exp == 31) return __uint_as_float(man == 0 ? (sign | 0x7F800000u) : (sign | 0x7FC00000u | (man << 13)));
-    return __uint_as_float(sign | ((exp + 112u) << 23) | (man << 13));
+    const float v = __half2float(__ushort_as_half((unsigned short)h));
+    const uint32_t nan = ((h & 0x8000u) << 16) | 0x7FC00000u | ((h & 0x3FFu) << 13);
+    return (h & 0x7FFFu) > 0x7C00u ? __uint_as_float(nan) : v;
 }
 
 template <int SRC>
@@ -49,39 +50,74 @@ __device__ __forceinline__ void store_one<bf16_t>(bf16_t* out, uint64_t i, float
     out[i] = f32_to_bf16(v);
 }
 
-// 16-byte groups: 4 source elements (F32) or 8 (F16 / BF16) per group
+// Items of E elements, sized so that every warp-wide store is contiguous (a
+// lane's 16 output bytes next to its neighbours'): 2-byte sources decoded to
+// f32 move 4 elements per item (8-byte load, 16-byte store), 2-byte sources to
+// bf16 8 (16 + 16 bytes), f32 sources 4 (16 bytes in, 16 or 8 out).  Each
+// thread has WD_UNROLL item loads in flight before it converts and stores.
+constexpr int WD_UNROLL = 4;
+
+template <int SRC, typename O>
+struct DecodeItem {
+    static constexpr bool HALF = SRC != OXIDE_WDT_F32;
+    static constexpr int E = HALF && sizeof(O) == 2 ? 8 : 4;  // elements per item
+    static constexpr int SB = E * (HALF ? 2 : 4);                // source bytes per item
+};
+
+template <int SRC>
+__device__ __forceinline__ float decode_bits(uint32_t h) {
+    return SRC == OXIDE_WDT_F16 ? f16_bits_to_f32(h) : __uint_as_float(h << 16);
+}
+
+template <int SRC, typename O>
+__device__ __forceinline__ void decode_item(const uint4 w, O* out, uint64_t g) {
+    constexpr int E = DecodeItem<SRC, O>::E;
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+    float v[E];
+    if (SRC == OXIDE_WDT_F32) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = __uint_as_float(wv[k]);
+    } else {
+#pragma unroll
+        for (int k = 0; k < E / 2; ++k) {
+            v[2 * k] = decode_bits<SRC>(wv[k] & 0xFFFFu);
+            v[2 * k + 1] = decode_bits<SRC>(wv[k] >> 16);
+        }
+    }
+    if constexpr (std::is_same<O, float>::value) {
+        st_stream(out + g * 4, make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]), __float_as_uint(v[2]),
+                                          __float_as_uint(v[3])));
+    } else if constexpr (E == 8) {
+        st_stream(out + g * 8, make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                          pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7])));
+    } else {
+        *reinterpret_cast<uint2*>(out + g * 4) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+    }
+}
+
 template <int SRC, typename O>
 __global__ void __launch_bounds__(WD_THREADS)
-    decode_vec_kernel(const unsigned char* src, O* out, uint64_t groups) {
-    constexpr int E = SRC == OXIDE_WDT_F32 ? 4 : 8;
-    for (uint64_t g = (uint64_t)blockIdx.x * WD_THREADS + threadIdx.x; g < groups;
-         g += (uint64_t)gridDim.x * WD_THREADS) {
-        const uint4 w = ld_stream(src + g * 16);
-        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-        float v[E];
+    decode_vec_kernel(const unsigned char* src, O* out, uint64_t items) {
+    constexpr int SB = DecodeItem<SRC, O>::SB;
+    constexpr uint64_t STEP = (uint64_t)WD_THREADS * WD_UNROLL;
+    for (uint64_t g0 = (uint64_t)blockIdx.x * STEP + threadIdx.x; g0 < items; g0 += (uint64_t)gridDim.x * STEP) {
+        uint4 w[WD_UNROLL];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            if (SRC == OXIDE_WDT_F32) {
-                v[k] = __uint_as_float(wv[k]);
-            } else {
-                const uint32_t lo = wv[k] & 0xFFFFu, hi = wv[k] >> 16;
-                v[2 * k] = SRC == OXIDE_WDT_F16 ? f16_bits_to_f32(lo) : __uint_as_float(lo << 16);
-                v[2 * k + 1] = SRC == OXIDE_WDT_F16 ? f16_bits_to_f32(hi) : __uint_as_float(hi << 16);
+        for (int u = 0; u < WD_UNROLL; ++u) {
+            const uint64_t g = g0 + (uint64_t)u * WD_THREADS;
+            if (g < items) {
+                if constexpr (SB == 16) {
+                    w[u] = ld_stream(src + g * 16);
+                } else {
+                    const uint2 h = __ldcs(reinterpret_cast<const uint2*>(src + g * 8));
+                    w[u] = make_uint4(h.x, h.y, 0u, 0u);
+                }
             }
         }
-        if constexpr (std::is_same<O, float>::value) {
 #pragma unroll
-            for (int k = 0; k < E; k += 4)
-                st_stream(out + g * E + k, make_uint4(__float_as_uint(v[k]), __float_as_uint(v[k + 1]),
-                                                      __float_as_uint(v[k + 2]), __float_as_uint(v[k + 3])));
-        } else {
-            if (E == 8) {
-                st_stream(out + g * E, make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
-                                                  pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7])));
-            } else {
-                uint2* o = reinterpret_cast<uint2*>(out + g * E);
-                *o = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
-            }
+        for (int u = 0; u < WD_UNROLL; ++u) {
+            const uint64_t g = g0 + (uint64_t)u * WD_THREADS;
+            if (g < items) decode_item<SRC, O>(w[u], out, g);
         }
     }
 }
@@ -95,14 +131,16 @@ __global__ void __launch_bounds__(WD_THREADS)
 
 template <int SRC, typename O>
 static void launch_decode(const unsigned char* src, O* out, uint64_t n, cudaStream_t st) {
-    constexpr uint64_t E = SRC == OXIDE_WDT_F32 ? 4 : 8;
-    constexpr uint64_t OB = sizeof(O) * E;  // output bytes per group
-    const bool vec = aligned16(src) && (reinterpret_cast<uintptr_t>(out) % (OB < 16 ? OB : 16)) == 0 && n % E == 0;
+    constexpr uint64_t E = DecodeItem<SRC, O>::E, SB = DecodeItem<SRC, O>::SB;
+    constexpr uint64_t OB = sizeof(O) * E;  // output bytes per item
+    const bool vec = reinterpret_cast<uintptr_t>(src) % SB == 0 && reinterpret_cast<uintptr_t>(out) % OB == 0 &&
+                     n % E == 0;
     const uint64_t items = vec ? n / E : n;
     const void* k = vec ? reinterpret_cast<const void*>(decode_vec_kernel<SRC, O>)
                         : reinterpret_cast<const void*>(decode_scalar_kernel<SRC, O>);
     const uint64_t cap = (uint64_t)resident_blocks(k, WD_THREADS, 0);
-    uint64_t grid = (items + WD_THREADS - 1) / WD_THREADS;
+    const uint64_t per = vec ? (uint64_t)WD_THREADS * WD_UNROLL : WD_THREADS;
+    uint64_t grid = (items + per - 1) / per;
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
     if (vec) decode_vec_kernel<SRC, O><<<(unsigned)grid, WD_THREADS, 0, st>>>(src, out, items);

@@ -99,11 +99,13 @@ def test_decode_every_16bit_pattern_matches_oracle(cuda, orc, code):
     from oxide_b200 import _lib
 
     raw = torch.from_numpy(ALL16.view(np.uint8).copy()).to(cuda)
-    for misalign in (0, 2):  # 16-byte vector path, then the element path
+    # aligned vector paths; 8-byte source alignment (the f32 output's 8-byte
+    # loads, the bf16 output's element path); then the element path
+    for misalign, short in ((0, 0), (8, 4), (2, 3)):
         src = torch.empty(raw.numel() + 16, dtype=torch.uint8, device=cuda)
         src[misalign:misalign + raw.numel()] = raw
         ptr = src.data_ptr() + misalign
-        n = 65536 - (3 if misalign else 0)
+        n = 65536 - short
         out = torch.empty(n, dtype=torch.float32, device=cuda)
         _lib.call("oxide_decode_weights_f32", ptr, n, code, out.data_ptr(), 0)
         ref = orc.decode_weights(ALL16[:n].view(np.uint8), code)
