@@ -6,10 +6,12 @@
 // MultiHeadAttention::forward (src/layers/attention.rs:88-94) become one
 // launch.  Tables follow precompute_rope_cache (src/models/mistral.rs:91-115).
 //
-// Design: one CTA per token.  Its threads cover (head, 16-byte chunk of the
-// first half) items of q and then k; each item reads the matching chunk of
-// the second half, the token's cos/sin chunk (shared by all heads of the
-// token, so it is served by L1 after the first head), and writes both halves.
+// Design: one CTA per group of ROPE_TOK tokens.  Its threads cover (head,
+// 16-byte chunk of the first half) items of q and then k, each for every
+// token of the group (all their loads issued first); an item reads the
+// matching chunk of the second half, the token's cos/sin chunk (shared by all
+// heads of the token, so it is served by L1 after the first head), and writes
+// both halves.
 // Arithmetic is f32 with each product and sum rounded separately, as in the
 // reference; bf16 results are rounded once at the store.  A position beyond
 // the table yields NaN for that token instead of an out-of-bounds read.
@@ -36,6 +38,10 @@ __device__ __forceinline__ void rot(float x1, float x2, float c, float s, float&
     o1 = fsub(fmul(x1, c), fmul(x2, s));
     o2 = fadd(fmul(x1, s), fmul(x2, c));
 }
+// Tokens per CTA pass: a thread issues the loads of its item for all of them
+// before it rotates any, so more bytes are in flight per thread.
+constexpr int ROPE_TOK = 2;
+
 template <typename T>
 __global__ void __launch_bounds__(512)
     rope_vec_kernel(const T* q, T* qo, const T* k, T* ko, const float* cos_t, const float* sin_t,
@@ -44,42 +50,56 @@ __global__ void __launch_bounds__(512)
     const uint32_t half = p.head_dim / 2;
     const uint32_t cph = half / V;  // chunks per head
     const uint32_t items = (p.q_heads + (k ? p.k_heads : 0)) * cph;
-    for (uint64_t t = blockIdx.x; t < p.tokens; t += gridDim.x) {
-        const int64_t pr = pos ? (int64_t)pos[t] : (int64_t)t;
-        const bool ok = pr >= 0 && (uint64_t)pr < p.table_rows;
+    for (uint64_t t0 = (uint64_t)blockIdx.x * ROPE_TOK; t0 < p.tokens; t0 += (uint64_t)gridDim.x * ROPE_TOK) {
         for (uint32_t it = threadIdx.x; it < items; it += blockDim.x) {
             const uint32_t hh = p.cph_div.div(it), c = it - hh * cph;
             const bool isq = hh < p.q_heads;
             const uint32_t h = isq ? hh : hh - p.q_heads;
-            const uint64_t base = rope_base(p, t, h, isq ? p.q_heads : p.k_heads) + c * V;
+            const uint32_t heads = isq ? p.q_heads : p.k_heads;
             const T* src = isq ? q : k;
             T* dst = isq ? qo : ko;
-            const uint4 r1 = ld_stream(src + base);
-            const uint4 r2 = ld_stream(src + base + half);
-            float x1[V], x2[V], cs[V], sn[V], o1[V], o2[V];
-            Vec<T>::unpack(r1, x1);
-            Vec<T>::unpack(r2, x2);
-            if (ok) {
-                const float* cp = cos_t + (uint64_t)pr * half + c * V;
-                const float* sp = sin_t + (uint64_t)pr * half + c * V;
+            uint4 r1[ROPE_TOK], r2[ROPE_TOK];
+            int64_t pr[ROPE_TOK];
 #pragma unroll
-                for (int e = 0; e < V; e += 4) {
-                    uint4 cv = ld_keep(cp + e), sv = ld_keep(sp + e);
-                    Vec<float>::unpack(cv, cs + e);
-                    Vec<float>::unpack(sv, sn + e);
+            for (int u = 0; u < ROPE_TOK; ++u) {
+                const uint64_t t = t0 + u;
+                if (t < p.tokens) {
+                    const uint64_t base = rope_base(p, t, h, heads) + c * V;
+                    r1[u] = ld_stream(src + base);
+                    r2[u] = ld_stream(src + base + half);
+                    pr[u] = pos ? (int64_t)pos[t] : (int64_t)t;
                 }
-                // Scalar on purpose: a paired multiply feeding a paired add was
-                // measured to come out fused (one rounding) on sm_100a, which
-                // would break the bit-exact match with the reference's
-                // separately rounded x1*c - x2*s.
-#pragma unroll
-                for (int e = 0; e < V; ++e) rot(x1[e], x2[e], cs[e], sn[e], o1[e], o2[e]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < V; ++e) o1[e] = o2[e] = __int_as_float(0x7fc00000);
             }
-            st_stream(dst + base, Vec<T>::pack(o1));
-            st_stream(dst + base + half, Vec<T>::pack(o2));
+#pragma unroll
+            for (int u = 0; u < ROPE_TOK; ++u) {
+                const uint64_t t = t0 + u;
+                if (t >= p.tokens) break;
+                const uint64_t base = rope_base(p, t, h, heads) + c * V;
+                float x1[V], x2[V], cs[V], sn[V], o1[V], o2[V];
+                Vec<T>::unpack(r1[u], x1);
+                Vec<T>::unpack(r2[u], x2);
+                if (pr[u] >= 0 && (uint64_t)pr[u] < p.table_rows) {
+                    const float* cp = cos_t + (uint64_t)pr[u] * half + c * V;
+                    const float* sp = sin_t + (uint64_t)pr[u] * half + c * V;
+#pragma unroll
+                    for (int e = 0; e < V; e += 4) {
+                        uint4 cv = ld_keep(cp + e), sv = ld_keep(sp + e);
+                        Vec<float>::unpack(cv, cs + e);
+                        Vec<float>::unpack(sv, sn + e);
+                    }
+                    // Scalar on purpose: a paired multiply feeding a paired add was
+                    // measured to come out fused (one rounding) on sm_100a, which
+                    // would break the bit-exact match with the reference's
+                    // separately rounded x1*c - x2*s.
+#pragma unroll
+                    for (int e = 0; e < V; ++e) rot(x1[e], x2[e], cs[e], sn[e], o1[e], o2[e]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < V; ++e) o1[e] = o2[e] = __int_as_float(0x7fc00000);
+                }
+                st_stream(dst + base, Vec<T>::pack(o1));
+                st_stream(dst + base + half, Vec<T>::pack(o2));
+            }
         }
     }
 }
@@ -144,7 +164,8 @@ static int rope_entry(const char* name, const T* q, T* qo, uint64_t qh, const T*
         const uint64_t items = (qh + (k ? kh : 0)) * (half / V);
         uint64_t threads = (items + 31) / 32 * 32;
         if (threads > 512) threads = 256;
-        rope_vec_kernel<T><<<(unsigned)(tokens < cap ? tokens : cap), (unsigned)threads, 0, st>>>(
+        const uint64_t groups = (tokens + ROPE_TOK - 1) / ROPE_TOK;
+        rope_vec_kernel<T><<<(unsigned)(groups < cap ? groups : cap), (unsigned)threads, 0, st>>>(
             q, qo, k, ko, cos_t, sin_t, pos, p);
     } else {
         const uint64_t total = tokens * (qh + (k ? kh : 0)) * half;

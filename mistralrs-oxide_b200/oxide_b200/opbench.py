@@ -140,6 +140,17 @@ def build(op: str, rows: int | None, dev):
         run = lambda s: ops.rope(s[0], s[1], cos, sin, q_out=s[2], k_out=s[3])  # noqa: E731
         nb = 2 * T * (c.q_heads + c.k_heads) * c.head_dim * 2 + 2 * T * (c.head_dim // 2) * 4
         return mk, run, nb, [T, c.q_heads + c.k_heads, c.head_dim]
+    if op == "rope_bf16_c5":
+        # the decoder-layer chain's RoPE: 64 x 2048 tokens in place, positions t mod 2048
+        c = C5()
+        T = rows or c.rows
+        cos, sin = ops.rope_table(c.theta, c.head_dim, c.seq_len)
+        cos, sin = cos.to(dev), sin.to(dev)
+        pos = (torch.arange(T, device=dev, dtype=torch.int32) % c.seq_len).contiguous()
+        mk = lambda: (rn(T, c.q_heads, c.head_dim, dtype=BF16), rn(T, c.k_heads, c.head_dim, dtype=BF16))  # noqa: E731
+        run = lambda s: ops.rope(s[0], s[1], cos, sin, pos, q_out=s[0], k_out=s[1])  # noqa: E731
+        nb = 2 * T * (c.q_heads + c.k_heads) * c.head_dim * 2 + T * 4
+        return mk, run, nb, [T, c.q_heads + c.k_heads, c.head_dim]
     if op in ("gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2"):
         # remaining activations (src/ops/activation.rs) at the C2 MLP shape
         c = C2()
@@ -231,7 +242,7 @@ def build(op: str, rows: int | None, dev):
 
 
 OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softmax_f32_c3",
-       "argmax_f32_c3", "rope_bf16_c4", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
+       "argmax_f32_c3", "rope_bf16_c4", "rope_bf16_c5", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
        "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5",
        "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5",
        "repeat_kv_bf16_c5", "kv_append_bf16_c5", "decode_attn_bf16_c3", "decode_attn_f32_c3",
