@@ -140,6 +140,15 @@ def build(op: str, rows: int | None, dev):
         run = lambda s: ops.rope(s[0], s[1], cos, sin, q_out=s[2], k_out=s[3])  # noqa: E731
         nb = 2 * T * (c.q_heads + c.k_heads) * c.head_dim * 2 + 2 * T * (c.head_dim // 2) * 4
         return mk, run, nb, [T, c.q_heads + c.k_heads, c.head_dim]
+    if op in ("copy_like_c1", "copy_like_c3", "copy_like_argmax_c3"):
+        # the size-matched ceiling of the small configs: a device-to-device copy
+        # (torch copy_) that moves as many bytes as the op's algorithmic count
+        moved = {"copy_like_c1": C1().bytes(), "copy_like_c3": C3().bytes_softmax(C3().inputs()[1]),
+                 "copy_like_argmax_c3": C3().bytes_argmax()}[op]
+        n = moved // 8  # f32 elements read and written
+        mk = lambda: (torch.empty(n, device=dev), torch.empty(n, device=dev))  # noqa: E731
+        run = lambda s: s[1].copy_(s[0])  # noqa: E731
+        return mk, run, 8 * n, [n]
     if op == "rope_bf16_c5":
         # the decoder-layer chain's RoPE: 64 x 2048 tokens in place, positions t mod 2048
         c = C5()
@@ -247,7 +256,8 @@ OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softma
        "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5",
        "repeat_kv_bf16_c5", "kv_append_bf16_c5", "decode_attn_bf16_c3", "decode_attn_f32_c3",
        "softmax_temperature_f32_c3", "sample_topk_f32_c3", "sample_topp_f32_c3",
-       "decode_weights_bf16_f32", "decode_weights_f16_f32"]
+       "decode_weights_bf16_f32", "decode_weights_f16_f32", "copy_like_c1", "copy_like_c3",
+       "copy_like_argmax_c3"]
 
 
 def main(argv=None):
