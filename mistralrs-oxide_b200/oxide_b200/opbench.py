@@ -141,14 +141,30 @@ def build(op: str, rows: int | None, dev):
         nb = 2 * T * (c.q_heads + c.k_heads) * c.head_dim * 2 + 2 * T * (c.head_dim // 2) * 4
         return mk, run, nb, [T, c.q_heads + c.k_heads, c.head_dim]
     if op in ("copy_like_c1", "copy_like_c3", "copy_like_argmax_c3"):
-        # the size-matched ceiling of the small configs: a device-to-device copy
-        # (torch copy_) that moves as many bytes as the op's algorithmic count
+        # the size-matched ceiling of the small configs: this library's own
+        # one-read-one-write elementwise kernel (f32 relu) over as many bytes
+        # as the op's algorithmic count, and torch's device copy of the same
         moved = {"copy_like_c1": C1().bytes(), "copy_like_c3": C3().bytes_softmax(C3().inputs()[1]),
                  "copy_like_argmax_c3": C3().bytes_argmax()}[op]
-        n = moved // 8  # f32 elements read and written
+        n = moved // 8 // 4 * 4  # f32 elements read and written (whole vectors)
+        mk = lambda: (torch.empty(n, device=dev), torch.empty(n, device=dev))  # noqa: E731
+        run = lambda s: ops.unary(_lib.RELU, s[0], out=s[1])  # noqa: E731
+        return mk, run, 8 * n, [n]
+    if op in ("torch_copy_like_c1", "torch_copy_like_c3"):
+        moved = {"torch_copy_like_c1": C1().bytes(), "torch_copy_like_c3": C3().bytes_softmax(C3().inputs()[1])}[op]
+        n = moved // 8 // 4 * 4
         mk = lambda: (torch.empty(n, device=dev), torch.empty(n, device=dev))  # noqa: E731
         run = lambda s: s[1].copy_(s[0])  # noqa: E731
         return mk, run, 8 * n, [n]
+    if op == "add_bf16_c5":
+        # the decoder-layer chain's residual add, [131072 x 4096] bf16
+        c = C5()
+        R = rows or c.rows
+        mk = lambda: (rn(R, c.hidden, dtype=BF16), rn(R, c.hidden, dtype=BF16),  # noqa: E731
+                      torch.empty(R, c.hidden, dtype=BF16, device=dev))
+        run = lambda s: call("oxide_add_bf16", s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(),  # noqa: E731
+                             R * c.hidden, _stream())
+        return mk, run, 3 * R * c.hidden * 2, [R, c.hidden]
     if op == "rope_bf16_c5":
         # the decoder-layer chain's RoPE: 64 x 2048 tokens in place, positions t mod 2048
         c = C5()
@@ -251,13 +267,13 @@ def build(op: str, rows: int | None, dev):
 
 
 OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softmax_f32_c3",
-       "argmax_f32_c3", "rope_bf16_c4", "rope_bf16_c5", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
+       "argmax_f32_c3", "rope_bf16_c4", "rope_bf16_c5", "add_bf16_c5", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
        "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5",
        "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5",
        "repeat_kv_bf16_c5", "kv_append_bf16_c5", "decode_attn_bf16_c3", "decode_attn_f32_c3",
        "softmax_temperature_f32_c3", "sample_topk_f32_c3", "sample_topp_f32_c3",
        "decode_weights_bf16_f32", "decode_weights_f16_f32", "copy_like_c1", "copy_like_c3",
-       "copy_like_argmax_c3"]
+       "copy_like_argmax_c3", "torch_copy_like_c1", "torch_copy_like_c3"]
 
 
 def main(argv=None):

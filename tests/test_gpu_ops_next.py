@@ -289,6 +289,9 @@ def _attn_exact(q, kc, vc, lens, scale):
     (1, 16, 2, 4500, 128, [4321]),        # rep 8, many splits
     (2, 6, 3, 129, 128, None),            # rep 2, no lengths
     (2, 4, 2, 50, 64, [50, 33]),          # head_dim 64: the generic kernel
+    # many short sequences (some empty): with more units than CTAs each CTA of
+    # the balanced bf16 schedule covers several (sequence, kv head) groups
+    (200, 32, 8, 128, 128, [int(x) for x in np.random.default_rng(7).integers(0, 129, 200)]),
 ])
 def test_decode_attention_matches_oracle(cuda, orc, dtype, b, hq, hkv, m, d, lens):
     from oxide_b200 import ops

@@ -475,6 +475,28 @@ def test_rope_in_place_no_positions_no_k(cuda, orc):
     assert_bits_equal(to_np(tq), orc.rope(q, tokens, h, d, 0, cos, sin))
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_rope_vector_path_ragged_group_many_heads_bad_position(cuda, orc, dtype):
+    """The vector kernel with an odd token count (a token group cut short),
+    more (head, chunk) items per token than threads (the item loop), q and k
+    rotated in place, and one position beyond the table (that token NaN)."""
+    from oxide_b200 import ops
+
+    tokens, qh, kh, d = 301, 64, 16, 128
+    cos, sin = orc.rope_table(1e6, d, 400)
+    q, k = rand((tokens, qh, d), 46, dtype, orc=orc), rand((tokens, kh, d), 47, dtype, orc=orc)
+    pos = np.random.default_rng(48).integers(0, 400, tokens).astype(np.int32)
+    pos[tokens - 1] = 400
+    tq, tk = to_dev(q), to_dev(k)
+    ops.rope(tq, tk, to_dev(cos), to_dev(sin), to_dev(pos), q_out=tq, k_out=tk)
+    okpos = np.where(pos == 400, 0, pos)
+    for got, x, h in ((to_np(tq), q, qh), (to_np(tk), k, kh)):
+        ref = orc.rope(x, tokens, h, d, 0, cos, sin, okpos)
+        gf = bf16_to_f32(got) if dtype == "bf16" else got
+        assert np.all(np.isnan(gf[tokens - 1]))
+        assert_bits_equal(got[: tokens - 1], ref[: tokens - 1])
+
+
 def test_apply_rotary_emb_reference_layout(cuda, orc):
     """ops::apply_rotary_emb: x [batch, heads, seq, d] with tables [seq, half]."""
     from oxide_b200 import ops
