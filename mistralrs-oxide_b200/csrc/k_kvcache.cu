@@ -19,27 +19,39 @@ namespace oxide {
 
 constexpr int KV_THREADS = 256;
 
-// One 16-byte vector per iteration: bytes are copied as uint4 regardless of T.
-// Index divisions use precomputed 32-bit multiply-shift division while every
-// vector index fits 32 bits (narrow), 64-bit division otherwise.
+// 16-byte vectors (bytes are copied as uint4 regardless of T), KV_UNROLL
+// loads in flight per thread before their stores.  Index divisions use
+// precomputed 32-bit multiply-shift division while every vector index fits 32
+// bits (narrow), 64-bit division otherwise.
+constexpr int KV_UNROLL = 4;
 __global__ void __launch_bounds__(KV_THREADS)
     repeat_kv_vec_kernel(const uint4* x, uint4* out, uint64_t heads_total, uint32_t vec_per_head,
                          uint32_t kv_heads, uint32_t n_rep, FastDiv vdiv, FastDiv hdiv, bool narrow) {
     const uint64_t n = heads_total * vec_per_head;
-    for (uint64_t i = (uint64_t)blockIdx.x * KV_THREADS + threadIdx.x; i < n;
-         i += (uint64_t)gridDim.x * KV_THREADS) {
-        uint64_t bh, b;
-        if (narrow) {
-            bh = vdiv.div((uint32_t)i);
-            b = hdiv.div((uint32_t)bh);
-        } else {
-            bh = i / vec_per_head;
-            b = bh / kv_heads;
+    const uint64_t stride = (uint64_t)gridDim.x * KV_THREADS;
+    for (uint64_t i0 = (uint64_t)blockIdx.x * KV_THREADS + threadIdx.x; i0 < n; i0 += stride * KV_UNROLL) {
+        uint4 v[KV_UNROLL];
+#pragma unroll
+        for (int u = 0; u < KV_UNROLL; ++u) {
+            const uint64_t i = i0 + u * stride;
+            if (i < n) v[u] = ld_stream(x + i);
         }
-        const uint64_t off = i - bh * vec_per_head, h = bh - b * kv_heads;
-        const uint4 v = ld_stream(x + i);
-        uint4* dst = out + ((b * kv_heads + h) * n_rep) * vec_per_head + off;
-        for (uint32_t r = 0; r < n_rep; ++r) st_stream(dst + (uint64_t)r * vec_per_head, v);
+#pragma unroll
+        for (int u = 0; u < KV_UNROLL; ++u) {
+            const uint64_t i = i0 + u * stride;
+            if (i >= n) break;
+            uint64_t bh, b;
+            if (narrow) {
+                bh = vdiv.div((uint32_t)i);
+                b = hdiv.div((uint32_t)bh);
+            } else {
+                bh = i / vec_per_head;
+                b = bh / kv_heads;
+            }
+            const uint64_t off = i - bh * vec_per_head, h = bh - b * kv_heads;
+            uint4* dst = out + ((b * kv_heads + h) * n_rep) * vec_per_head + off;
+            for (uint32_t r = 0; r < n_rep; ++r) st_stream(dst + (uint64_t)r * vec_per_head, v[u]);
+        }
     }
 }
 

@@ -62,15 +62,28 @@ __global__ void __launch_bounds__(256)
         float acc = red_init<OP>();
         if (row < rows) {
             const T* xr = x + row * cols;
-            for (uint32_t u = t; u < n; u += tpr) {
-                if (VEC) {
-                    float f[Vec<T>::N];
-                    Vec<T>::unpack(ld_stream(xr + (uint64_t)u * Vec<T>::N), f);
+            if (VEC) {
+                // RU loads in flight per thread, accumulated in index order
+                constexpr int RU = 4;
+                for (uint32_t u0 = t; u0 < n; u0 += (uint32_t)tpr * RU) {
+                    uint4 raw[RU];
 #pragma unroll
-                    for (int e = 0; e < Vec<T>::N; ++e) acc = red_step<OP>(acc, f[e]);
-                } else {
-                    acc = red_step<OP>(acc, Vec<T>::load1(xr + u));
+                    for (int k = 0; k < RU; ++k) {
+                        const uint32_t u = u0 + k * tpr;
+                        if (u < n) raw[k] = ld_stream(xr + (uint64_t)u * Vec<T>::N);
+                    }
+#pragma unroll
+                    for (int k = 0; k < RU; ++k) {
+                        if (u0 + k * tpr < n) {
+                            float f[Vec<T>::N];
+                            Vec<T>::unpack(raw[k], f);
+#pragma unroll
+                            for (int e = 0; e < Vec<T>::N; ++e) acc = red_step<OP>(acc, f[e]);
+                        }
+                    }
                 }
+            } else {
+                for (uint32_t u = t; u < n; u += tpr) acc = red_step<OP>(acc, Vec<T>::load1(xr + u));
             }
         }
         acc = group_reduce(acc, red, tpr, OpCombF<OP>());
@@ -91,7 +104,9 @@ __global__ void __launch_bounds__(RED_THREADS)
     float lane[V];
 #pragma unroll
     for (int e = 0; e < V; ++e) lane[e] = red_init<OP>();
-    constexpr int UNROLL = 4;
+    // 8 loads in flight per thread (4: 186.8 us for the bf16 [131072 x 4096] sum
+    // of squares, 8: 151.5 us); the per-lane accumulation order is the same
+    constexpr int UNROLL = 8;
     for (uint64_t u0 = (uint64_t)blockIdx.x * RED_THREADS + threadIdx.x; u0 < nvec; u0 += stride * UNROLL) {
         uint4 raw[UNROLL];
 #pragma unroll

@@ -156,6 +156,15 @@ def build(op: str, rows: int | None, dev):
         mk = lambda: (torch.empty(n, device=dev), torch.empty(n, device=dev))  # noqa: E731
         run = lambda s: s[1].copy_(s[0])  # noqa: E731
         return mk, run, 8 * n, [n]
+    if op == "reduce_rows_sumsq_bf16_c5":
+        # per-row sum of squares (RMSNorm's inner loop as its own op), [131072 x 4096] bf16
+        c = C5()
+        R = rows or c.rows
+        res = torch.empty(R, dtype=torch.float32, device=dev)
+        mk = lambda: (rn(R, c.hidden, dtype=BF16),)  # noqa: E731
+        run = lambda s: call("oxide_reduce_rows_bf16", _lib.RED_SUMSQ, s[0].data_ptr(), R, c.hidden,  # noqa: E731
+                             res.data_ptr(), _stream())
+        return mk, run, R * c.hidden * 2 + R * 4, [R, c.hidden]
     if op == "add_bf16_c5":
         # the decoder-layer chain's residual add, [131072 x 4096] bf16
         c = C5()
@@ -267,7 +276,7 @@ def build(op: str, rows: int | None, dev):
 
 
 OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softmax_f32_c3",
-       "argmax_f32_c3", "rope_bf16_c4", "rope_bf16_c5", "add_bf16_c5", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
+       "argmax_f32_c3", "rope_bf16_c4", "rope_bf16_c5", "add_bf16_c5", "reduce_rows_sumsq_bf16_c5", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
        "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5",
        "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5",
        "repeat_kv_bf16_c5", "kv_append_bf16_c5", "decode_attn_bf16_c3", "decode_attn_f32_c3",
