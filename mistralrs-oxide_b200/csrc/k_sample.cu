@@ -357,6 +357,35 @@ __device__ uint32_t walk_sorted(const unsigned long long* buf, uint32_t n, bool 
 __device__ __forceinline__ float load_logit(const float* x, uint64_t i) { return __ldg(x + i); }
 __device__ __forceinline__ float load_logit(const bf16_t* x, uint64_t i) { return bf16_to_f32(__ldg(x + i)); }
 
+// Logits 4q .. 4q + 3 of the segment into v (0 past seg): one vector load when
+// the segment start is aligned to 4 elements (vx) and the group is whole.
+__device__ __forceinline__ void load_group(const float* x, uint32_t q, uint32_t seg, bool vx, float (&v)[4]) {
+    if (vx && 4 * q + 3 < seg) {
+        const float4 f = __ldg(reinterpret_cast<const float4*>(x) + q);
+        v[0] = f.x;
+        v[1] = f.y;
+        v[2] = f.z;
+        v[3] = f.w;
+        return;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] = 4 * q + c < seg ? load_logit(x, 4 * q + c) : 0.0f;
+}
+__device__ __forceinline__ void load_group(const bf16_t* x, uint32_t q, uint32_t seg, bool vx, float (&v)[4]) {
+    if (vx && 4 * q + 3 < seg) {
+        const uint2 h = __ldg(reinterpret_cast<const uint2*>(x) + q);
+        v[0] = bf16_lo(h.x);
+        v[1] = bf16_hi(h.x);
+        v[2] = bf16_lo(h.y);
+        v[3] = bf16_hi(h.y);
+        return;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] = 4 * q + c < seg ? load_logit(x, 4 * q + c) : 0.0f;
+}
+constexpr int SMP_QB = 8;  // logit groups in flight per thread in the first pass
+static_assert(SMP_GROUPS % (SMP_THREADS * SMP_QB) == 0, "whole batches of groups");
+
 template <typename T, int CL>
 __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -396,22 +425,26 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
         // row max (NaN skipped, as f32::max does) and a NaN flag
         float mx = -INFINITY;
         bool nan = false;
-#pragma unroll 4
-        for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
-            float v[4];
+        const bool vx = (reinterpret_cast<uintptr_t>(x) & (4 * sizeof(T) - 1)) == 0;
+        for (uint32_t q0 = threadIdx.x; q0 < SMP_GROUPS; q0 += SMP_THREADS * SMP_QB) {
+            float v[SMP_QB][4];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) v[c] = 4 * q + c < seg ? load_logit(x, 4 * q + c) : 0.0f;
+            for (int k = 0; k < SMP_QB; ++k) load_group(x, q0 + k * SMP_THREADS, seg, vx, v[k]);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                if (4 * q + c < seg) {
-                    v[c] = div_t(v[c]);
-                    nan |= v[c] != v[c];
-                    mx = fmaxf(mx, v[c]);
-                } else {
-                    v[c] = -INFINITY;
+            for (int k = 0; k < SMP_QB; ++k) {
+                const uint32_t q = q0 + k * SMP_THREADS;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    if (4 * q + c < seg) {
+                        v[k][c] = div_t(v[k][c]);
+                        nan |= v[k][c] != v[k][c];
+                        mx = fmaxf(mx, v[k][c]);
+                    } else {
+                        v[k][c] = -INFINITY;
+                    }
                 }
+                sp4[q] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
             }
-            sp4[q] = make_float4(v[0], v[1], v[2], v[3]);
         }
         const double2 mr = rd.template run<RMAX, RMAX>((double)mx, nan ? 1.0 : 0.0);
         const float m = (float)mr.x;
@@ -433,17 +466,20 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
         const float S = (float)rd.template run<RSUM, RSUM>((double)ls, 0.0).x;
         const RowDiv div_s(S);
         float* prow = a.probs ? a.probs + r * a.vocab + row.base : nullptr;
+        const bool vp = (reinterpret_cast<uintptr_t>(prow) & 15) == 0;
 #pragma unroll 4
         for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
             float4 w = sp4[q];
             float* v = reinterpret_cast<float*>(&w);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                if (4 * q + c < seg) {
-                    v[c] = div_s(v[c]);
-                    if (prow) prow[4 * q + c] = v[c];
+            for (int c = 0; c < 4; ++c) v[c] = 4 * q + c < seg ? div_s(v[c]) : -1.0f;
+            if (prow) {
+                if (vp && 4 * q + 3 < seg) {
+                    reinterpret_cast<float4*>(prow)[q] = w;
                 } else {
-                    v[c] = -1.0f;
+#pragma unroll
+                    for (int c = 0; c < 4; ++c)
+                        if (4 * q + c < seg) prow[4 * q + c] = v[c];
                 }
             }
             sp4[q] = w;

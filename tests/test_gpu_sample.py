@@ -101,8 +101,8 @@ def _softmax_exact(x, t):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("rows,vocab", [(4, 1000), (3, 32000), (2, 32768), (2, 40000), (1, 70000),
-                                        (1, 150000), (1, 262144)])
+@pytest.mark.parametrize("rows,vocab", [(4, 1000), (3, 1001), (3, 32000), (2, 32768), (2, 40000),
+                                        (3, 40003), (1, 70000), (1, 150000), (1, 262144)])
 def test_softmax_with_temperature_matches_oracle(cuda, orc, rows, vocab):
     from oxide_b200 import ops
 
@@ -138,6 +138,7 @@ CASES = [  # (rows, vocab, temperature, top_k, top_p, logit scale)
     (64, 32000, 1.0, 50, 0.9, 0.5),        # top-p with a flat row: a long nucleus
     (64, 32000, 1.3, 50, 0.5, 2.0),
     (16, 1000, 1.0, 7, 1.0, 1.0),
+    (8, 32001, 1.0, 50, 0.9, 2.0),         # rows not 16-byte aligned: element loads and stores
     (8, 70000, 1.0, 50, 0.95, 2.0),        # cluster of 4 CTAs
     (4, 150000, 0.9, 100, 1.0, 3.0),       # cluster of 8
     (4, 262144, 1.0, 50, 0.8, 1.0),
