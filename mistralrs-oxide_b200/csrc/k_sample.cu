@@ -301,22 +301,52 @@ struct Row {
     }
 };
 
-__device__ __forceinline__ void bitonic_desc(unsigned long long* buf, uint32_t n) {
-    for (uint32_t k = 2; k <= n; k <<= 1) {
-        for (uint32_t j = k >> 1; j > 0; j >>= 1) {
-            for (uint32_t i = threadIdx.x; i < n; i += SMP_THREADS) {
-                const uint32_t ixj = i ^ j;
-                if (ixj > i) {
-                    const unsigned long long x = buf[i], y = buf[ixj];
-                    const bool desc = (i & k) == 0;
-                    if (desc ? x < y : x > y) {
-                        buf[i] = y;
-                        buf[ixj] = x;
-                    }
-                }
+// One compare-exchange step (k, j) across shared memory.
+__device__ __forceinline__ void bitonic_step_smem(unsigned long long* buf, uint32_t n, uint32_t k, uint32_t j) {
+    for (uint32_t i = threadIdx.x; i < n; i += SMP_THREADS) {
+        const uint32_t ixj = i ^ j;
+        if (ixj > i) {
+            const unsigned long long x = buf[i], y = buf[ixj];
+            const bool desc = (i & k) == 0;
+            if (desc ? x < y : x > y) {
+                buf[i] = y;
+                buf[ixj] = x;
             }
-            __syncthreads();
         }
+    }
+    __syncthreads();
+}
+// The steps j = j0, j0 / 2, .. 1 of stage k for n >= 32: element i lives in
+// lane i % 32 of its warp, so partners i ^ j (j < 32) are exchanged by shuffle
+// and each element is read and written once.
+__device__ __forceinline__ void bitonic_steps_warp(unsigned long long* buf, uint32_t n, uint32_t k, uint32_t j0) {
+    const uint32_t lane = threadIdx.x & 31u;
+    for (uint32_t base = threadIdx.x & ~31u; base < n; base += SMP_THREADS) {
+        const uint32_t i = base + lane;
+        unsigned long long x = buf[i];
+        const bool desc = (i & k) == 0;
+        for (uint32_t j = j0; j > 0; j >>= 1) {
+            const unsigned long long y = __shfl_xor_sync(0xffffffffu, x, j);
+            // the lower index of a pair keeps the larger key in a descending
+            // block, the smaller in an ascending one; the upper the other
+            const bool take_max = desc == ((lane & j) == 0);
+            x = take_max ? (x > y ? x : y) : (x < y ? x : y);
+        }
+        buf[i] = x;
+    }
+    __syncthreads();
+}
+// Sorts buf[0, n) in descending order, n a power of two.
+__device__ __forceinline__ void bitonic_desc(unsigned long long* buf, uint32_t n) {
+    if (n < 32) {
+        for (uint32_t k = 2; k <= n; k <<= 1)
+            for (uint32_t j = k >> 1; j > 0; j >>= 1) bitonic_step_smem(buf, n, k, j);
+        return;
+    }
+    for (uint32_t k = 2; k <= n; k <<= 1) {
+        uint32_t j = k >> 1;
+        for (; j >= 32; j >>= 1) bitonic_step_smem(buf, n, k, j);
+        bitonic_steps_warp(buf, n, k, j);
     }
 }
 
