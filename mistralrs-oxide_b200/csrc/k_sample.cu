@@ -14,9 +14,11 @@
 // generator; everything after it runs on the device.
 //
 // Design: one CTA per row of up to 32768 logits, or a thread-block cluster of
-// 2-8 CTAs (up to 262144), each CTA holding its contiguous 32768-element
-// segment of the row in shared memory (128 KB, natural order; thread t owns
-// the float4 groups t, t + 512, ...).  No full sort:
+// 2-8 CTAs (up to 262144), each CTA holding a contiguous segment of the row of
+// up to 32768 elements in shared memory (128 KB, natural order; thread t owns
+// the float4 groups t, t + 512, ...).  Rows are split over more CTAs than
+// their length needs when the grid would otherwise leave SMs idle (few rows:
+// one decode step's logits), down to 4096 logits per CTA.  No full sort:
 //   1. softmax_with_temperature with three passes over shared memory and two
 //      block reductions (max, then sum); x / T and e / sum are IEEE quotients;
 //   2. a threshold v whose candidates (every probability >= v) hold the kept
@@ -55,7 +57,6 @@ namespace oxide {
 constexpr int SMP_THREADS = 512;
 constexpr int SMP_WARPS = SMP_THREADS / 32;
 constexpr uint32_t SMP_SPAN = 32768;                      // logits per CTA
-constexpr uint32_t SMP_GROUPS = SMP_SPAN / 4;             // float4 groups per CTA
 constexpr int SMP_GATHER = 2048;                          // candidates walked exactly
 constexpr uint32_t SMP_FALLBACK = 0xFFFFFFFEu;            // the walk needs more than was gathered
 constexpr size_t SMP_SMEM = (size_t)SMP_SPAN * 4 + (size_t)SMP_GATHER * 8;  // 147,456 B
@@ -70,6 +71,7 @@ struct SmpArgs {
     const float* uniforms;
     uint32_t* tokens;  // null: probabilities only
     float* probs;      // null: not stored
+    uint32_t span;     // logits per CTA of a row's cluster: a multiple of 4, <= SMP_SPAN
 };
 
 enum { RSUM = 0, RMAX = 1, RMIN = 2 };
@@ -162,6 +164,7 @@ struct Coarse {
 template <int CL>
 struct Row {
     const float4* sp;  // this CTA's segment, natural order
+    uint32_t ng;       // its float4 groups (span / 4)
     uint32_t base;     // row index of sp[0]
     uint32_t vocab;
     Reducer<CL>* rd;
@@ -172,7 +175,7 @@ struct Row {
         float s = 0.0f;
         uint32_t c = 0;
 #pragma unroll 4
-        for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+        for (uint32_t q = threadIdx.x; q < ng; q += SMP_THREADS) {
             const float4 v = sp[q];
             if (v.x >= x) { s = fadd(s, v.x); ++c; }
             if (v.y >= x) { s = fadd(s, v.y); ++c; }
@@ -186,7 +189,7 @@ struct Row {
     __device__ uint32_t tie_index(float v, double ties, double j) {
         if (ties == 1.0) {
             double mi = 4294967296.0;
-            for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+            for (uint32_t q = threadIdx.x; q < ng; q += SMP_THREADS) {
                 const float4 w = sp[q];
                 const double i0 = (double)(base + 4 * q);
                 if (w.x == v) mi = fmin(mi, i0);
@@ -201,7 +204,7 @@ struct Row {
         while (lo < hi) {
             const uint32_t mid = lo + (hi - lo) / 2;
             uint32_t c = 0;
-            for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+            for (uint32_t q = threadIdx.x; q < ng; q += SMP_THREADS) {
                 const float4 w = sp[q];
                 const uint32_t i0 = base + 4 * q;
                 c += (w.x == v && i0 <= mid) + (w.y == v && i0 + 1 <= mid) + (w.z == v && i0 + 2 <= mid) +
@@ -414,7 +417,6 @@ __device__ __forceinline__ void load_group(const bf16_t* x, uint32_t q, uint32_t
     for (int c = 0; c < 4; ++c) v[c] = 4 * q + c < seg ? load_logit(x, 4 * q + c) : 0.0f;
 }
 constexpr int SMP_QB = 8;  // logit groups in flight per thread in the first pass
-static_assert(SMP_GROUPS % (SMP_THREADS * SMP_QB) == 0, "whole batches of groups");
 
 template <typename T, int CL>
 __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
@@ -443,10 +445,11 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
     };
     Row<CL> row;
     row.sp = sp4;
-    row.base = crank * SMP_SPAN;
+    row.ng = a.span / 4;
+    row.base = crank * a.span;
     row.vocab = a.vocab;
     row.rd = &rd;
-    const uint32_t seg = a.vocab > row.base ? min(a.vocab - row.base, SMP_SPAN) : 0u;  // valid slots
+    const uint32_t seg = a.vocab > row.base ? min(a.vocab - row.base, a.span) : 0u;  // valid slots
     const RowDiv div_t(a.temperature);
     const uint64_t groups = gridDim.x / CL;
     for (uint64_t r = blockIdx.x / CL; r < a.rows; r += groups) {
@@ -456,13 +459,14 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
         float mx = -INFINITY;
         bool nan = false;
         const bool vx = (reinterpret_cast<uintptr_t>(x) & (4 * sizeof(T) - 1)) == 0;
-        for (uint32_t q0 = threadIdx.x; q0 < SMP_GROUPS; q0 += SMP_THREADS * SMP_QB) {
+        for (uint32_t q0 = threadIdx.x; q0 < row.ng; q0 += SMP_THREADS * SMP_QB) {
             float v[SMP_QB][4];
 #pragma unroll
             for (int k = 0; k < SMP_QB; ++k) load_group(x, q0 + k * SMP_THREADS, seg, vx, v[k]);
 #pragma unroll
             for (int k = 0; k < SMP_QB; ++k) {
                 const uint32_t q = q0 + k * SMP_THREADS;
+                if (q >= row.ng) break;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     if (4 * q + c < seg) {
@@ -481,7 +485,7 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
         const bool invalid = mr.y != 0.0 || isinf(m);  // exp(inf - inf) / exp(-inf + inf) is NaN
         float ls = 0.0f;
 #pragma unroll 4
-        for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+        for (uint32_t q = threadIdx.x; q < row.ng; q += SMP_THREADS) {
             float4 w = sp4[q];
             float* v = reinterpret_cast<float*>(&w);
 #pragma unroll
@@ -498,7 +502,7 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
         float* prow = a.probs ? a.probs + r * a.vocab + row.base : nullptr;
         const bool vp = (reinterpret_cast<uintptr_t>(prow) & 15) == 0;
 #pragma unroll 4
-        for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+        for (uint32_t q = threadIdx.x; q < row.ng; q += SMP_THREADS) {
             float4 w = sp4[q];
             float* v = reinterpret_cast<float*>(&w);
 #pragma unroll
@@ -572,7 +576,7 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
             }
             done = false;
             if (short_prefix) {
-                for (uint32_t q = threadIdx.x; q < SMP_GROUPS; q += SMP_THREADS) {
+                for (uint32_t q = threadIdx.x; q < row.ng; q += SMP_THREADS) {
                     const float4 w = sp4[q];
                     const float v[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -665,11 +669,18 @@ static int sample_entry(const char* name, const T* logits, uint64_t rows, uint64
     OXIDE_REQUIRE(logits, name, "null pointer");
     OXIDE_REQUIRE(vocab <= 8ull * SMP_SPAN, name, "vocab must be <= 262144");
     OXIDE_REQUIRE(rows <= UINT64_MAX / vocab, name, "logits size overflows");
+    // the fewest CTAs per row whose segments hold it; then, while the grid
+    // (one CTA per SM: the segment takes 128 KB of shared memory) would leave
+    // SMs idle, split rows over twice as many, down to 4096 logits per CTA
     int cl = 1;
     while ((uint64_t)cl * SMP_SPAN < vocab) cl *= 2;
+    while (cl < 8 && rows * (uint64_t)(2 * cl) <= (uint64_t)sm_count() && vocab / (uint64_t)(2 * cl) >= 4096)
+        cl *= 2;
+    const uint64_t per_cta = (vocab + cl - 1) / cl;
+    const uint32_t span = (uint32_t)((per_cta + 3) / 4 * 4);
     const uint64_t cap = ((uint64_t)1 << 30) / (uint64_t)cl;
     const uint64_t groups = rows < cap ? rows : cap;
-    SmpArgs a{logits, rows, (uint32_t)vocab, temperature, top_k, top_p, uniforms, tokens, probs};
+    SmpArgs a{logits, rows, (uint32_t)vocab, temperature, top_k, top_p, uniforms, tokens, probs, span};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(groups * cl), 1, 1);
     cfg.blockDim = dim3(SMP_THREADS, 1, 1);
