@@ -8,7 +8,8 @@ expf / logf / tanhf / powf replace glibc's (each within 2 ulp of the exact
 value; the reference's chain then rounds the same steps); gelu additionally
 allows 2^-22 |x| absolute where 1 + tanh(..) cancels for x << 0.  bf16 results
 are within one bf16 ulp (gelu: or the same absolute slack).  layer_norm: within
-1e-5 of the exact (f64) value relative to |normalized * w| + |b| and to the
+1e-5 of the exact (f64) value relative to |normalized * w| + |b| +
+|w| * mean|x| / sd (the last term: the conditioning of x - mean) and to the
 reference within that plus the reference's own sequential-sum drift.
 """
 import numpy as np
@@ -123,17 +124,26 @@ def test_unary_argument_errors(cuda):
 
 
 def _ln_scale(x, w, b):
+    """The exact (f64) layer_norm and the magnitude its f32 result is measured
+    against: |n * w| + |b|, plus |w| * mean(|x|) / sd -- the deviation x - mean
+    is formed from an f32 row mean whose rounding is relative to the row's
+    values, not to the deviation, so where x is close to the mean the f32
+    result (the reference's as much as the kernel's) carries that much."""
     x = x.astype(np.float64)
     mean = x.mean(axis=1, keepdims=True)
     sd = np.sqrt(((x - mean) ** 2).mean(axis=1, keepdims=True) + np.float64(F(1e-5)))
     nrm = (x - mean) / sd
-    exact = nrm * w.astype(np.float64) + b.astype(np.float64)
-    return exact, np.abs(nrm * w.astype(np.float64)) + np.abs(b.astype(np.float64))
+    wd = w.astype(np.float64)
+    exact = nrm * wd + b.astype(np.float64)
+    cond = np.abs(wd) * np.abs(x).mean(axis=1, keepdims=True) / sd
+    return exact, np.abs(nrm * wd) + np.abs(b.astype(np.float64)) + cond
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
-@pytest.mark.parametrize("rows,cols", [(3, 1), (8, 33), (16, 768), (4, 4096), (3, 5000), (2, 20000)])
+@pytest.mark.parametrize("rows,cols", [(3, 1), (8, 33), (16, 768), (4, 4096), (3, 5000), (2, 20000),
+                                       # many rows: rows near their mean (x - mean conditioning)
+                                       (20000, 256), (5000, 4096)])
 def test_layer_norm_matches_oracle(cuda, orc, dtype, rows, cols):
     from oxide_b200 import ops
 
