@@ -192,6 +192,17 @@ int oxide_layer_norm_bf16(const oxide_bf16* x, const oxide_bf16* w, const oxide_
                           oxide_bf16* out, uint64_t rows, uint64_t cols, float eps,
                           oxide_stream_t stream);
 
+/* out = layer_norm(x + r) with the same w, b and eps: the fused form of
+ * layer_norm_fused_add_f32 (src/kernels/normalization.rs:123-167), one pass
+ * over x and r.  The sum is rounded to the I/O type before the normalisation
+ * (exact for f32), so the result equals oxide_add_* followed by
+ * oxide_layer_norm_*; the sum itself is not stored.  out may alias x or r. */
+int oxide_add_layer_norm_f32(const float* x, const float* r, const float* w, const float* b, float* out,
+                             uint64_t rows, uint64_t cols, float eps, oxide_stream_t stream);
+int oxide_add_layer_norm_bf16(const oxide_bf16* x, const oxide_bf16* r, const oxide_bf16* w,
+                              const oxide_bf16* b, oxide_bf16* out, uint64_t rows, uint64_t cols, float eps,
+                              oxide_stream_t stream);
+
 /* ---- softmax ---------------------------------------------------------------
  * softmax(x, dim) of a tensor viewed as [outer, dim, inner] (inner = product
  * of the dims after `dim`).  Replaces ops::softmax (src/ops/activation.rs:76-124)

@@ -5,6 +5,11 @@
 // ((x - mean) / std) * w + b) and KernelManager::launch_layer_norm
 // (src/cuda_backend/kernels.rs:334-356).
 //
+// The fused add variant (oxide_add_layer_norm_*) normalises x + r, as the
+// reference's layer_norm_fused_add_f32 (src/kernels/normalization.rs:123-167)
+// intends, with the sum rounded to the I/O type first (exact for f32), so the
+// fused op equals add followed by layer_norm; the sum is not stored.
+//
 // Design: the row layout of the RMSNorm kernels -- a group of `tpr` threads
 // per row (a warp for short rows, 64..256 threads with several rows per
 // 256-thread CTA, or one CTA of up to 1024 threads), the whole row read once
@@ -86,9 +91,9 @@ __device__ __forceinline__ void ln_store(T* yrow, const T* w, const T* b, const 
 
 // 5 CTAs of 256 threads per SM (51 registers): measured 446 us on the C5 rows
 // (bf16) against 457 at 4 and 464 at 6; 15.7 us against 16.4 / 21.3 at C1 (f32).
-template <typename T, int VPT, bool BIG>
-__global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : 5)
-    layernorm_vec_kernel(const T* x, const T* w, const T* b, T* y, LnArgs p) {
+template <typename T, int VPT, bool BIG, bool ADD>
+__global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : (ADD ? 4 : 5))
+    layernorm_vec_kernel(const T* x, const T* r, const T* w, const T* b, T* y, LnArgs p) {
     constexpr int V = Vec<T>::N;
     __shared__ float red[32];
     const int rpc = blockDim.x / p.tpr;
@@ -103,6 +108,26 @@ __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : 5)
         for (int k = 0; k < VPT; ++k) {
             const uint32_t j = t + k * p.tpr;
             if (active && j < nvec) raw[k] = ld_stream(x + off + (uint64_t)j * V);
+        }
+        if (ADD) {  // the row is x + r, rounded to T as the add's output would be
+            uint4 rr[VPT];
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const uint32_t j = t + k * p.tpr;
+                if (active && j < nvec) rr[k] = ld_stream(r + off + (uint64_t)j * V);
+            }
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const uint32_t j = t + k * p.tpr;
+                if (active && j < nvec) {
+                    float u[V], v[V];
+                    Vec<T>::unpack(raw[k], u);
+                    Vec<T>::unpack(rr[k], v);
+#pragma unroll
+                    for (int e = 0; e < V; ++e) u[e] = fadd(u[e], v[e]);
+                    raw[k] = Vec<T>::pack(u);
+                }
+            }
         }
         // pass 1: the mean
         float2 acc = f2(0.0f, 0.0f);
@@ -140,18 +165,23 @@ __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : 5)
 
 // Three-pass fallback: any cols, any alignment; one CTA per row.  The output
 // pass re-reads x with coherent loads, so in-place use is safe.
-template <typename T>
-__global__ void __launch_bounds__(256) layernorm_scalar_kernel(const T* x, const T* w, const T* b, T* y,
-                                                               LnArgs p) {
+template <typename T, bool ADD>
+__global__ void __launch_bounds__(256) layernorm_scalar_kernel(const T* x, const T* r, const T* w, const T* b,
+                                                               T* y, LnArgs p) {
     __shared__ float red[32];
+    // element i of the row: x, or x + r rounded to T
+    auto val = [&](uint64_t i) {
+        const float v = Vec<T>::load1(x + i);
+        return ADD ? Vec<T>::rnd(fadd(v, Vec<T>::load1(r + i))) : v;
+    };
     for (uint64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
         const uint64_t off = row * p.cols;
         float s = 0.0f;
-        for (uint32_t i = threadIdx.x; i < p.cols; i += blockDim.x) s = fadd(s, Vec<T>::load1(x + off + i));
+        for (uint32_t i = threadIdx.x; i < p.cols; i += blockDim.x) s = fadd(s, val(off + i));
         const float mean = fdiv(group_reduce(s, red, (int)blockDim.x, OpAddF()), (float)p.cols);
         float ss = 0.0f;
         for (uint32_t i = threadIdx.x; i < p.cols; i += blockDim.x) {
-            const float d = fsub(Vec<T>::load1(x + off + i), mean);
+            const float d = fsub(val(off + i), mean);
             ss = __fmaf_rn(d, d, ss);
         }
         const float var = fdiv(group_reduce(ss, red, (int)blockDim.x, OpAddF()), (float)p.cols);
@@ -161,10 +191,12 @@ __global__ void __launch_bounds__(256) layernorm_scalar_kernel(const T* x, const
         const float inv = __frcp_rn(sd);
         __syncthreads();  // every thread has read its inputs before any write (in place)
         for (uint32_t i = threadIdx.x; i < p.cols; i += blockDim.x) {
-            const T* q = x + off + i;
-            float v;
-            if (sizeof(T) == 4) v = *reinterpret_cast<const volatile float*>(q);
-            else v = bf16_to_f32(*reinterpret_cast<const volatile uint16_t*>(q));
+            auto vload = [](const T* q) {
+                return sizeof(T) == 4 ? *reinterpret_cast<const volatile float*>(q)
+                                      : bf16_to_f32(*reinterpret_cast<const volatile uint16_t*>(q));
+            };
+            float v = vload(x + off + i);
+            if (ADD) v = Vec<T>::rnd(fadd(v, vload(r + off + i)));
             const float d = fsub(v, mean);
             const float nrm = recip ? fmul(d, inv) : div(d);
             Vec<T>::store1(y + off + i, __fmaf_rn(nrm, Vec<T>::load1(w + i), Vec<T>::load1(b + i)));
@@ -173,40 +205,46 @@ __global__ void __launch_bounds__(256) layernorm_scalar_kernel(const T* x, const
 }
 
 template <typename T, int VPT, bool BIG>
-static void launch_ln_vec(const T* x, const T* w, const T* b, T* y, LnArgs p, cudaStream_t st) {
+static void launch_ln_vec(const T* x, const T* r, const T* w, const T* b, T* y, LnArgs p, cudaStream_t st) {
     const int rpc = p.tpr >= 256 ? 1 : 256 / p.tpr;
     const uint64_t want = (p.rows + rpc - 1) / rpc, cap = (uint64_t)1 << 30;
-    layernorm_vec_kernel<T, VPT, BIG>
-        <<<(unsigned)(want < cap ? want : cap), p.tpr * rpc, 0, st>>>(x, w, b, y, p);
+    const unsigned grid = (unsigned)(want < cap ? want : cap);
+    if (r) layernorm_vec_kernel<T, VPT, BIG, true><<<grid, p.tpr * rpc, 0, st>>>(x, r, w, b, y, p);
+    else layernorm_vec_kernel<T, VPT, BIG, false><<<grid, p.tpr * rpc, 0, st>>>(x, r, w, b, y, p);
 }
 
+// add: layer_norm(x + r); otherwise layer_norm(x) (r unused).
 template <typename T>
-static int ln_entry(const char* name, const T* x, const T* w, const T* b, T* y, uint64_t rows,
-                    uint64_t cols, float eps, cudaStream_t st) {
+static int ln_entry(const char* name, const T* x, bool add, const T* r, const T* w, const T* b, T* y,
+                    uint64_t rows, uint64_t cols, float eps, cudaStream_t st) {
     constexpr int V = Vec<T>::N, VT = LN_VPT;
     OXIDE_INJECT(name);
     if (rows == 0) return OXIDE_OK;
-    OXIDE_REQUIRE(x && w && b && y, name, "null pointer");
+    OXIDE_REQUIRE(x && w && b && y && (!add || r), name, "null pointer");
+    if (!add) r = nullptr;
     OXIDE_REQUIRE(cols >= 1 && cols < (1ull << 31), name, "cols must be in [1, 2^31)");
     OXIDE_REQUIRE(rows <= UINT64_MAX / cols, name, "rows * cols overflows");
     LnArgs p{rows, (uint32_t)cols, 32, eps};
-    const bool vec = cols % V == 0 && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(y);
+    const bool vec = cols % V == 0 && aligned16(x) && aligned16(w) && aligned16(b) && aligned16(y) &&
+                     (!r || aligned16(r));
     const uint64_t nvec = cols / V;
     if (vec && nvec <= 32ull * VT) {  // a warp per row
-        if (nvec <= 32) launch_ln_vec<T, 1, false>(x, w, b, y, p, st);
-        else if (nvec <= 64) launch_ln_vec<T, 2, false>(x, w, b, y, p, st);
-        else launch_ln_vec<T, VT, false>(x, w, b, y, p, st);
+        if (nvec <= 32) launch_ln_vec<T, 1, false>(x, r, w, b, y, p, st);
+        else if (nvec <= 64) launch_ln_vec<T, 2, false>(x, r, w, b, y, p, st);
+        else launch_ln_vec<T, VT, false>(x, r, w, b, y, p, st);
     } else if (vec && nvec <= 256ull * VT) {  // 64..256 threads per row
         uint64_t tpr = 64;
         while (tpr * VT < nvec) tpr *= 2;
         p.tpr = (int)tpr;
-        launch_ln_vec<T, VT, false>(x, w, b, y, p, st);
+        launch_ln_vec<T, VT, false>(x, r, w, b, y, p, st);
     } else if (vec && nvec <= 1024ull * VT) {  // one CTA of up to 1024 threads per row
         p.tpr = (int)(((nvec + VT - 1) / VT + 31) / 32 * 32);
-        launch_ln_vec<T, VT, true>(x, w, b, y, p, st);
+        launch_ln_vec<T, VT, true>(x, r, w, b, y, p, st);
     } else {
         const uint64_t cap = (uint64_t)1 << 30;
-        layernorm_scalar_kernel<T><<<(unsigned)(rows < cap ? rows : cap), 256, 0, st>>>(x, w, b, y, p);
+        const unsigned grid = (unsigned)(rows < cap ? rows : cap);
+        if (r) layernorm_scalar_kernel<T, true><<<grid, 256, 0, st>>>(x, r, w, b, y, p);
+        else layernorm_scalar_kernel<T, false><<<grid, 256, 0, st>>>(x, r, w, b, y, p);
     }
     return check_launch(name);
 }
@@ -219,12 +257,22 @@ extern "C" {
 
 int oxide_layer_norm_f32(const float* x, const float* w, const float* b, float* out, uint64_t rows,
                          uint64_t cols, float eps, oxide_stream_t stream) {
-    return oxide::ln_entry<float>("oxide_layer_norm_f32", x, w, b, out, rows, cols, eps, stream);
+    return oxide::ln_entry<float>("oxide_layer_norm_f32", x, false, nullptr, w, b, out, rows, cols, eps, stream);
 }
 int oxide_layer_norm_bf16(const oxide_bf16* x, const oxide_bf16* w, const oxide_bf16* b,
                           oxide_bf16* out, uint64_t rows, uint64_t cols, float eps,
                           oxide_stream_t stream) {
-    return oxide::ln_entry<bf16_t>("oxide_layer_norm_bf16", x, w, b, out, rows, cols, eps, stream);
+    return oxide::ln_entry<bf16_t>("oxide_layer_norm_bf16", x, false, nullptr, w, b, out, rows, cols, eps, stream);
+}
+int oxide_add_layer_norm_f32(const float* x, const float* r, const float* w, const float* b, float* out,
+                             uint64_t rows, uint64_t cols, float eps, oxide_stream_t stream) {
+    return oxide::ln_entry<float>("oxide_add_layer_norm_f32", x, true, r, w, b, out, rows, cols, eps, stream);
+}
+int oxide_add_layer_norm_bf16(const oxide_bf16* x, const oxide_bf16* r, const oxide_bf16* w,
+                              const oxide_bf16* b, oxide_bf16* out, uint64_t rows, uint64_t cols, float eps,
+                              oxide_stream_t stream) {
+    return oxide::ln_entry<bf16_t>("oxide_add_layer_norm_bf16", x, true, r, w, b, out, rows, cols, eps,
+                                   stream);
 }
 
 }  // extern "C"

@@ -58,6 +58,8 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_tanh_f32": (i32, [vp, vp, u64, vp]),
     "oxide_layer_norm_f32": (i32, [vp, vp, vp, vp, u64, u64, f32, vp]),
     "oxide_layer_norm_bf16": (i32, [vp, vp, vp, vp, u64, u64, f32, vp]),
+    "oxide_add_layer_norm_f32": (i32, [vp, vp, vp, vp, vp, u64, u64, f32, vp]),
+    "oxide_add_layer_norm_bf16": (i32, [vp, vp, vp, vp, vp, u64, u64, f32, vp]),
     "oxide_decode_weights_f32": (i32, [vp, u64, i32, vp, vp]),
     "oxide_decode_weights_bf16": (i32, [vp, u64, i32, vp, vp]),
     "oxide_repeat_kv_f32": (i32, [vp, vp, u64, u64, u64, u64, u64, vp]),

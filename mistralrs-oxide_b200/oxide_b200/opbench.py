@@ -210,6 +210,15 @@ def build(op: str, rows: int | None, dev):
         mk = lambda: (rn(R, c.hidden, dtype=BF16), torch.empty(R, c.hidden, dtype=BF16, device=dev))  # noqa: E731
         run = lambda s: ops.layer_norm(s[0], w, bias, c.eps, out=s[1])  # noqa: E731
         return mk, run, 2 * R * c.hidden * 2 + 2 * c.hidden * 2, [R, c.hidden]
+    if op == "add_layer_norm_bf16_c5":
+        # layer_norm(x + r) at the C5 hidden shape
+        R = rows or c.rows
+        w = torch.ones(c.hidden, dtype=BF16, device=dev)
+        bias = torch.zeros(c.hidden, dtype=BF16, device=dev)
+        mk = lambda: (rn(R, c.hidden, dtype=BF16), rn(R, c.hidden, dtype=BF16),  # noqa: E731
+                      torch.empty(R, c.hidden, dtype=BF16, device=dev))
+        run = lambda s: ops.add_layer_norm(s[0], s[1], w, bias, c.eps, out=s[2])  # noqa: E731
+        return mk, run, 3 * R * c.hidden * 2 + 2 * c.hidden * 2, [R, c.hidden]
     if op == "repeat_kv_bf16_c5":
         # GQA head repetition of the C5 key cache: [64, 8, 2048, 128] -> [64, 32, 2048, 128]
         R = rows or c.seqs
@@ -278,7 +287,7 @@ def build(op: str, rows: int | None, dev):
 OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softmax_f32_c3",
        "argmax_f32_c3", "rope_bf16_c4", "rope_bf16_c5", "add_bf16_c5", "reduce_rows_sumsq_bf16_c5", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
        "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5",
-       "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5",
+       "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5", "add_layer_norm_bf16_c5",
        "repeat_kv_bf16_c5", "kv_append_bf16_c5", "decode_attn_bf16_c3", "decode_attn_f32_c3",
        "softmax_temperature_f32_c3", "sample_topk_f32_c3", "sample_topp_f32_c3",
        "decode_weights_bf16_f32", "decode_weights_f16_f32", "copy_like_c1", "copy_like_c3",

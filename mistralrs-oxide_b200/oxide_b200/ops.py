@@ -196,6 +196,28 @@ def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float,
     return out
 
 
+def add_layer_norm(x: torch.Tensor, r: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """layer_norm(x + r): the fused add + layer_norm of src/kernels/normalization.rs:123-167
+    (the sum rounded to x's dtype first, not stored)."""
+    _check(x, r, w, b, out)
+    if r.shape != x.shape or r.dtype != x.dtype:
+        raise OxideError(_lib.ERR_INVALID_ARG, "add_layer_norm", "residual must match the input's shape and dtype")
+    if x.dim() < 1:
+        raise OxideError(_lib.ERR_INVALID_ARG, "add_layer_norm", "layer_norm requires at least 1D tensor")
+    cols = x.shape[-1]
+    if w.dim() != 1 or w.shape[0] != cols:
+        raise OxideError(_lib.ERR_INVALID_ARG, "add_layer_norm",
+                         f"layer_norm weight shape {list(w.shape)} doesn't match input last dim {cols}")
+    if b.dim() != 1 or b.shape[0] != cols:
+        raise OxideError(_lib.ERR_INVALID_ARG, "add_layer_norm",
+                         f"layer_norm bias shape {list(b.shape)} doesn't match input last dim {cols}")
+    out = torch.empty_like(x) if out is None else out
+    call(f"oxide_add_layer_norm_{_sfx(x)}", _p(x), _p(r), _p(w), _p(b), _p(out), x.numel() // cols, cols,
+         float(eps), _stream())
+    return out
+
+
 def _norm_check(x: torch.Tensor, w: torch.Tensor) -> int:
     if x.dim() < 1:
         raise OxideError(_lib.ERR_INVALID_ARG, "rms_norm", "rms_norm requires at least 1D tensor")

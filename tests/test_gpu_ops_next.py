@@ -15,7 +15,7 @@ reference within that plus the reference's own sequential-sum drift.
 import numpy as np
 import pytest
 
-from _util import bf16_to_f32, misaligned_copy, to_dev, to_np, ulp_bf16, ulp_f32
+from _util import assert_bits_equal, bf16_to_f32, misaligned_copy, to_dev, to_np, ulp_bf16, ulp_f32
 
 F = np.float32
 
@@ -169,6 +169,60 @@ def test_layer_norm_matches_oracle(cuda, orc, dtype, rows, cols):
         gd = np.abs(bf16_to_f32(got).astype(np.float64) - bf16_to_f32(ref))
         ok = (d <= 1) | (gd <= 2.0 ** -8 * scale)  # cancellation in w * n + b
         assert ok.all(), f"max {d.max()} bf16 ulp"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,cols", [(8, 33), (16, 768), (64, 4096), (2, 20000), (5000, 1024)])
+def test_add_layer_norm_matches_oracle_and_unfused(cuda, orc, dtype, rows, cols):
+    """layer_norm(x + r) (the reference's fused-add intent): against the
+    oracle's add then layer_norm, within the layer_norm bar; bit-equal to the
+    device's own add followed by layer_norm (the sum is rounded to the I/O type
+    first); in place over x."""
+    from oxide_b200 import ops
+
+    rng = np.random.default_rng(rows * 104729 + cols)
+    x = (rng.standard_normal((rows, cols)) * 2 + 0.5).astype(F)
+    r = rng.standard_normal((rows, cols)).astype(F)
+    w = rng.uniform(0.5, 1.5, cols).astype(F)
+    b = rng.uniform(-0.5, 0.5, cols).astype(F)
+    if dtype == "bf16":
+        x, r, w, b = (orc.f32_to_bf16(a) for a in (x, r, w, b))
+    tx, tr, tw, tb = to_dev(x), to_dev(r), to_dev(w), to_dev(b)
+    got = to_np(ops.add_layer_norm(tx, tr, tw, tb, 1e-5))
+    h = orc.binary(orc.ADD, x.reshape(-1), r.reshape(-1)).reshape(rows, cols)
+    ref = orc.layer_norm(h, w, b, 1e-5)
+    f = (lambda a: bf16_to_f32(a)) if dtype == "bf16" else (lambda a: a)
+    exact, scale = _ln_scale(f(h), f(w), f(b))
+    if dtype == "f32":
+        g = got.astype(np.float64)
+        lim = 1e-5 * scale + 1e-30
+        assert np.all(np.abs(g - exact) <= lim), "kernel vs exact"
+        assert np.all(np.abs(g - ref) <= lim + np.abs(ref - exact)), "kernel vs reference + its drift"
+    else:
+        d = ulp_bf16(got, ref)
+        gd = np.abs(bf16_to_f32(got).astype(np.float64) - bf16_to_f32(ref))
+        assert np.all((d <= 1) | (gd <= 2.0 ** -8 * scale))
+    unfused = to_np(ops.layer_norm(ops.add(tx, tr), tw, tb, 1e-5))
+    assert_bits_equal(got, unfused)
+    ops.add_layer_norm(tx, tr, tw, tb, 1e-5, out=tx)
+    assert_bits_equal(to_np(tx), got)
+
+
+@pytest.mark.gpu
+def test_add_layer_norm_argument_errors(cuda):
+    import torch
+
+    from oxide_b200 import OxideError, _lib, ops
+
+    x = torch.ones(4, 64, device=cuda)
+    w, b = torch.ones(64, device=cuda), torch.zeros(64, device=cuda)
+    with pytest.raises(OxideError, match="residual"):
+        ops.add_layer_norm(x, x[:, :32].contiguous(), w, b, 1e-5)
+    st = torch.cuda.current_stream().cuda_stream
+    assert _lib.raw("oxide_add_layer_norm_f32", x.data_ptr(), None, w.data_ptr(), b.data_ptr(),
+                    x.data_ptr(), 4, 64, 1e-5, st) == _lib.ERR_INVALID_ARG
+    assert "null pointer" in _lib.last_error()
 
 
 @pytest.mark.gpu
