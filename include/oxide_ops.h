@@ -118,6 +118,15 @@ int oxide_mul_rowbcast_f32(const float* x, const float* s, float* out, uint64_t 
                            uint64_t cols, oxide_stream_t stream);
 int oxide_mul_rowbcast_bf16(const oxide_bf16* x, const oxide_bf16* s, oxide_bf16* out,
                             uint64_t rows, uint64_t cols, oxide_stream_t stream);
+/* out = (a + b) * s[col] over a, b [rows, cols]: the residual add followed by
+ * the row-broadcast multiply (ops::add then ops::mul, matmul.rs:74-108) in one
+ * pass.  The sum is rounded to the I/O type before the multiply, so the result
+ * equals oxide_add_* then oxide_mul_rowbcast_* bit for bit; the sum is not
+ * stored. */
+int oxide_add_mul_rowbcast_f32(const float* a, const float* b, const float* s, float* out, uint64_t rows,
+                               uint64_t cols, oxide_stream_t stream);
+int oxide_add_mul_rowbcast_bf16(const oxide_bf16* a, const oxide_bf16* b, const oxide_bf16* s,
+                                oxide_bf16* out, uint64_t rows, uint64_t cols, oxide_stream_t stream);
 
 /* out = x * scale.  Replaces KernelManager::launch_scale
  * (src/cuda_backend/kernels.rs:159-177; PTX scale_f32 build.rs:240-276). */

@@ -307,6 +307,78 @@ static int rowbcast_entry(const char* name, const T* x, const T* s, T* out, uint
     return ew_dispatch<T, FBin<OXIDE_MUL>, 2>(name, x, n, s, cols, out, n, {}, st);
 }
 
+// ---- (a + b) * s[col]: residual add then row-broadcast multiply in one pass ----
+// The sum is rounded to T before the product (the add's output, exact for
+// f32's own rounding), so the result equals oxide_add_* then
+// oxide_mul_rowbcast_* bit for bit.  Three operands, so not the two-input
+// template: the same persistent grid and vectors in flight per thread.
+template <typename T>
+__global__ void __launch_bounds__(EW_THREADS, ew_min_blocks<T>())
+    add_mul_vec_kernel(const T* a, const T* b, const T* s, T* out, uint64_t nvec, uint64_t nsv, FastDiv sdiv,
+                       bool wide) {
+    constexpr int V = Vec<T>::N;
+    constexpr int U = 4;  // vectors in flight per operand
+    const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
+    for (uint64_t base = (uint64_t)blockIdx.x * EW_THREADS + threadIdx.x; base < nvec; base += stride * U) {
+        uint4 va[U], vb[U], vs[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint64_t i = base + k * stride;
+            if (i < nvec) {
+                const uint64_t is = wide ? i % nsv : sdiv.mod((uint32_t)i);
+                va[k] = ld_stream(a + i * V);
+                vb[k] = ld_stream(b + i * V);
+                vs[k] = ld_keep(s + is * V);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint64_t i = base + k * stride;
+            if (i < nvec) {
+                float x[V], y[V], z[V];
+                Vec<T>::unpack(va[k], x);
+                Vec<T>::unpack(vb[k], y);
+                Vec<T>::unpack(vs[k], z);
+#pragma unroll
+                for (int e = 0; e < V; ++e) x[e] = fmul(Vec<T>::rnd(fadd(x[e], y[e])), z[e]);
+                st_stream(out + i * V, Vec<T>::pack(x));
+            }
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(EW_THREADS)
+    add_mul_scalar_kernel(const T* a, const T* b, const T* s, T* out, uint64_t n, uint64_t cols) {
+    const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
+    for (uint64_t i = (uint64_t)blockIdx.x * EW_THREADS + threadIdx.x; i < n; i += stride) {
+        const float h = Vec<T>::rnd(fadd(Vec<T>::load1(a + i), Vec<T>::load1(b + i)));
+        Vec<T>::store1(out + i, fmul(h, Vec<T>::load1(s + i % cols)));
+    }
+}
+
+template <typename T>
+static int add_mul_entry(const char* name, const T* a, const T* b, const T* s, T* out, uint64_t rows,
+                         uint64_t cols, cudaStream_t st) {
+    constexpr int V = Vec<T>::N;
+    OXIDE_INJECT(name);
+    if (rows == 0 || cols == 0) return OXIDE_OK;
+    OXIDE_REQUIRE(a && b && s && out, name, "null pointer");
+    OXIDE_REQUIRE(rows <= UINT64_MAX / cols, name, "rows * cols overflows");
+    const uint64_t n = rows * cols;
+    if (cols % V == 0 && aligned16(a) && aligned16(b) && aligned16(s) && aligned16(out)) {
+        const uint64_t nvec = n / V, nsv = cols / V;
+        const bool wide = nvec >= 0xffffffffull;
+        auto kern = add_mul_vec_kernel<T>;
+        const int grid = resident_grid(kern, (nvec + 3) / 4);
+        kern<<<grid, EW_THREADS, 0, st>>>(a, b, s, out, nvec, nsv, FastDiv(wide ? 1u : (uint32_t)nsv), wide);
+    } else {
+        auto kern = add_mul_scalar_kernel<T>;
+        kern<<<resident_grid(kern, n), EW_THREADS, 0, st>>>(a, b, s, out, n, cols);
+    }
+    return check_launch(name);
+}
+
 template <typename T, typename F, int NIN>
 static int full_entry(const char* name, const T* a, const T* b, T* out, uint64_t n, F f,
                       cudaStream_t st) {
@@ -420,6 +492,14 @@ int oxide_mul_rowbcast_bf16(const oxide_bf16* x, const oxide_bf16* s, oxide_bf16
                             uint64_t rows, uint64_t cols, oxide_stream_t stream) {
     return oxide::rowbcast_entry<bf16_t>("oxide_mul_rowbcast_bf16", x, s, out, rows, cols,
                                          stream);
+}
+int oxide_add_mul_rowbcast_f32(const float* a, const float* b, const float* s, float* out, uint64_t rows,
+                               uint64_t cols, oxide_stream_t stream) {
+    return oxide::add_mul_entry<float>("oxide_add_mul_rowbcast_f32", a, b, s, out, rows, cols, stream);
+}
+int oxide_add_mul_rowbcast_bf16(const oxide_bf16* a, const oxide_bf16* b, const oxide_bf16* s, oxide_bf16* out,
+                                uint64_t rows, uint64_t cols, oxide_stream_t stream) {
+    return oxide::add_mul_entry<bf16_t>("oxide_add_mul_rowbcast_bf16", a, b, s, out, rows, cols, stream);
 }
 int oxide_scale_f32(const float* x, float* out, float scale, uint64_t n, oxide_stream_t stream) {
     return oxide::full_entry<float, oxide::FScale, 1>("oxide_scale_f32", x, nullptr, out, n,

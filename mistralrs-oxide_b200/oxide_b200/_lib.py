@@ -31,6 +31,8 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_div_f32": (i32, [vp, vp, vp, u64, vp]),
     "oxide_mul_rowbcast_f32": (i32, [vp, vp, vp, u64, u64, vp]),
     "oxide_mul_rowbcast_bf16": (i32, [vp, vp, vp, u64, u64, vp]),
+    "oxide_add_mul_rowbcast_f32": (i32, [vp, vp, vp, vp, u64, u64, vp]),
+    "oxide_add_mul_rowbcast_bf16": (i32, [vp, vp, vp, vp, u64, u64, vp]),
     "oxide_scale_f32": (i32, [vp, vp, f32, u64, vp]),
     "oxide_scale_bf16": (i32, [vp, vp, f32, u64, vp]),
     "oxide_silu_f32": (i32, [vp, vp, u64, vp]),

@@ -66,6 +66,14 @@ def build(op: str, rows: int | None, dev):
         run = lambda s: call("oxide_mul_rowbcast_f32", s[0].data_ptr(), sv.data_ptr(),  # noqa: E731
                              s[1].data_ptr(), R, c.cols, _stream())
         return mk, run, 2 * R * c.cols * 4 + c.cols * 4, [R, c.cols]
+    if op == "add_mul_f32_c2":
+        # (a + b) * s: the C2 residual add and row-broadcast multiply in one pass
+        c = C2()
+        R = rows or c.rows
+        sv = torch.rand(c.cols, generator=g, device=dev) + 0.5
+        mk = lambda: (rn(R, c.cols), rn(R, c.cols), torch.empty(R, c.cols, device=dev))  # noqa: E731
+        run = lambda s: ops.add_mul_rowbcast(s[0], s[1], sv, out=s[2])  # noqa: E731
+        return mk, run, 3 * R * c.cols * 4 + c.cols * 4, [R, c.cols]
     if op == "softmax_f32_c3":
         c = C3()
         _, lens, _ = c.inputs()
@@ -284,7 +292,7 @@ def build(op: str, rows: int | None, dev):
     raise SystemExit(f"unknown op {op}")
 
 
-OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "silu_mul_f32_c2", "softmax_f32_c3",
+OPS = ["rms_norm_f32_c1", "add_f32_c2", "mul_f32_c2", "add_mul_f32_c2", "silu_mul_f32_c2", "softmax_f32_c3",
        "argmax_f32_c3", "rope_bf16_c4", "rope_bf16_c5", "add_bf16_c5", "reduce_rows_sumsq_bf16_c5", "rms_norm_bf16_c5", "add_rms_norm_bf16_c5",
        "softmax_bf16_c5", "silu_mul_bf16_c5", "argmax_bf16_c5", "sumsq_bf16_c5",
        "gelu_f32_c2", "tanh_f32_c2", "relu_f32_c2", "layer_norm_f32_c1", "layer_norm_bf16_c5", "add_layer_norm_bf16_c5",

@@ -94,6 +94,23 @@ def mul_rowbcast(x: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def add_mul_rowbcast(a: torch.Tensor, b: torch.Tensor, s: torch.Tensor,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """(a + b)[rows, cols] * s[cols] in one pass: ops::add then ops::mul with a
+    trailing-dim broadcast (src/ops/matmul.rs:74-108), the sum rounded to a's
+    dtype first and not stored."""
+    _check(a, b, s, out)
+    if b.shape != a.shape or b.dtype != a.dtype or s.dtype != a.dtype:
+        raise OxideError(_lib.ERR_INVALID_ARG, "add_mul_rowbcast", "operands must share shape and dtype")
+    cols = s.numel()
+    if a.dim() < 1 or a.shape[-1] != cols:
+        raise OxideError(_lib.ERR_INVALID_ARG, "add_mul_rowbcast",
+                         f"broadcast operand of {cols} elements doesn't match the last dim of {list(a.shape)}")
+    out = torch.empty_like(a) if out is None else out
+    call(f"oxide_add_mul_rowbcast_{_sfx(a)}", _p(a), _p(b), _p(s), _p(out), a.numel() // cols, cols, _stream())
+    return out
+
+
 def scale(x: torch.Tensor, s: float) -> torch.Tensor:
     """x * s (KernelManager::launch_scale, src/cuda_backend/kernels.rs:159)."""
     _check(x)

@@ -135,6 +135,28 @@ def test_scale(cuda, orc, dtype):
     assert_bits_equal(to_np(got), orc.scale(x, 0.0883883))
 
 
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("rows,cols", [(64, 4096), (7, 33), (3, 8), (1, 100000)])
+def test_add_mul_rowbcast_bit_exact(cuda, orc, dtype, rows, cols):
+    """(a + b) * s[col] in one pass: bit-equal to the oracle's add then
+    row-broadcast mul and to the device's own two ops; cols = 33 takes the
+    element kernel; in place over a."""
+    from oxide_b200 import ops
+
+    a, b = rand((rows, cols), 60, dtype, orc=orc), rand((rows, cols), 61, dtype, orc=orc)
+    sv = np.random.default_rng(62).uniform(0.5, 1.5, cols).astype(F)
+    if dtype == "bf16":
+        sv = orc.f32_to_bf16(sv)
+    ta, tb, ts = to_dev(a), to_dev(b), to_dev(sv)
+    got = to_np(ops.add_mul_rowbcast(ta, tb, ts))
+    h = orc.binary(orc.ADD, a.reshape(-1), b.reshape(-1))
+    ref = orc.binary(orc.MUL, h, sv).reshape(rows, cols)
+    assert_bits_equal(got, ref)
+    assert_bits_equal(got, to_np(ops.mul_rowbcast(ops.add(ta, tb), ts)))
+    ops.add_mul_rowbcast(ta, tb, ts, out=ta)
+    assert_bits_equal(to_np(ta), got)
+
+
 # ---------------------------------------------------------------- activations
 @pytest.mark.parametrize("n", [1, 7, 4096, 1 << 20, (1 << 20) + 3])
 def test_silu_mul_f32(cuda, orc, n):
