@@ -91,6 +91,8 @@ __device__ __forceinline__ void ln_store(T* yrow, const T* w, const T* b, const 
 
 // 5 CTAs of 256 threads per SM (51 registers): measured 446 us on the C5 rows
 // (bf16) against 457 at 4 and 464 at 6; 15.7 us against 16.4 / 21.3 at C1 (f32).
+// The add variant holds both inputs in flight: 4 CTAs per SM, 568 us for the
+// bf16 C5 rows against 602 at 3.
 template <typename T, int VPT, bool BIG, bool ADD>
 __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : (ADD ? 4 : 5))
     layernorm_vec_kernel(const T* x, const T* r, const T* w, const T* b, T* y, LnArgs p) {
