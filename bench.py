@@ -6,25 +6,36 @@ broadcast), o = silu(gate) * up (gate, up [8192, 14336] f32) -- three kernels
 of liboxide_b200.so per step.  Metric: achieved HBM GB/s = algorithmic bytes
 (each input read once, each output written once) / time.
 
-  value     device time (CUDA events), inputs resident in HBM; inputs are
-            1.2 GB per rank, larger than L2, so no flush is needed.
-  e2e       the same step through the host-buffer C ABI (oxide_pipe_*),
-            pinned host inputs copied in and outputs copied back every step.
-  roofline  the dominant kernel (silu_mul): its bytes per launch / its mean
-            CUDA-event launch time, against the measured HBM copy bandwidth.
-  per_op    every other op at its config's shape, timed by CUDA-graph replay
-            over rotating buffer sets larger than L2 (C1, C3, C4) and the full
-            bf16 decoder-layer chain at 64 x 2048 tokens (C5).
+Multi-GPU (torchrun, one rank per GPU): the 8192 token rows are split into
+contiguous blocks, one per rank (strong scaling, no data-path collective);
+every other config is split the same way (C1 rows, C3 rows / batches, C4
+tokens, the C5 chain by sequence, whose global sum of squares ends in one
+NCCL all-reduce of a single f64).  Times are device times (CUDA events on the
+launching stream), max over ranks; GB/s = all ranks' bytes / that time.
 
-Multi-GPU (torchrun, one rank per GPU): every rank runs its own batch (weak
-scaling, no data-path collective); time = max over ranks.
+  value        device time per step, inputs resident in HBM, L2 flushed
+               (256 MiB write) before every timed step.
+  e2e          the same step through the host-buffer C ABI (oxide_pipe_*,
+               deferred so the two ops' copies overlap): pinned host inputs
+               uploaded and outputs downloaded every step, host wall clock.
+               pcie_bound_gbs: the step's bytes over the time of its own
+               uploads and downloads run at once in the same process.
+  roofline     the dominant kernel (silu_mul): bytes per launch / its mean
+               CUDA-event time, against the measured HBM copy bandwidth.
+  parity       the timed step's outputs against the CPU oracle.
+  per_op       every other config at its shape (CUDA-graph replay over
+               rotating buffer sets larger than L2), its host-buffer e2e,
+               and (one GPU) the CPU oracle timed beside it.
+  chain_c5     the bf16 non-GEMM chain of a decoder layer, 64 x 2048 tokens.
 
-`--impl reference` times the reference's CPU arithmetic (the oracle restatement
-of src/ops, compiled C) with all host threads on the same step and metric.
+`--impl reference` times the reference's CPU arithmetic (the oracle
+restatement of src/ops, compiled C) with all host threads on the same step,
+metric and config.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes as C
 import json
 import math
 import os
@@ -43,10 +54,18 @@ METRIC = "achieved HBM GB/s (% of B200 peak) per op at Mistral-7B shapes, 1/2/4/
 UNIT = "GB/s"
 WORKLOAD = "C2 elementwise+broadcast f32: add [8192x4096] + rowbcast mul [4096] + silu*mul [8192x14336]"
 FALLBACK_HBM_GBS = 6650.0
+FLUSH_BYTES = 256 << 20
 
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
+
+
+def bench_config(world: int) -> dict:
+    """The workload description both arms print (identical for one world size)."""
+    return {"workload": WORKLOAD, "rows": 8192, "seed": 1,
+            "partition": f"contiguous token-row blocks over {world} rank(s)",
+            "l2": "flushed (256 MiB write) before every timed step; inputs 1.2 GB in total"}
 
 
 def measured_peak():
@@ -69,6 +88,20 @@ def profiled_traffic(kernel: str):
     except OSError:
         pass
     return None
+
+
+def host_cpu() -> dict:
+    """The box's host: logical CPUs (nproc) and the CPU model."""
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "cpu_model": model}
 
 
 # --------------------------------------------------------------------- clocks
@@ -116,7 +149,7 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------- dist
-def dist_init(n_gpus: int):
+def dist_init():
     import torch
     import torch.distributed as dist
 
@@ -129,6 +162,10 @@ def dist_init(n_gpus: int):
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
+        # Bring every rank's NCCL communicator up before any timing.
+        t = torch.ones(1, device="cuda")
+        dist.all_reduce(t)
+        assert int(t.item()) == world
     else:
         torch.cuda.set_device(0)
     return rank, world, local
@@ -141,19 +178,36 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(x: float, world: int) -> float:
+def reduce_over_ranks(x: float, world: int, op: str = "max") -> float:
     if world == 1:
         return x
     import torch
     import torch.distributed as dist
 
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN,
+                           "sum": dist.ReduceOp.SUM}[op])
     return float(t.item())
 
 
-# --------------------------------------------------------------------- CPU arms
+# --------------------------------------------------------------------- CPU legs
+# The oracle is the reference's src/ops loop bodies restated in C (compiled
+# -O3 -ffp-contract=off); the reference itself is single-threaded, so the
+# baseline is one thread, with an all-threads run (OpenMP over rows, same
+# results) beside it.  Outputs are preallocated; only the compute is timed.
 _CPU_CACHE: dict = {}
+
+
+def cpu_time(fn, budget_s: float, min_reps: int = 2) -> float:
+    """Median seconds of fn() over repetitions filling about budget_s."""
+    fn()  # fault the pages in, warm the caches
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < min_reps:
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times)
 
 
 def cpu_step_sample(rows: int, threads: int):
@@ -166,10 +220,7 @@ def cpu_step_sample(rows: int, threads: int):
         _CPU_CACHE.clear()
         cfg = C2(rows=rows)
         a, b, s, gate, up = cfg.inputs()
-        outs = (np.empty(a.size, np.float32), np.empty(a.size, np.float32),
-                np.empty(gate.size, np.float32))
-        for o in outs:
-            o.fill(0.0)  # fault the pages in before timing
+        outs = (np.zeros(a.size, np.float32), np.zeros(a.size, np.float32), np.zeros(gate.size, np.float32))
         _CPU_CACHE[rows] = (cfg, a, b, s, gate, up, outs)
     cfg, a, b, s, gate, up, (h, y, o) = _CPU_CACHE[rows]
     t0 = time.perf_counter()
@@ -179,37 +230,150 @@ def cpu_step_sample(rows: int, threads: int):
     return time.perf_counter() - t0, cfg.bytes()
 
 
-def host_cpu() -> dict:
-    """The box's host: logical CPUs (nproc) and the CPU model."""
-    model = "unknown"
-    try:
-        with open("/proc/cpuinfo") as f:
-            for line in f:
-                if line.startswith("model name"):
-                    model = line.split(":", 1)[1].strip()
-                    break
-    except OSError:
-        pass
-    return {"nproc": os.cpu_count(), "cpu_model": model}
+def cpu_baseline(budget_s: float = 4.0):
+    """The C2 step through the oracle on the host cores: one thread (the
+    reference's own threading) on a 1024-row sample, and all threads on the
+    whole step."""
+    from oracle import oracle as orc
 
-
-def cpu_baseline(budget_s: float = 12.0):
-    """Single-thread oracle port (the reference is single-threaded) on a
-    bounded sample of the C2 step, repeated for about `budget_s` seconds."""
-    rows = 1024
-    times, nbytes = [], 0
+    rows, times, nbytes = 1024, [], 0
+    cpu_step_sample(rows, 1)
     t_end = time.perf_counter() + budget_s
     while time.perf_counter() < t_end or len(times) < 2:
         dt, nbytes = cpu_step_sample(rows, 1)
         times.append(dt)
     gbs = nbytes / statistics.median(times) / 1e9
+    threads = orc.max_threads()
+    cpu_step_sample(8192, threads)
+    tall = statistics.median([cpu_step_sample(8192, threads)[0] for _ in range(3)])
+    _CPU_CACHE.clear()
+    from oxide_b200.workloads import C2
+
     return {"value": round(gbs, 3), "unit": UNIT, "cores": 1, "kind": "port",
             "sample": f"C2 step on {rows} of 8192 rows, single thread, {len(times)} reps, median",
+            "all_threads": {"value": round(C2().bytes() / tall / 1e9, 3), "cores": threads,
+                            "sample": "C2 step on all 8192 rows, OpenMP over rows, median of 3"},
             "host": host_cpu()}
+
+
+def _bf16(rng, *shape):
+    from oracle import oracle as orc
+
+    return orc.f32_to_bf16(rng.standard_normal(shape, dtype=np.float32)).reshape(shape)
+
+
+def cpu_rate(fn, nbytes: int, elems: int, threads_all: int, budget_s: float = 0.6) -> dict:
+    """GB/s and elements/s of fn(threads) at 1 thread and at all threads."""
+    t1 = cpu_time(lambda: fn(1), budget_s)
+    ta = cpu_time(lambda: fn(threads_all), budget_s / 2)
+    return {"gbs_1t": round(nbytes / t1 / 1e9, 3), "elems_per_s_1t": round(elems / t1, 1),
+            "gbs_all": round(nbytes / ta / 1e9, 3), "elems_per_s_all": round(elems / ta, 1),
+            "threads_all": threads_all}
+
+
+def cpu_per_op() -> dict:
+    """The oracle (the reference's CPU loops) beside every per-op config:
+    same shapes and seeds as the GPU rows (sampled where stated)."""
+    from oracle import oracle as orc
+    from oxide_b200.workloads import C1, C3, C4, NKV
+
+    T = orc.max_threads()
+    res = {}
+    c1 = C1()
+    x, w = c1.inputs()
+    o = np.zeros_like(x)
+    res["rms_norm_f32[C1]"] = dict(cpu_rate(lambda t: orc.rms_norm(x, w, c1.eps, threads=t, out=o), c1.bytes(),
+                                            x.size, T), sample="whole config")
+    c3 = C3()
+    scores, lens, logits = c3.inputs()
+    po = np.zeros_like(scores)
+    res["scale_mask_softmax_f32[C3]"] = dict(cpu_rate(
+        lambda t: orc.scale_mask_softmax(scores, c3.keys, c3.scale, lens=lens, rows_per_len=c3.heads,
+                                         threads=t, out=po), c3.bytes_softmax(lens), scores.size, T),
+        sample="whole config")
+    idx = np.zeros(c3.logit_rows, np.uint32)
+    res["argmax_f32[C3]"] = dict(cpu_rate(lambda t: orc.argmax_rows(logits, c3.vocab, threads=t, out=idx),
+                                          c3.bytes_argmax(), logits.size, T), sample="whole config")
+    c4 = C4()
+    q, k = c4.inputs()
+    cos, sin = orc.rope_table(c4.theta, c4.head_dim, c4.tokens)
+    qo, ko = np.zeros_like(q), np.zeros_like(k)
+
+    def rope(t):
+        orc.rope(q, c4.tokens, c4.q_heads, c4.head_dim, 0, cos, sin, threads=t, out=qo)
+        orc.rope(k, c4.tokens, c4.k_heads, c4.head_dim, 0, cos, sin, threads=t, out=ko)
+    res["rope_bf16[C4]"] = dict(cpu_rate(rope, c4.bytes(), q.size + k.size, T), sample="whole config")
+    # decode attention: batch 0 of C3 (its length) against bf16 caches
+    rng = np.random.default_rng(3)
+    kc, vc = _bf16(rng, 1, NKV, c3.keys, c3.head_dim), _bf16(rng, 1, NKV, c3.keys, c3.head_dim)
+    qd = _bf16(rng, 1, c3.heads, c3.head_dim)
+    l0 = lens[:1].copy()
+    nb = int(l0[0]) * NKV * c3.head_dim * 2 * 2 + 2 * c3.heads * c3.head_dim * 2
+    res["decode_attention_bf16[C3]"] = dict(cpu_rate(
+        lambda t: orc.decode_attention(qd, kc, vc, l0, threads=t), nb, int(l0[0]) * NKV * c3.head_dim, T),
+        sample=f"sequence 0 of 8 (len {int(l0[0])})")
+    u = np.random.default_rng(5).random(c3.logit_rows, dtype=np.float32)
+    lg3 = (logits * np.float32(3)).astype(np.float32)
+    res["sample_topk50_f32[C3]"] = dict(cpu_rate(lambda t: orc.sample(lg3, 1.0, 50, 1.0, u, threads=t),
+                                                 c3.bytes_argmax(), logits.size, T), sample="whole config")
+    return res
+
+
+def cpu_chain_c5() -> dict:
+    """The C5 chain's eight ops through the oracle on a sample of rows of each
+    op (256 token rows; 2 heads x 2048 queries for the causal softmax, so the
+    full causal range is covered); the chain's rate is its full bytes over the
+    sum of each op's full bytes at that op's sampled rate."""
+    from oracle import oracle as orc
+    from oxide_b200.workloads import C5
+
+    c = C5()
+    T, H, I, V = c.seq_len, c.hidden, c.inter, c.vocab
+    rng = np.random.default_rng(c.seed)
+    R = 256
+    x, r, mlp = _bf16(rng, R, H), _bf16(rng, R, H), _bf16(rng, R, H)
+    w = orc.f32_to_bf16(np.ones(H, np.float32))
+    q, k = _bf16(rng, R, c.q_heads, c.head_dim), _bf16(rng, R, c.k_heads, c.head_dim)
+    sc = _bf16(rng, 2 * T, T)
+    gate, up = _bf16(rng, R, I), _bf16(rng, R, I)
+    logits = _bf16(rng, R, V)
+    cos, sin = orc.rope_table(c.theta, c.head_dim, T)
+    pos = (np.arange(R) % T).astype(np.int32)
+    h, y, h2, yf, o = (np.zeros_like(x) for _ in range(5))
+    qo, ko, so, ao = np.zeros_like(q), np.zeros_like(k), np.zeros_like(sc), np.zeros_like(gate)
+    idx = np.zeros(R, np.uint32)
+    full = c.step_bytes()
+    frac_rows = R / c.rows
+    samples = {
+        "add_rms_norm": (lambda t: orc.add_rms_norm(x, r, w, c.eps, threads=t, h=h, y=y), full["add_rms_norm"] * frac_rows),
+        "rope": (lambda t: (orc.rope(q, R, c.q_heads, c.head_dim, 0, cos, sin, pos, threads=t, out=qo),
+                            orc.rope(k, R, c.k_heads, c.head_dim, 0, cos, sin, pos, threads=t, out=ko)),
+                 full["rope"] * frac_rows),
+        "softmax": (lambda t: orc.scale_mask_softmax(sc, T, 1.0 / math.sqrt(c.head_dim), causal_q_len=T, threads=t,
+                                                     out=so), full["softmax"] * 2 / (c.seqs * c.q_heads)),
+        "silu_mul": (lambda t: orc.silu_mul(gate, up, threads=t, out=ao), full["silu_mul"] * frac_rows),
+        "add": (lambda t: orc.binary(0, h, mlp, threads=t, out=h2), full["add"] * frac_rows),
+        "rms_norm": (lambda t: orc.rms_norm(h2, w, c.eps, threads=t, out=yf), full["rms_norm"] * frac_rows),
+        "argmax": (lambda t: orc.argmax_rows(logits, V, threads=t, out=idx), full["argmax"] * frac_rows),
+        "sumsq": (lambda t: orc.reduce(2, yf, threads=t), full["sumsq"] * frac_rows),
+    }
+    T_all = orc.max_threads()
+    ops_out, secs1, secsa = {}, 0.0, 0.0
+    for name, (fn, nbytes) in samples.items():
+        t1 = cpu_time(lambda: fn(1), 0.5)
+        ta = cpu_time(lambda: fn(T_all), 0.25)
+        ops_out[name] = {"gbs_1t": round(nbytes / t1 / 1e9, 3), "gbs_all": round(nbytes / ta / 1e9, 3)}
+        secs1 += full[name] / (nbytes / t1)
+        secsa += full[name] / (nbytes / ta)
+    return {"gbs_1t": round(c.bytes() / secs1 / 1e9, 3), "gbs_all": round(c.bytes() / secsa / 1e9, 3),
+            "ms_per_step_1t": round(secs1 * 1e3, 1), "ms_per_step_all": round(secsa * 1e3, 1),
+            "threads_all": T_all, "ops": ops_out,
+            "sample": "256 token rows per op; causal softmax on 2 heads x 2048 queries; scaled to the full step"}
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     from oracle import oracle as orc
@@ -231,15 +395,13 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample_rows": rows},
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
-                         "kind": "port",
+        "ms_per_step": round(total / args.steps * 1e3 * 8192 / rows, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": bench_config(world),
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"C2 step on {rows} of 8192 rows per step, {threads} OpenMP threads",
                          "host": host_cpu()},
-        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -279,136 +441,236 @@ def rotating_sets(bytes_per_set: int):
     """Enough buffer sets to cycle through more than twice the L2 size."""
     import torch
 
-    l2 = getattr(torch.cuda.get_device_properties(0), "L2_cache_size", 126 << 20)
+    l2 = getattr(torch.cuda.get_device_properties(torch.cuda.current_device()), "L2_cache_size", 126 << 20)
     return max(2, math.ceil(2.5 * l2 / max(1, bytes_per_set)))
 
 
-def per_op_lines(peak):
-    """Per-op GB/s at the C1/C3/C4 shapes (CUDA-graph replay, rotating inputs)."""
+def host_seconds(fn, reps=3):
+    """Median host wall time of fn() (fn returns after its results are in host memory)."""
+    fn()
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts)
+
+
+class Pipe:
+    """A host-buffer pipeline (oxide_pipe_*) on this rank's device."""
+
+    def __init__(self, device: int, chunk_bytes=16 << 20, depth=4):
+        from oxide_b200._lib import call
+
+        self.h = C.c_void_p()
+        call("oxide_pipe_create", device, chunk_bytes, depth, C.byref(self.h))
+
+    def __call__(self, name, *args):
+        from oxide_b200._lib import call
+
+        call(name, self.h, *args)
+
+    def close(self):
+        from oxide_b200._lib import call
+
+        call("oxide_pipe_destroy", self.h)
+
+
+def pinned(a: np.ndarray):
+    import torch
+
+    if a.dtype == np.uint16:
+        return torch.from_numpy(a.view(np.int16)).pin_memory()
+    return torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+
+
+def per_op_lines(peak, rank, world, local, pipe):
+    """Per-op GB/s at the C1/C3/C4 shapes (CUDA-graph replay, rotating inputs),
+    each config's rows split across the ranks; plus each op's host-buffer e2e."""
     import torch
 
     from oxide_b200 import ops
-    from oxide_b200.workloads import C1, C3, C4
+    from oxide_b200._lib import call
+    from oxide_b200.dist import row_range
+    from oxide_b200.workloads import C1, C3, C4, NKV
 
-    dev = torch.device("cuda")
+    dev = torch.device("cuda", local)
     res = {}
 
-    def rec(name, nbytes, secs, shape):
-        gbs = nbytes / secs / 1e9
-        res[name] = {"gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4),
-                     "us_per_launch": round(secs * 1e6, 2), "bytes": nbytes, "shape": shape}
+    def stream():
+        return torch.cuda.current_stream().cuda_stream
 
-    # C1 RMSNorm f32
+    def rec(name, nbytes_rank, secs, shape, elems_rank, e2e_secs=None, h2d=0, d2h=0):
+        secs_max = reduce_over_ranks(secs, world)
+        total = reduce_over_ranks(float(nbytes_rank), world, "sum")
+        elems = reduce_over_ranks(float(elems_rank), world, "sum")
+        gbs = total / secs_max / 1e9
+        r = {"gbs": round(gbs, 1), "frac_of_peak": round(gbs / (world * peak), 4),
+             "us_per_launch": round(secs_max * 1e6, 2),
+             "elems_per_s": round(elems / secs_max, 1), "bytes": int(total), "shape": shape}
+        if e2e_secs is not None:
+            e_max = reduce_over_ranks(e2e_secs, world)
+            r["e2e"] = {"gbs": round(total / e_max / 1e9, 2), "ms": round(e_max * 1e3, 3),
+                        "h2d_bytes": int(reduce_over_ranks(float(h2d), world, "sum")),
+                        "d2h_bytes": int(reduce_over_ranks(float(d2h), world, "sum")),
+                        "api": "oxide_pipe_* (pinned host buffers)"}
+        res[name] = r
+        barrier(world)
+
+    # C1 RMSNorm f32 over this rank's rows
     c1 = C1()
     x, w = c1.inputs()
-    nset = rotating_sets(c1.bytes())
-    xs = [torch.from_numpy(x).to(dev) for _ in range(nset)]
+    lo, hi = row_range(c1.rows, rank, world)
+    xr = np.ascontiguousarray(x[lo:hi])
+    nb = 2 * xr.size * 4 + w.size * 4
+    nset = rotating_sets(nb)
+    xs = [torch.from_numpy(xr).to(dev) for _ in range(nset)]
     outs = [torch.empty_like(xs[0]) for _ in range(nset)]
     tw = torch.from_numpy(w).to(dev)
     fns = [(lambda i=i: ops.rms_norm(xs[i], tw, c1.eps, out=outs[i])) for i in range(nset)]
-    rec("rms_norm_f32[C1]", c1.bytes(), graph_time_per_launch(fns), "[2048,4096]")
+    secs = graph_time_per_launch(fns)
+    px, pw, po = pinned(xr), pinned(w), pinned(np.zeros_like(xr))
+    e2e = host_seconds(lambda: pipe("oxide_pipe_rms_norm_f32", px.data_ptr(), pw.data_ptr(), po.data_ptr(),
+                                    hi - lo, c1.cols, c1.eps))
+    rec("rms_norm_f32[C1]", nb, secs, "[2048,4096]", xr.size, e2e, xr.size * 4 + w.size * 4, xr.size * 4)
     del xs, outs
 
-    # C3 masked decode softmax f32 + argmax
+    # C3 masked decode softmax f32 (rows = batch x heads; a rank takes whole
+    # sequences' rows when the world divides the batch) + argmax
     c3 = C3()
     scores, lens, logits = c3.inputs()
-    sb = c3.bytes_softmax(lens)
-    nset = rotating_sets(c3.bytes_softmax_full())
-    ss = [torch.from_numpy(scores).to(dev) for _ in range(nset)]
-    po = [torch.empty_like(ss[0]) for _ in range(nset)]
-    tl = torch.from_numpy(lens).to(dev)
-    fns = [(lambda i=i: ops.scale_mask_softmax(ss[i], c3.scale, lens=tl, rows_per_len=c3.heads,
-                                               out=po[i])) for i in range(nset)]
-    rec("scale_mask_softmax_f32[C3]", sb, graph_time_per_launch(fns), "[8,32,1,32768] lens-masked")
-    del ss, po
-    nset = rotating_sets(c3.bytes_argmax())
-    ls = [torch.from_numpy(logits).to(dev) for _ in range(nset)]
-    idx = torch.empty(c3.logit_rows, dtype=torch.int32, device=dev)
-    from oxide_b200._lib import call
-
-    fns = [(lambda i=i: call("oxide_argmax_rows_f32", ls[i].data_ptr(), c3.logit_rows, c3.vocab,
-                             idx.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    rows3 = c3.batch * c3.heads
+    lo, hi = row_range(rows3, rank, world)
+    s2 = scores.reshape(rows3, c3.keys)[lo:hi]
+    sr = np.ascontiguousarray(s2)
+    # lengths of this block: one per sequence when the block holds whole
+    # sequences (every world size that divides 8), else one per row
+    if lo % c3.heads == 0 and (hi - lo) % c3.heads == 0:
+        rpl, lr = c3.heads, np.ascontiguousarray(lens[lo // c3.heads:hi // c3.heads]).astype(np.int32)
+    else:
+        rpl, lr = 1, np.ascontiguousarray(lens[np.arange(lo, hi) // c3.heads]).astype(np.int32)
+    valid = int(np.sum(np.minimum(lr, c3.keys))) * rpl
+    nb = valid * 4 + sr.size * 4 + lr.size * 4
+    nset = rotating_sets(2 * sr.size * 4)
+    ss = [torch.from_numpy(sr).to(dev) for _ in range(nset)]
+    po3 = [torch.empty_like(ss[0]) for _ in range(nset)]
+    tl = torch.from_numpy(lr).to(dev)
+    fns = [(lambda i=i: ops.scale_mask_softmax(ss[i], c3.scale, lens=tl, rows_per_len=rpl, out=po3[i]))
            for i in range(nset)]
-    rec("argmax_f32[C3]", c3.bytes_argmax(), graph_time_per_launch(fns), "[64,32000]")
+    secs = graph_time_per_launch(fns)
+    ps, pl, pso = pinned(sr), pinned(lr), pinned(np.zeros_like(sr))
+    e2e = host_seconds(lambda: pipe("oxide_pipe_scale_mask_softmax_f32", ps.data_ptr(), pso.data_ptr(), hi - lo,
+                                    c3.keys, c3.scale, None, 0, pl.data_ptr(), rpl, 0))
+    h2d = valid * 4 + lr.size * 4
+    rec("scale_mask_softmax_f32[C3]", nb, secs, "[8,32,1,32768] lens-masked", sr.size, e2e, h2d, sr.size * 4)
+    del ss, po3
+
+    lo, hi = row_range(c3.logit_rows, rank, world)
+    lg = np.ascontiguousarray(logits[lo:hi])
+    nb = lg.size * 4 + (hi - lo) * 4
+    nset = rotating_sets(nb)
+    ls = [torch.from_numpy(lg).to(dev) for _ in range(nset)]
+    idx = torch.empty(hi - lo, dtype=torch.int32, device=dev)
+    fns = [(lambda i=i: call("oxide_argmax_rows_f32", ls[i].data_ptr(), hi - lo, c3.vocab, idx.data_ptr(), stream()))
+           for i in range(nset)]
+    secs = graph_time_per_launch(fns)
+    plg, pidx = pinned(lg), pinned(np.zeros(hi - lo, np.int32))
+    e2e = host_seconds(lambda: pipe("oxide_pipe_argmax_rows_f32", plg.data_ptr(), hi - lo, c3.vocab,
+                                    pidx.data_ptr()), reps=10)
+    rec("argmax_f32[C3]", nb, secs, "[64,32000]", lg.size, e2e, lg.size * 4, (hi - lo) * 4)
     del ls
 
-    # C4 RoPE bf16
+    # C4 RoPE bf16 over this rank's tokens (positions = global token index)
     c4 = C4()
     q, k = c4.inputs()
+    lo, hi = row_range(c4.tokens, rank, world)
+    qr, kr = np.ascontiguousarray(q[lo:hi]), np.ascontiguousarray(k[lo:hi])
     cos, sin = ops.rope_table(c4.theta, c4.head_dim, c4.tokens)
     tc, tsn = cos.to(dev), sin.to(dev)
-    nset = rotating_sets(c4.bytes())
-    qs = [torch.from_numpy(q.view(np.int16)).to(dev).view(torch.bfloat16) for _ in range(nset)]
-    ks = [torch.from_numpy(k.view(np.int16)).to(dev).view(torch.bfloat16) for _ in range(nset)]
+    pos = torch.arange(lo, hi, dtype=torch.int32)
+    tpos = pos.to(dev)
+    nb = 2 * (qr.size + kr.size) * 2 + 2 * (hi - lo) * (c4.head_dim // 2) * 4
+    nset = rotating_sets(nb)
+    qs = [torch.from_numpy(qr.view(np.int16)).to(dev).view(torch.bfloat16) for _ in range(nset)]
+    ks = [torch.from_numpy(kr.view(np.int16)).to(dev).view(torch.bfloat16) for _ in range(nset)]
     qo = [torch.empty_like(qs[0]) for _ in range(nset)]
     ko = [torch.empty_like(ks[0]) for _ in range(nset)]
-    fns = [(lambda i=i: ops.rope(qs[i], ks[i], tc, tsn, q_out=qo[i], k_out=ko[i]))
-           for i in range(nset)]
-    rec("rope_bf16[C4]", c4.bytes(), graph_time_per_launch(fns), "q[4096,32,128] k[4096,8,128]")
+    fns = [(lambda i=i: ops.rope(qs[i], ks[i], tc, tsn, tpos, q_out=qo[i], k_out=ko[i])) for i in range(nset)]
+    secs = graph_time_per_launch(fns)
+    pq, pk, pqo, pko = pinned(qr), pinned(kr), pinned(np.zeros_like(qr)), pinned(np.zeros_like(kr))
+    pc, psn, ppos = cos.pin_memory(), sin.pin_memory(), pos.pin_memory()
+    e2e = host_seconds(lambda: pipe("oxide_pipe_rope_bf16", pq.data_ptr(), pqo.data_ptr(), c4.q_heads,
+                                    pk.data_ptr(), pko.data_ptr(), c4.k_heads, pc.data_ptr(), psn.data_ptr(),
+                                    c4.tokens, ppos.data_ptr(), hi - lo, c4.head_dim))
+    rec("rope_bf16[C4]", nb, secs, "q[4096,32,128] k[4096,8,128]", qr.size + kr.size, e2e,
+        (qr.size + kr.size) * 2 + 2 * cos.numel() * 4 + (hi - lo) * 4, (qr.size + kr.size) * 2)
     del qs, ks, qo, ko
 
     # C3 decode step of attention over bf16 KV caches (q [8,32,128], caches
-    # [8,8,32768,128], the C3 lengths) and token sampling over the C3 logits
-    from oxide_b200.workloads import NKV
-
-    g = torch.Generator(device=dev).manual_seed(3)
-    nb = int(np.sum(np.minimum(lens, c3.keys))) * NKV * c3.head_dim * 2 * 2 + 2 * c3.batch * c3.heads * c3.head_dim * 2
+    # [8,8,32768,128], the C3 lengths; sequences split across ranks) and token
+    # sampling over the C3 logits (rows split across ranks)
+    lo, hi = row_range(c3.batch, rank, world)
+    nbat = hi - lo
+    g = torch.Generator(device=dev).manual_seed(3 + rank)
+    lens_r = np.ascontiguousarray(lens[lo:hi])
+    nb = int(np.sum(np.minimum(lens_r, c3.keys))) * NKV * c3.head_dim * 2 * 2 + 2 * nbat * c3.heads * c3.head_dim * 2
     nset = rotating_sets(nb)
-    kvs = [(torch.randn(c3.batch, NKV, c3.keys, c3.head_dim, generator=g, device=dev).to(torch.bfloat16),
-            torch.randn(c3.batch, NKV, c3.keys, c3.head_dim, generator=g, device=dev).to(torch.bfloat16))
+    kvs = [(torch.randn(nbat, NKV, c3.keys, c3.head_dim, generator=g, device=dev).to(torch.bfloat16),
+            torch.randn(nbat, NKV, c3.keys, c3.head_dim, generator=g, device=dev).to(torch.bfloat16))
            for _ in range(nset)]
-    qd = torch.randn(c3.batch, c3.heads, c3.head_dim, generator=g, device=dev).to(torch.bfloat16)
+    qd = torch.randn(nbat, c3.heads, c3.head_dim, generator=g, device=dev).to(torch.bfloat16)
     od = torch.empty_like(qd)
-    ws = torch.empty(int(ops._lib.lib().oxide_decode_attention_workspace_bytes(c3.batch, c3.heads, c3.keys,
+    tlr = torch.from_numpy(lens_r).to(dev)
+    ws = torch.empty(int(ops._lib.lib().oxide_decode_attention_workspace_bytes(nbat, c3.heads, c3.keys,
                                                                                 c3.head_dim)),
                      dtype=torch.uint8, device=dev)
-    fns = [(lambda i=i: ops.decode_attention(qd, kvs[i][0], kvs[i][1], tl, workspace=ws, out=od))
+    fns = [(lambda i=i: ops.decode_attention(qd, kvs[i][0], kvs[i][1], tlr, workspace=ws, out=od))
            for i in range(nset)]
-    rec("decode_attention_bf16[C3]", nb, graph_time_per_launch(fns), "q[8,32,128] kv[8,8,32768,128] lens")
+    rec("decode_attention_bf16[C3]", nb, graph_time_per_launch(fns), "q[8,32,128] kv[8,8,32768,128] lens",
+        int(np.sum(np.minimum(lens_r, c3.keys))) * NKV * c3.head_dim)
     del kvs
-    nset = rotating_sets(c3.bytes_argmax())
-    ls = [torch.from_numpy(logits).to(dev) * 3 for _ in range(nset)]
-    u = torch.rand(c3.logit_rows, generator=g, device=dev)
+    lo, hi = row_range(c3.logit_rows, rank, world)
+    nb = (hi - lo) * c3.vocab * 4 + (hi - lo) * 4
+    nset = rotating_sets(nb)
+    ls = [torch.from_numpy(np.ascontiguousarray(logits[lo:hi])).to(dev) * 3 for _ in range(nset)]
+    u = torch.rand(hi - lo, generator=g, device=dev)
     fns = [(lambda i=i: ops.sample_next_token(ls[i], u, 1.0, 50, 1.0)) for i in range(nset)]
-    rec("sample_topk50_f32[C3]", c3.bytes_argmax(), graph_time_per_launch(fns), "[64,32000] T=1 top-k 50")
+    rec("sample_topk50_f32[C3]", nb, graph_time_per_launch(fns), "[64,32000] T=1 top-k 50", (hi - lo) * c3.vocab)
     del ls
     torch.cuda.empty_cache()
     return res
 
 
-def chain_c5(peak, world, steps=3, warmup=2):
-    """Full bf16 non-GEMM chain of a decoder layer at 64 x 2048 tokens (C5)."""
+def chain_c5(peak, rank, world, local, steps=3, warmup=2):
+    """Full bf16 non-GEMM chain of a decoder layer at 64 x 2048 tokens (C5):
+    the 64 sequences are split into contiguous blocks across the ranks; the
+    global sum of squares of the final hidden state combines the ranks' f64
+    partials with one NCCL all-reduce inside the timed region."""
     import torch
 
     from oxide_b200 import ops
-    from oxide_b200.dist import combine_partial
+    from oxide_b200._lib import call
+    from oxide_b200.dist import combine_partial, row_range
     from oxide_b200.workloads import C5
 
     c = C5()
-    dev = torch.device("cuda")
-    g = torch.Generator(device=dev)
-    g.manual_seed(c.seed)
-    R, H, I, T = c.rows, c.hidden, c.inter, c.seq_len
-    bf = torch.bfloat16
-
-    def randn(*shape):
-        return torch.randn(shape, generator=g, device=dev, dtype=bf)
-
-    x, r = randn(R, H), randn(R, H)
-    w = torch.ones(H, dtype=bf, device=dev)
-    q, k = randn(R, c.q_heads, c.head_dim), randn(R, c.k_heads, c.head_dim)
-    scores = randn(c.seqs * c.q_heads * T, T)
+    dev = torch.device("cuda", local)
+    s_lo, s_hi = row_range(c.seqs, rank, world)
+    d = c.device_inputs(s_lo, s_hi, dev)
+    T = c.seq_len
+    R = (s_hi - s_lo) * T
+    H = c.hidden
+    x, r, w, q, k = d["x"], d["r"], d["w"], d["q"], d["k"]
+    scores, gate, up, mlp, logits = d["scores"], d["gate"], d["up"], d["mlp"], d["logits"]
     probs = torch.empty_like(scores)
-    gate, up = randn(R, I), randn(R, I)
     act = torch.empty_like(gate)
-    mlp = randn(R, H)
-    logits = randn(R, c.vocab)
     h, y, h2, yf = (torch.empty_like(x) for _ in range(4))
     cos, sin = ops.rope_table(c.theta, c.head_dim, T)
     cos, sin = cos.to(dev), sin.to(dev)
     pos = (torch.arange(R, device=dev, dtype=torch.int32) % T).contiguous()
     ws = torch.empty(ops.workspace_bytes(R * H), dtype=torch.uint8, device=dev)
     ssq = torch.empty((), dtype=torch.float64, device=dev)
+    idx = torch.empty(R, dtype=torch.int32, device=dev)
     scale = 1.0 / math.sqrt(c.head_dim)
     names = ["add_rms_norm", "rope", "softmax", "silu_mul", "add", "rms_norm", "argmax", "sumsq"]
 
@@ -416,6 +678,7 @@ def chain_c5(peak, world, steps=3, warmup=2):
         def mark(i):
             if ev is not None:
                 ev[i].record()
+        st = torch.cuda.current_stream().cuda_stream
         mark(0)
         ops.add_rms_norm(x, r, w, c.eps, h=h, y=y)
         mark(1)
@@ -425,19 +688,16 @@ def chain_c5(peak, world, steps=3, warmup=2):
         mark(3)
         ops.silu_mul(gate, up, out=act)
         mark(4)
-        from oxide_b200._lib import call
-        st = torch.cuda.current_stream().cuda_stream
         call("oxide_add_bf16", h.data_ptr(), mlp.data_ptr(), h2.data_ptr(), R * H, st)
         mark(5)
         ops.rms_norm(h2, w, c.eps, out=yf)
         mark(6)
-        idx = ops.argmax(logits)
+        call("oxide_argmax_rows_bf16", logits.data_ptr(), R, c.vocab, idx.data_ptr(), st)
         mark(7)
         ops.reduce(yf, 2, workspace=ws, out=ssq)
         if world > 1:  # the one cross-GPU exchange: this rank's f64 partial
             combine_partial(ssq, 2)
         mark(8)
-        return idx
 
     for _ in range(warmup):
         step()
@@ -446,57 +706,91 @@ def chain_c5(peak, world, steps=3, warmup=2):
     total = 0.0
     for _ in range(steps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(9)]
+        barrier(world)
+        torch.cuda.synchronize()
         step(ev)
         torch.cuda.synchronize()
         for i, n in enumerate(names):
             per[n] += ev[i].elapsed_time(ev[i + 1]) / 1e3
         total += ev[0].elapsed_time(ev[8]) / 1e3
+    t_max = reduce_over_ranks(total / steps, world)
     sb = c.step_bytes()
-    out = {"ms_per_step": round(total / steps * 1e3, 3),
-           "gbs": round(c.bytes() / (total / steps) / 1e9, 1),
-           "frac_of_peak": round(c.bytes() / (total / steps) / 1e9 / peak, 4),
-           "bytes_per_step": c.bytes(), "ops": {}}
+    gbs = c.bytes() / t_max / 1e9
+    out = {"ms_per_step": round(t_max * 1e3, 3), "gbs": round(gbs, 1), "frac_of_peak": round(gbs / world / peak, 4),
+           "bytes_per_step": c.bytes(), "seqs_per_rank": f"{s_hi - s_lo} of {c.seqs}", "ops": {}}
     for n in names:
-        secs = per[n] / steps
-        out["ops"][n] = {"gbs": round(sb[n] / secs / 1e9, 1),
-                         "frac_of_peak": round(sb[n] / secs / 1e9 / peak, 4),
-                         "ms": round(secs * 1e3, 4)}
-    del x, r, q, k, scores, probs, gate, up, act, mlp, logits, h, y, h2, yf
+        secs = reduce_over_ranks(per[n] / steps, world)
+        g = sb[n] / secs / 1e9
+        out["ops"][n] = {"gbs": round(g, 1), "frac_of_peak": round(g / world / peak, 4), "ms": round(secs * 1e3, 4)}
+    del d, x, r, q, k, scores, probs, gate, up, act, mlp, logits, h, y, h2, yf
     torch.cuda.empty_cache()
+    return out
+
+
+def step_parity(a, b, s, gate, up, th, ty, to, world):
+    """The timed step's outputs against the oracle on this rank's rows:
+    add and row-broadcast mul bit-exact; silu*up within its ulp bar."""
+    from oracle import oracle as orc
+
+    threads = max(1, (os.cpu_count() or 1) // world)
+    rh = orc.binary(0, a, b, threads=threads)
+    ry = orc.binary(2, rh, s, n=rh.size, threads=threads)
+    ro = orc.silu_mul(gate, up, threads=threads)
+    gh, gy, go = (t.cpu().numpy().reshape(-1) for t in (th, ty, to))
+
+    def ulps(x, r):
+        xi, ri = x.view(np.int32).astype(np.int64), r.view(np.int32).astype(np.int64)
+        xi = np.where(xi < 0, -(xi & 0x7FFFFFFF), xi)
+        ri = np.where(ri < 0, -(ri & 0x7FFFFFFF), ri)
+        return np.abs(xi - ri)
+
+    out = {}
+    for name, g, r in (("add", gh, rh), ("mul_rowbcast", gy, ry), ("silu_mul", go, ro)):
+        u = ulps(g, r.reshape(-1))
+        mx = reduce_over_ranks(float(u.max(initial=0)), world, "max")
+        ex = reduce_over_ranks(float(np.mean(u == 0)), world, "min")
+        out[name] = {"max_ulp": int(mx), "bit_exact_frac": round(ex, 6)}
+    out["bar"] = "add, mul bit-exact; silu_mul f32 <= stated ulp bar (tests/_util.py SILU_F32_ULP)"
+    out["ok"] = out["add"]["max_ulp"] == 0 and out["mul_rowbcast"]["max_ulp"] == 0
     return out
 
 
 def run_oxide(args):
     import torch
 
-    from oxide_b200 import _lib, ops
+    from oxide_b200 import _lib
+    from oxide_b200.dist import row_range
     from oxide_b200.workloads import C2
 
-    rank, world, local = dist_init(args.gpus)
+    rank, world, local = dist_init()
     _lib.lib()
     peak, peak_kind = measured_peak()
     dev = torch.device("cuda", local)
     cfg = C2()
     a, b, s, gate, up = cfg.inputs()
+    lo, hi = row_range(cfg.rows, rank, world)
+    a, b, gate, up = (np.ascontiguousarray(v[lo:hi]) for v in (a, b, gate, up))
+    rows, cols = hi - lo, cfg.cols
+    rank_bytes = C2(rows=rows).bytes()
     ta, tb, ts = (torch.from_numpy(v).to(dev) for v in (a, b, s))
     tg, tu = torch.from_numpy(gate).to(dev), torch.from_numpy(up).to(dev)
     th, ty, to = torch.empty_like(ta), torch.empty_like(ta), torch.empty_like(tg)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     st = torch.cuda.current_stream()
-    rows, cols = cfg.rows, cfg.cols
 
-    def step(ev=None, k=0):
+    def step(ev=None):
         sp = st.cuda_stream
         if ev is not None:
-            ev[k][0].record()
+            ev[0].record()
         _lib.call("oxide_add_f32", ta.data_ptr(), tb.data_ptr(), th.data_ptr(), rows * cols, sp)
         if ev is not None:
-            ev[k][1].record()
+            ev[1].record()
         _lib.call("oxide_mul_rowbcast_f32", th.data_ptr(), ts.data_ptr(), ty.data_ptr(), rows, cols, sp)
         if ev is not None:
-            ev[k][2].record()
+            ev[2].record()
         _lib.call("oxide_silu_mul_f32", tg.data_ptr(), tu.data_ptr(), to.data_ptr(), tg.numel(), sp)
         if ev is not None:
-            ev[k][3].record()
+            ev[3].record()
 
     for _ in range(args.warmup):
         step()
@@ -517,39 +811,31 @@ def run_oxide(args):
     barrier(world)
     torch.cuda.synchronize()
     for k in range(args.steps):
-        step(ev, k)
+        flush.fill_(k & 0xFF)  # evict the previous step's data from L2 (not timed)
+        step(ev[k])
     torch.cuda.synchronize()
     barrier(world)
     clocks = sampler.stop()
-    total = ev[0][0].elapsed_time(ev[-1][3]) / 1e3
+    total = sum(e[0].elapsed_time(e[3]) for e in ev) / 1e3
     t_add = sum(e[0].elapsed_time(e[1]) for e in ev) / 1e3 / args.steps
     t_mul = sum(e[1].elapsed_time(e[2]) for e in ev) / 1e3 / args.steps
     t_sm = sum(e[2].elapsed_time(e[3]) for e in ev) / 1e3 / args.steps
-    total_max = max_over_ranks(total, world)
-    value = world * cfg.bytes() * args.steps / total_max / 1e9
+    total_max = reduce_over_ranks(total, world)
+    value = cfg.bytes() * args.steps / total_max / 1e9
     ms_per_step = total_max / args.steps * 1e3
+    parity = step_parity(a, b, s, gate, up, th, ty, to, world)
 
     # ---- e2e through the host-buffer C ABI ----
-    import ctypes as C
-
-    pa = torch.from_numpy(a).pin_memory()
-    pb = torch.from_numpy(b).pin_memory()
-    ps = torch.from_numpy(s).pin_memory()
-    pg = torch.from_numpy(gate).pin_memory()
-    pu = torch.from_numpy(up).pin_memory()
-    ph = torch.empty_like(pa).pin_memory()
-    py = torch.empty_like(pa).pin_memory()
-    po = torch.empty_like(pg).pin_memory()
-    pipe = C.c_void_p()
-    _lib.call("oxide_pipe_create", local, 16 << 20, 4, C.byref(pipe))
+    pa, pb, ps, pg, pu = (pinned(v) for v in (a, b, s, gate, up))
+    ph, py, po = (torch.empty_like(t).pin_memory() for t in (pa, pa, pg))
+    pipe = Pipe(local)
+    _lib.call("oxide_pipe_defer", pipe.h, 1)
 
     def e2e_step():
-        _lib.call("oxide_pipe_binary_f32", pipe, 0, pa.data_ptr(), pa.numel(), pb.data_ptr(),
-                  pb.numel(), ph.data_ptr(), pa.numel())
-        _lib.call("oxide_pipe_binary_f32", pipe, 2, ph.data_ptr(), ph.numel(), ps.data_ptr(),
-                  ps.numel(), py.data_ptr(), ph.numel())
-        _lib.call("oxide_pipe_silu_mul_f32", pipe, pg.data_ptr(), pu.data_ptr(), po.data_ptr(),
-                  pg.numel())
+        pipe("oxide_pipe_add_mul_rowbcast_f32", pa.data_ptr(), pb.data_ptr(), ps.data_ptr(), ph.data_ptr(),
+             py.data_ptr(), rows, cols)
+        pipe("oxide_pipe_silu_mul_f32", pg.data_ptr(), pu.data_ptr(), po.data_ptr(), pg.numel())
+        _lib.call("oxide_pipe_sync", pipe.h)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -557,38 +843,74 @@ def run_oxide(args):
     t0 = time.perf_counter()
     for _ in range(args.steps):
         e2e_step()
-    e2e_secs = max_over_ranks(time.perf_counter() - t0, world)
+    e2e_secs = reduce_over_ranks(time.perf_counter() - t0, world)
     barrier(world)
-    _lib.call("oxide_pipe_destroy", pipe)
-    e2e_ok = bool(np.array_equal(po.numpy().reshape(-1), to.cpu().numpy().reshape(-1)) and
-                  np.array_equal(py.numpy().reshape(-1), ty.cpu().numpy().reshape(-1)))
-    h2d = 4 * (a.size + b.size + a.size + s.size + gate.size + up.size)
-    d2h = 4 * (a.size + a.size + gate.size)
-    e2e_value = world * cfg.bytes() * args.steps / e2e_secs / 1e9
+    _lib.call("oxide_pipe_defer", pipe.h, 0)
+    e2e_ok = bool(torch.equal(po.view(-1), to.cpu().view(-1)) and torch.equal(py.view(-1), ty.cpu().view(-1))
+                  and torch.equal(ph.view(-1), th.cpu().view(-1)))
+    h2d = 4 * (a.size + b.size + s.size + gate.size + up.size)
+    d2h = 4 * (2 * a.size + gate.size)
+    e2e_value = cfg.bytes() * args.steps / e2e_secs / 1e9
 
-    sm_bytes = cfg.bytes_silu_mul()
+    # PCIe bound measured here: the step's own uploads and downloads (same
+    # buffers, same byte counts) issued alone and at once on two streams.
+    s_up, s_down = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def up_copies():
+        with torch.cuda.stream(s_up):
+            for dst, src in ((ta, pa), (tb, pb), (ts, ps), (tg, pg), (tu, pu)):
+                dst.copy_(src, non_blocking=True)
+
+    def down_copies():
+        with torch.cuda.stream(s_down):
+            for dst, src in ((ph, th), (py, ty), (po, to)):
+                dst.copy_(src, non_blocking=True)
+
+    def timed(fn):
+        best = float("inf")
+        for _ in range(3):
+            barrier(world)
+            torch.cuda.synchronize()
+            t1 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize()
+            best = min(best, time.perf_counter() - t1)
+        return reduce_over_ranks(best, world)
+
+    t_up, t_down = timed(up_copies), timed(down_copies)
+    t_both = timed(lambda: (up_copies(), down_copies()))
+    total_h2d = reduce_over_ranks(float(h2d), world, "sum")
+    total_d2h = reduce_over_ranks(float(d2h), world, "sum")
+    bound = cfg.bytes() / t_both / 1e9
+    pcie = {"h2d_gbs": round(total_h2d / t_up / 1e9, 2), "d2h_gbs": round(total_d2h / t_down / 1e9, 2),
+            "both_gbs": round((total_h2d + total_d2h) / t_both / 1e9, 2)}
+
+    sm_bytes = C2(rows=rows).bytes_silu_mul()
     achieved = sm_bytes / t_sm / 1e9
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (numpy PCG64 seed 1, N(0,1) / U(0.5,1.5))",
-        "config": {"workload": WORKLOAD, "bytes_per_step_per_gpu": cfg.bytes(),
-                   "l2": "inputs (1.2 GB per rank) larger than L2; no flush",
-                   "parallelism": f"rows: one batch per rank x{world} (weak)"},
+        "config": bench_config(world),
         "frac_of_peak": round(value / world / peak, 4),
-        "per_kernel_gbs": {"add": round(cfg.bytes_add() / t_add / 1e9, 1),
-                           "mul_rowbcast": round(cfg.bytes_mul() / t_mul / 1e9, 1),
+        "rows_per_rank": rows,
+        "per_kernel_gbs": {"add": round(C2(rows=rows).bytes_add() / t_add / 1e9, 1),
+                           "mul_rowbcast": round(C2(rows=rows).bytes_mul() / t_mul / 1e9, 1),
                            "silu_mul": round(achieved, 1)},
         "roofline": {"bound": "hbm", "kernel": "ew_vec_kernel<silu_mul f32>",
                      "achieved": round(achieved, 1), "peak": peak,
                      "peak_kind": f"{peak_kind} HBM copy GB/s", "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": profiled_traffic("silu_mul_f32_c2"),
+                     "frac": round(achieved / peak, 4),
+                     "traffic": profiled_traffic("silu_mul_f32_c2") if world == 1 else None,
                      "algorithmic_bytes_per_launch": sm_bytes},
-        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "api": "oxide_pipe_* (host buffers, pinned)",
-                "timing": "host wall clock around synchronous calls, max over ranks",
-                "output_matches_device": e2e_ok},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                "h2d_bytes_per_step": int(total_h2d), "d2h_bytes_per_step": int(total_d2h),
+                "api": "oxide_pipe_add_mul_rowbcast_f32 + oxide_pipe_silu_mul_f32, deferred, one sync per step",
+                "timing": "host wall clock over the timed steps, max over ranks",
+                "pcie_bound_gbs": round(bound, 2), "frac_of_pcie_bound": round(e2e_value / bound, 4),
+                "pcie": pcie, "output_matches_device": e2e_ok},
+        "parity": parity,
         "gpu_launches": 3 * args.steps,
         "clocks": clocks,
     }
@@ -596,13 +918,24 @@ def run_oxide(args):
         line["cpu_baseline"] = cpu_baseline()
     if not args.no_extras:
         try:
-            line["per_op"] = per_op_lines(peak)  # every rank: keeps the ranks in step for chain_c5
+            line["per_op"] = per_op_lines(peak, rank, world, local, pipe)
         except Exception as e:  # keep the headline line; report the failure
             line["per_op"] = {"error": repr(e)}
         try:
-            line["chain_c5"] = chain_c5(peak, world)
+            line["chain_c5"] = chain_c5(peak, rank, world, local)
         except Exception as e:
             line["chain_c5"] = {"error": repr(e)}
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            try:
+                cpu = cpu_per_op()
+                for name, v in cpu.items():
+                    if isinstance(line["per_op"].get(name), dict):
+                        line["per_op"][name]["cpu"] = v
+                if "ms_per_step" in line["chain_c5"]:
+                    line["chain_c5"]["cpu"] = cpu_chain_c5()
+            except Exception as e:
+                line["cpu_per_op_error"] = repr(e)
+    pipe.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -122,7 +122,8 @@ int oxide_mul_rowbcast_bf16(const oxide_bf16* x, const oxide_bf16* s, oxide_bf16
  * the row-broadcast multiply (ops::add then ops::mul, matmul.rs:74-108) in one
  * pass.  The sum is rounded to the I/O type before the multiply, so the result
  * equals oxide_add_* then oxide_mul_rowbcast_* bit for bit; the sum is not
- * stored. */
+ * stored.  out may alias a or b (in place); it must not overlap s, which
+ * every row reads again. */
 int oxide_add_mul_rowbcast_f32(const float* a, const float* b, const float* s, float* out, uint64_t rows,
                                uint64_t cols, oxide_stream_t stream);
 int oxide_add_mul_rowbcast_bf16(const oxide_bf16* a, const oxide_bf16* b, const oxide_bf16* s,
@@ -403,6 +404,9 @@ int oxide_reduce_bf16(int op, const oxide_bf16* x, uint64_t n, double* out, void
  * First call on a device: looks up the array's device address with the
  * calling thread's current device (cudaGetSymbolAddress), which may load the
  * library's device code; make that first call outside any stream capture.
+ * The address is kept per CUDA context, so the first call after a
+ * cudaDeviceReset (a new context) repeats the lookup and the same rule
+ * applies to it.
  * Concurrency: all calls on one device share the one array, so two calls
  * that can overlap on the GPU (different streams without an ordering event
  * between them) race and return wrong results.  Order them on one stream, or
@@ -434,6 +438,50 @@ int oxide_pipe_silu_mul_f32(oxide_pipe_t pipe, const float* gate_host, const flo
                             float* out_host, uint64_t n);
 int oxide_pipe_rms_norm_f32(oxide_pipe_t pipe, const float* x_host, const float* w_host,
                             float* out_host, uint64_t rows, uint64_t cols, float eps);
+
+/* Deferred mode (on != 0): the op calls below return once their copies and
+ * kernels are enqueued, so one op's uploads overlap the previous op's
+ * downloads; oxide_pipe_sync waits for everything enqueued.  Host buffers must
+ * stay valid, and outputs unread, until then.  Turning deferred mode off waits
+ * as oxide_pipe_sync does.  A failing call still waits before returning. */
+int oxide_pipe_defer(oxide_pipe_t pipe, int on);
+int oxide_pipe_sync(oxide_pipe_t pipe);
+
+/* h = a + b and y = h * s[col] (ops::add then the row-broadcast ops::mul,
+ * src/ops/matmul.rs:74-108) from one upload of a, b and s: h is downloaded as
+ * the next residual and not uploaded again for the multiply.  Results equal
+ * oxide_add_f32 then oxide_mul_rowbcast_f32. */
+int oxide_pipe_add_mul_rowbcast_f32(oxide_pipe_t pipe, const float* a_host, const float* b_host,
+                                    const float* s_host, float* h_host, float* y_host, uint64_t rows,
+                                    uint64_t cols);
+/* oxide_add_rms_norm_* on host rows (src/layers/transformer.rs:64-67). */
+int oxide_pipe_add_rms_norm_f32(oxide_pipe_t pipe, const float* x_host, const float* r_host,
+                                const float* w_host, float* h_host, float* y_host, uint64_t rows,
+                                uint64_t cols, float eps);
+int oxide_pipe_add_rms_norm_bf16(oxide_pipe_t pipe, const oxide_bf16* x_host, const oxide_bf16* r_host,
+                                 const oxide_bf16* w_host, oxide_bf16* h_host, oxide_bf16* y_host,
+                                 uint64_t rows, uint64_t cols, float eps);
+/* oxide_scale_mask_softmax_f32 on host rows (src/ops/attention.rs:41,60,63-79;
+ * ops::softmax src/ops/activation.rs:76).  mask (mask_len f32) and lens
+ * (int32, one per rows_per_len rows) are host arrays.  With lens, only the
+ * first lens[g] keys of each row of group g are uploaded -- the kernel never
+ * reads the others -- and the whole output row is downloaded.  A chunk holds
+ * whole lens groups and whole causal blocks. */
+int oxide_pipe_scale_mask_softmax_f32(oxide_pipe_t pipe, const float* x_host, float* out_host, uint64_t rows,
+                                      uint64_t cols, float scale, const float* mask_host, uint64_t mask_len,
+                                      const int32_t* lens_host, uint64_t rows_per_len, uint64_t causal_q_len);
+/* oxide_argmax_rows_f32 on host rows; idx_host [rows]. */
+int oxide_pipe_argmax_rows_f32(oxide_pipe_t pipe, const float* x_host, uint64_t rows, uint64_t cols,
+                               uint32_t* idx_host);
+/* oxide_rope_bf16, token-major layout, on host tensors: the two
+ * apply_rotary_emb calls of MultiHeadAttention::forward
+ * (src/layers/attention.rs:88-94; src/ops/attention.rs:96-159).  cos/sin
+ * [table_rows, head_dim/2] f32 and positions [tokens] (may be NULL) are host
+ * arrays; k may be NULL.  Outputs may alias inputs. */
+int oxide_pipe_rope_bf16(oxide_pipe_t pipe, const oxide_bf16* q_host, oxide_bf16* q_out_host, uint64_t q_heads,
+                         const oxide_bf16* k_host, oxide_bf16* k_out_host, uint64_t k_heads,
+                         const float* cos_host, const float* sin_host, uint64_t table_rows,
+                         const int32_t* positions_host, uint64_t tokens, uint64_t head_dim);
 
 #ifdef __cplusplus
 }

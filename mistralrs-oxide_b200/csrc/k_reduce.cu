@@ -226,11 +226,18 @@ static_assert(RED_BLOCKS <= OXIDE_REDUCE_STATIC_SLOTS, "stage 1 may use every sc
 static __device__ __align__(256) double g_static_partials[OXIDE_REDUCE_STATIC_SLOTS];
 
 constexpr int kMaxDevices = 64;
-static std::atomic<double*> g_static_addr[kMaxDevices];
+struct StaticAddr {
+    unsigned long long ctx = 0;  // cuCtxGetId of the context the address belongs to
+    double* addr = nullptr;
+};
+static StaticAddr g_static_addr[kMaxDevices];
 static std::mutex g_static_mu;
 
-// Device address of g_static_partials on the calling thread's current device,
-// looked up once per device (the lookup may load this module's device code).
+// Device address of g_static_partials on the calling thread's current device.
+// It is looked up (cudaGetSymbolAddress, which may load this module's device
+// code) on the first call in each CUDA context and kept for that context; a
+// new context on the device -- after cudaDeviceReset, say -- has a new id and
+// gets a fresh lookup, so an address from a destroyed context is never used.
 static int static_partials(const char* name, double** out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
@@ -238,21 +245,21 @@ static int static_partials(const char* name, double** out) {
         return set_error(OXIDE_ERR_CUDA, "%s: cudaGetDevice: %s", name, cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices)
         return set_error(OXIDE_ERR_UNSUPPORTED, "%s: device ordinal %d >= %d", name, dev, kMaxDevices);
-    double* p = g_static_addr[dev].load(std::memory_order_acquire);
-    if (!p) {
-        std::lock_guard<std::mutex> lock(g_static_mu);
-        p = g_static_addr[dev].load(std::memory_order_relaxed);
-        if (!p) {
-            void* addr = nullptr;
-            e = cudaGetSymbolAddress(&addr, g_static_partials);
-            if (e != cudaSuccess || !addr)
-                return set_error(OXIDE_ERR_CUDA, "%s: cudaGetSymbolAddress of the scratch array: %s",
-                                 name, cudaGetErrorString(e));
-            p = static_cast<double*>(addr);
-            g_static_addr[dev].store(p, std::memory_order_release);
-        }
+    const unsigned long long ctx = current_context_id();
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    StaticAddr& slot = g_static_addr[dev];
+    if (!slot.addr || ctx == 0 || slot.ctx != ctx) {
+        void* addr = nullptr;
+        e = cudaGetSymbolAddress(&addr, g_static_partials);
+        if (e != cudaSuccess || !addr)
+            return set_error(OXIDE_ERR_CUDA, "%s: cudaGetSymbolAddress of the scratch array: %s",
+                             name, cudaGetErrorString(e));
+        slot.addr = static_cast<double*>(addr);
+        // The id is read after the lookup: the lookup creates the primary
+        // context when the thread had none yet.
+        slot.ctx = current_context_id();
     }
-    *out = p;
+    *out = slot.addr;
     return OXIDE_OK;
 }
 

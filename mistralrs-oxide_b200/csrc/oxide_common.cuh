@@ -302,6 +302,8 @@ int set_error(int code, const char* fmt, ...);  // records message, returns code
 int check_launch(const char* op);    // cudaGetLastError -> status
 int injected_failure(const char* op);  // host-side fault injection hook
 bool aligned16(const void* p);
+void* driver_fn(const char* symbol);  // driver API entry point, nullptr if absent
+unsigned long long current_context_id();  // cuCtxGetId of the current context, 0 if none
 
 }  // namespace oxide
 

@@ -111,6 +111,41 @@ bool ensure_dyn_smem(const void* kernel, size_t smem) {
     return true;
 }
 
+// Driver API entry points, resolved through the runtime (the library links
+// only the static CUDA runtime, not libcuda directly).  nullptr if absent.
+void* driver_fn(const char* symbol) {
+    static std::mutex mu;
+    static std::map<std::string, void*> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(symbol);
+    if (it != cache.end()) return it->second;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint(symbol, &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+        cudaGetLastError();
+        fn = nullptr;
+    }
+    cache[symbol] = fn;
+    return fn;
+}
+
+// Unique id of the calling thread's current CUDA context (cuCtxGetId): a
+// context created after a cudaDeviceReset gets a new id even where the
+// driver reuses the old handle's address.  0 if there is none or the driver
+// lacks the call.
+unsigned long long current_context_id() {
+    typedef int (*GetCurrent)(void**);
+    typedef int (*GetId)(void*, unsigned long long*);
+    static GetCurrent get_current = reinterpret_cast<GetCurrent>(driver_fn("cuCtxGetCurrent"));
+    static GetId get_id = reinterpret_cast<GetId>(driver_fn("cuCtxGetId"));
+    if (!get_current || !get_id) return 0;
+    void* ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current(&ctx) != 0 || !ctx || get_id(ctx, &id) != 0) return 0;
+    return id;
+}
+
 // Self-test: RowDiv(b)(a) against the IEEE quotient for every pair (a_i, b_j).
 // out[0] counts the mismatching pairs, out[1] keeps the smallest mismatching
 // pair index (i * nb + j); the caller sets out = {0, UINT64_MAX} first.

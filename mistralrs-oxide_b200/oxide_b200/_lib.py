@@ -87,6 +87,14 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_pipe_binary_f32": (i32, [vp, i32, vp, u64, vp, u64, vp, u64]),
     "oxide_pipe_silu_mul_f32": (i32, [vp, vp, vp, vp, u64]),
     "oxide_pipe_rms_norm_f32": (i32, [vp, vp, vp, vp, u64, u64, f32]),
+    "oxide_pipe_defer": (i32, [vp, i32]),
+    "oxide_pipe_sync": (i32, [vp]),
+    "oxide_pipe_add_mul_rowbcast_f32": (i32, [vp, vp, vp, vp, vp, vp, u64, u64]),
+    "oxide_pipe_add_rms_norm_f32": (i32, [vp, vp, vp, vp, vp, vp, u64, u64, f32]),
+    "oxide_pipe_add_rms_norm_bf16": (i32, [vp, vp, vp, vp, vp, vp, u64, u64, f32]),
+    "oxide_pipe_scale_mask_softmax_f32": (i32, [vp, vp, vp, u64, u64, f32, vp, u64, vp, u64, u64]),
+    "oxide_pipe_argmax_rows_f32": (i32, [vp, vp, u64, u64, vp]),
+    "oxide_pipe_rope_bf16": (i32, [vp, vp, vp, u64, vp, vp, u64, vp, vp, u64, vp, u64, u64]),
 }
 
 # Status codes (oxide_status in include/oxide_ops.h).

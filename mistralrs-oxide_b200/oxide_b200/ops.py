@@ -37,6 +37,27 @@ def _check(*ts: Optional[torch.Tensor]) -> None:
             raise OxideError(_lib.ERR_INVALID_ARG, "oxide", "tensor is not contiguous")
 
 
+def _need(cond: bool, op: str, msg: str) -> None:
+    if not cond:
+        raise OxideError(_lib.ERR_INVALID_ARG, op, msg)
+
+
+def _same_dtype(op: str, ref: torch.Tensor, **named: Optional[torch.Tensor]) -> None:
+    """Every named operand has ref's dtype: the kernels size their reads by
+    the input's element type, so a narrower operand would be over-read."""
+    for name, t in named.items():
+        if t is not None:
+            _need(t.dtype == ref.dtype, op, f"{name} dtype {t.dtype} differs from the input's {ref.dtype}")
+
+
+def _out_like(op: str, ref: torch.Tensor, **named: Optional[torch.Tensor]) -> None:
+    """A caller-given output holds exactly ref's element count in ref's dtype."""
+    for name, t in named.items():
+        if t is not None:
+            _need(t.dtype == ref.dtype and t.numel() == ref.numel(), op,
+                  f"{name} must be {ref.dtype} with {ref.numel()} elements, got {t.dtype} with {t.numel()}")
+
+
 def _p(t: Optional[torch.Tensor]):
     return None if t is None else t.data_ptr()
 
@@ -87,8 +108,11 @@ def div(a, b):  # src/ops/matmul.rs:123
 
 def mul_rowbcast(x: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
     """x[rows, cols] * s[cols] (ops::mul with a trailing-dim broadcast)."""
-    _check(x, s)
     cols = s.numel()
+    _same_dtype("mul_rowbcast", x, s=s)
+    _need(x.dim() >= 1 and cols >= 1 and x.shape[-1] == cols, "mul_rowbcast",
+          f"broadcast operand of {cols} elements doesn't match the last dim of {list(x.shape)}")
+    _check(x, s)
     out = torch.empty_like(x)
     call(f"oxide_mul_rowbcast_{_sfx(x)}", _p(x), _p(s), _p(out), x.numel() // cols, cols, _stream())
     return out
@@ -98,14 +122,16 @@ def add_mul_rowbcast(a: torch.Tensor, b: torch.Tensor, s: torch.Tensor,
                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """(a + b)[rows, cols] * s[cols] in one pass: ops::add then ops::mul with a
     trailing-dim broadcast (src/ops/matmul.rs:74-108), the sum rounded to a's
-    dtype first and not stored."""
-    _check(a, b, s, out)
+    dtype first and not stored.  out may be a or b (in place), not s."""
     if b.shape != a.shape or b.dtype != a.dtype or s.dtype != a.dtype:
         raise OxideError(_lib.ERR_INVALID_ARG, "add_mul_rowbcast", "operands must share shape and dtype")
     cols = s.numel()
     if a.dim() < 1 or a.shape[-1] != cols:
         raise OxideError(_lib.ERR_INVALID_ARG, "add_mul_rowbcast",
                          f"broadcast operand of {cols} elements doesn't match the last dim of {list(a.shape)}")
+    _out_like("add_mul_rowbcast", a, out=out)
+    _need(out is None or out.data_ptr() != s.data_ptr(), "add_mul_rowbcast", "out must not alias s")
+    _check(a, b, s, out)
     out = torch.empty_like(a) if out is None else out
     call(f"oxide_add_mul_rowbcast_{_sfx(a)}", _p(a), _p(b), _p(s), _p(out), a.numel() // cols, cols, _stream())
     return out
@@ -129,9 +155,11 @@ def silu(x: torch.Tensor) -> torch.Tensor:
 
 def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """mul(silu(gate), up) in one pass (src/layers/attention.rs:144-145)."""
-    _check(gate, up, out)
     if gate.shape != up.shape:
         raise OxideError(_lib.ERR_INVALID_ARG, "silu_mul", "gate and up shapes differ")
+    _same_dtype("silu_mul", gate, up=up)
+    _out_like("silu_mul", gate, out=out)
+    _check(gate, up, out)
     out = torch.empty_like(gate) if out is None else out
     call(f"oxide_silu_mul_{_sfx(gate)}", _p(gate), _p(up), _p(out), gate.numel(), _stream())
     return out
@@ -140,6 +168,7 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] =
 def unary(op: int, x: torch.Tensor, a: float = 0.0, b: float = 0.0,
           out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out = op(x) elementwise (oxide_unop: src/ops/activation.rs, src/ops/math.rs)."""
+    _out_like("unary", x, out=out)
     _check(x, out)
     out = torch.empty_like(x) if out is None else out
     call(f"oxide_unary_{_sfx(x)}", op, _p(x), _p(out), x.numel(), float(a), float(b), _stream())
@@ -197,6 +226,8 @@ def abs(x):  # src/ops/math.rs:106-121
 def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float,
                out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """src/ops/norm.rs:53-117."""
+    _same_dtype("layer_norm", x, weight=w, bias=b)
+    _out_like("layer_norm", x, out=out)
     _check(x, w, b, out)
     if x.dim() < 1:
         raise OxideError(_lib.ERR_INVALID_ARG, "layer_norm", "layer_norm requires at least 1D tensor")
@@ -217,6 +248,10 @@ def add_layer_norm(x: torch.Tensor, r: torch.Tensor, w: torch.Tensor, b: torch.T
                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """layer_norm(x + r): the fused add + layer_norm of src/kernels/normalization.rs:123-167
     (the sum rounded to x's dtype first, not stored)."""
+    if r.shape != x.shape or r.dtype != x.dtype:
+        raise OxideError(_lib.ERR_INVALID_ARG, "add_layer_norm", "residual must match the input's shape and dtype")
+    _same_dtype("add_layer_norm", x, weight=w, bias=b)
+    _out_like("add_layer_norm", x, out=out)
     _check(x, r, w, b, out)
     if r.shape != x.shape or r.dtype != x.dtype:
         raise OxideError(_lib.ERR_INVALID_ARG, "add_layer_norm", "residual must match the input's shape and dtype")
@@ -241,13 +276,15 @@ def _norm_check(x: torch.Tensor, w: torch.Tensor) -> int:
     if w.dim() != 1 or w.shape[0] != x.shape[-1]:
         raise OxideError(_lib.ERR_INVALID_ARG, "rms_norm",
                          f"rms_norm weight shape {list(w.shape)} doesn't match input last dim {x.shape[-1]}")
+    _same_dtype("rms_norm", x, weight=w)
     return x.shape[-1]
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """src/ops/norm.rs:4-51."""
-    _check(x, w, out)
     cols = _norm_check(x, w)
+    _out_like("rms_norm", x, out=out)
+    _check(x, w, out)
     out = torch.empty_like(x) if out is None else out
     call(f"oxide_rms_norm_{_sfx(x)}", _p(x), _p(w), _p(out), x.numel() // cols, cols, float(eps),
          _stream())
@@ -257,8 +294,12 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.T
 def add_rms_norm(x: torch.Tensor, r: torch.Tensor, w: torch.Tensor, eps: float,
                  h: Optional[torch.Tensor] = None, y: Optional[torch.Tensor] = None):
     """(h, y) with h = x + r and y = rms_norm(h) (src/layers/transformer.rs:64-67)."""
-    _check(x, r, w, h, y)
     cols = _norm_check(x, w)
+    _need(r.shape == x.shape and r.dtype == x.dtype, "add_rms_norm",
+          "residual must match the input's shape and dtype")
+    _out_like("add_rms_norm", x, h=h, y=y)
+    _need(h is None or y is None or h.data_ptr() != y.data_ptr(), "add_rms_norm", "h and y must not alias")
+    _check(x, r, w, h, y)
     h = torch.empty_like(x) if h is None else h
     y = torch.empty_like(x) if y is None else y
     call(f"oxide_add_rms_norm_{_sfx(x)}", _p(x), _p(r), _p(w), _p(h), _p(y), x.numel() // cols, cols,
@@ -291,12 +332,19 @@ def scale_mask_softmax(x: torch.Tensor, scale: float, mask: Optional[torch.Tenso
     ``mask`` (f32) is added as mask[j % mask.numel()]; ``lens`` (int32, one per
     group of ``rows_per_len`` rows) and ``causal_q_len`` cut each row's valid
     length; keys beyond it are 0."""
-    _check(x, mask, lens, out)
     if mask is not None and mask.dtype != torch.float32:
         raise OxideError(_lib.ERR_INVALID_ARG, "scale_mask_softmax", "mask must be float32")
     if lens is not None and lens.dtype != torch.int32:
         raise OxideError(_lib.ERR_INVALID_ARG, "scale_mask_softmax", "lens must be int32")
+    _need(x.dim() >= 1, "scale_mask_softmax", "scores need at least one dim")
     cols = x.shape[-1]
+    rows = x.numel() // cols if cols else 0
+    if lens is not None:
+        _need(rows_per_len >= 1 and lens.numel() >= -(-rows // rows_per_len), "scale_mask_softmax",
+              f"lens needs one entry per {rows_per_len} rows ({-(-rows // max(1, rows_per_len))}), "
+              f"got {lens.numel()}")
+    _out_like("scale_mask_softmax", x, out=out)
+    _check(x, mask, lens, out)
     out = torch.empty_like(x) if out is None else out
     call(f"oxide_scale_mask_softmax_{_sfx(x)}", _p(x), _p(out), x.numel() // cols, cols,
          float(scale), _p(mask), 0 if mask is None else mask.numel(), _p(lens), rows_per_len,
@@ -320,6 +368,11 @@ def rope(q: torch.Tensor, k: Optional[torch.Tensor], cos: torch.Tensor, sin: tor
 
     layout "token": [tokens, heads, head_dim]; "head": [heads, tokens, head_dim]
     (any leading dims fold into heads).  Pass q_out=q / k_out=k for in-place."""
+    _same_dtype("rope", q, k=k)
+    _out_like("rope", q, q_out=q_out)
+    if k is not None:
+        _out_like("rope", k, k_out=k_out)
+    _need(cos.dtype == torch.float32 and sin.dtype == torch.float32, "rope", "cos/sin tables must be float32")
     _check(q, k, cos, sin, positions, q_out, k_out)
     head_dim = q.shape[-1]
     if layout == "token":
@@ -338,6 +391,8 @@ def rope(q: torch.Tensor, k: Optional[torch.Tensor], cos: torch.Tensor, sin: tor
                          f"cos/sin shape {list(cos.shape)} doesn't match [*, {head_dim // 2}]")
     if positions is not None and positions.dtype != torch.int32:
         raise OxideError(_lib.ERR_INVALID_ARG, "rope", "positions must be int32")
+    _need(positions is None or positions.numel() >= tokens, "rope",
+          f"positions needs {tokens} entries, got {0 if positions is None else positions.numel()}")
     q_out = torch.empty_like(q) if q_out is None else q_out
     if k is not None:
         k_out = torch.empty_like(k) if k_out is None else k_out
@@ -383,12 +438,17 @@ def workspace_bytes(n: int) -> int:
 def reduce(x: torch.Tensor, op: int, workspace: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Whole-tensor sum / max / sum of squares -> f64 scalar tensor on the device."""
-    _check(x)
     n = x.numel()
+    _need(workspace is None or workspace.numel() * workspace.element_size() >= workspace_bytes(n), "reduce",
+          f"workspace must hold {workspace_bytes(n)} bytes")
+    _need(out is None or (out.dtype == torch.float64 and out.numel() == 1), "reduce",
+          "out must be one float64 element")
+    _check(x, workspace, out)
     if workspace is None:
         workspace = torch.empty(workspace_bytes(n), dtype=torch.uint8, device=x.device)
     out = torch.empty((), dtype=torch.float64, device=x.device) if out is None else out
-    call(f"oxide_reduce_{_sfx(x)}", op, _p(x), n, _p(out), _p(workspace), workspace.numel(), _stream())
+    call(f"oxide_reduce_{_sfx(x)}", op, _p(x), n, _p(out), _p(workspace),
+         workspace.numel() * workspace.element_size(), _stream())
     return out
 
 
@@ -407,10 +467,13 @@ def reduce_sumsq(x):
 def repeat_kv(x: torch.Tensor, n_rep: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """src/ops/attention.rs:161-201: x [batch, kv_heads, seq, head_dim] ->
     [batch, kv_heads * n_rep, seq, head_dim] (head h * n_rep + r = head h)."""
-    _check(x, out)
     if x.dim() < 4:
         raise OxideError(_lib.ERR_INVALID_ARG, "repeat_kv",
                          "repeat_kv requires 4D tensor (batch, heads, seq_len, head_dim)")
+    _need(int(n_rep) >= 1, "repeat_kv", "n_rep must be >= 1")
+    _need(out is None or (out.dtype == x.dtype and out.numel() == x.numel() * int(n_rep)), "repeat_kv",
+          f"out must be {x.dtype} with {x.numel() * int(n_rep)} elements")
+    _check(x, out)
     b, h, s, d = x.shape[0], x.shape[1], x.shape[2], x.numel() // (x.shape[0] * x.shape[1] * x.shape[2])
     shape = list(x.shape)
     shape[1] *= n_rep
@@ -494,23 +557,28 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     every position), query head h reading kv head h // (q_heads // kv_heads).
     q [batch, q_heads, head_dim]; caches [batch, kv_heads, max_seq, head_dim].
     scale defaults to the reference's (head_dim as f32).sqrt().recip()."""
-    _check(q, k_cache, v_cache, lens, workspace, out)
     if q.dim() != 3 or k_cache.dim() != 4 or k_cache.shape != v_cache.shape or \
             k_cache.shape[0] != q.shape[0] or k_cache.shape[3] != q.shape[2]:
         raise OxideError(_lib.ERR_INVALID_ARG, "decode_attention",
                          f"q {list(q.shape)} and caches {list(k_cache.shape)} do not match")
     if lens is not None and lens.dtype != torch.int32:
         raise OxideError(_lib.ERR_INVALID_ARG, "decode_attention", "lens must be int32")
+    _same_dtype("decode_attention", q, k_cache=k_cache, v_cache=v_cache)
+    _out_like("decode_attention", q, out=out)
     b, hq, d = q.shape
     hkv, m = k_cache.shape[1], k_cache.shape[2]
+    _need(lens is None or lens.numel() >= b, "decode_attention", f"lens needs {b} entries")
+    need = int(_lib.lib().oxide_decode_attention_workspace_bytes(b, hq, m, d))
+    _need(workspace is None or workspace.numel() * workspace.element_size() >= need, "decode_attention",
+          f"workspace must hold {need} bytes")
+    _check(q, k_cache, v_cache, lens, workspace, out)
     if scale is None:
         scale = float(torch.tensor(float(d), dtype=torch.float32).sqrt().reciprocal())
-    need = int(_lib.lib().oxide_decode_attention_workspace_bytes(b, hq, m, d))
     if workspace is None:
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
     out = torch.empty_like(q) if out is None else out
     call(f"oxide_decode_attention_{_sfx(q)}", _p(q), _p(k_cache), _p(v_cache), _p(lens), _p(out), b, hq, hkv,
-         m, d, float(scale), _p(workspace), workspace.numel(), _stream())
+         m, d, float(scale), _p(workspace), workspace.numel() * workspace.element_size(), _stream())
     return out
 
 
@@ -521,6 +589,8 @@ SAMPLE_INVALID = -1  # OXIDE_SAMPLE_INVALID seen through an int32 tensor
 def softmax_with_temperature(logits: torch.Tensor, temperature: float,
                              out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """src/tokenizer.rs:166-180 over the last dim -> f32 probabilities."""
+    _need(out is None or (out.dtype == torch.float32 and out.numel() == logits.numel()),
+          "softmax_with_temperature", f"out must be float32 with {logits.numel()} elements")
     _check(logits, out)
     vocab = logits.shape[-1]
     if out is None:

@@ -16,11 +16,13 @@ Shapes, distributions and seeds of the five benchmark configurations:
 
 Host inputs come from numpy's PCG64 (``np.random.default_rng(seed)``) as f32
 and are rounded to bf16 (nearest-even) where a config is bf16.  C5's ~30 G
-elements are generated on the device with a seeded torch CUDA generator
-instead (numpy would take minutes); GEMM outputs the chain consumes are
-seeded N(0,1) tensors of the GEMM's output shape (the GEMMs are not part of
-this path).  Algorithmic bytes count each input read once and each output
-written once; masked softmax keys that are never read are not counted.
+elements are generated on the device instead (numpy would take minutes),
+one sequence block at a time, each block from its own seeded torch CUDA
+generator, so any range of sequences is reproducible on its own; GEMM
+outputs the chain consumes are seeded N(0,1) tensors of the GEMM's output
+shape (the GEMMs are not part of this path).  Algorithmic bytes count each
+input read once and each output written once; masked softmax keys that are
+never read are not counted.
 """
 from __future__ import annotations
 
@@ -188,3 +190,43 @@ class C5:
 
     def bytes(self) -> int:
         return sum(self.step_bytes().values())
+
+    # Tensors of the chain, in generation order; each is produced one
+    # sequence block at a time so that any sequence range is reproducible.
+    TENSORS = ("x", "r", "q", "k", "scores", "gate", "up", "mlp", "logits")
+
+    def block_shape(self, name: str, seqs: int) -> tuple:
+        t = seqs * self.seq_len
+        return {"x": (t, self.hidden), "r": (t, self.hidden), "mlp": (t, self.hidden),
+                "q": (t, self.q_heads, self.head_dim), "k": (t, self.k_heads, self.head_dim),
+                "scores": (seqs * self.q_heads * self.seq_len, self.seq_len),
+                "gate": (t, self.inter), "up": (t, self.inter), "logits": (t, self.vocab)}[name]
+
+    def block_seed(self, name: str, seq: int) -> int:
+        """Seed of tensor `name`'s block for sequence `seq` (seed 4 of the config
+        in the high bits): the chain's inputs for a range of sequences do not
+        depend on how the 64 sequences are split across ranks."""
+        return (self.seed << 40) | (self.TENSORS.index(name) << 20) | seq
+
+    def device_inputs(self, seq_lo: int, seq_hi: int, device) -> dict:
+        """bf16 N(0,1) inputs of sequences [seq_lo, seq_hi) on `device`, plus
+        the norm weight w = 1.  Each sequence's block of each tensor comes from
+        its own seeded torch generator, so the rows of sequence s are the same
+        whether generated alone, in a rank's shard or in the whole batch."""
+        import torch
+
+        n = seq_hi - seq_lo
+        if not 0 <= seq_lo <= seq_hi <= self.seqs:
+            raise ValueError(f"sequence range [{seq_lo}, {seq_hi}) outside [0, {self.seqs})")
+        out = {}
+        g = torch.Generator(device=device)
+        for name in self.TENSORS:
+            t = torch.empty(self.block_shape(name, n), dtype=torch.bfloat16, device=device)
+            per = t.shape[0] // max(n, 1)
+            for i in range(n):
+                g.manual_seed(self.block_seed(name, seq_lo + i))
+                blk = t[i * per:(i + 1) * per]
+                torch.randn(blk.shape, generator=g, out=blk)
+            out[name] = t
+        out["w"] = torch.ones(self.hidden, dtype=torch.bfloat16, device=device)
+        return out

@@ -1,6 +1,6 @@
 """Op-level benchmark: one hot-path op at a benchmark-config shape.
 
-    python -m oxide_b200.opbench --op rms_norm_f32_c1 [--rows R] [--iters N] [--sets S]
+    python opbench.py --op rms_norm_f32_c1 [--rows R] [--iters N] [--sets S]
 
 Runs the op `iters` times back to back over `sets` rotating input/output
 buffer sets (default: enough sets to exceed 2.5x the L2 size, so every launch
@@ -19,8 +19,7 @@ import sys
 import numpy as np
 import torch
 
-if __package__ in (None, ""):
-    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "mistralrs-oxide_b200"))
 
 from oxide_b200 import ops  # noqa: E402
 from oxide_b200 import _lib  # noqa: E402

@@ -267,20 +267,20 @@ def sample(logits, temperature, top_k, top_p, uniforms, threads=1):
     return tok, probs
 
 
-def rms_norm(x, w, eps, threads=1):
+def rms_norm(x, w, eps, threads=1, out=None):
     x, w = _c(x), _c(w)
     cols = w.size
-    out = np.empty_like(x)
+    out = np.empty_like(x) if out is None else out
     getattr(lib(), f"orc_rms_norm_{_sfx(x)}")(_p(x), _p(w), _p(out), x.size // cols, cols,
                                               float(eps), threads)
     return out
 
 
-def add_rms_norm(x, r, w, eps, threads=1):
+def add_rms_norm(x, r, w, eps, threads=1, h=None, y=None):
     x, r, w = _c(x), _c(r), _c(w)
     cols = w.size
-    h = np.empty_like(x)
-    y = np.empty_like(x)
+    h = np.empty_like(x) if h is None else h
+    y = np.empty_like(x) if y is None else y
     getattr(lib(), f"orc_add_rms_norm_{_sfx(x)}")(_p(x), _p(r), _p(w), _p(h), _p(y),
                                                   x.size // cols, cols, float(eps), threads)
     return h, y
@@ -294,11 +294,11 @@ def softmax(x, outer, dim, inner, threads=1):
 
 
 def scale_mask_softmax(x, cols, scale, mask=None, lens=None, rows_per_len=1, causal_q_len=0,
-                       threads=1):
+                       threads=1, out=None):
     x = _c(x)
     mask = None if mask is None else _c(np.asarray(mask, dtype=np.float32))
     lens = None if lens is None else _c(np.asarray(lens, dtype=np.int32))
-    out = np.empty_like(x)
+    out = np.empty_like(x) if out is None else out
     getattr(lib(), f"orc_scale_mask_softmax_{_sfx(x)}")(
         _p(x), _p(out), x.size // cols, cols, float(scale), _p(mask),
         0 if mask is None else mask.size, _p(lens), rows_per_len, causal_q_len, threads)
@@ -313,20 +313,20 @@ def rope_table(theta, head_dim, max_pos):
     return cos, sin
 
 
-def rope(x, tokens, heads, head_dim, layout, cos, sin, positions=None, threads=1):
+def rope(x, tokens, heads, head_dim, layout, cos, sin, positions=None, threads=1, out=None):
     x = _c(x)
     cos, sin = _c(cos), _c(sin)
     positions = None if positions is None else _c(np.asarray(positions, dtype=np.int32))
-    out = np.empty_like(x)
+    out = np.empty_like(x) if out is None else out
     getattr(lib(), f"orc_rope_{_sfx(x)}")(_p(x), _p(out), tokens, heads, head_dim, layout,
                                           _p(cos), _p(sin), _p(positions), threads)
     return out
 
 
-def argmax_rows(x, cols, threads=1):
+def argmax_rows(x, cols, threads=1, out=None):
     x = _c(x)
     rows = x.size // cols
-    idx = np.empty(rows, dtype=np.uint32)
+    idx = np.empty(rows, dtype=np.uint32) if out is None else out
     getattr(lib(), f"orc_argmax_rows_{_sfx(x)}")(_p(x), rows, cols, _p(idx), threads)
     return idx
 

@@ -173,7 +173,8 @@ def test_layer_norm_matches_oracle(cuda, orc, dtype, rows, cols):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
-@pytest.mark.parametrize("rows,cols", [(8, 33), (16, 768), (64, 4096), (2, 20000), (5000, 1024)])
+@pytest.mark.parametrize("rows,cols", [(8, 33), (16, 768), (64, 4096), (2, 20000), (5000, 1024),
+                                       (4096, 4096)])
 def test_add_layer_norm_matches_oracle_and_unfused(cuda, orc, dtype, rows, cols):
     """layer_norm(x + r) (the reference's fused-add intent): against the
     oracle's add then layer_norm, within the layer_norm bar; bit-equal to the
@@ -207,6 +208,39 @@ def test_add_layer_norm_matches_oracle_and_unfused(cuda, orc, dtype, rows, cols)
     assert_bits_equal(got, unfused)
     ops.add_layer_norm(tx, tr, tw, tb, 1e-5, out=tx)
     assert_bits_equal(to_np(tx), got)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_add_layer_norm_misaligned_residual(cuda, orc, dtype):
+    """x aligned, r one element off a 16-byte boundary: the row kernel's vector
+    path needs both, so this alone sends the call to the element kernel (which
+    sums in another order); within the same bar of the oracle as the vector
+    path."""
+    from oxide_b200 import ops
+
+    rows, cols = 96, 4096
+    rng = np.random.default_rng(77)
+    x = rng.standard_normal((rows, cols)).astype(F)
+    r = rng.standard_normal((rows, cols)).astype(F)
+    w = rng.uniform(0.5, 1.5, cols).astype(F)
+    b = rng.uniform(-0.5, 0.5, cols).astype(F)
+    if dtype == "bf16":
+        x, r, w, b = (orc.f32_to_bf16(a) for a in (x, r, w, b))
+    got = to_np(ops.add_layer_norm(to_dev(x), misaligned_copy(r), to_dev(w), to_dev(b), 1e-5))
+    h = orc.binary(orc.ADD, x.reshape(-1), r.reshape(-1)).reshape(rows, cols)
+    ref = orc.layer_norm(h, w, b, 1e-5)
+    f = (lambda a: bf16_to_f32(a)) if dtype == "bf16" else (lambda a: a)
+    exact, scale = _ln_scale(f(h), f(w), f(b))
+    if dtype == "f32":
+        g = got.astype(np.float64)
+        lim = 1e-5 * scale + 1e-30
+        assert np.all(np.abs(g - exact) <= lim), "kernel vs exact"
+        assert np.all(np.abs(g - ref) <= lim + np.abs(ref - exact)), "kernel vs reference + its drift"
+    else:
+        d = ulp_bf16(got, ref)
+        gd = np.abs(bf16_to_f32(got).astype(np.float64) - bf16_to_f32(ref))
+        assert np.all((d <= 1) | (gd <= 2.0 ** -8 * scale))
 
 
 @pytest.mark.gpu

@@ -16,17 +16,11 @@ import pytest
 import torch
 
 from _util import (assert_bits_equal, assert_close_rel, assert_parity_rel, assert_ulp, bf16_to_f32,
-                   misaligned_copy, rms_norm_exact, softmax_exact, to_dev, to_np)
+                   misaligned_copy, rms_norm_exact, smax_close, softmax_exact, to_dev, to_np)
 
 pytestmark = pytest.mark.gpu
 
-F32_REL = 1e-5
-# CUDA expf is within 2 ulp of e^x and glibc expf within 1 ulp; that gap passes
-# through the four rounded steps of x * (1 / (1 + e)) * up.  Measured on 16 Mi
-# C2-distributed elements: 88.9% bit-exact, max 6 ulp (<= 7.2e-7 relative).
-SILU_F32_ULP = 8
-SILU_F32_MIN_EXACT = 0.8
-BF16_ULP = 1
+from _util import BF16_ULP, F32_REL, SILU_F32_MIN_EXACT, SILU_F32_ULP  # noqa: E402
 
 F = np.float32
 
@@ -155,6 +149,30 @@ def test_add_mul_rowbcast_bit_exact(cuda, orc, dtype, rows, cols):
     assert_bits_equal(got, to_np(ops.mul_rowbcast(ops.add(ta, tb), ts)))
     ops.add_mul_rowbcast(ta, tb, ts, out=ta)
     assert_bits_equal(to_np(ta), got)
+    ta = to_dev(a)
+    ops.add_mul_rowbcast(ta, tb, ts, out=tb)  # in place over b
+    assert_bits_equal(to_np(tb), got)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("which", ["b", "s", "out"])
+def test_add_mul_rowbcast_one_misaligned_operand(cuda, orc, dtype, which):
+    """One operand one element off a 16-byte boundary while the others are
+    aligned: the entry point must take the element kernel for that alone."""
+    from oxide_b200 import ops
+
+    rows, cols = 48, 4096
+    a, b = rand((rows, cols), 63, dtype, orc=orc), rand((rows, cols), 64, dtype, orc=orc)
+    sv = np.random.default_rng(65).uniform(0.5, 1.5, cols).astype(F)
+    if dtype == "bf16":
+        sv = orc.f32_to_bf16(sv)
+    ta = to_dev(a)
+    tb = misaligned_copy(b) if which == "b" else to_dev(b)
+    ts = misaligned_copy(sv) if which == "s" else to_dev(sv)
+    out = misaligned_copy(np.zeros_like(a)) if which == "out" else None
+    got = to_np(ops.add_mul_rowbcast(ta, tb, ts, out=out))
+    ref = orc.binary(orc.MUL, orc.binary(orc.ADD, a.reshape(-1), b.reshape(-1)), sv).reshape(rows, cols)
+    assert_bits_equal(got, ref)
 
 
 # ---------------------------------------------------------------- activations
@@ -308,25 +326,6 @@ def test_softmax_rows(cuda, orc, dtype, rows, cols):
     x = rand((rows, cols), 30 + cols, dtype, 3.0, orc)
     got = ops.softmax(to_dev(x), 1)
     smax_close(to_np(got), orc.softmax(x, rows, cols, 1), x, cols, dtype)
-
-
-def smax_close(got, ref, x, cols, dtype, scale=1.0, mask=None, lens=None, rows_per_len=1,
-               causal_q=0):
-    """f32: parity within 1e-5 relative of the exact softmax of the same f32
-    scores (plus the reference's own sequential-sum drift); bf16: 1 ulp."""
-    if dtype == "bf16":
-        assert_ulp(got, ref, BF16_ULP)
-        return
-    s = (np.asarray(x, F).reshape(-1, cols) * F(scale)).astype(F)
-    if mask is not None:
-        s = (s + np.asarray(mask, F)[np.arange(cols) % mask.size]).astype(F)
-    rows = s.shape[0]
-    n = np.full(rows, cols, np.int64)
-    if lens is not None:
-        n = np.minimum(n, np.maximum(np.asarray(lens, np.int64)[np.arange(rows) // rows_per_len], 0))
-    if causal_q:
-        n = np.minimum(n, np.arange(rows) % causal_q + 1 + cols - causal_q)
-    assert_parity_rel(got, ref, softmax_exact(s, n), F32_REL)
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
