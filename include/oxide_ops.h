@@ -316,6 +316,12 @@ int oxide_kv_cache_append_bf16(oxide_bf16* k_cache, oxide_bf16* v_cache, const o
  * the reference computes it through repeat_kv + matmul + softmax + matmul. */
 uint64_t oxide_decode_attention_workspace_bytes(uint64_t batch, uint64_t q_heads, uint64_t max_seq,
                                                 uint64_t head_dim);
+/* Kernel choice of oxide_decode_attention_bf16 (diagnostic; no reference
+ * counterpart): 0 (default) = the tcgen05 / TMA kernel wherever it applies
+ * (sm_100, head_dim 128, q_heads / kv_heads in {1, 2, 4, 8}, batch <= 1024,
+ * max_seq >= 256), else the split-K mma.sync kernel; 1 = always the split-K
+ * kernel.  Process-wide; set it between calls, not while one is enqueued. */
+void oxide_debug_decode_attention_path(int path);
 int oxide_decode_attention_f32(const float* q, const float* k_cache, const float* v_cache, const int32_t* lens,
                                float* out, uint64_t batch, uint64_t q_heads, uint64_t kv_heads, uint64_t max_seq,
                                uint64_t head_dim, float scale, void* workspace, uint64_t workspace_bytes,

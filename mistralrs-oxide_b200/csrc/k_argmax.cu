@@ -70,6 +70,7 @@ __device__ __forceinline__ uint32_t block_min_u32(uint32_t v, uint32_t* red) {
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(256)
     argmax_kernel(const T* x, uint64_t rows, uint32_t cols, uint32_t* idx, int cl) {
+    pdl_begin();
     constexpr int V = VEC ? Vec<T>::N : 1;
     // 8 loads in flight per thread: bf16 [131072 x 32000] 1287 -> 1216 us and f32
     // [64 x 32000] 5.24 -> 5.11 us against 4
@@ -184,13 +185,13 @@ static int argmax_entry(const char* name, const T* x, uint64_t rows, uint64_t co
     cfg.gridDim = dim3((unsigned)(groups * cl), 1, 1);
     cfg.blockDim = dim3(256, 1, 1);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = cl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = add_pdl_attr(attr, 1);
     const uint32_t c32 = (uint32_t)cols;
     cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, argmax_kernel<T, true>, x, rows, c32, idx, cl)
                         : cudaLaunchKernelEx(&cfg, argmax_kernel<T, false>, x, rows, c32, idx, cl);

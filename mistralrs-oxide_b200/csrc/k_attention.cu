@@ -26,6 +26,7 @@
 // reference's sequential f32 sums by rounding only.  head_dim 128 with rep in
 // {1, 2, 4, 8} takes this path; other shapes take a one-CTA-per-(batch, head)
 // kernel.  A sequence of length 0 yields zeros.
+#include <atomic>
 #include <type_traits>
 
 #include "oxide_common.cuh"
@@ -112,6 +113,7 @@ template <int NR>
 __global__ void __launch_bounds__(DW_WARPS * 32, 2)
     decode_attn_warp_kernel(const bf16_t* q, const bf16_t* kc, const bf16_t* vc, float* part_ml, float* part_o,
                             DecArgs p) {
+    pdl_begin();
     static_assert(DW_WARPS * 32 == DA_D, "the merge maps one thread to one output dim");
     extern __shared__ __align__(16) unsigned char smem[];
     const uint32_t split = blockIdx.x, kvh = blockIdx.y;
@@ -323,6 +325,7 @@ template <int NR>
 __global__ void __launch_bounds__(DW_WARPS * 32, 3)
     decode_attn_warp_f32_kernel(const float* q, const float* kc, const float* vc, float* part_ml, float* part_o,
                                 DecArgs p) {
+    pdl_begin();
     extern __shared__ __align__(16) unsigned char smem[];
     float* qs = reinterpret_cast<float*>(smem + DF_RING);  // [NR][D]
     const uint32_t split = blockIdx.x, kvh = blockIdx.y;
@@ -489,6 +492,7 @@ constexpr int DA_MAX_SPLITS = 1024;
 template <typename T>
 __global__ void __launch_bounds__(DA_THREADS)
     decode_attn_combine_kernel(const float* part_ml, const float* part_o, T* out, DecArgs p) {
+    pdl_begin();
     __shared__ float wts[DA_MAX_SPLITS];
     __shared__ float red[32];
     const uint64_t bh = blockIdx.x;
@@ -517,6 +521,7 @@ __global__ void __launch_bounds__(DA_THREADS)
 template <typename T>
 __global__ void __launch_bounds__(256)
     decode_attn_generic_kernel(const T* q, const T* kc, const T* vc, T* out, float* scores, DecArgs p) {
+    pdl_begin();
     __shared__ float red[32];
     const uint64_t bh = blockIdx.x, b = bh / p.q_heads;
     const uint32_t qh = (uint32_t)(bh % p.q_heads), kvh = qh / p.rep;
@@ -565,16 +570,26 @@ static cudaError_t launch_split(const T* q, const T* kc, const T* vc, T* out, fl
     if constexpr (std::is_same<T, bf16_t>::value) {  // tensor-core tile products
         auto kern = decode_attn_warp_kernel<NR>;
         if (!ensure_dyn_smem(reinterpret_cast<const void*>(kern), DW_SMEM)) return cudaErrorInvalidConfiguration;
-        kern<<<grid, DW_WARPS * 32, DW_SMEM, st>>>(q, kc, vc, part_ml, part_o, p);
+        launch_k(kern, grid, DW_WARPS * 32, DW_SMEM, st, q, kc, vc, part_ml, part_o, p);
     } else {  // f32: CUDA-core tile products
         auto kern = decode_attn_warp_f32_kernel<NR>;
         const size_t smem = df_smem<NR>();
         if (!ensure_dyn_smem(reinterpret_cast<const void*>(kern), smem)) return cudaErrorInvalidConfiguration;
-        kern<<<grid, DW_WARPS * 32, smem, st>>>(q, kc, vc, part_ml, part_o, p);
+        launch_k(kern, grid, DW_WARPS * 32, smem, st, q, kc, vc, part_ml, part_o, p);
     }
-    decode_attn_combine_kernel<T><<<(unsigned)(p.batch * p.q_heads), DA_THREADS, 0, st>>>(part_ml, part_o, out, p);
+    launch_k(decode_attn_combine_kernel<T>, (unsigned)(p.batch * p.q_heads), DA_THREADS, 0, st, part_ml, part_o, out, p);
     return cudaSuccess;
 }
+
+// The tcgen05 / TMA kernel of k_attention_tc.cu (bf16, head_dim 128); *used
+// is false when the shapes or the device do not allow it.
+cudaError_t decode_attention_tc_bf16(const bf16_t* q, const bf16_t* kc, const bf16_t* vc, const int32_t* lens,
+                                     bf16_t* out, uint64_t batch, uint64_t q_heads, uint64_t kv_heads,
+                                     uint64_t max_seq, float scale, void* ws, uint64_t ws_bytes, cudaStream_t st,
+                                     bool* used);
+// 0: the tcgen05 kernel where it applies, else the split-K kernel; 1: always
+// the split-K (mma.sync) kernel (oxide_debug_decode_attention_path).
+static std::atomic<int> g_decode_path{0};
 
 template <typename T>
 static int decode_entry(const char* name, const T* q, const T* kc, const T* vc, const int32_t* lens, T* out,
@@ -605,7 +620,15 @@ static int decode_entry(const char* name, const T* q, const T* kc, const T* vc, 
     const bool fast = head_dim == DA_D && (rep == 1 || rep == 2 || rep == 4 || rep == 8) && aligned16(q) &&
                       aligned16(kc) && aligned16(vc) && kv_heads < 65536;
     cudaError_t e = cudaSuccess;
-    if (fast) {
+    bool done = false;  // the tcgen05 kernel ran
+    if constexpr (std::is_same<T, bf16_t>::value) {
+        if (fast && g_decode_path.load(std::memory_order_relaxed) == 0)
+            e = decode_attention_tc_bf16(q, kc, vc, lens, out, batch, q_heads, kv_heads, max_seq, scale, ws, ws_bytes,
+                                         st, &done);
+    }
+    if (done) {
+        // nothing more to launch
+    } else if (fast) {
         // splits: enough CTAs for ~4 waves, whole tiles per split
         const uint64_t tk = split_granule<T>();
         const uint64_t groups = batch * kv_heads;
@@ -626,7 +649,7 @@ static int decode_entry(const char* name, const T* q, const T* kc, const T* vc, 
             default: e = launch_split<T, 8>(q, kc, vc, out, w, p, st); break;
         }
     } else {
-        decode_attn_generic_kernel<T><<<(unsigned)(batch * q_heads), 256, 0, st>>>(q, kc, vc, out,
+        launch_k(decode_attn_generic_kernel<T>, (unsigned)(batch * q_heads), 256, 0, st, q, kc, vc, out,
                                                                                   static_cast<float*>(ws), p);
     }
     if (e != cudaSuccess) {
@@ -641,6 +664,8 @@ static int decode_entry(const char* name, const T* q, const T* kc, const T* vc, 
 using oxide::bf16_t;
 
 extern "C" {
+
+void oxide_debug_decode_attention_path(int path) { oxide::g_decode_path.store(path == 1 ? 1 : 0); }
 
 uint64_t oxide_decode_attention_workspace_bytes(uint64_t batch, uint64_t q_heads, uint64_t max_seq,
                                                 uint64_t head_dim) {

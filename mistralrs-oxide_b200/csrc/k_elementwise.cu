@@ -55,14 +55,24 @@ struct FBin {
 
 // silu(x) = x * (1 / (1 + exp(-x))), src/ops/activation.rs:30-33.  The
 // reciprocal is __frcp_rn: the correctly rounded 1/d, i.e. the reference's
-// IEEE 1.0 / d.
+// IEEE 1.0 / d.  ACCURATE (the f32 kernels): exp is exp_rn_f32, the correctly
+// rounded e^x the reference's glibc expf returns on all but 4e-5 of the
+// floats, so every later step rounds as the reference's does and the result
+// is its bits except there; otherwise (bf16 results, rounded to 8 bits after
+// the f32 math) CUDA's expf, within 2 ulp and a third of the instructions.
+template <bool ACCURATE>
+__device__ __forceinline__ float silu_exp(float nx) {
+    return ACCURATE ? exp_rn_f32(nx) : expf(nx);
+}
+template <bool ACCURATE = true>
 __device__ __forceinline__ float silu_f(float x) {
-    float e = expf(-x);
+    float e = silu_exp<ACCURATE>(-x);
     float r = __frcp_rn(fadd(1.0f, e));
     return fmul(x, r);
 }
+template <bool ACCURATE = true>
 __device__ __forceinline__ float2 silu_f2(float2 x) {
-    const float2 d = fadd2(f2(1.0f, 1.0f), f2(expf(-x.x), expf(-x.y)));
+    const float2 d = fadd2(f2(1.0f, 1.0f), f2(silu_exp<ACCURATE>(-x.x), silu_exp<ACCURATE>(-x.y)));
     return fmul2(x, f2(__frcp_rn(d.x), __frcp_rn(d.y)));
 }
 
@@ -82,15 +92,16 @@ struct FSiluMul {  // mul(silu(g), u); silu(g) rounded to T as the pair stores i
     // f32 product is subnormal and its own rounding would come first (a
     // double rounding the single one avoids): within 1 bf16 ulp there.
     static constexpr bool PACKED = sizeof(T) == 2;
+    static constexpr bool ACC = sizeof(T) == 4;
     __device__ __forceinline__ float operator()(float g, float u) const {
-        return fmul(Vec<T>::rnd(silu_f(g)), u);
+        return fmul(Vec<T>::rnd(silu_f<ACC>(g)), u);
     }
     __device__ __forceinline__ float2 pair(float2 g, float2 u) const {
-        const float2 s = silu_f2(g);
+        const float2 s = silu_f2<ACC>(g);
         return fmul2(f2(Vec<T>::rnd(s.x), Vec<T>::rnd(s.y)), u);
     }
     __device__ __forceinline__ uint32_t packed(uint32_t g, uint32_t u) const {
-        const float2 s = silu_f2(f2(__uint_as_float(g << 16), __uint_as_float(g & 0xFFFF0000u)));
+        const float2 s = silu_f2<false>(f2(__uint_as_float(g << 16), __uint_as_float(g & 0xFFFF0000u)));
         return mul_bf16x2(pack_bf16x2(s.x, s.y), u);
     }
 };
@@ -105,9 +116,11 @@ struct HasPacked<F, std::void_t<decltype(F::PACKED)>> {
     static constexpr bool value = F::PACKED;
 };
 
+template <typename T>
 struct FSilu {
-    __device__ __forceinline__ float operator()(float x, float) const { return silu_f(x); }
-    __device__ __forceinline__ float2 pair(float2 x, float2) const { return silu_f2(x); }
+    static constexpr bool ACC = sizeof(T) == 4;
+    __device__ __forceinline__ float operator()(float x, float) const { return silu_f<ACC>(x); }
+    __device__ __forceinline__ float2 pair(float2 x, float2) const { return silu_f2<ACC>(x); }
 };
 
 struct FScale {
@@ -165,6 +178,7 @@ template <typename T, typename F, int NIN, bool AMOD, bool BMOD>
 __global__ void __launch_bounds__(EW_THREADS, ew_min_blocks<T>())
     ew_vec_kernel(const T* a, const T* b, T* out, uint64_t nvec, uint64_t nav, uint64_t nbv,
                   FastDiv adiv, FastDiv bdiv, bool wide, uint64_t tail_lo, uint64_t n, F f) {
+    pdl_begin();
     constexpr int V = Vec<T>::N;
     constexpr int EW_UNROLL = ew_unroll<T>();
     const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
@@ -218,6 +232,7 @@ __global__ void __launch_bounds__(EW_THREADS, ew_min_blocks<T>())
 template <typename T, typename F, int NIN>
 __global__ void __launch_bounds__(EW_THREADS)
     ew_scalar_kernel(const T* a, uint64_t na, const T* b, uint64_t nb, T* out, uint64_t n, F f) {
+    pdl_begin();
     const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
     for (uint64_t i = (uint64_t)blockIdx.x * EW_THREADS + threadIdx.x; i < n; i += stride) {
         float x = Vec<T>::load1(a + (na == n ? i : i % na));
@@ -248,7 +263,7 @@ static void launch_vec(const T* a, uint64_t na, const T* b, uint64_t nb, T* out,
     constexpr uint64_t U = ew_unroll<T>();
     uint64_t items = (nvec + U - 1) / U;
     int grid = resident_grid(kern, items > 0 ? items : 1);
-    kern<<<grid, EW_THREADS, 0, st>>>(a, b, out, nvec, nav, nbv, adiv, bdiv, wide, nvec * V, n,
+    launch_k(kern, grid, EW_THREADS, 0, st, a, b, out, nvec, nav, nbv, adiv, bdiv, wide, nvec * V, n,
                                       f);
 }
 
@@ -270,7 +285,7 @@ static int ew_dispatch(const char* name, const T* a, uint64_t na, const T* b, ui
     } else {
         auto kern = ew_scalar_kernel<T, F, NIN>;
         int grid = resident_grid(kern, n);
-        kern<<<grid, EW_THREADS, 0, st>>>(a, na, b, nb, out, n, f);
+        launch_k(kern, grid, EW_THREADS, 0, st, a, na, b, nb, out, n, f);
     }
     return check_launch(name);
 }
@@ -316,6 +331,7 @@ template <typename T>
 __global__ void __launch_bounds__(EW_THREADS, ew_min_blocks<T>())
     add_mul_vec_kernel(const T* a, const T* b, const T* s, T* out, uint64_t nvec, uint64_t nsv, FastDiv sdiv,
                        bool wide) {
+    pdl_begin();
     constexpr int V = Vec<T>::N;
     constexpr int U = 4;  // vectors in flight per operand
     const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
@@ -350,6 +366,7 @@ __global__ void __launch_bounds__(EW_THREADS, ew_min_blocks<T>())
 template <typename T>
 __global__ void __launch_bounds__(EW_THREADS)
     add_mul_scalar_kernel(const T* a, const T* b, const T* s, T* out, uint64_t n, uint64_t cols) {
+    pdl_begin();
     const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
     for (uint64_t i = (uint64_t)blockIdx.x * EW_THREADS + threadIdx.x; i < n; i += stride) {
         const float h = Vec<T>::rnd(fadd(Vec<T>::load1(a + i), Vec<T>::load1(b + i)));
@@ -371,10 +388,10 @@ static int add_mul_entry(const char* name, const T* a, const T* b, const T* s, T
         const bool wide = nvec >= 0xffffffffull;
         auto kern = add_mul_vec_kernel<T>;
         const int grid = resident_grid(kern, (nvec + 3) / 4);
-        kern<<<grid, EW_THREADS, 0, st>>>(a, b, s, out, nvec, nsv, FastDiv(wide ? 1u : (uint32_t)nsv), wide);
+        launch_k(kern, grid, EW_THREADS, 0, st, a, b, s, out, nvec, nsv, FastDiv(wide ? 1u : (uint32_t)nsv), wide);
     } else {
         auto kern = add_mul_scalar_kernel<T>;
-        kern<<<resident_grid(kern, n), EW_THREADS, 0, st>>>(a, b, s, out, n, cols);
+        launch_k(kern, resident_grid(kern, n), EW_THREADS, 0, st, a, b, s, out, n, cols);
     }
     return check_launch(name);
 }
@@ -396,7 +413,7 @@ static int unary_dispatch(const char* name, const T* x, T* out, uint64_t n, F f,
         launch_vec<T, F, 1, false, false>(x, n, x, n, out, n, f, st);
     } else {
         auto kern = ew_scalar_kernel<T, F, 1>;
-        kern<<<resident_grid(kern, n), EW_THREADS, 0, st>>>(x, n, x, n, out, n, f);
+        launch_k(kern, resident_grid(kern, n), EW_THREADS, 0, st, x, n, x, n, out, n, f);
     }
     return check_launch(name);
 }
@@ -511,11 +528,11 @@ int oxide_scale_bf16(const oxide_bf16* x, oxide_bf16* out, float scale, uint64_t
                                                        oxide::FScale{scale}, stream);
 }
 int oxide_silu_f32(const float* x, float* out, uint64_t n, oxide_stream_t stream) {
-    return oxide::full_entry<float, oxide::FSilu, 1>("oxide_silu_f32", x, nullptr, out, n, {},
+    return oxide::full_entry<float, oxide::FSilu<float>, 1>("oxide_silu_f32", x, nullptr, out, n, {},
                                                      stream);
 }
 int oxide_silu_bf16(const oxide_bf16* x, oxide_bf16* out, uint64_t n, oxide_stream_t stream) {
-    return oxide::full_entry<bf16_t, oxide::FSilu, 1>("oxide_silu_bf16", x, nullptr, out, n, {},
+    return oxide::full_entry<bf16_t, oxide::FSilu<bf16_t>, 1>("oxide_silu_bf16", x, nullptr, out, n, {},
                                                       stream);
 }
 int oxide_silu_mul_f32(const float* gate, const float* up, float* out, uint64_t n,

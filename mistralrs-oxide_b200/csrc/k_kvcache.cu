@@ -27,6 +27,7 @@ constexpr int KV_UNROLL = 4;
 __global__ void __launch_bounds__(KV_THREADS)
     repeat_kv_vec_kernel(const uint4* x, uint4* out, uint64_t heads_total, uint32_t vec_per_head,
                          uint32_t kv_heads, uint32_t n_rep, FastDiv vdiv, FastDiv hdiv, bool narrow) {
+    pdl_begin();
     const uint64_t n = heads_total * vec_per_head;
     const uint64_t stride = (uint64_t)gridDim.x * KV_THREADS;
     for (uint64_t i0 = (uint64_t)blockIdx.x * KV_THREADS + threadIdx.x; i0 < n; i0 += stride * KV_UNROLL) {
@@ -59,6 +60,7 @@ template <typename T>
 __global__ void __launch_bounds__(KV_THREADS)
     repeat_kv_scalar_kernel(const T* x, T* out, uint64_t heads_total, uint64_t per_head, uint64_t kv_heads,
                             uint32_t n_rep) {
+    pdl_begin();
     const uint64_t n = heads_total * per_head;
     for (uint64_t i = (uint64_t)blockIdx.x * KV_THREADS + threadIdx.x; i < n;
          i += (uint64_t)gridDim.x * KV_THREADS) {
@@ -75,6 +77,7 @@ __global__ void __launch_bounds__(KV_THREADS)
 __global__ void __launch_bounds__(KV_THREADS)
     kv_append_vec_kernel(uint4* kc, uint4* vc, const uint4* k, const uint4* v, uint64_t heads_total,
                          uint64_t new_vec, uint64_t max_vec, uint64_t cur_vec, FastDiv ndiv, bool narrow) {
+    pdl_begin();
     const uint64_t half = heads_total * new_vec;
     for (uint64_t i = (uint64_t)blockIdx.x * KV_THREADS + threadIdx.x; i < 2 * half;
          i += (uint64_t)gridDim.x * KV_THREADS) {
@@ -90,6 +93,7 @@ template <typename T>
 __global__ void __launch_bounds__(KV_THREADS)
     kv_append_scalar_kernel(T* kc, T* vc, const T* k, const T* v, uint64_t heads_total, uint64_t new_elems,
                             uint64_t max_elems, uint64_t cur_elems) {
+    pdl_begin();
     const uint64_t half = heads_total * new_elems;
     for (uint64_t i = (uint64_t)blockIdx.x * KV_THREADS + threadIdx.x; i < 2 * half;
          i += (uint64_t)gridDim.x * KV_THREADS) {
@@ -123,14 +127,13 @@ static int repeat_kv_entry(const char* name, const T* x, T* out, uint64_t batch,
     if (aligned16(x) && aligned16(out) && per_head % V == 0 && per_head / V < (1ull << 32)) {
         const uint64_t vph = per_head / V, items = heads_total * vph;
         const bool narrow = items < (1ull << 32);
-        repeat_kv_vec_kernel<<<copy_grid(reinterpret_cast<const void*>(repeat_kv_vec_kernel), items),
-                               KV_THREADS, 0, st>>>(reinterpret_cast<const uint4*>(x), reinterpret_cast<uint4*>(out),
+        launch_k(repeat_kv_vec_kernel, copy_grid(reinterpret_cast<const void*>(repeat_kv_vec_kernel), items), KV_THREADS, 0, st, reinterpret_cast<const uint4*>(x), reinterpret_cast<uint4*>(out),
                                                     heads_total, (uint32_t)vph, (uint32_t)kv_heads,
                                                     (uint32_t)n_rep, FastDiv((uint32_t)vph),
                                                     FastDiv((uint32_t)kv_heads), narrow);
     } else {
         auto kern = repeat_kv_scalar_kernel<T>;
-        kern<<<copy_grid(reinterpret_cast<const void*>(kern), heads_total * per_head), KV_THREADS, 0, st>>>(
+        launch_k(kern, copy_grid(reinterpret_cast<const void*>(kern), heads_total * per_head), KV_THREADS, 0, st, 
             x, out, heads_total, per_head, kv_heads, (uint32_t)n_rep);
     }
     return check_launch(name);
@@ -152,16 +155,14 @@ static int kv_append_entry(const char* name, T* kc, T* vc, const T* k, const T* 
     if (aligned16(kc) && aligned16(vc) && aligned16(k) && aligned16(v) && head_dim % V == 0) {
         const uint64_t hv = head_dim / V, new_vec = new_len * hv;
         const bool narrow = heads_total * new_vec < (1ull << 32);
-        kv_append_vec_kernel<<<copy_grid(reinterpret_cast<const void*>(kv_append_vec_kernel),
-                                         2 * heads_total * new_vec),
-                               KV_THREADS, 0, st>>>(reinterpret_cast<uint4*>(kc), reinterpret_cast<uint4*>(vc),
+        launch_k(kv_append_vec_kernel, copy_grid(reinterpret_cast<const void*>(kv_append_vec_kernel),
+                                         2 * heads_total * new_vec), KV_THREADS, 0, st, reinterpret_cast<uint4*>(kc), reinterpret_cast<uint4*>(vc),
                                                     reinterpret_cast<const uint4*>(k), reinterpret_cast<const uint4*>(v),
                                                     heads_total, new_vec, max_seq * hv, cur_len * hv,
                                                     FastDiv((uint32_t)(narrow ? new_vec : 1)), narrow);
     } else {
         auto kern = kv_append_scalar_kernel<T>;
-        kern<<<copy_grid(reinterpret_cast<const void*>(kern), 2 * heads_total * new_len * head_dim), KV_THREADS,
-               0, st>>>(kc, vc, k, v, heads_total, new_len * head_dim, max_seq * head_dim, cur_len * head_dim);
+        launch_k(kern, copy_grid(reinterpret_cast<const void*>(kern), 2 * heads_total * new_len * head_dim), KV_THREADS, 0, st, kc, vc, k, v, heads_total, new_len * head_dim, max_seq * head_dim, cur_len * head_dim);
     }
     return check_launch(name);
 }

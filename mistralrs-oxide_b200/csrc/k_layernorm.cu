@@ -96,6 +96,7 @@ __device__ __forceinline__ void ln_store(T* yrow, const T* w, const T* b, const 
 template <typename T, int VPT, bool BIG, bool ADD>
 __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : (ADD ? 4 : 5))
     layernorm_vec_kernel(const T* x, const T* r, const T* w, const T* b, T* y, LnArgs p) {
+    pdl_begin();
     constexpr int V = Vec<T>::N;
     __shared__ float red[32];
     const int rpc = blockDim.x / p.tpr;
@@ -170,6 +171,7 @@ __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : (ADD ? 4 : 5))
 template <typename T, bool ADD>
 __global__ void __launch_bounds__(256) layernorm_scalar_kernel(const T* x, const T* r, const T* w, const T* b,
                                                                T* y, LnArgs p) {
+    pdl_begin();
     __shared__ float red[32];
     // element i of the row: x, or x + r rounded to T
     auto val = [&](uint64_t i) {
@@ -211,8 +213,8 @@ static void launch_ln_vec(const T* x, const T* r, const T* w, const T* b, T* y, 
     const int rpc = p.tpr >= 256 ? 1 : 256 / p.tpr;
     const uint64_t want = (p.rows + rpc - 1) / rpc, cap = (uint64_t)1 << 30;
     const unsigned grid = (unsigned)(want < cap ? want : cap);
-    if (r) layernorm_vec_kernel<T, VPT, BIG, true><<<grid, p.tpr * rpc, 0, st>>>(x, r, w, b, y, p);
-    else layernorm_vec_kernel<T, VPT, BIG, false><<<grid, p.tpr * rpc, 0, st>>>(x, r, w, b, y, p);
+    if (r) launch_k(layernorm_vec_kernel<T, VPT, BIG, true>, grid, p.tpr * rpc, 0, st, x, r, w, b, y, p);
+    else launch_k(layernorm_vec_kernel<T, VPT, BIG, false>, grid, p.tpr * rpc, 0, st, x, r, w, b, y, p);
 }
 
 // add: layer_norm(x + r); otherwise layer_norm(x) (r unused).
@@ -245,8 +247,8 @@ static int ln_entry(const char* name, const T* x, bool add, const T* r, const T*
     } else {
         const uint64_t cap = (uint64_t)1 << 30;
         const unsigned grid = (unsigned)(rows < cap ? rows : cap);
-        if (r) layernorm_scalar_kernel<T, true><<<grid, 256, 0, st>>>(x, r, w, b, y, p);
-        else layernorm_scalar_kernel<T, false><<<grid, 256, 0, st>>>(x, r, w, b, y, p);
+        if (r) launch_k(layernorm_scalar_kernel<T, true>, grid, 256, 0, st, x, r, w, b, y, p);
+        else launch_k(layernorm_scalar_kernel<T, false>, grid, 256, 0, st, x, r, w, b, y, p);
     }
     return check_launch(name);
 }

@@ -52,6 +52,7 @@ struct OpCombF {
 template <typename T, int OP, bool VEC>
 __global__ void __launch_bounds__(256)
     reduce_rows_kernel(const T* x, uint64_t rows, uint32_t cols, float* out, int tpr) {
+    pdl_begin();
     constexpr int V = VEC ? Vec<T>::N : 1;
     __shared__ float red[8];
     const int rpc = blockDim.x / tpr;
@@ -98,6 +99,7 @@ __global__ void __launch_bounds__(256)
 template <typename T, int OP>
 __global__ void __launch_bounds__(RED_THREADS)
     reduce_stage1_kernel(const T* x, uint64_t n, uint64_t nvec, double* partial) {
+    pdl_begin();
     constexpr int V = Vec<T>::N;
     __shared__ double red[RED_THREADS / 32];
     const uint64_t stride = (uint64_t)gridDim.x * RED_THREADS;
@@ -143,6 +145,7 @@ __global__ void __launch_bounds__(RED_THREADS)
 template <int OP>
 __global__ void __launch_bounds__(RED_THREADS)
     reduce_stage2_kernel(const double* partial, int nblocks, double* out) {
+    pdl_begin();
     __shared__ double red[RED_THREADS / 32];
     double acc = OP == OXIDE_RED_MAX ? -INFINITY : 0.0;
     for (int i = threadIdx.x; i < nblocks; i += RED_THREADS) acc = red_comb<OP>(acc, partial[i]);
@@ -154,6 +157,7 @@ __global__ void __launch_bounds__(RED_THREADS)
 template <typename T, int OP>
 __global__ void __launch_bounds__(RED_THREADS)
     reduce_stage1_scalar_kernel(const T* x, uint64_t n, uint64_t per_block, double* partial) {
+    pdl_begin();
     __shared__ double red[RED_THREADS / 32];
     const uint64_t lo = (uint64_t)blockIdx.x * per_block;
     const uint64_t hi = lo + per_block < n ? lo + per_block : n;
@@ -179,13 +183,13 @@ static void launch_reduce(const T* x, uint64_t n, double* out, double* partial, 
     if (aligned16(x)) {
         const uint64_t nvec = n / V;
         const uint64_t blocks = stage1_blocks(nvec);
-        reduce_stage1_kernel<T, OP><<<(unsigned)blocks, RED_THREADS, 0, st>>>(x, n, nvec, partial);
-        reduce_stage2_kernel<OP><<<1, RED_THREADS, 0, st>>>(partial, (int)blocks, out);
+        launch_k(reduce_stage1_kernel<T, OP>, (unsigned)blocks, RED_THREADS, 0, st, x, n, nvec, partial);
+        launch_k(reduce_stage2_kernel<OP>, 1, RED_THREADS, 0, st, partial, (int)blocks, out);
     } else {
         const uint64_t blocks = stage1_blocks(n);
         const uint64_t per = (n + blocks - 1) / blocks;
-        reduce_stage1_scalar_kernel<T, OP><<<(unsigned)blocks, RED_THREADS, 0, st>>>(x, n, per, partial);
-        reduce_stage2_kernel<OP><<<1, RED_THREADS, 0, st>>>(partial, (int)blocks, out);
+        launch_k(reduce_stage1_scalar_kernel<T, OP>, (unsigned)blocks, RED_THREADS, 0, st, x, n, per, partial);
+        launch_k(reduce_stage2_kernel<OP>, 1, RED_THREADS, 0, st, partial, (int)blocks, out);
     }
 }
 
@@ -204,9 +208,9 @@ static int reduce_entry(const char* name, int op, const T* x, uint64_t n, double
         // Empty input: the identity of the operation, written by a kernel so
         // the result is stream-ordered like every other result.
         if (op == OXIDE_RED_MAX)
-            reduce_stage2_kernel<OXIDE_RED_MAX><<<1, RED_THREADS, 0, st>>>(partial, 0, out);
+            launch_k(reduce_stage2_kernel<OXIDE_RED_MAX>, 1, RED_THREADS, 0, st, partial, 0, out);
         else
-            reduce_stage2_kernel<OXIDE_RED_SUM><<<1, RED_THREADS, 0, st>>>(partial, 0, out);
+            launch_k(reduce_stage2_kernel<OXIDE_RED_SUM>, 1, RED_THREADS, 0, st, partial, 0, out);
         return check_launch(name);
     }
     switch (op) {
@@ -302,8 +306,8 @@ static int reduce_rows_entry(const char* name, int op, const T* x, uint64_t rows
     const unsigned grid = (unsigned)(want < cap ? want : cap);
     const uint32_t c32 = (uint32_t)cols;
 #define OXIDE_ROWS_LAUNCH(OPV)                                                              \
-    (vec ? reduce_rows_kernel<T, OPV, true><<<grid, 256, 0, st>>>(x, rows, c32, out, tpr) \
-         : reduce_rows_kernel<T, OPV, false><<<grid, 256, 0, st>>>(x, rows, c32, out, tpr))
+    (vec ? launch_k(reduce_rows_kernel<T, OPV, true>, grid, 256, 0, st, x, rows, c32, out, tpr) \
+         : launch_k(reduce_rows_kernel<T, OPV, false>, grid, 256, 0, st, x, rows, c32, out, tpr))
     switch (op) {
         case OXIDE_RED_SUM: OXIDE_ROWS_LAUNCH(OXIDE_RED_SUM); break;
         case OXIDE_RED_MAX: OXIDE_ROWS_LAUNCH(OXIDE_RED_MAX); break;

@@ -129,6 +129,7 @@ __device__ __forceinline__ void norm_store_rms(T* yrow, const T* w, const uint4 
 template <typename T, int VPT, bool ADD, bool BIG>
 __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : (ADD ? 4 : 6))
     rmsnorm_vec_kernel(const T* x, const T* r, const T* w, T* h, T* y, NormArgs p) {
+    pdl_begin();
     constexpr int V = Vec<T>::N;
     __shared__ float red[32];
     const int rpc = blockDim.x / p.tpr;
@@ -184,6 +185,7 @@ __global__ void __launch_bounds__(BIG ? 1024 : 256, BIG ? 1 : (ADD ? 4 : 6))
 template <typename T, bool ADD>
 __global__ void __launch_bounds__(256)
     rmsnorm_scalar_kernel(const T* x, const T* r, const T* w, T* h, T* y, NormArgs p) {
+    pdl_begin();
     __shared__ float red[32];
     for (uint64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
         const uint64_t off = row * p.cols;
@@ -219,8 +221,7 @@ static void launch_norm_vec(const T* x, const T* r, const T* w, T* h, T* y, Norm
     const int threads = p.tpr * rpc;
     const uint64_t want = (p.rows + rpc - 1) / rpc;
     const uint64_t cap = (uint64_t)1 << 30;
-    rmsnorm_vec_kernel<T, VPT, ADD, BIG>
-        <<<(unsigned)(want < cap ? want : cap), threads, 0, st>>>(x, r, w, h, y, p);
+    launch_k(rmsnorm_vec_kernel<T, VPT, ADD, BIG>, (unsigned)(want < cap ? want : cap), threads, 0, st, x, r, w, h, y, p);
 }
 
 template <typename T, bool ADD>
@@ -249,8 +250,7 @@ static int norm_dispatch(const char* name, const T* x, const T* r, const T* w, T
         launch_norm_vec<T, VT, ADD, true>(x, r, w, h, y, p, st);
     } else {
         const uint64_t cap = (uint64_t)1 << 30;
-        rmsnorm_scalar_kernel<T, ADD>
-            <<<(unsigned)(rows < cap ? rows : cap), 256, 0, st>>>(x, r, w, h, y, p);
+        launch_k(rmsnorm_scalar_kernel<T, ADD>, (unsigned)(rows < cap ? rows : cap), 256, 0, st, x, r, w, h, y, p);
     }
     return check_launch(name);
 }

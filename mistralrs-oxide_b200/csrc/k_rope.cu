@@ -46,6 +46,7 @@ template <typename T>
 __global__ void __launch_bounds__(512)
     rope_vec_kernel(const T* q, T* qo, const T* k, T* ko, const float* cos_t, const float* sin_t,
                     const int32_t* pos, RopeArgs p) {
+    pdl_begin();
     constexpr int V = Vec<T>::N;
     const uint32_t half = p.head_dim / 2;
     const uint32_t cph = half / V;  // chunks per head
@@ -109,6 +110,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
     rope_scalar_kernel(const T* q, T* qo, const T* k, T* ko, const float* cos_t,
                        const float* sin_t, const int32_t* pos, RopeArgs p) {
+    pdl_begin();
     const uint32_t half = p.head_dim / 2;
     const uint64_t heads = p.q_heads + (k ? p.k_heads : 0);
     const uint64_t total = p.tokens * heads * half;
@@ -165,13 +167,13 @@ static int rope_entry(const char* name, const T* q, T* qo, uint64_t qh, const T*
         uint64_t threads = (items + 31) / 32 * 32;
         if (threads > 512) threads = 256;
         const uint64_t groups = (tokens + ROPE_TOK - 1) / ROPE_TOK;
-        rope_vec_kernel<T><<<(unsigned)(groups < cap ? groups : cap), (unsigned)threads, 0, st>>>(
+        launch_k(rope_vec_kernel<T>, (unsigned)(groups < cap ? groups : cap), (unsigned)threads, 0, st, 
             q, qo, k, ko, cos_t, sin_t, pos, p);
     } else {
         const uint64_t total = tokens * (qh + (k ? kh : 0)) * half;
         const uint64_t blocks = (total + 255) / 256;
         const uint64_t bcap = (uint64_t)sm_count() * 8;
-        rope_scalar_kernel<T><<<(unsigned)(blocks < bcap ? blocks : bcap), 256, 0, st>>>(
+        launch_k(rope_scalar_kernel<T>, (unsigned)(blocks < bcap ? blocks : bcap), 256, 0, st, 
             q, qo, k, ko, cos_t, sin_t, pos, p);
     }
     return check_launch(name);

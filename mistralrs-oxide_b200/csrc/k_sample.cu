@@ -420,6 +420,7 @@ constexpr int SMP_QB = 8;  // logit groups in flight per thread in the first pas
 
 template <typename T, int CL>
 __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
+    pdl_begin();
     extern __shared__ __align__(16) unsigned char smem[];
     float* sp = reinterpret_cast<float*>(smem);                                           // [SMP_SPAN]
     unsigned long long* gbuf = reinterpret_cast<unsigned long long*>(smem + SMP_SPAN * 4);  // [SMP_GATHER]
@@ -686,13 +687,13 @@ static int sample_entry(const char* name, const T* logits, uint64_t rows, uint64
     cfg.blockDim = dim3(SMP_THREADS, 1, 1);
     cfg.dynamicSmemBytes = SMP_SMEM;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = cl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = add_pdl_attr(attr, 1);
     const void* kern;
     switch (cl) {
         case 1: kern = reinterpret_cast<const void*>(sample_kernel<T, 1>); break;

@@ -176,6 +176,7 @@ constexpr int SMAX_VPT = 4;
 // VPT packed vectors of its row in registers between the max, exp and store.
 template <typename T, int VPT, bool MASK>
 __global__ void __launch_bounds__(256, 3) smax_rows_kernel(const T* x, T* out, SmaxArgs p) {
+    pdl_begin();
     constexpr int V = Vec<T>::N;
     __shared__ float red[32];
     const uint32_t nvec = p.cols / V;
@@ -238,6 +239,7 @@ __device__ __forceinline__ void online_merge(float& M, float& S, float m, float 
 template <typename T, bool MASK, int NT, int U>
 __global__ void __launch_bounds__(NT, 2048 / NT / 2)
     smax_stream_kernel(const T* x, T* out, SmaxArgs p) {
+    pdl_begin();
     constexpr int V = Vec<T>::N;
     __shared__ float red[32];
     __shared__ float slot[2];
@@ -367,6 +369,7 @@ constexpr int stream_unroll() { return MASK ? 2 : 4; }
 // unmasked part of the row three times (max, sum, write).
 template <typename T>
 __global__ void __launch_bounds__(256) smax_rows_scalar_kernel(const T* x, T* out, SmaxArgs p) {
+    pdl_begin();
     __shared__ float red[8];
     for (uint64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
         const uint32_t len = valid_len(p, row);
@@ -396,6 +399,7 @@ __global__ void __launch_bounds__(256) smax_rows_scalar_kernel(const T* x, T* ou
 template <typename T>
 __global__ void __launch_bounds__(256)
     smax_inner_kernel(const T* x, T* out, uint64_t outer, uint64_t dim, uint64_t inner) {
+    pdl_begin();
     const uint64_t total = outer * inner;
     for (uint64_t c = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; c < total;
          c += (uint64_t)gridDim.x * blockDim.x) {
@@ -421,13 +425,13 @@ static cudaError_t launch_cluster(const void* kern, void** args, SmaxArgs& p, cu
     cfg.blockDim = dim3(p.tpr, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = p.cl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = add_pdl_attr(attr, 1);
     return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
@@ -437,8 +441,7 @@ static cudaError_t launch_tiled(const T* x, T* out, SmaxArgs p, cudaStream_t st)
     // next CTAs' loads in flight while resident ones compute.
     const int rpc = 256 / p.tpr;
     const uint64_t tiles = (p.rows + rpc - 1) / rpc, cap = (uint64_t)1 << 30;
-    smax_rows_kernel<T, VPT, MASK>
-        <<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, st>>>(x, out, p);
+    launch_k(smax_rows_kernel<T, VPT, MASK>, (unsigned)(tiles < cap ? tiles : cap), 256, 0, st, x, out, p);
     return cudaSuccess;
 }
 
@@ -461,7 +464,7 @@ static cudaError_t launch_stream(const T* x, T* out, SmaxArgs p, cudaStream_t st
         return launch_cluster(reinterpret_cast<const void*>(kern), args, p, st);
     }
     const uint64_t cap = (uint64_t)1 << 30;
-    kern<<<(unsigned)(p.rows < cap ? p.rows : cap), STREAM_THREADS, 0, st>>>(x, out, p);
+    launch_k(kern, (unsigned)(p.rows < cap ? p.rows : cap), STREAM_THREADS, 0, st, x, out, p);
     return cudaSuccess;
 }
 
@@ -512,6 +515,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 template <int VPT>
 __global__ void __launch_bounds__(256, 4)
     smax_bf16_warp_kernel(const bf16_t* __restrict__ x, bf16_t* __restrict__ out, SmaxArgs p) {
+    pdl_begin();
     const uint32_t lane = threadIdx.x & 31u;
     const uint64_t warp0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -584,7 +588,7 @@ static cudaError_t launch_bf16_warp(const bf16_t* x, bf16_t* out, const SmaxArgs
     // two CTAs per resident slot: measured ~2% faster than one
     const uint64_t cap = 2ull * resident_blocks(reinterpret_cast<const void*>(kern), 256, 0);
     const unsigned grid = (unsigned)(want < cap ? want : cap);
-    kern<<<grid, 256, 0, st>>>(x, out, p);
+    launch_k(kern, grid, 256, 0, st, x, out, p);
     return cudaSuccess;
 }
 
@@ -641,7 +645,7 @@ static int rows_dispatch(const char* name, const T* x, T* out, SmaxArgs p, cudaS
     }
     cudaError_t e = cudaSuccess;
     if (!vec) {
-        smax_rows_scalar_kernel<T><<<(unsigned)(p.rows < cap ? p.rows : cap), 256, 0, st>>>(x, out, p);
+        launch_k(smax_rows_scalar_kernel<T>, (unsigned)(p.rows < cap ? p.rows : cap), 256, 0, st, x, out, p);
     } else if (p.mask) {
         e = launch_vec<T, true>(x, out, p, vpt, st);
     } else {
@@ -703,7 +707,7 @@ static int softmax_entry(const char* name, const T* x, T* out, uint64_t outer, u
     const uint64_t total = outer * inner;
     const uint64_t blocks = (total + 255) / 256;
     const uint64_t cap = (uint64_t)sm_count() * 8;
-    smax_inner_kernel<T><<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, st>>>(x, out, outer, dim,
+    launch_k(smax_inner_kernel<T>, (unsigned)(blocks < cap ? blocks : cap), 256, 0, st, x, out, outer, dim,
                                                                                   inner);
     return check_launch(name);
 }

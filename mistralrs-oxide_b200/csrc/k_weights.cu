@@ -98,6 +98,7 @@ __device__ __forceinline__ void decode_item(const uint4 w, O* out, uint64_t g) {
 template <int SRC, typename O>
 __global__ void __launch_bounds__(WD_THREADS)
     decode_vec_kernel(const unsigned char* src, O* out, uint64_t items) {
+    pdl_begin();
     constexpr int SB = DecodeItem<SRC, O>::SB;
     constexpr uint64_t STEP = (uint64_t)WD_THREADS * WD_UNROLL;
     for (uint64_t g0 = (uint64_t)blockIdx.x * STEP + threadIdx.x; g0 < items; g0 += (uint64_t)gridDim.x * STEP) {
@@ -125,6 +126,7 @@ __global__ void __launch_bounds__(WD_THREADS)
 template <int SRC, typename O>
 __global__ void __launch_bounds__(WD_THREADS)
     decode_scalar_kernel(const unsigned char* src, O* out, uint64_t n) {
+    pdl_begin();
     for (uint64_t i = (uint64_t)blockIdx.x * WD_THREADS + threadIdx.x; i < n; i += (uint64_t)gridDim.x * WD_THREADS)
         store_one<O>(out, i, decode_one<SRC>(src, i));
 }
@@ -143,8 +145,8 @@ static void launch_decode(const unsigned char* src, O* out, uint64_t n, cudaStre
     uint64_t grid = (items + per - 1) / per;
     if (grid > cap) grid = cap;
     if (grid < 1) grid = 1;
-    if (vec) decode_vec_kernel<SRC, O><<<(unsigned)grid, WD_THREADS, 0, st>>>(src, out, items);
-    else decode_scalar_kernel<SRC, O><<<(unsigned)grid, WD_THREADS, 0, st>>>(src, out, n);
+    if (vec) launch_k(decode_vec_kernel<SRC, O>, (unsigned)grid, WD_THREADS, 0, st, src, out, items);
+    else launch_k(decode_scalar_kernel<SRC, O>, (unsigned)grid, WD_THREADS, 0, st, src, out, n);
 }
 
 template <typename O>

@@ -215,6 +215,119 @@ struct FastDiv {
 };
 
 // ---------------------------------------------------------------------------
+// e^x rounded to f32, for parity with a correctly rounded host expf (glibc's,
+// which the reference's f32::exp calls).  Method: the table-driven reduction
+// of P. T. P. Tang (ACM TOMS 15(2), 1989) with an N-entry table, in double
+// with fused multiply-adds: x = (kN + j) ln2 / N + r with k N + j =
+// round(x N / ln2), |r| <= ln2 / (2N); e^x = 2^k * 2^(j/N) * e^r, e^r from
+// its Taylor series to the degree D that keeps the truncation below 2^-43
+// (N = 1: D = 10; N = 4: D = 7; N = 8: D = 6), Horner in double; 2^(j/N) is
+// the nearest double (picked by selects, no memory access) and 2^k goes into
+// its exponent field; the product is rounded once to f32.  The result is
+// RN(e^x) except where e^x lies within ~2^-43 (relative) of a rounding
+// boundary between two floats.  |x| is clamped to 110 first, beyond the f32
+// overflow (88.73) and underflow (-103.98) points; NaN propagates.  Every
+// step is an IEEE double operation, so the host compilation of this function
+// gives the device's bits (tests/test_exp_rn.py compares it with glibc expf
+// over every float).
+// ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ double exp_dfma(double a, double b, double c) {
+#ifdef __CUDA_ARCH__
+    return __fma_rn(a, b, c);
+#else
+    return __builtin_fma(a, b, c);
+#endif
+}
+__host__ __device__ __forceinline__ double exp_bits_double(uint64_t b) {
+#ifdef __CUDA_ARCH__
+    return __longlong_as_double((long long)b);
+#else
+    double d;
+    __builtin_memcpy(&d, &b, 8);
+    return d;
+#endif
+}
+__host__ __device__ __forceinline__ uint64_t exp_double_bits(double d) {
+#ifdef __CUDA_ARCH__
+    return (uint64_t)__double_as_longlong(d);
+#else
+    uint64_t b;
+    __builtin_memcpy(&b, &d, 8);
+    return b;
+#endif
+}
+// 2^(j/N) for j in [0, N): the nearest doubles.
+template <int N>
+__host__ __device__ __forceinline__ double exp_table(int j) {
+    if (N == 1) return 1.0;
+    if (N == 4) {
+        const double a = (j & 1) ? 0x1.306fe0a31b715p+0 : 1.0;                  // 2^(1/4) : 1
+        const double b = (j & 1) ? 0x1.ae89f995ad3adp+0 : 0x1.6a09e667f3bcdp+0;  // 2^(3/4) : 2^(1/2)
+        return (j & 2) ? b : a;
+    }
+    // N == 8
+    const double a = (j & 1) ? 0x1.172b83c7d517bp+0 : 1.0;
+    const double b = (j & 1) ? 0x1.4bfdad5362a27p+0 : 0x1.306fe0a31b715p+0;
+    const double c = (j & 1) ? 0x1.8ace5422aa0dbp+0 : 0x1.6a09e667f3bcdp+0;
+    const double d = (j & 1) ? 0x1.d5818dcfba487p+0 : 0x1.ae89f995ad3adp+0;
+    const double lo = (j & 2) ? b : a, hi = (j & 2) ? d : c;
+    return (j & 4) ? hi : lo;
+}
+template <int N = 4>
+__host__ __device__ __forceinline__ float exp_rn_f32(float x) {
+    static_assert(N == 1 || N == 4 || N == 8, "table sizes 1, 4, 8");
+    // N / ln 2 and ln 2 / N: the nearest doubles (N a power of two, so only
+    // the exponent differs from 1 / ln 2 and ln 2)
+    const double kInv = 0x1.71547652b82fep+0 * N;
+    const double kLn2 = 0x1.62e42fefa39efp-1 / N;
+    const double kLn2Lo = 0x1.abc9e3b39803fp-56 / N;  // ln 2 / N - kLn2 (used for N = 1)
+    const double kShift = 0x1.8p52;                    // 1.5 * 2^52: rounds to an integer in the low bits
+    double xd = (double)x;
+    xd = xd < -110.0 ? -110.0 : xd;  // comparisons are false for NaN: it passes through
+    xd = xd > 110.0 ? 110.0 : xd;
+    const double t = exp_dfma(xd, kInv, kShift);
+    const double kd = t - kShift;  // round(x N / ln 2)
+    const int kj = (int)(uint32_t)exp_double_bits(t);
+    // r = x - kd ln2 / N: one fused step is exact to |kd| * 2^-53 ln2 / N
+    // <= 2^-46 for N >= 4; N = 1 (|kd| <= 159) adds the low part of ln 2.
+    double r = exp_dfma(-kd, kLn2, xd);
+    if (N == 1) r = exp_dfma(-kd, kLn2Lo, r);
+    double p;
+    if (N == 1) {  // 1/n!, n = 10 .. 2: the nearest doubles
+        p = 0x1.27e4fb7789f5cp-22;
+        p = exp_dfma(p, r, 0x1.71de3a556c734p-19);
+        p = exp_dfma(p, r, 0x1.a01a01a01a01ap-16);
+        p = exp_dfma(p, r, 0x1.a01a01a01a01ap-13);
+        p = exp_dfma(p, r, 0x1.6c16c16c16c17p-10);
+        p = exp_dfma(p, r, 0x1.1111111111111p-7);
+        p = exp_dfma(p, r, 0x1.5555555555555p-5);
+        p = exp_dfma(p, r, 0x1.5555555555555p-3);
+        p = exp_dfma(p, r, 0.5);
+    } else if (N == 4) {  // n = 7 .. 2
+        p = 0x1.a01a01a01a01ap-13;
+        p = exp_dfma(p, r, 0x1.6c16c16c16c17p-10);
+        p = exp_dfma(p, r, 0x1.1111111111111p-7);
+        p = exp_dfma(p, r, 0x1.5555555555555p-5);
+        p = exp_dfma(p, r, 0x1.5555555555555p-3);
+        p = exp_dfma(p, r, 0.5);
+    } else {  // n = 6 .. 2
+        p = 0x1.6c16c16c16c17p-10;
+        p = exp_dfma(p, r, 0x1.1111111111111p-7);
+        p = exp_dfma(p, r, 0x1.5555555555555p-5);
+        p = exp_dfma(p, r, 0x1.5555555555555p-3);
+        p = exp_dfma(p, r, 0.5);
+    }
+    p = exp_dfma(p, r, 1.0);
+    p = exp_dfma(p, r, 1.0);  // e^r
+    // 2^(j/N) * 2^k: k = floor(kj / N) added to the table entry's exponent
+    // (|k| <= 159 after the clamp; for a NaN input kj is arbitrary and the
+    // product stays NaN)
+    const int k = kj >> (N == 1 ? 0 : N == 4 ? 2 : 3);
+    const uint64_t sbits = exp_double_bits(exp_table<N>(kj & (N - 1))) + ((uint64_t)(int64_t)k << 52);
+    return (float)(p * exp_bits_double(sbits));
+}
+
+// ---------------------------------------------------------------------------
 // Special-function unit approximations (relative error ~2^-22; subnormal
 // results kept).  Used only where the result is rounded to bf16 afterwards or
 // the tolerance is stated beside the caller.
@@ -287,6 +400,60 @@ struct OpMaxU64 {
         return a > b ? a : b;
     }
 };
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel is launched with programmatic
+// stream serialization (launch_k below), so its CTAs may be scheduled while
+// the kernel before it on the stream is still finishing.  pdl_begin() is the
+// first statement of every kernel: it lets the next kernel launch early
+// (griddepcontrol.launch_dependents -- that kernel's own pdl_begin() then
+// waits) and waits until the previous kernel has completed with its memory
+// visible (griddepcontrol.wait) before this kernel touches global memory.  A
+// kernel launched without the attribute returns from the wait at once.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+bool pdl_enabled();  // false when OXIDE_NO_PDL=1 is set (read once)
+
+// Append the programmatic-serialization attribute to attr[0..n) (room for one
+// more) when it is enabled; returns the new count.
+inline int add_pdl_attr(cudaLaunchAttribute* attr, int n) {
+    if (!pdl_enabled()) return n;
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    return n + 1;
+}
+
+// cudaLaunchKernelEx with programmatic stream serialization; launch_kx adds
+// the extra attributes given (e.g. a cluster shape).
+template <typename... P, typename... A>
+cudaError_t launch_kx(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                      const cudaLaunchAttribute* extra, int n_extra, A&&... args) {
+    cudaLaunchAttribute attr[4];
+    int n = 0;
+    for (int i = 0; i < n_extra && n < 3; ++i) attr[n++] = extra[i];
+    if (pdl_enabled()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+}
+template <typename... P, typename... A>
+cudaError_t launch_k(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
+    return launch_kx(kernel, grid, block, smem, st, (const cudaLaunchAttribute*)nullptr, 0,
+                     static_cast<A&&>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // Host-side helpers (defined in oxide_runtime.cu)

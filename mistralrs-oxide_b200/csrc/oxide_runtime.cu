@@ -6,6 +6,7 @@
 // every failure is returned to the caller, none aborts the process.
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -53,6 +54,14 @@ int injected_failure(const char* op) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("OXIDE_NO_PDL");
+        return !(v && v[0] == '1');
+    }();
+    return on;
+}
 
 int sm_count() {
     static int cache[64] = {0};
@@ -152,6 +161,8 @@ unsigned long long current_context_id() {
 __global__ void __launch_bounds__(256)
     selftest_rowdiv_kernel(const float* a, uint64_t na, const float* b, uint64_t nb,
                            unsigned long long* out) {
+    pdl_begin();
+    pdl_begin();
     const uint64_t total = na * nb;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (uint64_t)gridDim.x * blockDim.x) {
@@ -179,7 +190,7 @@ int oxide_selftest_rowdiv(const float* a, uint64_t na, const float* b, uint64_t 
     if (na == 0 || nb == 0) return OXIDE_OK;
     OXIDE_REQUIRE(a && b, name, "null pointer");
     OXIDE_REQUIRE(na <= UINT64_MAX / nb, name, "na * nb overflows");
-    oxide::selftest_rowdiv_kernel<<<oxide::sm_count() * 8, 256, 0, stream>>>(a, na, b, nb, out);
+    oxide::launch_k(oxide::selftest_rowdiv_kernel, oxide::sm_count() * 8, 256, 0, stream, a, na, b, nb, out);
     return oxide::check_launch(name);
 }
 

@@ -69,6 +69,7 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_kv_cache_append_f32": (i32, [vp, vp, vp, vp, u64, u64, u64, u64, u64, u64, vp]),
     "oxide_kv_cache_append_bf16": (i32, [vp, vp, vp, vp, u64, u64, u64, u64, u64, u64, vp]),
     "oxide_decode_attention_workspace_bytes": (u64, [u64, u64, u64, u64]),
+    "oxide_debug_decode_attention_path": (None, [i32]),
     "oxide_decode_attention_f32": (i32, [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, vp, u64, vp]),
     "oxide_decode_attention_bf16": (i32, [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, vp, u64, vp]),
     "oxide_sample_f32": (i32, [vp, u64, u64, f32, u64, f32, vp, vp, vp, vp]),

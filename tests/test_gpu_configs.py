@@ -12,8 +12,8 @@ import numpy as np
 import pytest
 import torch
 
-from _util import (BF16_ULP, F32_REL, SILU_F32_MIN_EXACT, SILU_F32_ULP, assert_bits_equal,
-                   assert_parity_rel, assert_ulp, rms_norm_exact, smax_close, to_dev, to_np)
+from _util import (BF16_ULP, F32_REL, assert_bits_equal, assert_parity_rel, assert_silu_f32_parity, assert_ulp,
+                   rms_norm_exact, smax_close, to_dev, to_np)
 
 pytestmark = pytest.mark.gpu
 
@@ -57,8 +57,7 @@ def test_c2_add_mul_silu_mul_f32(cuda, orc, threads):
     call("oxide_silu_mul_f32", tg.data_ptr(), tu.data_ptr(), to.data_ptr(), gate.size, None)
     torch.cuda.synchronize()
     got, ref = to_np(to), orc.silu_mul(gate, up, threads=threads)
-    assert_ulp(got, ref, SILU_F32_ULP)
-    assert np.mean(got.view(np.uint32) == ref.view(np.uint32)) >= SILU_F32_MIN_EXACT
+    assert_silu_f32_parity(got, ref, gate, orc, threads)
 
 
 def test_c3_masked_decode_softmax_and_argmax_f32(cuda, orc, threads):

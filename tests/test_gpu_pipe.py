@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from _util import assert_bits_equal, assert_parity_rel, assert_ulp, rms_norm_exact
+from _util import assert_bits_equal, assert_parity_rel, assert_silu_f32_parity, assert_ulp, rms_norm_exact
 
 pytestmark = pytest.mark.gpu
 F = np.float32
@@ -61,7 +61,7 @@ def test_pipe_silu_mul(pipe, orc, pinned):
 
     dev = ops.silu_mul(torch.from_numpy(np.array(g)).cuda(), torch.from_numpy(np.array(u)).cuda())
     assert_bits_equal(out, dev.cpu().numpy())
-    assert_ulp(out, orc.silu_mul(g, u), 8)
+    assert_silu_f32_parity(out, orc.silu_mul(g, u), g, orc)
 
 
 def test_pipe_rms_norm(pipe, orc):
@@ -211,7 +211,7 @@ def test_pipe_deferred_ops_overlap_and_keep_their_broadcasts(pipe, orc):
     call("oxide_pipe_defer", pipe, 0)
     for x, w, out in zip(xs, ws, outs):
         assert_parity_rel(out, orc.rms_norm(x, w, 1e-5), rms_norm_exact(x, w, 1e-5), 1e-5)
-    assert_ulp(o, orc.silu_mul(g, u), 8)
+    assert_silu_f32_parity(o, orc.silu_mul(g, u), g, orc)
 
 
 def test_pipe_new_forms_reject_bad_arguments(pipe, olib):
