@@ -456,24 +456,18 @@ def host_seconds(fn, reps=3):
     return statistics.median(ts)
 
 
-class Pipe:
-    """A host-buffer pipeline (oxide_pipe_*) on this rank's device."""
+def make_pipe(device: int):
+    """oxide_b200.pipe.Pipe on this rank's device; calling it with an entry
+    point's name and its arguments (after the handle) runs that oxide_pipe_*
+    function on pinned host pointers."""
+    from oxide_b200._lib import call
+    from oxide_b200.pipe import Pipe
 
-    def __init__(self, device: int, chunk_bytes=16 << 20, depth=4):
-        from oxide_b200._lib import call
+    class RawPipe(Pipe):
+        def __call__(self, name, *args):
+            call(name, self.handle, *args)
 
-        self.h = C.c_void_p()
-        call("oxide_pipe_create", device, chunk_bytes, depth, C.byref(self.h))
-
-    def __call__(self, name, *args):
-        from oxide_b200._lib import call
-
-        call(name, self.h, *args)
-
-    def close(self):
-        from oxide_b200._lib import call
-
-        call("oxide_pipe_destroy", self.h)
+    return RawPipe(device, chunk_bytes=16 << 20, depth=4)
 
 
 def pinned(a: np.ndarray):
@@ -844,14 +838,14 @@ def run_oxide(args):
     # ---- e2e through the host-buffer C ABI ----
     pa, pb, ps, pg, pu = (pinned(v) for v in (a, b, s, gate, up))
     ph, py, po = (torch.empty_like(t).pin_memory() for t in (pa, pa, pg))
-    pipe = Pipe(local)
-    _lib.call("oxide_pipe_defer", pipe.h, 1)
+    pipe = make_pipe(local)
+    _lib.call("oxide_pipe_defer", pipe.handle, 1)
 
     def e2e_step():
         pipe("oxide_pipe_add_mul_rowbcast_f32", pa.data_ptr(), pb.data_ptr(), ps.data_ptr(), ph.data_ptr(),
              py.data_ptr(), rows, cols)
         pipe("oxide_pipe_silu_mul_f32", pg.data_ptr(), pu.data_ptr(), po.data_ptr(), pg.numel())
-        _lib.call("oxide_pipe_sync", pipe.h)
+        _lib.call("oxide_pipe_sync", pipe.handle)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -861,7 +855,7 @@ def run_oxide(args):
         e2e_step()
     e2e_secs = reduce_over_ranks(time.perf_counter() - t0, world)
     barrier(world)
-    _lib.call("oxide_pipe_defer", pipe.h, 0)
+    _lib.call("oxide_pipe_defer", pipe.handle, 0)
     e2e_ok = bool(torch.equal(po.view(-1), to.cpu().view(-1)) and torch.equal(py.view(-1), ty.cpu().view(-1))
                   and torch.equal(ph.view(-1), th.cpu().view(-1)))
     h2d = 4 * (a.size + b.size + s.size + gate.size + up.size)

@@ -320,8 +320,22 @@ uint64_t oxide_decode_attention_workspace_bytes(uint64_t batch, uint64_t q_heads
  * counterpart): 0 (default) = the tcgen05 / TMA kernel wherever it applies
  * (sm_100, head_dim 128, q_heads / kv_heads in {1, 2, 4, 8}, batch <= 1024,
  * max_seq >= 256), else the split-K mma.sync kernel; 1 = always the split-K
- * kernel.  Process-wide; set it between calls, not while one is enqueued. */
+ * kernel; 2 = the tcgen05 kernel with its tile loads withheld, so that every
+ * bounded wait in it runs out (about two seconds) and the launch ends with
+ * NaN outputs and OXIDE_DEVICE_WAIT_TIMEOUT raised -- for failure-detection
+ * tests only.  Process-wide; set it between calls, not while one is
+ * enqueued. */
 void oxide_debug_decode_attention_path(int path);
+
+/* Device-side failure flags (no reference counterpart: the reference has no
+ * device waits).  A kernel whose bounded wait runs out -- a copy or product
+ * that never completes -- stops, writes NaN outputs and raises a flag in a
+ * per-device word instead of hanging; the flags are sticky, like CUDA's own
+ * errors, until reset.  oxide_device_status waits for the calling thread's
+ * current device to finish its work, stores the flags raised since the last
+ * reset in *flags and clears them if reset != 0. */
+#define OXIDE_DEVICE_WAIT_TIMEOUT 1u
+int oxide_device_status(int reset, uint32_t* flags);
 int oxide_decode_attention_f32(const float* q, const float* k_cache, const float* v_cache, const int32_t* lens,
                                float* out, uint64_t batch, uint64_t q_heads, uint64_t kv_heads, uint64_t max_seq,
                                uint64_t head_dim, float scale, void* workspace, uint64_t workspace_bytes,

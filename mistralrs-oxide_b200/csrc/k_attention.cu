@@ -586,9 +586,11 @@ static cudaError_t launch_split(const T* q, const T* kc, const T* vc, T* out, fl
 cudaError_t decode_attention_tc_bf16(const bf16_t* q, const bf16_t* kc, const bf16_t* vc, const int32_t* lens,
                                      bf16_t* out, uint64_t batch, uint64_t q_heads, uint64_t kv_heads,
                                      uint64_t max_seq, float scale, void* ws, uint64_t ws_bytes, cudaStream_t st,
-                                     bool* used);
+                                     bool withhold, bool* used);
+int device_status(int reset, uint32_t* flags);
 // 0: the tcgen05 kernel where it applies, else the split-K kernel; 1: always
-// the split-K (mma.sync) kernel (oxide_debug_decode_attention_path).
+// the split-K (mma.sync) kernel; 2: the tcgen05 kernel with its loads
+// withheld (oxide_debug_decode_attention_path).
 static std::atomic<int> g_decode_path{0};
 
 template <typename T>
@@ -622,9 +624,10 @@ static int decode_entry(const char* name, const T* q, const T* kc, const T* vc, 
     cudaError_t e = cudaSuccess;
     bool done = false;  // the tcgen05 kernel ran
     if constexpr (std::is_same<T, bf16_t>::value) {
-        if (fast && g_decode_path.load(std::memory_order_relaxed) == 0)
+        const int path = g_decode_path.load(std::memory_order_relaxed);
+        if (fast && path != 1)
             e = decode_attention_tc_bf16(q, kc, vc, lens, out, batch, q_heads, kv_heads, max_seq, scale, ws, ws_bytes,
-                                         st, &done);
+                                         st, path == 2, &done);
     }
     if (done) {
         // nothing more to launch
@@ -665,7 +668,15 @@ using oxide::bf16_t;
 
 extern "C" {
 
-void oxide_debug_decode_attention_path(int path) { oxide::g_decode_path.store(path == 1 ? 1 : 0); }
+void oxide_debug_decode_attention_path(int path) {
+    oxide::g_decode_path.store(path == 1 || path == 2 ? path : 0);
+}
+
+int oxide_device_status(int reset, uint32_t* flags) {
+    OXIDE_INJECT("oxide_device_status");
+    OXIDE_REQUIRE(flags, "oxide_device_status", "null flags pointer");
+    return oxide::device_status(reset, flags);
+}
 
 uint64_t oxide_decode_attention_workspace_bytes(uint64_t batch, uint64_t q_heads, uint64_t max_seq,
                                                 uint64_t head_dim) {

@@ -92,7 +92,13 @@ struct TcArgs {
     float* part_ml;
     float* part_o;
     uint32_t* err;
+    uint32_t withhold;  // failure-detection tests: the producer issues no loads, so every wait runs out
 };
+
+// Sticky device-side failure flags of this library on each device (bit 0:
+// a bounded wait in the tcgen05 decode-attention kernel ran out), read and
+// cleared by oxide_device_status.
+__device__ unsigned int g_device_status;
 
 __device__ __forceinline__ uint32_t tc_len(const TcArgs& p, uint64_t b) {
     if (!p.lens) return (uint32_t)p.max_seq;
@@ -142,7 +148,10 @@ template <int NR>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     decode_attn_tc_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                           const __grid_constant__ CUtensorMap tmq, TcArgs p) {
-    pdl_begin();
+    // Set-up that touches no global memory (barriers, TMEM, the tensor maps'
+    // descriptors) overlaps the previous kernel; the wait comes before the
+    // first global access.
+    pdl_trigger();
     static_assert(NR == 1 || NR == 2 || NR == 4 || NR == 8, "rep in {1, 2, 4, 8}");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -159,12 +168,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t nb = (uint32_t)p.batch, hkv = p.kv_heads;
 
     if (tid == 0) {
-        uint32_t s = 0;
-        for (uint32_t b = 0; b < nb; ++b) {
-            pre[b] = s;
-            s += (tc_len(p, b) + TC_TK - 1) / TC_TK;
-        }
-        pre[nb] = s;
         *abort = 0;
         *consumed = 0;
         *qconsumed = 0;
@@ -184,7 +187,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         mbar_init(bar(B_DONE), 1);
         mbar_init_fence();
-        if (blockIdx.x == 0) *p.err = 0u;
     }
     if (warp == 0 && lane == 0) {
         tma_prefetch_map(&tmk);
@@ -195,6 +197,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tmem_alloc(smem_u32(tmem_slot), TC_TMEM_COLS);
         tmem_relinquish();
     }
+    pdl_wait();  // the previous kernel's writes (lengths, caches, queries) are visible
+    if (warp == 2) {  // tiles per kv head of each batch, and their prefix sums
+        uint32_t carry = 0;
+        for (uint32_t b0 = 0; b0 < nb; b0 += 32) {
+            const uint32_t b = b0 + lane;
+            uint32_t v = b < nb ? (tc_len(p, b) + TC_TK - 1) / TC_TK : 0u;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {  // inclusive scan over the warp
+                const uint32_t u = __shfl_up_sync(0xffffffffu, v, off);
+                if (lane >= off) v += u;
+            }
+            const uint32_t incl = carry + v;
+            if (b < nb) pre[b + 1] = incl;
+            carry = __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) pre[0] = 0;
+    }
+    if (tid == 0 && blockIdx.x == 0) *p.err = 0u;
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -207,7 +227,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         uint32_t n = 0, q = 0;
-        if (lane == 0 && t0 < t1) {
+        if (lane == 0 && t0 < t1 && !p.withhold) {
             w.seek(t0);
             for (uint32_t t = t0; t < t1 && !*abort; ++t, w.next()) {
                 if (t == t0 || w.lt == 0) {  // first tile of a pair in this CTA: its query heads
@@ -486,65 +506,66 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, TC_TMEM_COLS);
-    if (tid == 0 && *abort) atomicOr(p.err, 1u);
+    if (tid == 0 && *abort) {
+        atomicOr(p.err, 1u);
+        atomicOr(&g_device_status, OXIDE_DEVICE_WAIT_TIMEOUT);
+    }
 }
 
-struct OpAddU32 {
-    __device__ __forceinline__ uint32_t operator()(uint32_t a, uint32_t b) const { return a + b; }
-};
-
 // Merge the split partials of one (batch, q head): the same tile division as
-// the main kernel gives the pair's first and last CTA, hence its slot count.
-// out = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M); a pair without keys
-// gives zeros; NaN everywhere if the main kernel reported an abort.
+// the main kernel gives the CTAs that took part of the pair, and the slot of
+// each (its first tile's offset within the pair).  out = sum_s o_s
+// e^(m_s - M) / sum_s l_s e^(m_s - M); a pair without keys gives zeros; NaN
+// everywhere if the main kernel reported an abort.
+constexpr int TC_MAX_PARTS = 1024;  // CTAs sharing one pair: at most the grid size
 template <int NR>
 __global__ void __launch_bounds__(128)
     decode_attn_tc_combine_kernel(bf16_t* out, TcArgs p, uint32_t G) {
     pdl_begin();
-    __shared__ float wts[TC_MAX_TILES];
-    __shared__ float redf[32];
-    __shared__ uint32_t redu[32];
+    __shared__ unsigned long long redu[32];
+    __shared__ uint32_t slot[TC_MAX_PARTS];
+    __shared__ int nslot;
     const uint64_t bh = blockIdx.x, b = bh / p.q_heads;
     const uint32_t h = (uint32_t)(bh % p.q_heads), kvh = h / NR;
     const int d = threadIdx.x;
-    uint32_t before = 0, all = 0;
+    // tiles per kv head of the batches before b (high word) and of all (low)
+    unsigned long long acc2 = 0;
     for (uint64_t bb = d; bb < p.batch; bb += 128) {
-        const uint32_t tl = (tc_len(p, bb) + TC_TK - 1) / TC_TK;
-        all += tl;
-        if (bb < b) before += tl;
+        const unsigned long long tl = (tc_len(p, bb) + TC_TK - 1) / TC_TK;
+        acc2 += tl | (bb < b ? tl << 32 : 0ull);
     }
-    before = group_reduce(before, redu, 128, OpAddU32());
-    all = group_reduce(all, redu, 128, OpAddU32());
+    struct OpAddU64 {
+        __device__ unsigned long long operator()(unsigned long long x, unsigned long long y) const { return x + y; }
+    };
+    acc2 = group_reduce(acc2, redu, 128, OpAddU64());
+    const uint32_t before = (uint32_t)(acc2 >> 32), all = (uint32_t)acc2;
     const uint32_t tb = (tc_len(p, b) + TC_TK - 1) / TC_TK;
     const uint32_t T = all * p.kv_heads;
-    const uint64_t base = bh * p.stride;
-    // Slot j (a tile offset within the pair) holds a partial when a CTA's
-    // share of the pair starts at tile j: j = 0, or tiles j - 1 and j belong
-    // to different CTAs.
-    const uint32_t tfirst = before * p.kv_heads + kvh * tb;
-    auto starts = [&](uint32_t j) {
-        return j == 0 || tc_owner(tfirst + j, T, G) != tc_owner(tfirst + j - 1, T, G);
-    };
-    float M = -INFINITY;
-    for (uint32_t j = d; j < tb; j += 128)
-        if (starts(j)) M = fmaxf(M, p.part_ml[(base + j) * 2]);
-    M = group_reduce(M, redf, 128, OpMaxF());
-    float lp = 0.0f;
-    for (uint32_t j = d; j < tb; j += 128) {
-        float wv = -1.0f;  // no partial
-        if (starts(j)) {
-            const float ms = p.part_ml[(base + j) * 2];
-            wv = (M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(fsub(ms, M));
-            lp = __fmaf_rn(p.part_ml[(base + j) * 2 + 1], wv, lp);
+    if (d == 0) {
+        int n = 0;
+        if (tb) {
+            const uint32_t tfirst = before * p.kv_heads + kvh * tb, tlast = tfirst + tb - 1;
+            for (uint32_t c = tc_owner(tfirst, T, G); c <= tc_owner(tlast, T, G) && n < TC_MAX_PARTS; ++c) {
+                const uint32_t f0 = (uint32_t)((uint64_t)c * T / G), f1 = (uint32_t)((uint64_t)(c + 1) * T / G);
+                if (f0 < f1) slot[n++] = (f0 > tfirst ? f0 : tfirst) - tfirst;
+            }
         }
-        wts[j] = wv;
+        nslot = n;
     }
-    const float Ls = group_reduce(lp, redf, 128, OpAddF());  // its barrier also publishes wts
-    float acc = 0.0f;
-    const float* po = p.part_o + base * TC_D + d;
-    for (uint32_t j = 0; j < tb; ++j)
-        if (wts[j] >= 0.0f) acc = __fmaf_rn(po[(uint64_t)j * TC_D], wts[j], acc);
-    float r = M == -INFINITY ? 0.0f : fdiv(acc, Ls);
+    __syncthreads();
+    const int n = nslot;
+    const uint64_t base = bh * p.stride;
+    float M = -INFINITY;
+    for (int i = 0; i < n; ++i) M = fmaxf(M, p.part_ml[(base + slot[i]) * 2]);
+    float L = 0.0f, acc = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        const uint64_t sl = base + slot[i];
+        const float ms = p.part_ml[sl * 2];
+        const float w = (M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(fsub(ms, M));
+        L = __fmaf_rn(p.part_ml[sl * 2 + 1], w, L);
+        acc = __fmaf_rn(p.part_o[sl * TC_D + d], w, acc);
+    }
+    float r = M == -INFINITY ? 0.0f : fdiv(acc, L);
     if (*p.err) r = __uint_as_float(0x7fc00000u);
     Vec<bf16_t>::store1(out + bh * TC_D + d, r);
 }
@@ -599,7 +620,7 @@ static cudaError_t tc_launch(const CUtensorMap& mk, const CUtensorMap& mv, const
 cudaError_t decode_attention_tc_bf16(const bf16_t* q, const bf16_t* kc, const bf16_t* vc, const int32_t* lens,
                                      bf16_t* out, uint64_t batch, uint64_t q_heads, uint64_t kv_heads,
                                      uint64_t max_seq, float scale, void* ws, uint64_t ws_bytes, cudaStream_t st,
-                                     bool* used) {
+                                     bool withhold, bool* used) {
     *used = false;
     const uint64_t rep = q_heads / kv_heads;
     if (!tc_enabled() || batch > (uint64_t)TC_MAX_BATCH || max_seq < 256 ||
@@ -607,6 +628,7 @@ cudaError_t decode_attention_tc_bf16(const bf16_t* q, const bf16_t* kc, const bf
         !(rep == 1 || rep == 2 || rep == 4 || rep == 8))
         return cudaSuccess;
     const uint32_t G = (uint32_t)sm_count();
+    if (G > (uint32_t)TC_MAX_PARTS) return cudaSuccess;
     const uint64_t tiles_max = (max_seq + TC_TK - 1) / TC_TK;
     if (tiles_max > (uint64_t)TC_MAX_TILES) return cudaSuccess;
     const uint32_t stride = (uint32_t)tiles_max;  // a partial slot per tile offset of a sequence
@@ -627,6 +649,7 @@ cudaError_t decode_attention_tc_bf16(const bf16_t* q, const bf16_t* kc, const bf
     a.part_ml = static_cast<float*>(ws);
     a.part_o = a.part_ml + (size_t)2 * batch * q_heads * stride;
     a.err = reinterpret_cast<uint32_t*>(a.part_o + (size_t)batch * q_heads * stride * TC_D);
+    a.withhold = withhold ? 1u : 0u;
     *used = true;
     switch (rep) {
         case 1: return tc_launch<1>(mk, mv, mq, out, a, G, st);
@@ -634,6 +657,20 @@ cudaError_t decode_attention_tc_bf16(const bf16_t* q, const bf16_t* kc, const bf
         case 4: return tc_launch<4>(mk, mv, mq, out, a, G, st);
         default: return tc_launch<8>(mk, mv, mq, out, a, G, st);
     }
+}
+
+int device_status(int reset, uint32_t* flags) {
+    unsigned int v = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v));
+    if (e == cudaSuccess && reset) {
+        const unsigned int zero = 0;
+        e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero));
+    }
+    if (e != cudaSuccess)
+        return set_error(OXIDE_ERR_CUDA, "oxide_device_status: %s", cudaGetErrorString(e));
+    *flags = v;
+    return OXIDE_OK;
 }
 
 }  // namespace oxide

@@ -32,6 +32,37 @@ template <typename T>
 constexpr int ew_min_blocks() {
     return sizeof(T) == 4 ? 2 : 4;
 }
+// A functor may set its own UNROLL / MIN_BLOCKS (e.g. the f32 SiLU with the
+// double-precision exponential, whose arithmetic per byte needs more warps
+// per SM to hide memory latency than the plain ops).
+template <typename F, typename = void>
+struct FunUnroll {
+    static constexpr int value = 0;
+};
+template <typename F>
+struct FunUnroll<F, std::void_t<decltype(F::UNROLL)>> {
+    static constexpr int value = F::UNROLL;
+};
+template <typename F, typename = void>
+struct FunMinBlocks {
+    static constexpr int value = 0;
+};
+template <typename F>
+struct FunMinBlocks<F, std::void_t<decltype(F::MIN_BLOCKS)>> {
+    static constexpr int value = F::MIN_BLOCKS;
+};
+template <typename T, typename F>
+constexpr int ew_unroll_f() {
+    return FunUnroll<F>::value ? FunUnroll<F>::value : ew_unroll<T>();
+}
+template <typename T, typename F>
+constexpr int ew_min_blocks_f() {
+    return FunMinBlocks<F>::value ? FunMinBlocks<F>::value : ew_min_blocks<T>();
+}
+// f32 SiLU with the correctly rounded exponential: vectors in flight per
+// thread and operand, and CTAs per SM.
+constexpr int SILU_ACC_UNROLL = 4;
+constexpr int SILU_ACC_MIN_BLOCKS = 3;
 
 // ---- per-element functors (f32 math, IEEE rounding per reference step) ----
 // operator() is one element; pair() is two elements on Blackwell's paired
@@ -93,6 +124,8 @@ struct FSiluMul {  // mul(silu(g), u); silu(g) rounded to T as the pair stores i
     // double rounding the single one avoids): within 1 bf16 ulp there.
     static constexpr bool PACKED = sizeof(T) == 2;
     static constexpr bool ACC = sizeof(T) == 4;
+    static constexpr int UNROLL = ACC ? SILU_ACC_UNROLL : 0;
+    static constexpr int MIN_BLOCKS = ACC ? SILU_ACC_MIN_BLOCKS : 0;
     __device__ __forceinline__ float operator()(float g, float u) const {
         return fmul(Vec<T>::rnd(silu_f<ACC>(g)), u);
     }
@@ -119,6 +152,8 @@ struct HasPacked<F, std::void_t<decltype(F::PACKED)>> {
 template <typename T>
 struct FSilu {
     static constexpr bool ACC = sizeof(T) == 4;
+    static constexpr int UNROLL = ACC ? SILU_ACC_UNROLL : 0;
+    static constexpr int MIN_BLOCKS = ACC ? SILU_ACC_MIN_BLOCKS : 0;
     __device__ __forceinline__ float operator()(float x, float) const { return silu_f<ACC>(x); }
     __device__ __forceinline__ float2 pair(float2 x, float2) const { return silu_f2<ACC>(x); }
 };
@@ -175,12 +210,12 @@ struct FUnary {
 // bf16: 64 registers (4 CTAs of 256 threads per SM), measured 10% faster than
 // the unbounded allocation (70 registers, 3 CTAs) for silu * up.
 template <typename T, typename F, int NIN, bool AMOD, bool BMOD>
-__global__ void __launch_bounds__(EW_THREADS, ew_min_blocks<T>())
+__global__ void __launch_bounds__(EW_THREADS, (ew_min_blocks_f<T, F>()))
     ew_vec_kernel(const T* a, const T* b, T* out, uint64_t nvec, uint64_t nav, uint64_t nbv,
                   FastDiv adiv, FastDiv bdiv, bool wide, uint64_t tail_lo, uint64_t n, F f) {
     pdl_begin();
     constexpr int V = Vec<T>::N;
-    constexpr int EW_UNROLL = ew_unroll<T>();
+    constexpr int EW_UNROLL = ew_unroll_f<T, F>();
     const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
     for (uint64_t base = (uint64_t)blockIdx.x * EW_THREADS + threadIdx.x; base < nvec;
          base += stride * EW_UNROLL) {
@@ -260,7 +295,7 @@ static void launch_vec(const T* a, uint64_t na, const T* b, uint64_t nb, T* out,
     FastDiv adiv(AMOD && !wide ? (uint32_t)nav : 1u);
     FastDiv bdiv(BMOD && !wide ? (uint32_t)nbv : 1u);
     auto kern = ew_vec_kernel<T, F, NIN, AMOD, BMOD>;
-    constexpr uint64_t U = ew_unroll<T>();
+    constexpr uint64_t U = ew_unroll_f<T, F>();
     uint64_t items = (nvec + U - 1) / U;
     int grid = resident_grid(kern, items > 0 ? items : 1);
     launch_k(kern, grid, EW_THREADS, 0, st, a, b, out, nvec, nav, nbv, adiv, bdiv, wide, nvec * V, n,

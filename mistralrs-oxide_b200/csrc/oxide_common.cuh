@@ -216,20 +216,16 @@ struct FastDiv {
 
 // ---------------------------------------------------------------------------
 // e^x rounded to f32, for parity with a correctly rounded host expf (glibc's,
-// which the reference's f32::exp calls).  Method: the table-driven reduction
-// of P. T. P. Tang (ACM TOMS 15(2), 1989) with an N-entry table, in double
-// with fused multiply-adds: x = (kN + j) ln2 / N + r with k N + j =
-// round(x N / ln2), |r| <= ln2 / (2N); e^x = 2^k * 2^(j/N) * e^r, e^r from
-// its Taylor series to the degree D that keeps the truncation below 2^-43
-// (N = 1: D = 10; N = 4: D = 7; N = 8: D = 6), Horner in double; 2^(j/N) is
-// the nearest double (picked by selects, no memory access) and 2^k goes into
-// its exponent field; the product is rounded once to f32.  The result is
-// RN(e^x) except where e^x lies within ~2^-43 (relative) of a rounding
-// boundary between two floats.  |x| is clamped to 110 first, beyond the f32
-// overflow (88.73) and underflow (-103.98) points; NaN propagates.  Every
-// step is an IEEE double operation, so the host compilation of this function
-// gives the device's bits (tests/test_exp_rn.py compares it with glibc expf
-// over every float).
+// which the reference's f32::exp calls).
+//
+// exp_rn_f32 evaluates e^x in f32 float-float arithmetic and checks, with
+// Ziv's rounding test (A. Ziv, ACM TOMS 17(3), 1991), that the f32 nearest
+// to the approximation is the f32 nearest to e^x; on the rare inputs where
+// that cannot be decided (about 1 in 1000) it calls exp_rn_f32_dp, the same
+// reduction in double.  Every step of both is an IEEE f32 or f64 operation
+// written out explicitly (no contraction), so the host compilation of these
+// functions returns the device's bits (tests/test_exp_rn.py runs it over
+// every float).
 // ---------------------------------------------------------------------------
 __host__ __device__ __forceinline__ double exp_dfma(double a, double b, double c) {
 #ifdef __CUDA_ARCH__
@@ -256,6 +252,57 @@ __host__ __device__ __forceinline__ uint64_t exp_double_bits(double d) {
     return b;
 #endif
 }
+// f32 operations with one rounding each, the same on host and device.
+__host__ __device__ __forceinline__ float exp_ffma(float a, float b, float c) {
+#ifdef __CUDA_ARCH__
+    return __fmaf_rn(a, b, c);
+#else
+    return __builtin_fmaf(a, b, c);
+#endif
+}
+__host__ __device__ __forceinline__ float exp_fadd(float a, float b) {
+#ifdef __CUDA_ARCH__
+    return __fadd_rn(a, b);
+#else
+    volatile float s = a + b;  // volatile: never contracted with a product
+    return s;
+#endif
+}
+__host__ __device__ __forceinline__ float exp_fsub(float a, float b) {
+#ifdef __CUDA_ARCH__
+    return __fsub_rn(a, b);
+#else
+    volatile float s = a - b;
+    return s;
+#endif
+}
+__host__ __device__ __forceinline__ float exp_fmul(float a, float b) {
+#ifdef __CUDA_ARCH__
+    return __fmul_rn(a, b);
+#else
+    volatile float s = a * b;
+    return s;
+#endif
+}
+__host__ __device__ __forceinline__ int exp_f2i(float f) {
+#ifdef __CUDA_ARCH__
+    return __float_as_int(f);
+#else
+    int i;
+    __builtin_memcpy(&i, &f, 4);
+    return i;
+#endif
+}
+__host__ __device__ __forceinline__ float exp_i2f(int i) {
+#ifdef __CUDA_ARCH__
+    return __int_as_float(i);
+#else
+    float f;
+    __builtin_memcpy(&f, &i, 4);
+    return f;
+#endif
+}
+
 // 2^(j/N) for j in [0, N): the nearest doubles.
 template <int N>
 __host__ __device__ __forceinline__ double exp_table(int j) {
@@ -273,8 +320,20 @@ __host__ __device__ __forceinline__ double exp_table(int j) {
     const double lo = (j & 2) ? b : a, hi = (j & 2) ? d : c;
     return (j & 4) ? hi : lo;
 }
+
+// The double path: the table-driven reduction of P. T. P. Tang (ACM TOMS
+// 15(2), 1989) with an N-entry table, in double with fused multiply-adds:
+// x = (kN + j) ln2 / N + r with k N + j = round(x N / ln2), |r| <= ln2 / (2N);
+// e^x = 2^k * 2^(j/N) * e^r, e^r from its Taylor series to the degree D that
+// keeps the truncation below 2^-43 (N = 1: D = 10; N = 4: D = 7; N = 8:
+// D = 6), Horner in double; 2^(j/N) is the nearest double (picked by
+// selects, no memory access) and 2^k goes into its exponent field; the
+// product is rounded once to f32.  The result is RN(e^x) except where e^x
+// lies within ~2^-43 (relative) of a rounding boundary between two floats
+// (36 of the 2^32 inputs).  |x| is clamped to 110 first, beyond the f32
+// overflow (88.73) and underflow (-103.98) points; NaN propagates.
 template <int N = 4>
-__host__ __device__ __forceinline__ float exp_rn_f32(float x) {
+__host__ __device__ __forceinline__ float exp_rn_f32_dp(float x) {
     static_assert(N == 1 || N == 4 || N == 8, "table sizes 1, 4, 8");
     // N / ln 2 and ln 2 / N: the nearest doubles (N a power of two, so only
     // the exponent differs from 1 / ln 2 and ln 2)
@@ -325,6 +384,111 @@ __host__ __device__ __forceinline__ float exp_rn_f32(float x) {
     const int k = kj >> (N == 1 ? 0 : N == 4 ? 2 : 3);
     const uint64_t sbits = exp_double_bits(exp_table<N>(kj & (N - 1))) + ((uint64_t)(int64_t)k << 52);
     return (float)(p * exp_bits_double(sbits));
+}
+
+// 2^(j/64) = hi + lo for j in [0, 64): hi the nearest float, lo the float
+// nearest to the remainder (|lo| <= 2^-24, relative error of the pair
+// <= 2^-47).
+#define OXIDE_EXP2_64_TABLE                                                                                 \
+    {0x1p+0f, 0.0f}, {0x1.02c9a4p+0f, -0x1.887fap-28f}, {0x1.059b0ep+0f, -0x1.9d4f52p-25f},                  \
+        {0x1.087452p+0f, -0x1.e2990ep-26f}, {0x1.0b5586p+0f, 0x1.9f3122p-25f},                             \
+        {0x1.0e3ec4p+0f, -0x1.a585ccp-25f}, {0x1.11301ep+0f, -0x1.fdb496p-25f},                            \
+        {0x1.1429aap+0f, 0x1.d525bcp-25f}, {0x1.172b84p+0f, -0x1.c15742p-27f},                             \
+        {0x1.1a35bep+0f, 0x1.6df96ep-25f}, {0x1.1d4874p+0f, -0x1.d2e8cap-25f},                             \
+        {0x1.2063b8p+0f, 0x1.0c519ap-25f}, {0x1.2387a6p+0f, 0x1.ceac48p-25f},                              \
+        {0x1.26b456p+0f, 0x1.789f38p-26f}, {0x1.29e9e0p+0f, -0x1.5c0424p-25f},                             \
+        {0x1.2d285ap+0f, 0x1.b900c2p-26f}, {0x1.306fe0p+0f, 0x1.4636e2p-25f},                              \
+        {0x1.33c08cp+0f, -0x1.b37d2p-25f}, {0x1.371a74p+0f, -0x1.18aac6p-25f},                             \
+        {0x1.3a7db4p+0f, -0x1.634c02p-25f}, {0x1.3dea64p+0f, 0x1.824684p-25f},                             \
+        {0x1.4160a2p+0f, 0x1.f72e2ap-28f}, {0x1.44e086p+0f, 0x1.8624b4p-30f},                              \
+        {0x1.486a2cp+0f, -0x1.47d866p-25f}, {0x1.4bfdaep+0f, -0x1.593abcp-25f},                            \
+        {0x1.4f9b28p+0f, -0x1.2c5a6cp-25f}, {0x1.5342b6p+0f, -0x1.2c561p-25f},                             \
+        {0x1.56f474p+0f, -0x1.295b04p-25f}, {0x1.5ab07ep+0f, -0x1.5bd5ecp-27f},                            \
+        {0x1.5e76f2p+0f, -0x1.4a5bd6p-25f}, {0x1.6247ecp+0f, -0x1.f8b55p-25f},                             \
+        {0x1.662388p+0f, 0x1.2a9112p-27f}, {0x1.6a09e6p+0f, 0x1.9fcef4p-26f},                              \
+        {0x1.6dfb24p+0f, -0x1.cd72e8p-27f}, {0x1.71f75ep+0f, 0x1.1d8beep-25f},                             \
+        {0x1.75feb6p+0f, -0x1.37b306p-25f}, {0x1.7a1148p+0f, -0x1.829fdp-25f},                             \
+        {0x1.7e2f34p+0f, -0x1.261634p-25f}, {0x1.82589ap+0f, -0x1.accc7cp-26f},                            \
+        {0x1.868d9ap+0f, -0x1.2edb44p-26f}, {0x1.8ace54p+0f, 0x1.15506ep-27f},                             \
+        {0x1.8f1aeap+0f, -0x1.baa232p-26f}, {0x1.93737cp+0f, -0x1.e64744p-25f},                            \
+        {0x1.97d82ap+0f, -0x1.0d8d84p-31f}, {0x1.9c4918p+0f, 0x1.51f848p-27f},                             \
+        {0x1.a0c668p+0f, -0x1.2886a6p-26f}, {0x1.a5503cp+0f, -0x1.b83b54p-25f},                            \
+        {0x1.a9e6b6p+0f, -0x1.50c048p-25f}, {0x1.ae89fap+0f, -0x1.a94b14p-26f},                            \
+        {0x1.b33a2cp+0f, -0x1.ec3a82p-26f}, {0x1.b7f770p+0f, -0x1.a09438p-25f},                            \
+        {0x1.bcc1eap+0f, -0x1.f687c6p-25f}, {0x1.c199bep+0f, -0x1.3d56b2p-27f},                            \
+        {0x1.c67f12p+0f, 0x1.cafa2ap-25f}, {0x1.cb720ep+0f, -0x1.8837ccp-27f},                             \
+        {0x1.d072d4p+0f, 0x1.40f13p-25f}, {0x1.d5818ep+0f, -0x1.822dbcp-27f},                              \
+        {0x1.da9e60p+0f, 0x1.ed9942p-27f}, {0x1.dfc974p+0f, -0x1.908c94p-25f},                             \
+        {0x1.e502eep+0f, 0x1.e2cffep-26f}, {0x1.ea4afap+0f, 0x1.52486cp-27f},                              \
+        {0x1.efa1bep+0f, 0x1.cc2b44p-25f}, {0x1.f50766p+0f, -0x1.246ebp-26f}, {0x1.fa7c18p+0f, 0x1.9e90d8p-28f}
+#ifdef __CUDA_ARCH__
+static __device__ const float2 kExp2Tab64[64] = {OXIDE_EXP2_64_TABLE};
+#else
+static const float2 kExp2Tab64[64] = {OXIDE_EXP2_64_TABLE};
+#endif
+__host__ __device__ __forceinline__ float2 exp2_64(int j) {
+#ifdef __CUDA_ARCH__
+    return __ldg(&kExp2Tab64[j]);  // 512 bytes: stays in L1 beside the streaming loads
+#else
+    return kExp2Tab64[j];
+#endif
+}
+
+// The f32 path.  Reduction (Tang's, N = 64): K = round(x 64 / ln2) from one
+// fused multiply-add against 1.5 * 2^23; x = K Lh + rh with Lh = RN(ln2 / 64)
+// (20 significant bits) -- rh is exact: x - K Lh is a multiple of
+// min(ulp(x), 2^-27) below 2^-7 in magnitude, so it fits in 24 bits and the
+// fused step does not round -- and rl = -K Ll, Ll = RN(ln2 / 64 - Lh)
+// (~2^-35), so r = rh + rl is within 2^-53 of x - K ln2 / 64 for |K| <= 8192.
+// e^r = 1 + rh + E with E = rl + s^2 (1/2 + s/6 + s^2/24), s = RN(rh + rl)
+// (truncation < 2^-44 for |r| <= ln2 / 128), held as the unevaluated pair
+// ah + al (Fast2Sum of 1 and rh, plus E); times the table pair Thi + Tlo by
+// Dekker's product (Thi ah exactly as yh + ye by one fused multiply-add); the
+// sum normalised by Fast2Sum into zh + zl (|zl| <= ulp(zh) / 2, zh in
+// [0.99, 2)).  With |zh + zl - e^x 2^-k| < EPS, the nearest float to e^x is
+// zh * 2^k whenever |zl| is below half the gap to zh's neighbour on zl's
+// side by more than EPS; the scaling by 2^k is exact for results in the
+// normal range, x in (-86, 88).  Otherwise ok = false.  EPS = 2^-36: the
+// largest |zh + zl - e^x 2^-k| over every float in that range is 2^-37.1
+// (measured against the 64-bit-significand expl).
+constexpr float EXP_FF_EPS = 0x1p-36f;
+__host__ __device__ __forceinline__ float exp_rn_f32_ff(float x, bool& ok) {
+    const float t = exp_ffma(x, 0x1.715476p+6f, 0x1.8p23f);  // 1.5 * 2^23 + K
+    const float kf = exp_fsub(t, 0x1.8p23f);
+    const int K = exp_f2i(t) - 0x4B400000;
+    const float rh = exp_ffma(-kf, 0x1.62e43p-7f, x);
+    const float rl = exp_fmul(kf, 0x1.05c61p-35f);  // -K Ll (Ll < 0)
+    const float s = exp_fadd(rh, rl);
+    const float q = exp_ffma(exp_ffma(s, 0x1.555556p-5f, 0x1.555556p-3f), s, 0.5f);
+    const float e = exp_ffma(exp_fmul(s, s), q, rl);
+    const float ah = exp_fadd(1.0f, rh);
+    const float al = exp_fadd(exp_fsub(rh, exp_fsub(ah, 1.0f)), e);
+    const float2 tb = exp2_64(K & 63);
+    const float yh = exp_fmul(tb.x, ah);
+    const float ye = exp_ffma(tb.x, ah, -yh);
+    const float yl = exp_ffma(tb.x, al, exp_ffma(tb.y, ah, ye));
+    const float zh = exp_fadd(yh, yl);
+    const float zl = exp_fsub(yl, exp_fsub(zh, yh));
+    // half the gap to the neighbour on zl's side: 2^-25 below 1 (and below
+    // zh = 1), 2^-24 from 1 up to 2
+    const float half = (zh < 1.0f) | ((zh == 1.0f) & (zl < 0.0f)) ? 0x1p-25f : 0x1p-24f;
+    ok = (x > -86.0f) & (x < 88.0f) & (fabsf(zl) < half - EXP_FF_EPS);
+    return exp_i2f(exp_f2i(zh) + ((K >> 6) << 23));
+}
+
+// The fallback is a real call on the device, so that the double path runs
+// only in the warps where some lane needs it (an inlined conditional would
+// be evaluated for every element).
+#ifdef __CUDA_ARCH__
+__device__ __noinline__ float exp_rn_f32_fallback(float x) { return exp_rn_f32_dp<4>(x); }
+#else
+inline float exp_rn_f32_fallback(float x) { return exp_rn_f32_dp<4>(x); }
+#endif
+__host__ __device__ __forceinline__ float exp_rn_f32(float x) {
+    bool ok;
+    float y = exp_rn_f32_ff(x, ok);
+    if (!ok) y = exp_rn_f32_fallback(x);
+    return y;
 }
 
 // ---------------------------------------------------------------------------
@@ -411,9 +575,15 @@ struct OpMaxU64 {
 // visible (griddepcontrol.wait) before this kernel touches global memory.  A
 // kernel launched without the attribute returns from the wait at once.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void pdl_begin() {
+__device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_begin() {
+    pdl_trigger();
+    pdl_wait();
 }
 
 bool pdl_enabled();  // false when OXIDE_NO_PDL=1 is set (read once)

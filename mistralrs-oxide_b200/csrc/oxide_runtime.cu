@@ -162,7 +162,6 @@ __global__ void __launch_bounds__(256)
     selftest_rowdiv_kernel(const float* a, uint64_t na, const float* b, uint64_t nb,
                            unsigned long long* out) {
     pdl_begin();
-    pdl_begin();
     const uint64_t total = na * nb;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (uint64_t)gridDim.x * blockDim.x) {

@@ -70,6 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "oxide_kv_cache_append_bf16": (i32, [vp, vp, vp, vp, u64, u64, u64, u64, u64, u64, vp]),
     "oxide_decode_attention_workspace_bytes": (u64, [u64, u64, u64, u64]),
     "oxide_debug_decode_attention_path": (None, [i32]),
+    "oxide_device_status": (i32, [i32, C.POINTER(C.c_uint32)]),
     "oxide_decode_attention_f32": (i32, [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, vp, u64, vp]),
     "oxide_decode_attention_bf16": (i32, [vp, vp, vp, vp, vp, u64, u64, u64, u64, u64, f32, vp, u64, vp]),
     "oxide_sample_f32": (i32, [vp, u64, u64, f32, u64, f32, vp, vp, vp, vp]),
@@ -105,6 +106,7 @@ ADD, SUB, MUL, DIV = 0, 1, 2, 3
 RELU, GELU, GELU_QUICK, SIGMOID, TANH, EXP, LOG, SQRT, POW, CLAMP, NEG, ABS = range(12)
 RED_SUM, RED_MAX, RED_SUMSQ = 0, 1, 2
 SAMPLE_INVALID = 0xFFFFFFFF
+DEVICE_WAIT_TIMEOUT = 1  # OXIDE_DEVICE_WAIT_TIMEOUT
 WDT_F32, WDT_F16, WDT_BF16 = 0, 1, 2
 
 _lock = threading.Lock()

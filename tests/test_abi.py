@@ -73,6 +73,7 @@ FAKE = 0x1000  # never dereferenced: every case below fails validation first
     lambda l: l.oxide_argmax_rows_f32(FAKE, 4, 0, FAKE, None),
     lambda l: l.oxide_reduce_rows_f32(5, FAKE, 4, 4, FAKE, None),
     lambda l: l.oxide_rope_table_host_f32(1e4, 3, 4, FAKE, FAKE),
+    lambda l: l.oxide_device_status(0, None),
 ])
 def test_invalid_arguments(olib, call):
     assert call(olib.lib()) == olib.ERR_INVALID_ARG

@@ -118,3 +118,36 @@ def test_tc_decode_attention_c3_shape(cuda, orc):
     _check(tc, exact, mag, "tcgen05 kernel")
     split = _attend(q, kc, vc, lens, 1)
     assert np.mean(ulp_bf16(tc, split) <= 1) >= 0.999
+
+
+def test_tc_wait_timeout_is_reported_and_the_context_survives(cuda, orc):
+    """Failure detection without a fault: with the kernel's tile loads withheld
+    (path 2) no copy ever completes, so every bounded wait runs out (two
+    seconds); the launch ends by itself with NaN outputs and
+    OXIDE_DEVICE_WAIT_TIMEOUT raised, and the next call on the same context
+    computes the right values with no flag raised."""
+    import ctypes as C
+    import time
+
+    from oxide_b200 import _lib
+
+    flags = C.c_uint32(0)
+    _lib.call("oxide_device_status", 1, C.byref(flags))  # start clear
+    rng = np.random.default_rng(11)
+    b, hq, hkv, m, d = 2, 8, 2, 1024, 128
+    q = orc.f32_to_bf16(rng.standard_normal((b, hq, d), dtype=F)).reshape(b, hq, d)
+    kc = orc.f32_to_bf16(rng.standard_normal((b, hkv, m, d), dtype=F)).reshape(b, hkv, m, d)
+    vc = orc.f32_to_bf16(rng.standard_normal((b, hkv, m, d), dtype=F)).reshape(b, hkv, m, d)
+    lz = np.array([1024, 77], np.int32)
+    t0 = time.monotonic()
+    bad = _attend(q, kc, vc, lz, 2)
+    waited = time.monotonic() - t0
+    _lib.call("oxide_device_status", 1, C.byref(flags))
+    assert flags.value & _lib.DEVICE_WAIT_TIMEOUT, "the run-out wait was not reported"
+    assert np.isnan(bf16_to_f32(bad)).all(), "an aborted launch must not leave values that look valid"
+    assert 1.5 < waited < 60, f"the launch took {waited:.1f} s"
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(d)))
+    exact, mag = _exact(bf16_to_f32(q), bf16_to_f32(kc), bf16_to_f32(vc), lz, scale)
+    _check(_attend(q, kc, vc, lz, 0), exact, mag, "the call after the timeout")
+    _lib.call("oxide_device_status", 0, C.byref(flags))
+    assert flags.value == 0

@@ -228,3 +228,35 @@ def test_pipe_new_forms_reject_bad_arguments(pipe, olib):
     assert lib.oxide_pipe_rope_bf16(pipe, p, p, 1, None, None, 0, p, p, 2, None, 4, 8) == olib.ERR_INVALID_ARG
     assert lib.oxide_pipe_add_mul_rowbcast_f32(pipe, p, None, p, p, p, 1, 16) == olib.ERR_INVALID_ARG
     assert lib.oxide_pipe_sync(None) == olib.ERR_INVALID_ARG
+
+
+def test_pipe_class_equals_device_ops(cuda, orc):
+    """oxide_b200.pipe.Pipe: every method bit-identical to the device-tensor op
+    of oxide_b200.ops on the same inputs, in immediate and deferred mode."""
+    from oxide_b200 import ops
+    from oxide_b200.pipe import Pipe
+
+    rng = np.random.default_rng(21)
+    rows, cols = 300, 1024
+    a, b, g, u = (rng.standard_normal((rows, cols), dtype=F) for _ in range(4))
+    s = rng.uniform(0.5, 1.5, cols).astype(F)
+    d = lambda x: torch.from_numpy(x).cuda()  # noqa: E731
+    h = lambda t: t.cpu().numpy()  # noqa: E731
+    with Pipe(0, chunk_bytes=1 << 18, depth=3) as p:
+        hh, yy = p.add_mul_rowbcast(a, b, s)
+        assert_bits_equal(hh, h(ops.add(d(a), d(b))))
+        assert_bits_equal(yy, h(ops.mul_rowbcast(d(hh), d(s))))
+        with p.deferred():
+            sm = p.silu_mul(g, u)
+            rn = p.rms_norm(a, s, 1e-5)
+            hx, yx = p.add_rms_norm(a, b, s, 1e-5)
+            am = p.argmax_rows(g)
+            sx = p.scale_mask_softmax(a, 0.125, lens=rng.integers(0, cols + 1, rows // 4).astype(np.int32),
+                                      rows_per_len=4)
+        assert_bits_equal(sm, h(ops.silu_mul(d(g), d(u))))
+        assert_bits_equal(rn, h(ops.rms_norm(d(a), d(s), 1e-5)))
+        hd, yd = ops.add_rms_norm(d(a), d(b), d(s), 1e-5)
+        assert_bits_equal(hx, h(hd))
+        assert_bits_equal(yx, h(yd))
+        assert np.array_equal(am, orc.argmax_rows(g, cols))
+        assert np.all(np.isfinite(sx)) and np.allclose(sx.sum(axis=1)[sx.sum(axis=1) > 0], 1, atol=1e-5)
