@@ -484,7 +484,7 @@ def per_op_lines(peak, rank, world, local, pipe):
     import torch
 
     from oxide_b200 import ops
-    from oxide_b200._lib import call
+    from oxide_b200._lib import RELU, call
     from oxide_b200.dist import row_range
     from oxide_b200.workloads import C1, C3, C4, NKV
 
@@ -494,7 +494,18 @@ def per_op_lines(peak, rank, world, local, pipe):
     def stream():
         return torch.cuda.current_stream().cuda_stream
 
-    def rec(name, nbytes_rank, secs, shape, elems_rank, e2e_secs=None, h2d=0, d2h=0):
+    def size_matched(nbytes_rank):
+        """This library's one-read-one-write kernel (f32 relu) over the same
+        byte count, timed the same way: what launch, ramp and tail leave of
+        the copy peak at this size."""
+        n = max(4, nbytes_rank // 8 // 4 * 4)
+        nset = rotating_sets(8 * n)
+        ins = [torch.empty(n, device=dev) for _ in range(nset)]
+        outs = [torch.empty(n, device=dev) for _ in range(nset)]
+        fns = [(lambda i=i: ops.unary(RELU, ins[i], out=outs[i])) for i in range(nset)]
+        return graph_time_per_launch(fns)
+
+    def rec(name, nbytes_rank, secs, shape, elems_rank, e2e_secs=None, h2d=0, d2h=0, ceil_secs=None):
         secs_max = reduce_over_ranks(secs, world)
         total = reduce_over_ranks(float(nbytes_rank), world, "sum")
         elems = reduce_over_ranks(float(elems_rank), world, "sum")
@@ -502,6 +513,10 @@ def per_op_lines(peak, rank, world, local, pipe):
         r = {"gbs": round(gbs, 1), "frac_of_peak": round(gbs / (world * peak), 4),
              "us_per_launch": round(secs_max * 1e6, 2),
              "elems_per_s": round(elems / secs_max, 1), "bytes": int(total), "shape": shape}
+        if ceil_secs is not None:
+            c_max = reduce_over_ranks(ceil_secs, world)
+            r["size_matched"] = {"us_per_launch": round(c_max * 1e6, 2), "frac": round(c_max / secs_max, 4),
+                                 "kernel": "oxide_relu_f32 over the same bytes"}
         if e2e_secs is not None:
             e_max = reduce_over_ranks(e2e_secs, world)
             r["e2e"] = {"gbs": round(total / e_max / 1e9, 2), "ms": round(e_max * 1e3, 3),
@@ -526,7 +541,8 @@ def per_op_lines(peak, rank, world, local, pipe):
     px, pw, po = pinned(xr), pinned(w), pinned(np.zeros_like(xr))
     e2e = host_seconds(lambda: pipe("oxide_pipe_rms_norm_f32", px.data_ptr(), pw.data_ptr(), po.data_ptr(),
                                     hi - lo, c1.cols, c1.eps))
-    rec("rms_norm_f32[C1]", nb, secs, "[2048,4096]", xr.size, e2e, xr.size * 4 + w.size * 4, xr.size * 4)
+    rec("rms_norm_f32[C1]", nb, secs, "[2048,4096]", xr.size, e2e, xr.size * 4 + w.size * 4, xr.size * 4,
+        ceil_secs=size_matched(nb))
     del xs, outs
 
     # C3 masked decode softmax f32 (rows = batch x heads; a rank takes whole
@@ -556,7 +572,8 @@ def per_op_lines(peak, rank, world, local, pipe):
     e2e = host_seconds(lambda: pipe("oxide_pipe_scale_mask_softmax_f32", ps.data_ptr(), pso.data_ptr(), hi - lo,
                                     c3.keys, c3.scale, None, 0, pl.data_ptr(), rpl, 0))
     h2d = valid * 4 + lr.size * 4
-    rec("scale_mask_softmax_f32[C3]", nb, secs, "[8,32,1,32768] lens-masked", sr.size, e2e, h2d, sr.size * 4)
+    rec("scale_mask_softmax_f32[C3]", nb, secs, "[8,32,1,32768] lens-masked", sr.size, e2e, h2d, sr.size * 4,
+        ceil_secs=size_matched(nb))
     del ss, po3
 
     lo, hi = row_range(c3.logit_rows, rank, world)
@@ -571,7 +588,8 @@ def per_op_lines(peak, rank, world, local, pipe):
     plg, pidx = pinned(lg), pinned(np.zeros(hi - lo, np.int32))
     e2e = host_seconds(lambda: pipe("oxide_pipe_argmax_rows_f32", plg.data_ptr(), hi - lo, c3.vocab,
                                     pidx.data_ptr()), reps=10)
-    rec("argmax_f32[C3]", nb, secs, "[64,32000]", lg.size, e2e, lg.size * 4, (hi - lo) * 4)
+    rec("argmax_f32[C3]", nb, secs, "[64,32000]", lg.size, e2e, lg.size * 4, (hi - lo) * 4,
+        ceil_secs=size_matched(nb))
     del ls
 
     # C4 RoPE bf16 over this rank's tokens (positions = global token index)
@@ -597,7 +615,8 @@ def per_op_lines(peak, rank, world, local, pipe):
                                     pk.data_ptr(), pko.data_ptr(), c4.k_heads, pc.data_ptr(), psn.data_ptr(),
                                     c4.tokens, ppos.data_ptr(), hi - lo, c4.head_dim))
     rec("rope_bf16[C4]", nb, secs, "q[4096,32,128] k[4096,8,128]", qr.size + kr.size, e2e,
-        (qr.size + kr.size) * 2 + 2 * cos.numel() * 4 + (hi - lo) * 4, (qr.size + kr.size) * 2)
+        (qr.size + kr.size) * 2 + 2 * cos.numel() * 4 + (hi - lo) * 4, (qr.size + kr.size) * 2,
+        ceil_secs=size_matched(nb))
     del qs, ks, qo, ko
 
     # C3 decode step of attention over bf16 KV caches (q [8,32,128], caches
@@ -908,7 +927,8 @@ def run_oxide(args):
         "per_kernel_gbs": {"add": round(C2(rows=rows).bytes_add() / t_add / 1e9, 1),
                            "mul_rowbcast": round(C2(rows=rows).bytes_mul() / t_mul / 1e9, 1),
                            "silu_mul": round(achieved, 1)},
-        "roofline": {"bound": "hbm", "kernel": "ew_vec_kernel<silu_mul f32>",
+        "roofline": {"bound": "hbm", "kernel": "ew_staged_f32_kernel<silu_mul f32>",
+                     "limiter": "instruction issue of the correctly rounded exp (profiles/silu_mul_f32_c2.md)",
                      "achieved": round(achieved, 1), "peak": peak,
                      "peak_kind": f"{peak_kind} HBM copy GB/s", "unit": "GB/s",
                      "frac": round(achieved / peak, 4),

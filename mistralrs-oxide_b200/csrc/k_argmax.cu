@@ -174,6 +174,8 @@ static int argmax_entry(const char* name, const T* x, uint64_t rows, uint64_t co
     const uint64_t units = vec ? cols / V : cols;
     // Split a row over a cluster of up to 8 CTAs while all CTAs still fit one
     // wave and each keeps at least 4 units per thread (one round of loads).
+    // (One 1024-thread CTA per row instead, with no cluster barrier: 5.95 us
+    // against 5.4 us at [64 x 32000] f32.)
     int cl = 1;
     const uint64_t slots = (uint64_t)resident_blocks(
         vec ? reinterpret_cast<const void*>(argmax_kernel<T, true>)
@@ -185,13 +187,16 @@ static int argmax_entry(const char* name, const T* x, uint64_t rows, uint64_t co
     cfg.gridDim = dim3((unsigned)(groups * cl), 1, 1);
     cfg.blockDim = dim3(256, 1, 1);
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = cl;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = add_pdl_attr(attr, 1);
+    // No programmatic-dependent-launch attribute on this cluster launch:
+    // measured at [64 x 32000] f32, 5.13 us per launch without it against
+    // 5.43 us with it (the kernel's griddepcontrol instructions are then no-ops).
+    cfg.numAttrs = 1;
     const uint32_t c32 = (uint32_t)cols;
     cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, argmax_kernel<T, true>, x, rows, c32, idx, cl)
                         : cudaLaunchKernelEx(&cfg, argmax_kernel<T, false>, x, rows, c32, idx, cl);

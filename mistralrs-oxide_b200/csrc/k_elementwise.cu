@@ -32,38 +32,6 @@ template <typename T>
 constexpr int ew_min_blocks() {
     return sizeof(T) == 4 ? 2 : 4;
 }
-// A functor may set its own UNROLL / MIN_BLOCKS (e.g. the f32 SiLU with the
-// double-precision exponential, whose arithmetic per byte needs more warps
-// per SM to hide memory latency than the plain ops).
-template <typename F, typename = void>
-struct FunUnroll {
-    static constexpr int value = 0;
-};
-template <typename F>
-struct FunUnroll<F, std::void_t<decltype(F::UNROLL)>> {
-    static constexpr int value = F::UNROLL;
-};
-template <typename F, typename = void>
-struct FunMinBlocks {
-    static constexpr int value = 0;
-};
-template <typename F>
-struct FunMinBlocks<F, std::void_t<decltype(F::MIN_BLOCKS)>> {
-    static constexpr int value = F::MIN_BLOCKS;
-};
-template <typename T, typename F>
-constexpr int ew_unroll_f() {
-    return FunUnroll<F>::value ? FunUnroll<F>::value : ew_unroll<T>();
-}
-template <typename T, typename F>
-constexpr int ew_min_blocks_f() {
-    return FunMinBlocks<F>::value ? FunMinBlocks<F>::value : ew_min_blocks<T>();
-}
-// f32 SiLU with the correctly rounded exponential: vectors in flight per
-// thread and operand, and CTAs per SM.
-constexpr int SILU_ACC_UNROLL = 4;
-constexpr int SILU_ACC_MIN_BLOCKS = 3;
-
 // ---- per-element functors (f32 math, IEEE rounding per reference step) ----
 // operator() is one element; pair() is two elements on Blackwell's paired
 // f32 pipe (__fmul2_rn / __fadd2_rn: the same IEEE round-to-nearest per lane,
@@ -101,6 +69,18 @@ __device__ __forceinline__ float silu_f(float x) {
     float r = __frcp_rn(fadd(1.0f, e));
     return fmul(x, r);
 }
+// The f32 path in two parts: silu_fast2 decides most inputs, two at a time,
+// with the f32 exponential (ok = false where its rounding test cannot),
+// silu_exact takes the rest through the double exponential.  Results are
+// silu_f<true>'s bits.
+__device__ __forceinline__ float2 silu_fast2(float2 x, bool& ok0, bool& ok1) {
+    const float2 e = exp_rn_f32x2_ff(f2(-x.x, -x.y), ok0, ok1);
+    const float2 d = fadd2(f2(1.0f, 1.0f), e);
+    return fmul2(x, f2(__frcp_rn(d.x), __frcp_rn(d.y)));
+}
+__device__ __forceinline__ float silu_exact(float x) {
+    return fmul(x, __frcp_rn(fadd(1.0f, exp_rn_f32_fallback(-x))));
+}
 template <bool ACCURATE = true>
 __device__ __forceinline__ float2 silu_f2(float2 x) {
     const float2 d = fadd2(f2(1.0f, 1.0f), f2(silu_exp<ACCURATE>(-x.x), silu_exp<ACCURATE>(-x.y)));
@@ -124,11 +104,14 @@ struct FSiluMul {  // mul(silu(g), u); silu(g) rounded to T as the pair stores i
     // double rounding the single one avoids): within 1 bf16 ulp there.
     static constexpr bool PACKED = sizeof(T) == 2;
     static constexpr bool ACC = sizeof(T) == 4;
-    static constexpr int UNROLL = ACC ? SILU_ACC_UNROLL : 0;
-    static constexpr int MIN_BLOCKS = ACC ? SILU_ACC_MIN_BLOCKS : 0;
+    static constexpr bool FIXUP = ACC;
     __device__ __forceinline__ float operator()(float g, float u) const {
         return fmul(Vec<T>::rnd(silu_f<ACC>(g)), u);
     }
+    __device__ __forceinline__ float2 fast2(float2 g, float2 u, bool& ok0, bool& ok1) const {
+        return fmul2(silu_fast2(g, ok0, ok1), u);
+    }
+    __device__ __forceinline__ float exact(float g, float u) const { return fmul(silu_exact(g), u); }
     __device__ __forceinline__ float2 pair(float2 g, float2 u) const {
         const float2 s = silu_f2<ACC>(g);
         return fmul2(f2(Vec<T>::rnd(s.x), Vec<T>::rnd(s.y)), u);
@@ -139,7 +122,9 @@ struct FSiluMul {  // mul(silu(g), u); silu(g) rounded to T as the pair stores i
     }
 };
 
-// Functors with a packed bf16 form declare PACKED = true.
+// Functors with a packed bf16 form declare PACKED = true; functors with a
+// fast form that may leave elements undecided declare FIXUP = true (fast2()
+// for two elements with their ok flags, exact() for the undecided ones).
 template <typename F, typename = void>
 struct HasPacked {
     static constexpr bool value = false;
@@ -148,14 +133,25 @@ template <typename F>
 struct HasPacked<F, std::void_t<decltype(F::PACKED)>> {
     static constexpr bool value = F::PACKED;
 };
+template <typename F, typename = void>
+struct HasFixup {
+    static constexpr bool value = false;
+};
+template <typename F>
+struct HasFixup<F, std::void_t<decltype(F::FIXUP)>> {
+    static constexpr bool value = F::FIXUP;
+};
 
 template <typename T>
 struct FSilu {
     static constexpr bool ACC = sizeof(T) == 4;
-    static constexpr int UNROLL = ACC ? SILU_ACC_UNROLL : 0;
-    static constexpr int MIN_BLOCKS = ACC ? SILU_ACC_MIN_BLOCKS : 0;
+    static constexpr bool FIXUP = ACC;
     __device__ __forceinline__ float operator()(float x, float) const { return silu_f<ACC>(x); }
     __device__ __forceinline__ float2 pair(float2 x, float2) const { return silu_f2<ACC>(x); }
+    __device__ __forceinline__ float2 fast2(float2 x, float2, bool& ok0, bool& ok1) const {
+        return silu_fast2(x, ok0, ok1);
+    }
+    __device__ __forceinline__ float exact(float x, float) const { return silu_exact(x); }
 };
 
 struct FScale {
@@ -210,12 +206,12 @@ struct FUnary {
 // bf16: 64 registers (4 CTAs of 256 threads per SM), measured 10% faster than
 // the unbounded allocation (70 registers, 3 CTAs) for silu * up.
 template <typename T, typename F, int NIN, bool AMOD, bool BMOD>
-__global__ void __launch_bounds__(EW_THREADS, (ew_min_blocks_f<T, F>()))
+__global__ void __launch_bounds__(EW_THREADS, (ew_min_blocks<T>()))
     ew_vec_kernel(const T* a, const T* b, T* out, uint64_t nvec, uint64_t nav, uint64_t nbv,
                   FastDiv adiv, FastDiv bdiv, bool wide, uint64_t tail_lo, uint64_t n, F f) {
     pdl_begin();
     constexpr int V = Vec<T>::N;
-    constexpr int EW_UNROLL = ew_unroll_f<T, F>();
+    constexpr int EW_UNROLL = ew_unroll<T>();
     const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
     for (uint64_t base = (uint64_t)blockIdx.x * EW_THREADS + threadIdx.x; base < nvec;
          base += stride * EW_UNROLL) {
@@ -263,6 +259,90 @@ __global__ void __launch_bounds__(EW_THREADS, (ew_min_blocks_f<T, F>()))
     }
 }
 
+// ---- staged kernel for functors with undecided elements (the f32 SiLU) --------
+// The correctly rounded f32 SiLU needs more arithmetic per byte than the
+// other ops, so more warps per SM to hide it, while the stream still needs
+// as many bytes in flight.  Here the bytes in flight live in shared memory:
+// each thread copies its own vectors (cp.async, 16 bytes each) into a
+// per-thread ring of STG_STAGES groups of STG_UNROLL vectors per operand,
+// and computes group j while groups j+1.. are in flight; registers hold only
+// the arithmetic.  No thread reads another's slots, so there is no block
+// barrier.  Every element goes through the fast form and is stored; the
+// undecided ones (about 1 in 10^4) are then recomputed one by one from the
+// staged copy (the output may be an input) and stored again.
+// Measured on silu * up f32 [8192 x 14336]: 2 stages of 2 vectors under a
+// 6-CTA bound 237 us; 2 x 2 under 5 CTAs 239, 4 x 1 under 6 CTAs 241, 3 x 2
+// under 4 CTAs 250, 3 x 1 under 6 CTAs 256.  (The same arithmetic from
+// registers, 4 vectors per thread under a 4-CTA bound: 237 us; CUDA's expf,
+// not correctly rounded, 208 us.)  The kernel is issue-bound: 53 instructions
+// per element, 75 % issue-active, ALU pipe 56 %, FMA pipe 50 %.
+constexpr int STG_STAGES = 2;
+constexpr int STG_UNROLL = 2;
+constexpr int STG_MIN_BLOCKS = 6;
+
+template <typename F, int NIN>
+__global__ void __launch_bounds__(EW_THREADS, STG_MIN_BLOCKS)
+    ew_staged_f32_kernel(const float* a, const float* b, float* out, uint64_t nvec, uint64_t n, F f) {
+    pdl_begin();
+    constexpr int V = 4, S = STG_STAGES, U = STG_UNROLL;
+    __shared__ __align__(16) float4 sa[S][U][EW_THREADS];
+    __shared__ __align__(16) float4 sb[NIN == 2 ? S : 1][U][EW_THREADS];
+    const int tid = threadIdx.x;
+    const uint64_t stride = (uint64_t)gridDim.x * EW_THREADS;
+    const uint64_t first = (uint64_t)blockIdx.x * EW_THREADS + tid;
+    // group j: vectors first + (j U + k) stride, k < U
+    auto issue = [&](uint64_t j, int stage) {
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint64_t i = first + (j * U + k) * stride;
+            if (i < nvec) {
+                cp_async16(&sa[stage][k][tid], a + i * V);
+                if (NIN == 2) cp_async16(&sb[stage][k][tid], b + i * V);
+            }
+        }
+        cp_async_commit();  // one group per call, empty or not, so the wait counts stay uniform
+    };
+#pragma unroll
+    for (int st = 0; st < S - 1; ++st) issue((uint64_t)st, st);
+    for (uint64_t j = 0; first + j * U * stride < nvec; ++j) {
+        const int stage = (int)(j % S);
+        issue(j + S - 1, (int)((j + S - 1) % S));
+        cp_async_wait<S - 1>();  // this thread's group j has landed
+        uint32_t bad = 0;
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint64_t i = first + (j * U + k) * stride;
+            const float4 x = sa[stage][k][tid];
+            const float4 y = NIN == 2 ? sb[stage][k][tid] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            bool o0, o1, o2, o3;
+            const float2 r0 = f.fast2(f2(x.x, x.y), f2(y.x, y.y), o0, o1);
+            const float2 r1 = f.fast2(f2(x.z, x.w), f2(y.z, y.w), o2, o3);
+            bad |= ((o0 ? 0u : 1u) | (o1 ? 0u : 2u) | (o2 ? 0u : 4u) | (o3 ? 0u : 8u)) << (k * V);
+            if (i < nvec)
+                st_stream(out + i * V, make_uint4(__float_as_uint(r0.x), __float_as_uint(r0.y), __float_as_uint(r1.x),
+                                                  __float_as_uint(r1.y)));
+        }
+        while (bad) {
+            const int bit = __ffs(bad) - 1;
+            bad &= bad - 1u;
+            const int k = bit / V, e = bit % V;
+            const uint64_t i = first + (j * U + k) * stride;
+            const float x = reinterpret_cast<const float*>(&sa[stage][k][tid])[e];
+            const float y = NIN == 2 ? reinterpret_cast<const float*>(&sb[stage][k][tid])[e] : 0.0f;
+            if (i < nvec) out[i * V + e] = f.exact(x, y);
+        }
+    }
+    cp_async_wait<0>();  // nothing in flight into shared memory at exit
+    // Scalar tail: elements [nvec V, n).
+    if (blockIdx.x == 0) {
+        for (uint64_t i = nvec * V + tid; i < n; i += EW_THREADS) {
+            const float x = a[i];
+            const float y = NIN == 2 ? b[i] : 0.0f;
+            out[i] = f(x, y);
+        }
+    }
+}
+
 // ---- scalar kernel (any alignment, any lengths) ------------------------------
 template <typename T, typename F, int NIN>
 __global__ void __launch_bounds__(EW_THREADS)
@@ -295,7 +375,7 @@ static void launch_vec(const T* a, uint64_t na, const T* b, uint64_t nb, T* out,
     FastDiv adiv(AMOD && !wide ? (uint32_t)nav : 1u);
     FastDiv bdiv(BMOD && !wide ? (uint32_t)nbv : 1u);
     auto kern = ew_vec_kernel<T, F, NIN, AMOD, BMOD>;
-    constexpr uint64_t U = ew_unroll_f<T, F>();
+    constexpr uint64_t U = ew_unroll<T>();
     uint64_t items = (nvec + U - 1) / U;
     int grid = resident_grid(kern, items > 0 ? items : 1);
     launch_k(kern, grid, EW_THREADS, 0, st, a, b, out, nvec, nav, nbv, adiv, bdiv, wide, nvec * V, n,
@@ -312,6 +392,16 @@ static int ew_dispatch(const char* name, const T* a, uint64_t na, const T* b, ui
     const bool amod = na != n, bmod = NIN == 2 && nb != n;
     bool vec = aligned16(a) && aligned16(out) && (NIN == 1 || aligned16(b));
     if (amod || bmod) vec = vec && n % V == 0 && na % V == 0 && (NIN == 1 || nb % V == 0);
+    if constexpr (HasFixup<F>::value && sizeof(T) == 4) {
+        if (vec && !amod && !bmod) {
+            auto kern = ew_staged_f32_kernel<F, NIN>;
+            const uint64_t nvec = n / 4;
+            int grid = resident_grid(kern, (nvec + STG_UNROLL - 1) / STG_UNROLL);
+            launch_k(kern, grid, EW_THREADS, 0, st, reinterpret_cast<const float*>(a),
+                     reinterpret_cast<const float*>(b), reinterpret_cast<float*>(out), nvec, n, f);
+            return check_launch(name);
+        }
+    }
     if (vec) {
         if (!amod && !bmod) launch_vec<T, F, NIN, false, false>(a, na, b, nb, out, n, f, st);
         else if (!amod && bmod) launch_vec<T, F, NIN, false, true>(a, na, b, nb, out, n, f, st);

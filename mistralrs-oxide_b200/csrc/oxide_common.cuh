@@ -434,46 +434,83 @@ __host__ __device__ __forceinline__ float2 exp2_64(int j) {
 #endif
 }
 
-// The f32 path.  Reduction (Tang's, N = 64): K = round(x 64 / ln2) from one
-// fused multiply-add against 1.5 * 2^23; x = K Lh + rh with Lh = RN(ln2 / 64)
-// (20 significant bits) -- rh is exact: x - K Lh is a multiple of
-// min(ulp(x), 2^-27) below 2^-7 in magnitude, so it fits in 24 bits and the
-// fused step does not round -- and rl = -K Ll, Ll = RN(ln2 / 64 - Lh)
-// (~2^-35), so r = rh + rl is within 2^-53 of x - K ln2 / 64 for |K| <= 8192.
-// e^r = 1 + rh + E with E = rl + s^2 (1/2 + s/6 + s^2/24), s = RN(rh + rl)
-// (truncation < 2^-44 for |r| <= ln2 / 128), held as the unevaluated pair
-// ah + al (Fast2Sum of 1 and rh, plus E); times the table pair Thi + Tlo by
-// Dekker's product (Thi ah exactly as yh + ye by one fused multiply-add); the
-// sum normalised by Fast2Sum into zh + zl (|zl| <= ulp(zh) / 2, zh in
-// [0.99, 2)).  With |zh + zl - e^x 2^-k| < EPS, the nearest float to e^x is
-// zh * 2^k whenever |zl| is below half the gap to zh's neighbour on zl's
-// side by more than EPS; the scaling by 2^k is exact for results in the
-// normal range, x in (-86, 88).  Otherwise ok = false.  EPS = 2^-36: the
-// largest |zh + zl - e^x 2^-k| over every float in that range is 2^-37.1
-// (measured against the 64-bit-significand expl).
+// f32x2 operations (Blackwell's paired f32 pipe: each lane one IEEE
+// round-to-nearest operation), the same on host and device.  No paired
+// product below feeds a paired add: the compiler may fuse such a pair into
+// one rounding.
+__host__ __device__ __forceinline__ float2 exp_ffma2(float2 a, float2 b, float2 c) {
+#ifdef __CUDA_ARCH__
+    return __ffma2_rn(a, b, c);
+#else
+    return make_float2(exp_ffma(a.x, b.x, c.x), exp_ffma(a.y, b.y, c.y));
+#endif
+}
+__host__ __device__ __forceinline__ float2 exp_fadd2(float2 a, float2 b) {
+#ifdef __CUDA_ARCH__
+    return __fadd2_rn(a, b);
+#else
+    return make_float2(exp_fadd(a.x, b.x), exp_fadd(a.y, b.y));
+#endif
+}
+__host__ __device__ __forceinline__ float2 exp_fmul2(float2 a, float2 b) {
+#ifdef __CUDA_ARCH__
+    return __fmul2_rn(a, b);
+#else
+    return make_float2(exp_fmul(a.x, b.x), exp_fmul(a.y, b.y));
+#endif
+}
+__host__ __device__ __forceinline__ float2 exp_c2(float c) { return make_float2(c, c); }
+
+// The f32 path, two inputs at a time.  Reduction (Tang's, N = 64):
+// K = round(x 64 / ln2) from one fused multiply-add against 1.5 * 2^23;
+// x = K Lh + rh with Lh = RN(ln2 / 64) (20 significant bits) -- rh is exact:
+// x - K Lh is a multiple of min(ulp(x), 2^-27) below 2^-7 in magnitude, so it
+// fits in 24 bits and the fused step does not round -- and r = rh + rl,
+// rl = -K Ll with Ll = RN(ln2 / 64 - Lh) (~2^-35): within 2^-53 of
+// x - K ln2 / 64 for |K| <= 8192.  e^r = 1 + rh + E with
+// E = rl + s^2 (1/2 + s/6 + s^2/24), s = RN(rh + rl) (truncation < 2^-44 for
+// |r| <= ln2 / 128), held as the unevaluated pair ah + al (Fast2Sum of 1 and
+// rh, plus E).  With 2^(j/64) = Th + Tl from the table, e^x 2^-k =
+// Th ah + yl + d, yl = RN(Th al + RN(Tl ah)); the largest |d| over every
+// float x of the fast range is 2^-37.1 (measured against the
+// 64-bit-significand expl), and EPS = 2^-36.  Ziv's test (A. Ziv, ACM TOMS
+// 17(3), 1991): the nearest floats to Th ah + (yl + EPS) and to
+// Th ah + (yl - EPS) -- each one fused multiply-add, the product exact --
+// agree, so (rounding being monotonic) so does every value in between, e^x 2^-k
+// among them; yl +- EPS is rounded first (|yl| < 2^-14.9: by at most 2^-39),
+// which leaves a margin of 1.9.  The scaling by 2^k goes into the exponent
+// field, exact for K in [-8000, 8063] (results in [2^-126, 2^126): x in
+// about [-86.6, 87.3]).  Where the test fails or K is outside, ok = false.
 constexpr float EXP_FF_EPS = 0x1p-36f;
+__host__ __device__ __forceinline__ float2 exp_rn_f32x2_ff(float2 x, bool& ok0, bool& ok1) {
+    const float2 t = exp_ffma2(x, exp_c2(0x1.715476p+6f), exp_c2(0x1.8p23f));  // 1.5 * 2^23 + K
+    const float2 kf = exp_fadd2(t, exp_c2(-0x1.8p23f));
+    // K = bits(t) - 0x4B400000; that constant's low 15 bits are zero, so
+    // K mod 64 = bits(t) mod 64 and (K >> 6) << 23 = (bits(t) >> 6) << 23
+    // modulo 2^32, and the range test is one unsigned comparison.
+    const uint32_t b0 = (uint32_t)exp_f2i(t.x), b1 = (uint32_t)exp_f2i(t.y);
+    const float2 rh = exp_ffma2(kf, exp_c2(-0x1.62e43p-7f), x);
+    const float2 rl = exp_fmul2(kf, exp_c2(0x1.05c61p-35f));  // -K Ll (Ll < 0)
+    const float2 s = exp_ffma2(kf, exp_c2(0x1.05c61p-35f), rh);
+    const float2 q = exp_ffma2(exp_ffma2(s, exp_c2(0x1.555556p-5f), exp_c2(0x1.555556p-3f)), s, exp_c2(0.5f));
+    const float2 e = exp_ffma2(exp_fmul2(s, s), q, rl);
+    const float2 ah = exp_fadd2(exp_c2(1.0f), rh);
+    const float2 al = exp_fadd2(exp_fadd2(rh, exp_ffma2(ah, exp_c2(-1.0f), exp_c2(1.0f))), e);  // rh - (ah - 1) exactly
+    const float2 t0 = exp2_64((int)(b0 & 63u)), t1 = exp2_64((int)(b1 & 63u));
+    const float2 th = make_float2(t0.x, t1.x), tl = make_float2(t0.y, t1.y);
+    const float2 yl = exp_ffma2(th, al, exp_fmul2(tl, ah));
+    const float2 zh = exp_ffma2(th, ah, exp_fadd2(yl, exp_c2(EXP_FF_EPS)));
+    const float2 zl = exp_ffma2(th, ah, exp_fadd2(yl, exp_c2(-EXP_FF_EPS)));
+    ok0 = (b0 - (0x4B400000u - 8000u) < 16064u) & (zh.x == zl.x);  // K in [-8000, 8063]
+    ok1 = (b1 - (0x4B400000u - 8000u) < 16064u) & (zh.y == zl.y);
+    return make_float2(exp_i2f((int)((uint32_t)exp_f2i(zh.x) + ((b0 >> 6) << 23))),
+                       exp_i2f((int)((uint32_t)exp_f2i(zh.y) + ((b1 >> 6) << 23))));
+}
+// One input through the same steps (the first lane of the pair).
 __host__ __device__ __forceinline__ float exp_rn_f32_ff(float x, bool& ok) {
-    const float t = exp_ffma(x, 0x1.715476p+6f, 0x1.8p23f);  // 1.5 * 2^23 + K
-    const float kf = exp_fsub(t, 0x1.8p23f);
-    const int K = exp_f2i(t) - 0x4B400000;
-    const float rh = exp_ffma(-kf, 0x1.62e43p-7f, x);
-    const float rl = exp_fmul(kf, 0x1.05c61p-35f);  // -K Ll (Ll < 0)
-    const float s = exp_fadd(rh, rl);
-    const float q = exp_ffma(exp_ffma(s, 0x1.555556p-5f, 0x1.555556p-3f), s, 0.5f);
-    const float e = exp_ffma(exp_fmul(s, s), q, rl);
-    const float ah = exp_fadd(1.0f, rh);
-    const float al = exp_fadd(exp_fsub(rh, exp_fsub(ah, 1.0f)), e);
-    const float2 tb = exp2_64(K & 63);
-    const float yh = exp_fmul(tb.x, ah);
-    const float ye = exp_ffma(tb.x, ah, -yh);
-    const float yl = exp_ffma(tb.x, al, exp_ffma(tb.y, ah, ye));
-    const float zh = exp_fadd(yh, yl);
-    const float zl = exp_fsub(yl, exp_fsub(zh, yh));
-    // half the gap to the neighbour on zl's side: 2^-25 below 1 (and below
-    // zh = 1), 2^-24 from 1 up to 2
-    const float half = (zh < 1.0f) | ((zh == 1.0f) & (zl < 0.0f)) ? 0x1p-25f : 0x1p-24f;
-    ok = (x > -86.0f) & (x < 88.0f) & (fabsf(zl) < half - EXP_FF_EPS);
-    return exp_i2f(exp_f2i(zh) + ((K >> 6) << 23));
+    bool ok1;
+    const float2 y = exp_rn_f32x2_ff(make_float2(x, x), ok, ok1);
+    return y.x;
 }
 
 // The fallback is a real call on the device, so that the double path runs

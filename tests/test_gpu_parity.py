@@ -254,6 +254,58 @@ def test_silu_f32_every_float(cuda, orc):
     assert differ <= libmiss  # differences only where the reference's exp misrounds
 
 
+def _silu_host_lib():
+    """tests/cpp/silu_host.cu built as a shared library (nvcc, host code only)."""
+    import ctypes
+    import os
+    import subprocess
+
+    from conftest import PKG, ROOT
+
+    src = os.path.join(ROOT, "tests", "cpp", "silu_host.cu")
+    so = os.path.join(ROOT, "tests", "cpp", "_build", "libsilu_host.so")
+    hdr = os.path.join(PKG, "csrc", "oxide_common.cuh")
+    if not os.path.exists(so) or os.path.getmtime(so) < max(os.path.getmtime(src), os.path.getmtime(hdr)):
+        os.makedirs(os.path.dirname(so), exist_ok=True)
+        subprocess.run(["/usr/local/cuda/bin/nvcc", "-O2", "-std=c++17", "-x", "cu", "-shared",
+                        "-gencode", "arch=compute_100a,code=sm_100a", "-I", os.path.join(ROOT, "include"),
+                        "-I", os.path.join(PKG, "csrc"), "-Xcompiler", "-fPIC,-fopenmp,-ffp-contract=off",
+                        "-o", so, src, "-lgomp"], check=True, timeout=600)
+    lib = ctypes.CDLL(so)
+    lib.silu_bits_host.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p]
+    lib.silu_bits_host.restype = None
+    return lib
+
+
+def test_silu_f32_device_bits_equal_host_build(cuda):
+    """The f32 SiLU kernels (the vector path: the paired f32 exponential, its
+    rounding test and the fix-ups of undecided elements; silu * up with up = 1;
+    and the scalar path of a misaligned view) against the host build of the
+    same arithmetic, bit for bit, on every 16th f32 bit pattern: the device
+    must compute exactly the operations written."""
+    from oxide_b200 import ops
+
+    lib = _silu_host_lib()
+    stride, n = 16, 1 << 24
+    ones = torch.ones(n, dtype=torch.float32, device=cuda)
+    for c in range((1 << 32) // (stride * n)):
+        first = c * stride * n
+        host = np.empty(n, dtype=F)
+        lib.silu_bits_host(first, stride, n, host.ctypes.data)
+        x = (first + np.arange(n, dtype=np.uint64) * stride).astype(np.uint32).view(F)
+        tx = torch.from_numpy(x).to(cuda)
+        outs = [to_np(ops.silu(tx)), to_np(ops.silu_mul(tx, ones))]
+        if c == 0:
+            buf = torch.empty(n + 1, dtype=torch.float32, device=cuda)
+            buf[1:].copy_(tx)
+            outs.append(to_np(ops.silu(buf[1:])))  # 4-byte offset: the scalar kernel
+        nan = np.isnan(host)
+        for got in outs:
+            assert np.array_equal(np.isnan(got), nan)
+            bad = np.nonzero(got[~nan].view(np.uint32) != host[~nan].view(np.uint32))[0]
+            assert bad.size == 0, f"{bad.size} differ from the host build, e.g. x = {x[~nan][bad[:4]]}"
+
+
 def test_fused_silu_mul_equals_unfused(cuda, orc):
     """silu then mul (two kernels) == the fused kernel, bit for bit, both dtypes
     (bf16 products away from the subnormal range, where the fused kernel's
@@ -575,21 +627,25 @@ def test_argmax(cuda, orc, dtype, rows, cols):
     assert np.array_equal(to_np(got).astype(np.uint32), orc.argmax_rows(x, cols))
 
 
-def test_argmax_ties_nan_signed_zero(cuda, orc):
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("cols", [4096, 32000, 40000])  # 256-thread CTAs / clusters, one 1024-thread CTA per row
+def test_argmax_ties_nan_signed_zero(cuda, orc, dtype, cols):
     from oxide_b200 import ops
 
-    x = np.random.default_rng(51).standard_normal((6, 4096), dtype=F)
-    x[0, [5, 77, 4000]] = 50.0                      # tie
+    x = np.random.default_rng(51).standard_normal((6, cols), dtype=F)
+    x[0, [5, 77, cols - 96]] = 50.0                 # tie, the last one in another CTA's part
     x[1] = -0.0
     x[1, 9] = 0.0                                    # -0 == +0 -> index 0
     x[2] = np.nan
     x[2, 1234] = -np.inf                             # NaN below everything
     x[3] = np.nan                                    # all NaN -> 0
-    x[4, 4095] = np.inf
+    x[4, cols - 1] = np.inf
     x[5] = -np.inf
+    if dtype == "bf16":
+        x = orc.f32_to_bf16(x).reshape(x.shape)
     got = to_np(ops.argmax(to_dev(x))).astype(np.uint32)
-    assert np.array_equal(got, orc.argmax_rows(x, 4096))
-    assert got.tolist()[:5] == [5, 0, 1234, 0, 4095]
+    assert np.array_equal(got, orc.argmax_rows(x, cols))
+    assert got.tolist()[:5] == [5, 0, 1234, 0, cols - 1]
 
 
 def test_argmax_misaligned(cuda, orc):
