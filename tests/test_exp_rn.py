@@ -1,6 +1,6 @@
 """The f32 exponential used by the f32 SiLU kernels (oxide::exp_rn_f32: an
 f32 float-float evaluation with a rounding test, falling back to a double
-evaluation where the test cannot decide) over every f32 bit pattern, against
+evaluation and an exception list where the test cannot decide) over every f32 bit pattern, against
 the host C library's expf -- the function the reference's f32::exp calls --
 and against the correctly rounded RN(expl(x)).  The function is IEEE f32 and
 f64 arithmetic only, so the host build checked here returns the device's
@@ -34,8 +34,7 @@ def test_exp_rn_matches_host_expf_on_every_float():
     # They differ where glibc's expf (0.502 ulp) is not the correctly rounded
     # value: 170,648 inputs (4.0e-5 of all floats) by this measurement.
     assert mism <= 5e-5 * total, f"{mism} of {total} differ"
-    # Correctly rounded on all but 17 inputs (hard cases the double fallback
-    # resolves within 2^-43 only), and the f32 path decides all but 1 in
+    # Correctly rounded on every input, and the f32 path decides all but 1 in
     # 10,000 of the inputs with normal results.
-    assert mism_rn <= 17, f"{mism_rn} inputs not correctly rounded"
+    assert mism_rn == 0, f"{mism_rn} inputs not correctly rounded"
     assert slow <= 1e-4 * total, f"{slow} inputs left to the double path"
