@@ -210,12 +210,21 @@ __global__ void __launch_bounds__(256, 3) smax_rows_kernel(const T* x, T* out, S
 // when the max grows); the CTA and then the cluster (through distributed
 // shared memory, in rank order) combine the (m, s) pairs into the row's max M
 // and sum S.  Pass 2 re-reads the slice -- from L2, where pass 1 left it -- and
-// writes p = exp(score - M) * RN(1 / S) (IEEE score, expf); S carries the
-// extra roundings of the rescaling and p those of the reciprocal, a few ulp
-// in all, far inside the f32 tolerance.  Nothing is held across
+// writes p = exp(score - M) * RN(1 / S) (IEEE score; exp_sfu below); S
+// carries the extra roundings of the rescaling and p those of the reciprocal
+// and of exp_sfu, a few 1e-6 in all, inside the f32 tolerance.  Nothing is held across
 // passes, so each thread keeps U vectors in flight with few registers and a
 // decode-sized batch of long rows runs in one wave.  In place (out == x) is
 // safe: a CTA writes only its own slice, after its own last read of it.
+// e^d for d = score - max <= 0 on the special-function unit: ex2 of
+// RN(d log2 e).  Relative error at most 2^-24 |d log2 e| ln 2 from the
+// argument's rounding plus ~2^-22 from ex2.approx -- under 6e-6 down to
+// the subnormal range (d log2 e >= -126), inside the f32 softmax tolerance
+// of 1e-5; subnormal results are kept (non-flushing ex2).  d is computed
+// first, as the reference does, so large scores lose nothing to it.
+// Measured on the C3 decode rows: 17.3 -> 15.9 us against expf.
+__device__ __forceinline__ float exp_sfu(float d) { return ex2_approx(fmul(d, 1.4426950408889634f)); }
+
 __device__ __forceinline__ void cluster_arrive() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
@@ -289,8 +298,8 @@ __global__ void __launch_bounds__(NT, 2048 / NT / 2)
 #pragma unroll
                     for (int e = 0; e < V; e += 2) {
                         const float2 d = diff2<MASK>(p, f[e], f[e + 1], j * V + e, nm);
-                        const float e0 = full || j * V + e < len ? expf(d.x) : 0.0f;
-                        const float e1 = full || j * V + e + 1 < len ? expf(d.y) : 0.0f;
+                        const float e0 = full || j * V + e < len ? exp_sfu(d.x) : 0.0f;
+                        const float e1 = full || j * V + e + 1 < len ? exp_sfu(d.y) : 0.0f;
                         acc = fadd2(acc, f2(e0, e1));
                     }
                     ssum = fadd(ssum, fadd(acc.x, acc.y));
@@ -342,7 +351,7 @@ __global__ void __launch_bounds__(NT, 2048 / NT / 2)
 #pragma unroll
                         for (int e = 0; e < V; e += 2) {
                             const float2 d = diff2<MASK>(p, f[e], f[e + 1], j * V + e, nm);
-                            const float2 q = fmul2(f2(expf(d.x), expf(d.y)), inv2);
+                            const float2 q = fmul2(f2(exp_sfu(d.x), exp_sfu(d.y)), inv2);
                             o[e] = full || j * V + e < len ? q.x : 0.0f;
                             o[e + 1] = full || j * V + e + 1 < len ? q.y : 0.0f;
                         }

@@ -168,9 +168,9 @@ def in_drift_band(tok, ref, p_ref):
 
 F32_REL = 1e-5
 BF16_ULP = 1
-# The f32 SiLU kernels take e^-x from exp_rn_f32, correctly rounded on all
-# but 36 floats; the reference's glibc expf is not on 4.0e-5 of all floats
-# and on 6.3e-4 of N(0,1)-distributed ones (1 ulp off there).  Where the two
+# The f32 SiLU kernels take e^-x from exp_rn_f32, correctly rounded on every
+# float; the reference's glibc expf is not on 4.0e-5 of all floats and on
+# 6.3e-4 of N(0,1)-distributed ones (1 ulp off there).  Where the two
 # exponentials agree every later step rounds the same, so the result must be
 # the reference's bits; elsewhere the 1-ulp difference passes through the
 # rounded steps of x * (1 / (1 + e)) * up: within 2^-21 relative (measured
@@ -183,8 +183,8 @@ def assert_silu_f32_parity(got, ref, x, orc, threads=None):
     """f32 silu / silu*up (x = the gate) against the oracle: bit-exact at
     every element whose e^-x the reference's expf rounds correctly -- apart
     from e^-x within 2^-40 (relative) of a rounding boundary between two
-    floats, closer than the 2^-43 accuracy of the kernels' exp_rn_f32
-    guarantees the same rounding -- elsewhere within SILU_F32_REL, NaN
+    floats, where the float64 exp used as the judge here cannot tell which
+    side of the boundary e^-x lies -- elsewhere within SILU_F32_REL, NaN
     exactly where the oracle has NaN."""
     u32 = np.uint32
     x = np.ascontiguousarray(x, np.float32).reshape(-1)
