@@ -92,6 +92,7 @@ struct TcArgs {
     float* part_ml;
     float* part_o;
     uint32_t* err;
+    uint32_t* pre_out;  // [batch + 1]: tiles per kv head before each batch, written by CTA 0 for the combine
     uint32_t withhold;  // failure-detection tests: the producer issues no loads, so every wait runs out
 };
 
@@ -213,6 +214,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             carry = __shfl_sync(0xffffffffu, incl, 31);
         }
         if (lane == 0) pre[0] = 0;
+        if (blockIdx.x == 0) {
+            __syncwarp();
+            for (uint32_t i = lane; i <= nb; i += 32) p.pre_out[i] = pre[i];
+        }
     }
     if (tid == 0 && blockIdx.x == 0) *p.err = 0u;
     tc_fence_before();
@@ -513,60 +518,73 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 }
 
 // Merge the split partials of one (batch, q head): the same tile division as
-// the main kernel gives the CTAs that took part of the pair, and the slot of
-// each (its first tile's offset within the pair).  out = sum_s o_s
-// e^(m_s - M) / sum_s l_s e^(m_s - M); a pair without keys gives zeros; NaN
-// everywhere if the main kernel reported an abort.
+// the main kernel (from the tile prefix it wrote) gives the CTAs that took part
+// of the pair -- enumerated in parallel, one thread per candidate -- and the
+// slot of each (its first tile's offset within the pair).  out = sum_s o_s
+// e^(m_s - M) / sum_s l_s e^(m_s - M), merged online over chunks of slots
+// whose loads are all issued first; a pair without keys gives zeros; NaN
+// everywhere if the main kernel reported an abort.  Two dependent memory
+// round trips in all (the prefix, then the partials).
 constexpr int TC_MAX_PARTS = 1024;  // CTAs sharing one pair: at most the grid size
+constexpr uint32_t TC_NOSLOT = 0xFFFFFFFFu;
 template <int NR>
 __global__ void __launch_bounds__(128)
     decode_attn_tc_combine_kernel(bf16_t* out, TcArgs p, uint32_t G) {
     pdl_begin();
-    __shared__ unsigned long long redu[32];
     __shared__ uint32_t slot[TC_MAX_PARTS];
-    __shared__ int nslot;
     const uint64_t bh = blockIdx.x, b = bh / p.q_heads;
     const uint32_t h = (uint32_t)(bh % p.q_heads), kvh = h / NR;
     const int d = threadIdx.x;
-    // tiles per kv head of the batches before b (high word) and of all (low)
-    unsigned long long acc2 = 0;
-    for (uint64_t bb = d; bb < p.batch; bb += 128) {
-        const unsigned long long tl = (tc_len(p, bb) + TC_TK - 1) / TC_TK;
-        acc2 += tl | (bb < b ? tl << 32 : 0ull);
-    }
-    struct OpAddU64 {
-        __device__ unsigned long long operator()(unsigned long long x, unsigned long long y) const { return x + y; }
-    };
-    acc2 = group_reduce(acc2, redu, 128, OpAddU64());
-    const uint32_t before = (uint32_t)(acc2 >> 32), all = (uint32_t)acc2;
-    const uint32_t tb = (tc_len(p, b) + TC_TK - 1) / TC_TK;
-    const uint32_t T = all * p.kv_heads;
-    if (d == 0) {
-        int n = 0;
-        if (tb) {
-            const uint32_t tfirst = before * p.kv_heads + kvh * tb, tlast = tfirst + tb - 1;
-            for (uint32_t c = tc_owner(tfirst, T, G); c <= tc_owner(tlast, T, G) && n < TC_MAX_PARTS; ++c) {
-                const uint32_t f0 = (uint32_t)((uint64_t)c * T / G), f1 = (uint32_t)((uint64_t)(c + 1) * T / G);
-                if (f0 < f1) slot[n++] = (f0 > tfirst ? f0 : tfirst) - tfirst;
-            }
+    const uint32_t before = p.pre_out[b], tb = p.pre_out[b + 1] - before;
+    const uint32_t T = p.pre_out[p.batch] * p.kv_heads;
+    const uint32_t failed = *p.err;
+    uint32_t nspan = 0;
+    if (tb) {
+        const uint32_t tfirst = before * p.kv_heads + kvh * tb, tlast = tfirst + tb - 1;
+        const uint32_t c0 = tc_owner(tfirst, T, G);
+        nspan = min(tc_owner(tlast, T, G) - c0 + 1, (uint32_t)TC_MAX_PARTS);
+        for (uint32_t i = (uint32_t)d; i < nspan; i += 128) {
+            const uint32_t c = c0 + i;
+            const uint32_t f0 = (uint32_t)((uint64_t)c * T / G), f1 = (uint32_t)((uint64_t)(c + 1) * T / G);
+            slot[i] = f0 < f1 ? (f0 > tfirst ? f0 : tfirst) - tfirst : TC_NOSLOT;
         }
-        nslot = n;
     }
     __syncthreads();
-    const int n = nslot;
     const uint64_t base = bh * p.stride;
-    float M = -INFINITY;
-    for (int i = 0; i < n; ++i) M = fmaxf(M, p.part_ml[(base + slot[i]) * 2]);
-    float L = 0.0f, acc = 0.0f;
-    for (int i = 0; i < n; ++i) {
-        const uint64_t sl = base + slot[i];
-        const float ms = p.part_ml[sl * 2];
-        const float w = (M == -INFINITY || ms == -INFINITY) ? 0.0f : expf(fsub(ms, M));
-        L = __fmaf_rn(p.part_ml[sl * 2 + 1], w, L);
-        acc = __fmaf_rn(p.part_o[sl * TC_D + d], w, acc);
+    float M = -INFINITY, L = 0.0f, acc = 0.0f;
+    constexpr int CH = 8;
+    for (uint32_t i0 = 0; i0 < nspan; i0 += CH) {
+        float ms[CH], ls[CH], os[CH];
+#pragma unroll
+        for (int k = 0; k < CH; ++k) {
+            const uint32_t sk = i0 + k < nspan ? slot[i0 + k] : TC_NOSLOT;
+            ms[k] = -INFINITY;
+            ls[k] = 0.0f;
+            os[k] = 0.0f;
+            if (sk != TC_NOSLOT) {
+                const uint64_t sl = base + sk;
+                ms[k] = p.part_ml[sl * 2];
+                ls[k] = p.part_ml[sl * 2 + 1];
+                os[k] = p.part_o[sl * TC_D + d];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < CH; ++k) {
+            if (ms[k] == -INFINITY) continue;  // no slot, or a CTA part without valid keys
+            if (ms[k] > M) {
+                const float w = M == -INFINITY ? 0.0f : expf(fsub(M, ms[k]));
+                L = __fmaf_rn(L, w, ls[k]);
+                acc = __fmaf_rn(acc, w, os[k]);
+                M = ms[k];
+            } else {
+                const float w = expf(fsub(ms[k], M));
+                L = __fmaf_rn(ls[k], w, L);
+                acc = __fmaf_rn(os[k], w, acc);
+            }
+        }
     }
     float r = M == -INFINITY ? 0.0f : fdiv(acc, L);
-    if (*p.err) r = __uint_as_float(0x7fc00000u);
+    if (failed) r = __uint_as_float(0x7fc00000u);
     Vec<bf16_t>::store1(out + bh * TC_D + d, r);
 }
 
@@ -632,7 +650,7 @@ cudaError_t decode_attention_tc_bf16(const bf16_t* q, const bf16_t* kc, const bf
     const uint64_t tiles_max = (max_seq + TC_TK - 1) / TC_TK;
     if (tiles_max > (uint64_t)TC_MAX_TILES) return cudaSuccess;
     const uint32_t stride = (uint32_t)tiles_max;  // a partial slot per tile offset of a sequence
-    const uint64_t need = (uint64_t)batch * q_heads * stride * (2 + TC_D) * sizeof(float) + 16;
+    const uint64_t need = (uint64_t)batch * q_heads * stride * (2 + TC_D) * sizeof(float) + 16 + (batch + 1) * 4;
     if (ws_bytes < need) return cudaSuccess;
     CUtensorMap mk, mv, mq;
     if (!tc_map(&mk, kc, batch * kv_heads * max_seq, TC_TK) || !tc_map(&mv, vc, batch * kv_heads * max_seq, TC_TK) ||
@@ -649,6 +667,7 @@ cudaError_t decode_attention_tc_bf16(const bf16_t* q, const bf16_t* kc, const bf
     a.part_ml = static_cast<float*>(ws);
     a.part_o = a.part_ml + (size_t)2 * batch * q_heads * stride;
     a.err = reinterpret_cast<uint32_t*>(a.part_o + (size_t)batch * q_heads * stride * TC_D);
+    a.pre_out = a.err + 4;
     a.withhold = withhold ? 1u : 0u;
     *used = true;
     switch (rep) {
