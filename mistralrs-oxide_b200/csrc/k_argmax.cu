@@ -161,6 +161,91 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Few long rows (decode logits), vector path: a cluster of CTAs per row.
+// Each CTA scans its slice keeping (best value, index) and the first index
+// that holds a number (not NaN), reduces both over the CTA, and thread 0
+// stores them into rank 0's shared memory (distributed shared memory); after
+// one cluster barrier (release / acquire) rank 0 merges the CTAs' pairs and
+// writes the row's index -- the first non-NaN index when the maximum is -inf
+// (0 if every element is NaN), as in argmax_kernel.  One cluster barrier per
+// row and no second scan; the slots are double-buffered by row parity, so a
+// CTA already on the next row cannot overwrite a pair rank 0 has not read.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    argmax_cluster_kernel(const T* x, uint64_t rows, uint32_t cols, uint32_t* idx) {
+    pdl_begin();
+    constexpr int V = Vec<T>::N;
+    constexpr int UNROLL = 8;
+    __shared__ Best red[8];
+    __shared__ uint32_t redn[8];
+    __shared__ Best slots[2][8];
+    __shared__ uint32_t nslots[2][8];
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t cl = cluster.num_blocks(), rank = cluster.block_rank();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t n = cols / V, per = (n + cl - 1) / cl;
+    const uint32_t lo = min(n, rank * per), hi = min(n, lo + per);
+    Best* slot0 = cluster.map_shared_rank(&slots[0][0], 0);
+    uint32_t* nslot0 = cluster.map_shared_rank(&nslots[0][0], 0);
+    uint32_t par = 0;
+    for (uint64_t row = blockIdx.x / cl; row < rows; row += gridDim.x / cl, par ^= 1u) {
+        const T* xr = x + row * cols;
+        float bv = -INFINITY;
+        uint32_t bi = NONE, nn = NONE;
+        for (uint32_t u0 = lo + threadIdx.x; u0 < hi; u0 += blockDim.x * UNROLL) {
+            uint4 raw[UNROLL];
+#pragma unroll
+            for (int k = 0; k < UNROLL; ++k) {
+                const uint32_t u = u0 + k * blockDim.x;
+                if (u < hi) raw[k] = ld_stream(xr + (uint64_t)u * V);
+            }
+#pragma unroll
+            for (int k = 0; k < UNROLL; ++k) {
+                const uint32_t u = u0 + k * blockDim.x;
+                if (u < hi) {
+                    float f[V];
+                    Vec<T>::unpack(raw[k], f);
+#pragma unroll
+                    for (int e = 0; e < V; ++e) {
+                        if (f[e] > bv) {
+                            bv = f[e];
+                            bi = u * V + e;
+                        }
+                        if (nn == NONE && f[e] == f[e]) nn = u * V + e;  // the thread scans in index order
+                    }
+                }
+            }
+        }
+        const Best b = warp_best(Best{bv, bi});
+        const uint32_t m = __reduce_min_sync(0xffffffffu, nn);
+        if (lane == 0) {
+            red[warp] = b;
+            redn[warp] = m;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            Best r = red[0];
+            uint32_t mm = redn[0];
+            for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+                r = better(r, red[w]);
+                mm = min(mm, redn[w]);
+            }
+            slot0[par * 8 + rank] = r;
+            nslot0[par * 8 + rank] = mm;
+        }
+        cluster.sync();  // rank 0 sees every CTA's pair; red[] may be written again
+        if (rank == 0 && threadIdx.x == 0) {
+            Best r = slots[par][0];
+            uint32_t mm = nslots[par][0];
+            for (uint32_t q = 1; q < cl; ++q) {
+                r = better(r, slots[par][q]);
+                mm = min(mm, nslots[par][q]);
+            }
+            idx[row] = r.i != NONE ? r.i : (mm == NONE ? 0u : mm);
+        }
+    }
+}
+
 template <typename T>
 static int argmax_entry(const char* name, const T* x, uint64_t rows, uint64_t cols,
                         uint32_t* idx, cudaStream_t st) {
@@ -198,8 +283,9 @@ static int argmax_entry(const char* name, const T* x, uint64_t rows, uint64_t co
     // 5.43 us with it (the kernel's griddepcontrol instructions are then no-ops).
     cfg.numAttrs = 1;
     const uint32_t c32 = (uint32_t)cols;
-    cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, argmax_kernel<T, true>, x, rows, c32, idx, cl)
-                        : cudaLaunchKernelEx(&cfg, argmax_kernel<T, false>, x, rows, c32, idx, cl);
+    cudaError_t e = vec && cl > 1 ? cudaLaunchKernelEx(&cfg, argmax_cluster_kernel<T>, x, rows, c32, idx)
+                    : vec         ? cudaLaunchKernelEx(&cfg, argmax_kernel<T, true>, x, rows, c32, idx, cl)
+                                  : cudaLaunchKernelEx(&cfg, argmax_kernel<T, false>, x, rows, c32, idx, cl);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return set_error(OXIDE_ERR_LAUNCH, "%s: launch failed: %s", name, cudaGetErrorString(e));
