@@ -78,6 +78,13 @@ __device__ __forceinline__ float2 silu_fast2(float2 x, bool& ok0, bool& ok1) {
     const float2 d = fadd2(f2(1.0f, 1.0f), e);
     return fmul2(x, f2(__frcp_rn(d.x), __frcp_rn(d.y)));
 }
+// The same without the flags: inputs in [-EXP_FF_XMAX, EXP_FF_XMAX] (checked
+// by the caller), undecided inputs leave nonzero bits in `diff`.
+__device__ __forceinline__ float2 silu_fast2r(float2 x, uint32_t& diff) {
+    const float2 e = exp_rn_f32x2_ffr(f2(-x.x, -x.y), diff);
+    const float2 d = fadd2(f2(1.0f, 1.0f), e);
+    return fmul2(x, f2(__frcp_rn(d.x), __frcp_rn(d.y)));
+}
 __device__ __forceinline__ float silu_exact(float x) {
     return fmul(x, __frcp_rn(fadd(1.0f, exp_rn_f32_fallback(-x))));
 }
@@ -110,6 +117,9 @@ struct FSiluMul {  // mul(silu(g), u); silu(g) rounded to T as the pair stores i
     }
     __device__ __forceinline__ float2 fast2(float2 g, float2 u, bool& ok0, bool& ok1) const {
         return fmul2(silu_fast2(g, ok0, ok1), u);
+    }
+    __device__ __forceinline__ float2 fast2r(float2 g, float2 u, uint32_t& diff) const {
+        return fmul2(silu_fast2r(g, diff), u);
     }
     __device__ __forceinline__ float exact(float g, float u) const { return fmul(silu_exact(g), u); }
     __device__ __forceinline__ float2 pair(float2 g, float2 u) const {
@@ -150,6 +160,9 @@ struct FSilu {
     __device__ __forceinline__ float2 pair(float2 x, float2) const { return silu_f2<ACC>(x); }
     __device__ __forceinline__ float2 fast2(float2 x, float2, bool& ok0, bool& ok1) const {
         return silu_fast2(x, ok0, ok1);
+    }
+    __device__ __forceinline__ float2 fast2r(float2 x, float2, uint32_t& diff) const {
+        return silu_fast2r(x, diff);
     }
     __device__ __forceinline__ float exact(float x, float) const { return silu_exact(x); }
 };
@@ -308,28 +321,41 @@ __global__ void __launch_bounds__(EW_THREADS, STG_MIN_BLOCKS)
         const int stage = (int)(j % S);
         issue(j + S - 1, (int)((j + S - 1) % S));
         cp_async_wait<S - 1>();  // this thread's group j has landed
-        uint32_t bad = 0;
+        // The fast path decides all U V elements unless an input lies outside
+        // [-EXP_FF_XMAX, EXP_FF_XMAX] (one comparison of the largest |x|) or
+        // a rounding test fails (nonzero diff); then, rarely, the vectors are
+        // redone element by element and stored again.
+        uint32_t diff = 0;
+        float xmax = 0.0f;
 #pragma unroll
         for (int k = 0; k < U; ++k) {
             const uint64_t i = first + (j * U + k) * stride;
             const float4 x = sa[stage][k][tid];
             const float4 y = NIN == 2 ? sb[stage][k][tid] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            bool o0, o1, o2, o3;
-            const float2 r0 = f.fast2(f2(x.x, x.y), f2(y.x, y.y), o0, o1);
-            const float2 r1 = f.fast2(f2(x.z, x.w), f2(y.z, y.w), o2, o3);
-            bad |= ((o0 ? 0u : 1u) | (o1 ? 0u : 2u) | (o2 ? 0u : 4u) | (o3 ? 0u : 8u)) << (k * V);
+            xmax = fmaxf(xmax, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+            const float2 r0 = f.fast2r(f2(x.x, x.y), f2(y.x, y.y), diff);
+            const float2 r1 = f.fast2r(f2(x.z, x.w), f2(y.z, y.w), diff);
             if (i < nvec)
                 st_stream(out + i * V, make_uint4(__float_as_uint(r0.x), __float_as_uint(r0.y), __float_as_uint(r1.x),
                                                   __float_as_uint(r1.y)));
         }
-        while (bad) {
-            const int bit = __ffs(bad) - 1;
-            bad &= bad - 1u;
-            const int k = bit / V, e = bit % V;
-            const uint64_t i = first + (j * U + k) * stride;
-            const float x = reinterpret_cast<const float*>(&sa[stage][k][tid])[e];
-            const float y = NIN == 2 ? reinterpret_cast<const float*>(&sb[stage][k][tid])[e] : 0.0f;
-            if (i < nvec) out[i * V + e] = f.exact(x, y);
+        if (diff != 0 || !(xmax <= EXP_FF_XMAX)) {
+#pragma unroll 1
+            for (int k = 0; k < U; ++k) {
+                const uint64_t i = first + (j * U + k) * stride;
+                const float4 x = sa[stage][k][tid];
+                const float4 y = NIN == 2 ? sb[stage][k][tid] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                bool o0, o1, o2, o3;
+                float2 r0 = f.fast2(f2(x.x, x.y), f2(y.x, y.y), o0, o1);
+                float2 r1 = f.fast2(f2(x.z, x.w), f2(y.z, y.w), o2, o3);
+                if (!o0) r0.x = f.exact(x.x, y.x);
+                if (!o1) r0.y = f.exact(x.y, y.y);
+                if (!o2) r1.x = f.exact(x.z, y.z);
+                if (!o3) r1.y = f.exact(x.w, y.w);
+                if (i < nvec)
+                    st_stream(out + i * V, make_uint4(__float_as_uint(r0.x), __float_as_uint(r0.y),
+                                                      __float_as_uint(r1.x), __float_as_uint(r1.y)));
+            }
         }
     }
     cp_async_wait<0>();  // nothing in flight into shared memory at exit

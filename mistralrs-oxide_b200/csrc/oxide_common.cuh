@@ -484,13 +484,16 @@ __host__ __device__ __forceinline__ float2 exp_c2(float c) { return make_float2(
 // field, exact for K in [-8000, 8063] (results in [2^-126, 2^126): x in
 // about [-86.6, 87.3]).  Where the test fails or K is outside, ok = false.
 constexpr float EXP_FF_EPS = 0x1p-36f;
-__host__ __device__ __forceinline__ float2 exp_rn_f32x2_ff(float2 x, bool& ok0, bool& ok1) {
+// The shared steps: zh and zl (Th ah + (yl +- EPS), before the scaling by
+// 2^k) and the bit patterns of t, whose low bits hold K.
+__host__ __device__ __forceinline__ void exp_ff_core(float2 x, float2& zh, float2& zl, uint32_t& b0, uint32_t& b1) {
     const float2 t = exp_ffma2(x, exp_c2(0x1.715476p+6f), exp_c2(0x1.8p23f));  // 1.5 * 2^23 + K
     const float2 kf = exp_fadd2(t, exp_c2(-0x1.8p23f));
     // K = bits(t) - 0x4B400000; that constant's low 15 bits are zero, so
     // K mod 64 = bits(t) mod 64 and (K >> 6) << 23 = (bits(t) >> 6) << 23
     // modulo 2^32, and the range test is one unsigned comparison.
-    const uint32_t b0 = (uint32_t)exp_f2i(t.x), b1 = (uint32_t)exp_f2i(t.y);
+    b0 = (uint32_t)exp_f2i(t.x);
+    b1 = (uint32_t)exp_f2i(t.y);
     const float2 rh = exp_ffma2(kf, exp_c2(-0x1.62e43p-7f), x);
     const float2 rl = exp_fmul2(kf, exp_c2(0x1.05c61p-35f));  // -K Ll (Ll < 0)
     const float2 s = exp_ffma2(kf, exp_c2(0x1.05c61p-35f), rh);
@@ -501,12 +504,34 @@ __host__ __device__ __forceinline__ float2 exp_rn_f32x2_ff(float2 x, bool& ok0, 
     const float2 t0 = exp2_64((int)(b0 & 63u)), t1 = exp2_64((int)(b1 & 63u));
     const float2 th = make_float2(t0.x, t1.x), tl = make_float2(t0.y, t1.y);
     const float2 yl = exp_ffma2(th, al, exp_fmul2(tl, ah));
-    const float2 zh = exp_ffma2(th, ah, exp_fadd2(yl, exp_c2(EXP_FF_EPS)));
-    const float2 zl = exp_ffma2(th, ah, exp_fadd2(yl, exp_c2(-EXP_FF_EPS)));
+    zh = exp_ffma2(th, ah, exp_fadd2(yl, exp_c2(EXP_FF_EPS)));
+    zl = exp_ffma2(th, ah, exp_fadd2(yl, exp_c2(-EXP_FF_EPS)));
+}
+__host__ __device__ __forceinline__ float exp_ff_scale(float z, uint32_t b) {
+    return exp_i2f((int)((uint32_t)exp_f2i(z) + ((b >> 6) << 23)));
+}
+__host__ __device__ __forceinline__ float2 exp_rn_f32x2_ff(float2 x, bool& ok0, bool& ok1) {
+    float2 zh, zl;
+    uint32_t b0, b1;
+    exp_ff_core(x, zh, zl, b0, b1);
     ok0 = (b0 - (0x4B400000u - 8000u) < 16064u) & (zh.x == zl.x);  // K in [-8000, 8063]
     ok1 = (b1 - (0x4B400000u - 8000u) < 16064u) & (zh.y == zl.y);
-    return make_float2(exp_i2f((int)((uint32_t)exp_f2i(zh.x) + ((b0 >> 6) << 23))),
-                       exp_i2f((int)((uint32_t)exp_f2i(zh.y) + ((b1 >> 6) << 23))));
+    return make_float2(exp_ff_scale(zh.x, b0), exp_ff_scale(zh.y, b1));
+}
+// The same value for inputs the caller has checked to lie in
+// [-EXP_FF_XMAX, EXP_FF_XMAX] (K within [-7988, 7988], so the scaling by 2^k
+// stays exact and the result normal): instead of two flags, the bits of
+// zh - zl of both lanes are OR-ed into `diff`.  zh - zl is exact, so `diff`
+// stays zero exactly when both rounding tests pass (a NaN or an infinity
+// leaves nonzero bits).
+constexpr float EXP_FF_XMAX = 86.5f;
+__host__ __device__ __forceinline__ float2 exp_rn_f32x2_ffr(float2 x, uint32_t& diff) {
+    float2 zh, zl;
+    uint32_t b0, b1;
+    exp_ff_core(x, zh, zl, b0, b1);
+    const float2 dz = exp_fadd2(zh, make_float2(-zl.x, -zl.y));
+    diff |= (uint32_t)exp_f2i(dz.x) | (uint32_t)exp_f2i(dz.y);
+    return make_float2(exp_ff_scale(zh.x, b0), exp_ff_scale(zh.y, b1));
 }
 // One input through the same steps (the first lane of the pair).
 __host__ __device__ __forceinline__ float exp_rn_f32_ff(float x, bool& ok) {
