@@ -58,8 +58,11 @@ constexpr int SMP_THREADS = 512;
 constexpr int SMP_WARPS = SMP_THREADS / 32;
 constexpr uint32_t SMP_SPAN = 32768;                      // logits per CTA
 constexpr int SMP_GATHER = 2048;                          // candidates walked exactly
+constexpr uint32_t SMP_SORT_CAP = 256;                    // candidates sorted after narrowing
+constexpr int SMP_NARROW_STEPS = 12;                      // bisection steps spent narrowing
 constexpr uint32_t SMP_FALLBACK = 0xFFFFFFFEu;            // the walk needs more than was gathered
-constexpr size_t SMP_SMEM = (size_t)SMP_SPAN * 4 + (size_t)SMP_GATHER * 8;  // 147,456 B
+// row segment, gathered keys, the walk's running sums
+constexpr size_t SMP_SMEM = (size_t)SMP_SPAN * 4 + (size_t)SMP_GATHER * 8 + (size_t)SMP_GATHER * 4;  // 155,648 B
 
 struct SmpArgs {
     const void* logits;
@@ -353,38 +356,123 @@ __device__ __forceinline__ void bitonic_desc(unsigned long long* buf, uint32_t n
     }
 }
 
-// sample_top_k / sample_top_p on the sorted keys (src/tokenizer.rs:182-232).
-__device__ uint32_t walk_sorted(const unsigned long long* buf, uint32_t n, bool whole_row, bool topp,
-                                uint64_t top_k, float top_p, float u) {
+// Narrows the gathered keys buf[0, n) (probability bits << 32 | ~index, a
+// prefix of the sorted order) to the keys of probability >= v for a higher
+// v the walk allows: for top-p (sum) those probabilities still sum to at
+// least t -- t carries the same margin over top_p as the first search, so
+// the reference's running sum reaches top_p inside them -- and for top-k at
+// least t of them remain, t = the walk's prefix length.  A bisection on the
+// probability bits between the smallest and the largest key, one block
+// reduction per step (f64 sums, fixed order), at most SMP_NARROW_STEPS
+// steps, stopping at the first pivot that keeps at most SMP_SORT_CAP keys;
+// the keys kept are moved to the front (their order does not matter: they
+// are sorted next).  The set stays a prefix of the sorted order, so the walk
+// over it takes the same steps.  Returns the new count (n if no pivot
+// qualified).  CTA-wide: every thread of the CTA calls it.
+__device__ uint32_t narrow_candidates(unsigned long long* buf, uint32_t n, double t, bool sum, Reducer<1>& rd,
+                                      uint32_t* cnt) {
+    constexpr int K = SMP_GATHER / SMP_THREADS;
+    unsigned long long key[K];
+    float pv[K];
+    float hi_p = -1.0f, lo_p = INFINITY;
+#pragma unroll
+    for (int c = 0; c < K; ++c) {
+        const uint32_t i = threadIdx.x + c * SMP_THREADS;
+        key[c] = i < n ? buf[i] : 0ull;
+        pv[c] = i < n ? __uint_as_float((uint32_t)(key[c] >> 32)) : -1.0f;
+        if (i < n) {
+            hi_p = fmaxf(hi_p, pv[c]);
+            lo_p = fminf(lo_p, pv[c]);
+        }
+    }
+    const double2 b = rd.template run<RMAX, RMIN>((double)hi_p, (double)lo_p);
+    uint32_t lo = __float_as_uint((float)b.y), hi = __float_as_uint((float)b.x) + 1u;
+    uint32_t best = lo;
+    double best_c = (double)n;
+    for (int step = 0; step < SMP_NARROW_STEPS && hi - lo > 1; ++step) {
+        const uint32_t mid = lo + (hi - lo) / 2;
+        const float x = __uint_as_float(mid);
+        double sm = 0.0, cn = 0.0;
+#pragma unroll
+        for (int c = 0; c < K; ++c)
+            if (pv[c] >= x) {
+                sm += (double)pv[c];
+                cn += 1.0;
+            }
+        const double2 m = rd.template run<RSUM, RSUM>(sm, cn);
+        if ((sum ? m.x : m.y) >= t) {
+            lo = mid;
+            best = mid;
+            best_c = m.y;
+            if (m.y <= (double)SMP_SORT_CAP) break;
+        } else {
+            hi = mid;
+        }
+    }
+    if (best_c >= (double)n) return n;  // uniform: every thread saw the same reductions
+    // every thread holds its keys in registers; move the kept ones forward
+    if (threadIdx.x == 0) *cnt = 0;
+    __syncthreads();
+    const float x = __uint_as_float(best);
+#pragma unroll
+    for (int c = 0; c < K; ++c)
+        if (threadIdx.x + c * SMP_THREADS < n && pv[c] >= x) buf[atomicAdd(cnt, 1u)] = key[c];
+    __syncthreads();
+    return *cnt;
+}
+
+// sample_top_k / sample_top_p on the sorted keys (src/tokenizer.rs:182-232),
+// CTA-wide.  The reference's loops repeat one sequential f32 running sum:
+// sample_top_p's cumsum up to the first value >= top_p, the running total
+// over the kept prefix (the same additions from 0 in the same order, so the
+// total is the last of those values) and the running sum compared with
+// r = u * total.  Thread 0 computes that sum once and stores every prefix
+// value; r's position -- the first prefix value >= r -- is then found by all
+// threads at once.  The result (a token, or SMP_FALLBACK when top-p needs
+// more than the n keys of a partial row) is written to *res.
+__device__ void walk_sorted_cta(const unsigned long long* buf, float* pfx, uint32_t n, bool whole_row, bool topp,
+                                uint64_t top_k, float top_p, float u, uint32_t* res, uint32_t* keep_s, float* r_s) {
     auto pr = [&](uint32_t i) { return __uint_as_float((uint32_t)(buf[i] >> 32)); };
     auto ix = [&](uint32_t i) { return ~(uint32_t)buf[i]; };
-    uint32_t keep;
-    if (topp) {
-        float cumsum = 0.0f;
-        keep = 0;
-        for (uint32_t i = 0; i < n; ++i) {
-            cumsum = fadd(cumsum, pr(i));
-            if (cumsum >= top_p) {
-                keep = i + 1;
-                break;
+    if (threadIdx.x == 0) {
+        uint32_t keep = 0;
+        const uint32_t lim = topp ? n : (uint32_t)(top_k < n ? top_k : n);
+        float acc = 0.0f;
+        for (uint32_t i0 = 0; i0 < lim && keep == 0; i0 += 8) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = i0 + e < lim ? pr(i0 + e) : 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                if (i0 + e < lim && keep == 0) {
+                    acc = fadd(acc, v[e]);
+                    pfx[i0 + e] = acc;
+                    if (topp && acc >= top_p) keep = i0 + e + 1;
+                }
             }
         }
-        if (keep == 0) {
-            if (!whole_row) return SMP_FALLBACK;
-            keep = n;
+        if (!topp) {
+            keep = lim;
+        } else if (keep == 0) {
+            keep = whole_row ? n : 0u;  // a whole row walks every key
         }
-    } else {
-        keep = (uint32_t)(top_k < n ? top_k : n);
+        *keep_s = keep;
+        if (keep == 0) {
+            *res = SMP_FALLBACK;
+        } else {
+            *r_s = fmul(u, pfx[keep - 1]);
+            *res = ix(keep - 1);  // the reference's answer when no running sum reaches r
+        }
     }
-    float total = 0.0f;
-    for (uint32_t i = 0; i < keep; ++i) total = fadd(total, pr(i));
-    const float r = fmul(u, total);
-    float cum = 0.0f;
-    for (uint32_t i = 0; i < keep; ++i) {
-        cum = fadd(cum, pr(i));
-        if (cum >= r) return ix(i);
-    }
-    return ix(keep - 1);
+    __syncthreads();
+    const uint32_t keep = *keep_s;
+    if (keep == 0) return;
+    const float r = *r_s;
+    // pfx is non-decreasing (each step adds a probability >= 0), so exactly
+    // one index (if any) is the first whose value reaches r
+    for (uint32_t i = threadIdx.x; i < keep; i += SMP_THREADS)
+        if (pfx[i] >= r && (i == 0 || pfx[i - 1] < r)) *res = ix(i);
+    __syncthreads();
 }
 
 __device__ __forceinline__ float load_logit(const float* x, uint64_t i) { return __ldg(x + i); }
@@ -424,10 +512,13 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     float* sp = reinterpret_cast<float*>(smem);                                           // [SMP_SPAN]
     unsigned long long* gbuf = reinterpret_cast<unsigned long long*>(smem + SMP_SPAN * 4);  // [SMP_GATHER]
+    float* pfx = reinterpret_cast<float*>(smem + SMP_SPAN * 4 + SMP_GATHER * 8);          // [SMP_GATHER]
     float4* sp4 = reinterpret_cast<float4*>(sp);
     __shared__ double2 red[2 * SMP_WARPS];
     __shared__ double2 cred[2];
-    __shared__ uint32_t gcount, gresult;
+    __shared__ double2 lred[2 * SMP_WARPS];
+    __shared__ uint32_t gcount, gresult, wkeep, ncount;
+    __shared__ float wr;
     Reducer<CL> rd{red, cred, 0u};
     const uint32_t crank = CL == 1 ? 0u : (uint32_t)cg::this_cluster().block_rank();
     if (threadIdx.x == 0) gcount = 0;  // visible to the cluster after the first reduction's barrier
@@ -577,15 +668,25 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
             }
             done = false;
             if (short_prefix) {
-                for (uint32_t q = threadIdx.x; q < row.ng; q += SMP_THREADS) {
-                    const float4 w = sp4[q];
+                // gather: one slot reservation per warp and component (most
+                // warps hold no candidate; every lane runs the same trip count)
+                const uint32_t lane = threadIdx.x & 31u;
+                const uint32_t ngr = (row.ng + SMP_THREADS - 1) / SMP_THREADS * SMP_THREADS;
+                for (uint32_t q = threadIdx.x; q < ngr; q += SMP_THREADS) {
+                    const float4 w = q < row.ng ? sp4[q] : make_float4(-1.0f, -1.0f, -1.0f, -1.0f);
                     const float v[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         const uint32_t i = row.base + 4 * q + c;
-                        if (v[c] > gv || (v[c] == gv && i <= gidx)) {
-                            const uint32_t pos = atomicAdd(gcount0, 1u);
-                            if (pos < (uint32_t)SMP_GATHER)
+                        const bool take = v[c] > gv || (v[c] == gv && i <= gidx);
+                        const uint32_t m = __ballot_sync(0xffffffffu, take);
+                        if (m) {
+                            const uint32_t lead = (uint32_t)__ffs(m) - 1u;
+                            uint32_t base = 0;
+                            if (lane == lead) base = atomicAdd(gcount0, (uint32_t)__popc(m));
+                            base = __shfl_sync(0xffffffffu, base, lead);
+                            const uint32_t pos = base + (uint32_t)__popc(m & ((1u << lane) - 1u));
+                            if (take && pos < (uint32_t)SMP_GATHER)
                                 gbuf0[pos] = ((unsigned long long)__float_as_uint(v[c]) << 32) |
                                              (unsigned long long)(~i);
                         }
@@ -593,16 +694,23 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
                 }
                 group_sync();
                 if (crank == 0) {
-                    const uint32_t n = gcount < (uint32_t)SMP_GATHER ? gcount : (uint32_t)SMP_GATHER;
+                    uint32_t n = gcount < (uint32_t)SMP_GATHER ? gcount : (uint32_t)SMP_GATHER;
+                    bool whole = n == a.vocab;
+                    if (n > SMP_SORT_CAP) {
+                        Reducer<1> lr{lred, nullptr, 0u};
+                        const uint32_t n2 = narrow_candidates(
+                            gbuf, n, topp ? tq : (double)(k_top < n ? k_top : (uint64_t)n), topp, lr, &ncount);
+                        whole = whole && n2 == n;
+                        n = n2;
+                    }
                     uint32_t np2 = 1;
                     while (np2 < n) np2 <<= 1;
                     for (uint32_t i = n + threadIdx.x; i < np2; i += SMP_THREADS) gbuf[i] = 0ull;
                     __syncthreads();
                     bitonic_desc(gbuf, np2);
-                    if (threadIdx.x == 0) {
-                        gresult = walk_sorted(gbuf, n, n == a.vocab, topp, a.top_k, a.top_p, a.uniforms[r]);
-                        gcount = 0;
-                    }
+                    walk_sorted_cta(gbuf, pfx, n, whole, topp, a.top_k, a.top_p, a.uniforms[r], &gresult, &wkeep,
+                                    &wr);
+                    if (threadIdx.x == 0) gcount = 0;
                 }
                 group_sync();
                 tok = *gresult0;
