@@ -506,6 +506,25 @@ __device__ __forceinline__ void load_group(const bf16_t* x, uint32_t q, uint32_t
 }
 constexpr int SMP_QB = 8;  // logit groups in flight per thread in the first pass
 
+// v[c] / d for a whole group of 4: RowDiv's paired fast path on two pairs,
+// the IEEE divide where it does not apply -- the same quotients as d(v[c]).
+__device__ __forceinline__ void div4(const RowDiv& d, float (&v)[4]) {
+    if (!d.ieee) {
+        bool redo = false;
+        const float2 q0 = d.fast2(make_float2(v[0], v[1]), redo);
+        const float2 q1 = d.fast2(make_float2(v[2], v[3]), redo);
+        if (!redo) {
+            v[0] = q0.x;
+            v[1] = q0.y;
+            v[2] = q1.x;
+            v[3] = q1.y;
+            return;
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] = __fdiv_rn(v[c], d.b);
+}
+
 template <typename T, int CL>
 __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
     pdl_begin();
@@ -559,14 +578,23 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
             for (int k = 0; k < SMP_QB; ++k) {
                 const uint32_t q = q0 + k * SMP_THREADS;
                 if (q >= row.ng) break;
+                if (4 * q + 3 < seg) {
+                    div4(div_t, v[k]);
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    if (4 * q + c < seg) {
-                        v[k][c] = div_t(v[k][c]);
+                    for (int c = 0; c < 4; ++c) {
                         nan |= v[k][c] != v[k][c];
                         mx = fmaxf(mx, v[k][c]);
-                    } else {
-                        v[k][c] = -INFINITY;
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        if (4 * q + c < seg) {
+                            v[k][c] = div_t(v[k][c]);
+                            nan |= v[k][c] != v[k][c];
+                            mx = fmaxf(mx, v[k][c]);
+                        } else {
+                            v[k][c] = -INFINITY;
+                        }
                     }
                 }
                 sp4[q] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
@@ -596,9 +624,14 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
 #pragma unroll 4
         for (uint32_t q = threadIdx.x; q < row.ng; q += SMP_THREADS) {
             float4 w = sp4[q];
-            float* v = reinterpret_cast<float*>(&w);
+            float v[4] = {w.x, w.y, w.z, w.w};
+            if (4 * q + 3 < seg) {
+                div4(div_s, v);
+            } else {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) v[c] = 4 * q + c < seg ? div_s(v[c]) : -1.0f;
+                for (int c = 0; c < 4; ++c) v[c] = 4 * q + c < seg ? div_s(v[c]) : -1.0f;
+            }
+            w = make_float4(v[0], v[1], v[2], v[3]);
             if (prow) {
                 if (vp && 4 * q + 3 < seg) {
                     reinterpret_cast<float4*>(prow)[q] = w;
@@ -616,6 +649,10 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
         // is reached by the first element, as is the smallest positive double:
         // t is raised to that.
         constexpr uint32_t top = 0x3F800001u;
+        // every probability is RN(e / S) with e <= 1 (the row max gives
+        // e = 1), so none exceeds RN(1 / S): the threshold search starts
+        // there instead of at 1
+        const uint32_t ptop = __float_as_uint(div_s(1.0f)) + 1u;
         constexpr double tiny = 4.9406564584124654e-324;
         const bool topp = a.top_p < 1.0f;
         const uint64_t k_top = a.top_k < a.vocab ? a.top_k : a.vocab;
@@ -646,11 +683,11 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
                     g = Coarse{0.0f, true, all.y, 0.0, 0.0, 0.0};
                     short_prefix = all.y <= (double)SMP_GATHER;
                 } else {
-                    g = row.template coarse<true>(tq, 0u, top, all.y, SMP_GATHER);
+                    g = row.template coarse<true>(tq, 0u, ptop, all.y, SMP_GATHER);
                     short_prefix = g.ok;
                 }
             } else {
-                g = row.template coarse<false>((double)k_top, 0u, top, (double)a.vocab, SMP_GATHER);
+                g = row.template coarse<false>((double)k_top, 0u, ptop, (double)a.vocab, SMP_GATHER);
                 short_prefix = g.ok;
             }
             const float gv = g.v;
