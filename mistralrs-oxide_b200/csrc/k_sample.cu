@@ -434,29 +434,42 @@ __device__ void walk_sorted_cta(const unsigned long long* buf, float* pfx, uint3
                                 uint64_t top_k, float top_p, float u, uint32_t* res, uint32_t* keep_s, float* r_s) {
     auto pr = [&](uint32_t i) { return __uint_as_float((uint32_t)(buf[i] >> 32)); };
     auto ix = [&](uint32_t i) { return ~(uint32_t)buf[i]; };
+    const uint32_t lim = topp ? n : (uint32_t)(top_k < n ? top_k : n);
     if (threadIdx.x == 0) {
-        uint32_t keep = 0;
-        const uint32_t lim = topp ? n : (uint32_t)(top_k < n ? top_k : n);
+        // the running sum in blocks of 32 additions without a branch; top-p
+        // stops after the block in which it reaches top_p
         float acc = 0.0f;
-        for (uint32_t i0 = 0; i0 < lim && keep == 0; i0 += 8) {
-            float v[8];
+        uint32_t i0 = 0;
+        while (i0 < lim) {
+            if (lim - i0 >= 32) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = i0 + e < lim ? pr(i0 + e) : 0.0f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                if (i0 + e < lim && keep == 0) {
-                    acc = fadd(acc, v[e]);
+                for (int e = 0; e < 32; ++e) {
+                    acc = fadd(acc, pr(i0 + e));
                     pfx[i0 + e] = acc;
-                    if (topp && acc >= top_p) keep = i0 + e + 1;
+                }
+                i0 += 32;
+            } else {
+                for (; i0 < lim; ++i0) {
+                    acc = fadd(acc, pr(i0));
+                    pfx[i0] = acc;
                 }
             }
+            if (topp && acc >= top_p) break;
         }
-        if (!topp) {
-            keep = lim;
-        } else if (keep == 0) {
-            keep = whole_row ? n : 0u;  // a whole row walks every key
-        }
-        *keep_s = keep;
+        *keep_s = topp ? (whole_row ? n : 0u) : lim;  // top-p: unless a running sum reaches top_p
+        *res = i0;                                     // prefix values computed
+    }
+    __syncthreads();
+    const uint32_t done = *res;
+    __syncthreads();
+    // top-p keeps up to the first running sum >= top_p (pfx never decreases,
+    // so exactly one index, if any, is the first to reach it)
+    if (topp)
+        for (uint32_t i = threadIdx.x; i < done; i += SMP_THREADS)
+            if (pfx[i] >= top_p && (i == 0 || pfx[i - 1] < top_p)) *keep_s = i + 1;
+    __syncthreads();
+    const uint32_t keep = *keep_s;
+    if (threadIdx.x == 0) {
         if (keep == 0) {
             *res = SMP_FALLBACK;
         } else {
@@ -465,11 +478,8 @@ __device__ void walk_sorted_cta(const unsigned long long* buf, float* pfx, uint3
         }
     }
     __syncthreads();
-    const uint32_t keep = *keep_s;
     if (keep == 0) return;
     const float r = *r_s;
-    // pfx is non-decreasing (each step adds a probability >= 0), so exactly
-    // one index (if any) is the first whose value reaches r
     for (uint32_t i = threadIdx.x; i < keep; i += SMP_THREADS)
         if (pfx[i] >= r && (i == 0 || pfx[i - 1] < r)) *res = ix(i);
     __syncthreads();
@@ -536,18 +546,16 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
     __shared__ double2 red[2 * SMP_WARPS];
     __shared__ double2 cred[2];
     __shared__ double2 lred[2 * SMP_WARPS];
-    __shared__ uint32_t gcount, gresult, wkeep, ncount;
+    __shared__ uint32_t gcount, gresult, wkeep, ncount, ccnt;
+    __shared__ uint32_t wsum[SMP_WARPS];
     __shared__ float wr;
     Reducer<CL> rd{red, cred, 0u};
     const uint32_t crank = CL == 1 ? 0u : (uint32_t)cg::this_cluster().block_rank();
-    if (threadIdx.x == 0) gcount = 0;  // visible to the cluster after the first reduction's barrier
     unsigned long long* gbuf0 = gbuf;
-    uint32_t* gcount0 = &gcount;
     uint32_t* gresult0 = &gresult;
     if (CL > 1) {
         cg::cluster_group cluster = cg::this_cluster();
         gbuf0 = cluster.map_shared_rank(gbuf, 0);
-        gcount0 = cluster.map_shared_rank(&gcount, 0);
         gresult0 = cluster.map_shared_rank(&gresult, 0);
     }
     auto group_sync = [&]() {
@@ -705,30 +713,64 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
             }
             done = false;
             if (short_prefix) {
-                // gather: one slot reservation per warp and component (most
-                // warps hold no candidate; every lane runs the same trip count)
-                const uint32_t lane = threadIdx.x & 31u;
-                const uint32_t ngr = (row.ng + SMP_THREADS - 1) / SMP_THREADS * SMP_THREADS;
-                for (uint32_t q = threadIdx.x; q < ngr; q += SMP_THREADS) {
-                    const float4 w = q < row.ng ? sp4[q] : make_float4(-1.0f, -1.0f, -1.0f, -1.0f);
+                // gather without atomics: each thread counts its candidates, a
+                // block scan gives its offset in the CTA's run, the CTAs of the
+                // cluster exchange their counts, and every thread then stores
+                // its candidates at its place in the first CTA's buffer
+                auto take = [&](float v, uint32_t i) { return v > gv || (v == gv && i <= gidx); };
+                uint32_t mine = 0;
+                for (uint32_t q = threadIdx.x; q < row.ng; q += SMP_THREADS) {
+                    const float4 w = sp4[q];
+                    const uint32_t i0 = row.base + 4 * q;
+                    mine += (uint32_t)take(w.x, i0) + (uint32_t)take(w.y, i0 + 1) + (uint32_t)take(w.z, i0 + 2) +
+                            (uint32_t)take(w.w, i0 + 3);
+                }
+                const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+                uint32_t incl = mine;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= (uint32_t)o) incl += y;
+                }
+                if (lane == 31) wsum[warp] = incl;
+                __syncthreads();
+                uint32_t off = incl - mine, ctot = 0;
+#pragma unroll
+                for (int w2 = 0; w2 < SMP_WARPS; ++w2) {
+                    const uint32_t c = wsum[w2];
+                    off += (uint32_t)w2 < warp ? c : 0u;
+                    ctot += c;
+                }
+                uint32_t base = 0, total = ctot;
+                if constexpr (CL > 1) {
+                    if (threadIdx.x == 0) ccnt = ctot;
+                    cg::cluster_group cluster = cg::this_cluster();
+                    cluster.sync();
+                    total = 0;
+#pragma unroll
+                    for (int q2 = 0; q2 < CL; ++q2) {
+                        const uint32_t c = *cluster.map_shared_rank(&ccnt, q2);
+                        base += (uint32_t)q2 < crank ? c : 0u;
+                        total += c;
+                    }
+                }
+                uint32_t pos = base + off;
+                for (uint32_t q = threadIdx.x; q < row.ng && mine != 0; q += SMP_THREADS) {
+                    const float4 w = sp4[q];
                     const float v[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         const uint32_t i = row.base + 4 * q + c;
-                        const bool take = v[c] > gv || (v[c] == gv && i <= gidx);
-                        const uint32_t m = __ballot_sync(0xffffffffu, take);
-                        if (m) {
-                            const uint32_t lead = (uint32_t)__ffs(m) - 1u;
-                            uint32_t base = 0;
-                            if (lane == lead) base = atomicAdd(gcount0, (uint32_t)__popc(m));
-                            base = __shfl_sync(0xffffffffu, base, lead);
-                            const uint32_t pos = base + (uint32_t)__popc(m & ((1u << lane) - 1u));
-                            if (take && pos < (uint32_t)SMP_GATHER)
+                        if (take(v[c], i)) {
+                            if (pos < (uint32_t)SMP_GATHER)
                                 gbuf0[pos] = ((unsigned long long)__float_as_uint(v[c]) << 32) |
                                              (unsigned long long)(~i);
+                            ++pos;
+                            --mine;
                         }
                     }
                 }
+                if (threadIdx.x == 0) gcount = total;
                 group_sync();
                 if (crank == 0) {
                     uint32_t n = gcount < (uint32_t)SMP_GATHER ? gcount : (uint32_t)SMP_GATHER;
@@ -747,7 +789,6 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
                     bitonic_desc(gbuf, np2);
                     walk_sorted_cta(gbuf, pfx, n, whole, topp, a.top_k, a.top_p, a.uniforms[r], &gresult, &wkeep,
                                     &wr);
-                    if (threadIdx.x == 0) gcount = 0;
                 }
                 group_sync();
                 tok = *gresult0;
