@@ -369,54 +369,110 @@ __device__ __forceinline__ void bitonic_desc(unsigned long long* buf, uint32_t n
 // are sorted next).  The set stays a prefix of the sorted order, so the walk
 // over it takes the same steps.  Returns the new count (n if no pivot
 // qualified).  CTA-wide: every thread of the CTA calls it.
-__device__ uint32_t narrow_candidates(unsigned long long* buf, uint32_t n, double t, bool sum, Reducer<1>& rd,
+// Block reductions of the narrowing: 32-bit counts and probability bits by
+// the warp reduction instructions, the f64 mass (top-p only) by shuffles;
+// warp partials in shared memory, double-buffered by phase so one barrier
+// per call suffices; warps combined in a fixed order (deterministic).
+struct NarrowRed {
+    uint32_t* wu;  // [2][SMP_WARPS][2]
+    double* wd;    // [2][SMP_WARPS]
+    uint32_t phase;
+    __device__ __forceinline__ uint2 run(uint32_t a, uint32_t b, double m, bool want_m, bool minmax, double& msum) {
+        if (minmax) {
+            a = __reduce_max_sync(0xffffffffu, a);
+            b = __reduce_min_sync(0xffffffffu, b);
+        } else {
+            a = __reduce_add_sync(0xffffffffu, a);
+        }
+        if (want_m) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m += __shfl_xor_sync(0xffffffffu, m, o);
+        }
+        const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+        uint32_t* su = wu + phase * SMP_WARPS * 2;
+        double* sd = wd + phase * SMP_WARPS;
+        if (lane == 0) {
+            su[2 * warp] = a;
+            su[2 * warp + 1] = b;
+            if (want_m) sd[warp] = m;
+        }
+        __syncthreads();
+        uint2 r = make_uint2(su[0], su[1]);
+        msum = want_m ? sd[0] : 0.0;
+#pragma unroll
+        for (int w = 1; w < SMP_WARPS; ++w) {
+            const uint32_t x = su[2 * w], y = su[2 * w + 1];
+            r.x = minmax ? (x > r.x ? x : r.x) : r.x + x;
+            r.y = minmax ? (y < r.y ? y : r.y) : r.y;
+            if (want_m) msum += sd[w];
+        }
+        phase ^= 1u;
+        return r;
+    }
+};
+
+// Narrows the gathered keys buf[0, n) (probability bits << 32 | ~index, a
+// prefix of the sorted order) to the keys of probability >= v for a higher
+// v the walk allows: for top-p (sum) those probabilities still sum to at
+// least t -- t carries the same margin over top_p as the first search, so
+// the reference's running sum reaches top_p inside them -- and for top-k at
+// least t of them remain, t = the walk's prefix length.  A bisection on the
+// probability bits (non-negative floats order like their bit patterns)
+// between the smallest and the largest key, one block reduction per step
+// (f64 sums, fixed order), at most SMP_NARROW_STEPS steps, stopping at the
+// first pivot that keeps at most SMP_SORT_CAP keys; the keys kept are moved
+// to the front (their order does not matter: they are sorted next).  The set
+// stays a prefix of the sorted order, so the walk over it takes the same
+// steps.  Returns the new count (n if no pivot qualified).  CTA-wide: every
+// thread of the CTA calls it.
+__device__ uint32_t narrow_candidates(unsigned long long* buf, uint32_t n, double t, bool sum, NarrowRed& rd,
                                       uint32_t* cnt) {
     constexpr int K = SMP_GATHER / SMP_THREADS;
     unsigned long long key[K];
-    float pv[K];
-    float hi_p = -1.0f, lo_p = INFINITY;
+    uint32_t pb[K];  // probability bits; keys past n get none
+    uint32_t hi_b = 0u, lo_b = 0xFFFFFFFFu;
 #pragma unroll
     for (int c = 0; c < K; ++c) {
         const uint32_t i = threadIdx.x + c * SMP_THREADS;
         key[c] = i < n ? buf[i] : 0ull;
-        pv[c] = i < n ? __uint_as_float((uint32_t)(key[c] >> 32)) : -1.0f;
+        pb[c] = (uint32_t)(key[c] >> 32);
         if (i < n) {
-            hi_p = fmaxf(hi_p, pv[c]);
-            lo_p = fminf(lo_p, pv[c]);
+            hi_b = pb[c] > hi_b ? pb[c] : hi_b;
+            lo_b = pb[c] < lo_b ? pb[c] : lo_b;
         }
     }
-    const double2 b = rd.template run<RMAX, RMIN>((double)hi_p, (double)lo_p);
-    uint32_t lo = __float_as_uint((float)b.y), hi = __float_as_uint((float)b.x) + 1u;
-    uint32_t best = lo;
-    double best_c = (double)n;
+    double unused;
+    const uint2 bb = rd.run(hi_b, lo_b, 0.0, false, true, unused);
+    uint32_t lo = bb.y, hi = bb.x + 1u;
+    uint32_t best = lo, best_c = n;
     for (int step = 0; step < SMP_NARROW_STEPS && hi - lo > 1; ++step) {
         const uint32_t mid = lo + (hi - lo) / 2;
-        const float x = __uint_as_float(mid);
-        double sm = 0.0, cn = 0.0;
+        uint32_t cn = 0;
+        double sm = 0.0;
 #pragma unroll
         for (int c = 0; c < K; ++c)
-            if (pv[c] >= x) {
-                sm += (double)pv[c];
-                cn += 1.0;
+            if (threadIdx.x + c * SMP_THREADS < n && pb[c] >= mid) {
+                ++cn;
+                if (sum) sm += (double)__uint_as_float(pb[c]);
             }
-        const double2 m = rd.template run<RSUM, RSUM>(sm, cn);
-        if ((sum ? m.x : m.y) >= t) {
+        double msum;
+        const uint32_t ct = rd.run(cn, 0u, sm, sum, false, msum).x;
+        if (sum ? msum >= t : (double)ct >= t) {
             lo = mid;
             best = mid;
-            best_c = m.y;
-            if (m.y <= (double)SMP_SORT_CAP) break;
+            best_c = ct;
+            if (ct <= SMP_SORT_CAP) break;
         } else {
             hi = mid;
         }
     }
-    if (best_c >= (double)n) return n;  // uniform: every thread saw the same reductions
+    if (best_c >= n) return n;  // uniform: every thread saw the same reductions
     // every thread holds its keys in registers; move the kept ones forward
     if (threadIdx.x == 0) *cnt = 0;
     __syncthreads();
-    const float x = __uint_as_float(best);
 #pragma unroll
     for (int c = 0; c < K; ++c)
-        if (threadIdx.x + c * SMP_THREADS < n && pv[c] >= x) buf[atomicAdd(cnt, 1u)] = key[c];
+        if (threadIdx.x + c * SMP_THREADS < n && pb[c] >= best) buf[atomicAdd(cnt, 1u)] = key[c];
     __syncthreads();
     return *cnt;
 }
@@ -545,7 +601,8 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
     float4* sp4 = reinterpret_cast<float4*>(sp);
     __shared__ double2 red[2 * SMP_WARPS];
     __shared__ double2 cred[2];
-    __shared__ double2 lred[2 * SMP_WARPS];
+    __shared__ uint32_t nred_u[2 * SMP_WARPS * 2];
+    __shared__ double nred_d[2 * SMP_WARPS];
     __shared__ uint32_t gcount, gresult, wkeep, ncount, ccnt;
     __shared__ uint32_t wsum[SMP_WARPS];
     __shared__ float wr;
@@ -776,7 +833,7 @@ __global__ void __launch_bounds__(SMP_THREADS, 1) sample_kernel(SmpArgs a) {
                     uint32_t n = gcount < (uint32_t)SMP_GATHER ? gcount : (uint32_t)SMP_GATHER;
                     bool whole = n == a.vocab;
                     if (n > SMP_SORT_CAP) {
-                        Reducer<1> lr{lred, nullptr, 0u};
+                        NarrowRed lr{nred_u, nred_d, 0u};
                         const uint32_t n2 = narrow_candidates(
                             gbuf, n, topp ? tq : (double)(k_top < n ? k_top : (uint64_t)n), topp, lr, &ncount);
                         whole = whole && n2 == n;
