@@ -92,6 +92,17 @@ def profiled_traffic(kernel: str):
     return None
 
 
+def host_threads() -> int:
+    """Host threads for the CPU legs: every core this process may run on.
+    torchrun sets OMP_NUM_THREADS=1 for its workers, so OpenMP's own default
+    would run the reference arm single-threaded under N > 1; the oracle's
+    num_threads clause takes this count instead."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def host_cpu() -> dict:
     """The box's host: logical CPUs (nproc) and the CPU model."""
     model = "unknown"
@@ -245,7 +256,7 @@ def cpu_baseline(budget_s: float = 4.0):
         dt, nbytes = cpu_step_sample(rows, 1)
         times.append(dt)
     gbs = nbytes / statistics.median(times) / 1e9
-    threads = orc.max_threads()
+    threads = host_threads()
     cpu_step_sample(8192, threads)
     tall = statistics.median([cpu_step_sample(8192, threads)[0] for _ in range(3)])
     _CPU_CACHE.clear()
@@ -279,7 +290,7 @@ def cpu_per_op() -> dict:
     from oracle import oracle as orc
     from oxide_b200.workloads import C1, C3, C4, NKV
 
-    T = orc.max_threads()
+    T = host_threads()
     res = {}
     c1 = C1()
     x, w = c1.inputs()
@@ -359,7 +370,7 @@ def cpu_chain_c5() -> dict:
         "argmax": (lambda t: orc.argmax_rows(logits, V, threads=t, out=idx), full["argmax"] * frac_rows),
         "sumsq": (lambda t: orc.reduce(2, yf, threads=t), full["sumsq"] * frac_rows),
     }
-    T_all = orc.max_threads()
+    T_all = host_threads()
     ops_out, secs1, secsa = {}, 0.0, 0.0
     for name, (fn, nbytes) in samples.items():
         t1 = cpu_time(lambda: fn(1), 0.5)
@@ -380,7 +391,7 @@ def run_reference(args):
         return
     from oracle import oracle as orc
 
-    threads = orc.max_threads()
+    threads = host_threads()
     rows = 8192
     dt, _ = cpu_step_sample(rows, threads)  # size the sample: <= ~3 s per step
     while dt > 3.0 and rows > 256:
