@@ -253,8 +253,6 @@ def add_layer_norm(x: torch.Tensor, r: torch.Tensor, w: torch.Tensor, b: torch.T
     _same_dtype("add_layer_norm", x, weight=w, bias=b)
     _out_like("add_layer_norm", x, out=out)
     _check(x, r, w, b, out)
-    if r.shape != x.shape or r.dtype != x.dtype:
-        raise OxideError(_lib.ERR_INVALID_ARG, "add_layer_norm", "residual must match the input's shape and dtype")
     if x.dim() < 1:
         raise OxideError(_lib.ERR_INVALID_ARG, "add_layer_norm", "layer_norm requires at least 1D tensor")
     cols = x.shape[-1]
