@@ -137,6 +137,9 @@ CASES = [  # (rows, vocab, temperature, top_k, top_p, logit scale)
     (64, 32000, 1.0, 50, 0.9, 3.0),        # top-p with a peaked row
     (64, 32000, 1.0, 50, 0.9, 0.5),        # top-p with a flat row: a long nucleus
     (64, 32000, 1.3, 50, 0.5, 2.0),
+    (64, 32000, 0.7, 50, 0.9, 3.0),        # the benchmark's top-p case: 500-1900 candidates narrowed in-CTA
+    (64, 32000, 1.0, 300, 1.0, 3.0),       # top-k above the narrowing's 256 cap: narrowed to >= 300 keys
+    (64, 32000, 1.5, 50, 0.99, 2.0),       # a long nucleus: the narrowing stops short of 256
     (16, 1000, 1.0, 7, 1.0, 1.0),
     (8, 32001, 1.0, 50, 0.9, 2.0),         # rows not 16-byte aligned: element loads and stores
     (8, 70000, 1.0, 50, 0.95, 2.0),        # cluster of 4 CTAs
